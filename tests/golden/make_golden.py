@@ -1,0 +1,97 @@
+"""Generate the golden fixtures in tests/golden/ from the reference itself.
+
+Run here, where the reference tree is mounted (it does not exist on the GPU
+host).  For every synthetic configuration it
+
+  1. writes the seeded HuggingFace directory (vc4b200.synth),
+  2. packs it with the reference's own packer, unchanged:
+       python engine/tools/mmcf_pack.py --in DIR --out F --quant Q --seq S
+              --rms-eps 1e-6 --template plain [--head-dedup] --verify
+  3. records the container's sha256 and size, and
+  4. loads it with the reference's own C++ loader (oracle/_ref, built from
+     engine/src/model.cpp et al. by oracle/Makefile) and records the decoded
+     summary (shapes, scales, FNV digests of every tensor's values).
+
+It also lifts the x_pack byte vectors out of engine/tests/test_xformat.cpp.
+Output: tests/golden/golden.json.
+
+    python tests/golden/make_golden.py [--ref /root/reference] [--full]
+"""
+from __future__ import annotations
+
+import argparse
+import hashlib
+import json
+import os
+import re
+import subprocess
+import sys
+import tempfile
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, os.path.join(ROOT, "vc4-gles2-inference_b200"))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+from vc4b200 import synth  # noqa: E402
+import oracle  # noqa: E402
+
+
+def xformat_vectors(ref: str) -> list:
+    """CHECK_BYTES(pack({values}, XFormat::F), bytes...) cases of test_xformat.cpp."""
+    text = open(os.path.join(ref, "engine/tests/test_xformat.cpp")).read()
+    text = re.sub(r"//[^\n]*", "", text)
+    out = []
+    for m in re.finditer(r"CHECK_BYTES\(\s*pack\(\{([^}]*)\},\s*XFormat::(\w+)\)\s*,(.*?)\);", text, re.S):
+        vals = [float(v.strip().rstrip("f")) for v in m.group(1).split(",") if v.strip()]
+        raw = [v.strip() for v in m.group(3).split(",") if v.strip()]
+        out.append({"format": m.group(2), "values": vals, "bytes": [int(b, 0) for b in raw]})
+    return out
+
+
+def pack_with_reference(ref: str, cfg: synth.Config, workdir: str) -> tuple:
+    d = os.path.join(workdir, cfg.key + "_hf")
+    synth.write_hf_dir(d, cfg)
+    out = os.path.join(workdir, cfg.key + ".mmcf")
+    cmd = [sys.executable, os.path.join(ref, "engine/tools/mmcf_pack.py"), "--in", d, "--out", out,
+           "--quant", cfg.quant, "--seq", str(cfg.seq), "--rms-eps", "1e-6", "--template", "plain",
+           "--verify"]
+    if cfg.head_dedup:
+        cmd.append("--head-dedup")
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise SystemExit("reference packer failed for %s:\n%s\n%s" % (cfg.key, r.stdout, r.stderr))
+    return out, r.stdout
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--full", action="store_true", help="also pack the five full-size configurations")
+    args = ap.parse_args()
+    subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), "ref", "REF=" + args.ref], check=True)
+    golden = {"xformat": xformat_vectors(args.ref), "containers": {}}
+    cfgs = dict(synth.TINY_CONFIGS)
+    if args.full:
+        cfgs.update({k: v for k, v in synth.CONFIGS.items() if k in ("c0", "c1", "c2", "c3", "c4")})
+    with tempfile.TemporaryDirectory() as wd:
+        for key, cfg in cfgs.items():
+            path, log = pack_with_reference(args.ref, cfg, wd)
+            data = open(path, "rb").read()
+            entry = {"sha256": hashlib.sha256(data).hexdigest(), "bytes": len(data),
+                     "packer_log": [l for l in log.splitlines() if l.startswith(("residual", "ffn hidden", "rope", "verify"))],
+                     "reference_load": oracle.ref_summary(path)}
+            golden["containers"][key] = entry
+            print(key, entry["bytes"], entry["sha256"][:16], flush=True)
+    prev = {}
+    gp = os.path.join(HERE, "golden.json")
+    if os.path.exists(gp):
+        prev = json.load(open(gp))
+    for k, v in prev.get("containers", {}).items():
+        golden["containers"].setdefault(k, v)
+    with open(gp, "w") as f:
+        json.dump(golden, f, indent=1, sort_keys=True)
+
+
+if __name__ == "__main__":
+    main()

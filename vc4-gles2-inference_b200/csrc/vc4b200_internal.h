@@ -1,0 +1,154 @@
+// vc4b200_internal.h -- shared definitions of the B200 decode engine.
+//
+// Device data layout (HBM):
+//   * A weight matrix is stored in 32-row blocks.  Inside a block the rows are
+//     interleaved at 16-byte granularity: chunk j of row (32*b + l) lives at
+//     byte ((b*nchunks + j)*32 + l)*16.  One warp-wide 16-byte load therefore
+//     reads 512 contiguous bytes, lane l getting its own row's chunk j.  A chunk
+//     is 16 q8 weights, 32 q4 weights (one scale group) or 64 t3 weights.
+//   * q8 weights are signed levels (the container's +128 bias removed).
+//   * q4 nibbles are re-paired so byte k of a 4-byte word holds column k in its
+//     low nibble and column k+4 in its high nibble; the group's int16 scale and
+//     min travel as one int32 per (row, group) in the same 32-row interleave.
+//   * t3 weights are 2-bit offset codes e = w + 1 in {0,1,2}; byte b of a
+//     32-bit word holds the codes of columns b, b+4, b+8, b+12 of a 16-column
+//     group at bits 0, 2, 4, 6, so (word >> 2i) & 0x03030303 is four
+//     consecutive columns as bytes.  The dot product subtracts sum(x) once.
+//   * Every matrix carries one float epilogue scale per row (the reference's
+//     `ws`, or (p16*ws)/65536 for a row-scaled matrix) and is padded to whole
+//     blocks and chunks with zero weights.
+//   * The KV cache keeps the reference's packed texel rows (K then V per
+//     position, q16 big-endian or q8 bytes), so MMKV1 save/restore is a copy.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+namespace vc4 {
+
+enum WType : int { W_Q8 = 0, W_Q4 = 1, W_T3 = 2, W_I16 = 3 };
+
+constexpr int kRowBlock = 32;      // rows per block (one per lane)
+constexpr int kChunkBytes = 16;    // bytes per chunk per row
+constexpr int kWarps = 8;          // warps per matvec CTA (split the chunks)
+constexpr int kLogitsGrid = 1536;  // logits tile height (logits_grid.h)
+
+inline int cols_per_chunk(int wt) { return wt == W_Q8 ? 16 : wt == W_Q4 ? 32 : 64; }
+
+// ---- host-side model (parsed container, reference semantics) -----------------
+
+struct HMat {
+    int rows = 0, cols = 0, wtype = W_Q8;
+    float scale = 1.0f;              // q8/i16 ws; t3 record scale*127; q4 ps
+    std::vector<int8_t> lev;         // q8 / t3 signed levels, rows*cols
+    std::vector<uint8_t> nib;        // q4 nibble values, rows*cols
+    std::vector<int16_t> s16, m16;   // q4 group planes, rows*groups
+    std::vector<int16_t> w16;        // i16
+    std::vector<uint16_t> p16;       // 16-bit row plane (empty: per-matrix scale)
+    std::vector<float> plane;        // container f32 plane
+    int groups() const { return cols / 32; }
+};
+
+struct HModel {
+    int version = 0, dim = 0, hidden = 0, layers = 0, heads = 0, kv_heads = 0, vocab = 0, seq = 0;
+    int head_dim = 0, kv_dim = 0, experts = 0, moe_hidden = 0;
+    bool qk_norm = false, rope_half = false, head_dedup = false;
+    float rope_theta = 10000.0f, rms_eps = 1e-5f;
+    std::vector<float> rope_factors;
+    std::vector<uint8_t> hid_scale;
+    uint64_t source_size = 0, source_mtime = 0;
+    std::vector<int8_t> emb;          // vocab*dim signed levels
+    std::vector<float> emb_scale;     // vocab
+    std::vector<float> rms_att, rms_ffn, rms_final, q_norm, k_norm;
+    std::vector<HMat> qkv, wo, w1, w3, w2, router;
+    std::vector<HMat> moe;            // [layer*experts + e]*3: w1, w3, w2
+    std::vector<HMat> tiles;
+    int ffn_width() const { return experts ? moe_hidden : hidden; }
+};
+
+// Parse an MMCF v2/v3 container (returns "" or an error message).
+std::string load_mmcf(const std::string& path, HModel& m);
+std::string load_mmcf_bytes(const uint8_t* data, size_t size, HModel& m);
+
+// ---- device-side model ------------------------------------------------------
+
+struct DMat {
+    int rows = 0, cols = 0, wtype = W_Q8;
+    int rblocks = 0, nchunks = 0;    // padded geometry
+    uint8_t* body = nullptr;         // rblocks*nchunks*32*16 bytes
+    float* rscale = nullptr;         // rblocks*32 epilogue scales
+    int32_t* q4p = nullptr;          // q4: rblocks*nchunks*32 packed (s16 | m16<<16)
+    int16_t* w16 = nullptr;          // i16 router, row-major
+    size_t bytes() const { return (size_t)rblocks * nchunks * 512 + (q4p ? (size_t)rblocks * nchunks * 128 : 0); }
+};
+
+struct DLayer {
+    DMat qkv, wo, w1, w3, w2a, w2b, router;   // w2b empty when the FFN is one chunk
+    DMat* ew1 = nullptr;                      // MoE: per-expert arrays (device copies of DMat)
+};
+
+struct DModel {
+    HModel h;                        // dims and host copies of small tensors (weights dropped)
+    int ffn_width = 0, ffn_chunk = 0;
+    bool ffn_chunked = false;
+    int wtype = W_Q8;
+    std::vector<DMat> mats;          // every matrix, owning
+    std::vector<int> qkv, wo, w1, w3, w2a, w2b, router;   // per layer: index into mats
+    std::vector<int> e_w1, e_w3, e_w2a, e_w2b;            // [layer*experts + e]
+    int emb_mat = -1, logits_mat = -1;
+    float* d_emb_scale = nullptr;
+    float *d_rms_att = nullptr, *d_rms_ffn = nullptr, *d_rms_final = nullptr;
+    float *d_q_norm = nullptr, *d_k_norm = nullptr;
+    DMat* d_mats = nullptr;          // device array mirror of `mats` (for kernels that pick experts)
+    size_t weight_bytes = 0;
+    int device = 0;
+};
+
+std::string upload_model(const HModel& h, DModel& d);
+void free_model(DModel& d);
+
+// ---- per-launch parameter blocks -------------------------------------------------
+
+// The step's batch: n sequences, each with its slot (KV cache / state index),
+// token id and position.  All arrays live on the device.
+struct Batch {
+    int n = 0;
+    const int* slot = nullptr;
+    const int* token = nullptr;
+    const int* pos = nullptr;
+};
+
+struct State {                      // per-slot activations, [slot][...]
+    int16_t* x = nullptr;            // residual, q16 ints [slots][dim]
+    int16_t* x1 = nullptr;           // residual after attention
+    float* qkv = nullptr;            // matvec_s output [slots][dim+2kv]
+    int16_t* att = nullptr;          // attention output, q16 [slots][dim]
+    int16_t* h = nullptr;            // SwiGLU hidden, q16 [slots][ffn]
+    int32_t* logits = nullptr;       // q16 ints [slots][vocab]
+    unsigned long long* best = nullptr;   // packed argmax key [slots]
+    int* next = nullptr;             // greedy token [slots]
+    int* route = nullptr;            // MoE expert [slots][layers]
+    uint8_t* kv = nullptr;           // [slots][layers][seq][row_bytes]
+    int kv_bits = 16, row_bytes = 0, seq = 0, slots = 0;
+    float* rope_cos = nullptr;       // [seq][head_dim/2]
+    float* rope_sin = nullptr;
+};
+
+// Kernel launchers (kernels.cu).  All enqueue on `st`; none synchronises.
+void launch_embed_qkv(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st);
+void launch_attention(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st);
+void launch_wo(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st);
+void launch_ffn_gate(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st);
+void launch_ffn_down(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st);
+void launch_logits(const DModel& m, const State& s, const Batch& b, cudaStream_t st);
+// A bare matvec of one model matrix over q16 inputs (the CPU-path entry,
+// GPU::matvec_s): xq are already scaled ints, out receives clamped q16 ints.
+void launch_matvec_raw(const DModel& m, int mat, const int16_t* xq, int n, int32_t* out, cudaStream_t st);
+
+int kernel_launches_per_step(const DModel& m);
+
+}  // namespace vc4
