@@ -1,0 +1,140 @@
+/*
+ * vc4b200.h -- C ABI of the B200 quantized decode engine.
+ *
+ * The reference engine has no plugin or FFI layer: its decode path sits
+ * behind the C++ class `GPU` (engine/src/gpu.h:41-633) as driven by
+ * `Session` (engine/src/session.h:28-93).  These entry points are what that
+ * class and the layer loop call, expressed as plain C: opaque handles,
+ * pointers and sizes, int status codes (0 = OK) and a thread-local message.
+ * Every entry point names the reference interface it replaces.
+ *
+ * Numerics: the reference CPU layer loop (session.cpp:373-556) with the
+ * shader arithmetic of each matrix it draws and the packed KV codec; all
+ * weight x activation products are exact integers.  Logits are on the q16
+ * grid (1/256).
+ */
+#ifndef VC4B200_H
+#define VC4B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define VC4_API __attribute__((visibility("default")))
+#else
+#define VC4_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define VC4_OK 0
+#define VC4_EINVAL 1      /* bad argument (shape, slot, position, kv axis) */
+#define VC4_EFORMAT 2     /* container refused (bad or unsupported file)    */
+#define VC4_ECUDA 3       /* a CUDA call failed                             */
+#define VC4_EIO 4         /* file I/O                                       */
+#define VC4_ESTATE 5      /* wrong call order / mismatched cache            */
+
+typedef struct vc4_gpu vc4_gpu;         /* device + stream (class GPU)            */
+typedef struct vc4_model vc4_model;     /* uploaded weights (Model + GPU::upload) */
+typedef struct vc4_session vc4_session; /* KV cache + activations, N slots        */
+
+typedef struct {
+    int dim, hidden, layers, heads, kv_heads, vocab, seq, head_dim, kv_dim;
+    int experts, moe_hidden, ffn_width, ffn_chunked, ffn_chunk;
+    int qk_norm, rope_half, head_dedup, wtype; /* wtype: 0 q8, 1 q4, 2 t3 */
+    float rope_theta, rms_eps;
+    uint64_t weight_bytes;                     /* device bytes of all matrices */
+    uint64_t source_size, source_mtime;        /* container identity (MMKV1)   */
+} vc4_model_info;
+
+/* Message of the last failed call on this thread ("" when none). */
+VC4_API const char* vc4_last_error(void);
+
+/* GPU::GPU() / ~GPU (gpu.cpp:31-42): bind a CUDA device, create the stream. */
+VC4_API int vc4_gpu_create(int device, vc4_gpu** out);
+VC4_API void vc4_gpu_destroy(vc4_gpu* g);
+/* GPU::sync (gpu.cpp:53): wait for all queued work. */
+VC4_API int vc4_gpu_sync(vc4_gpu* g);
+
+/* Model::load (model.cpp:23) + GPU::upload for every matrix
+   (gpu_upload.cpp:20-192): parse the MMCF container, re-lay the quantised
+   blocks into the device layout and copy them to HBM. */
+VC4_API int vc4_model_load(vc4_gpu* g, const char* mmcf_path, vc4_model** out);
+VC4_API int vc4_model_load_bytes(vc4_gpu* g, const void* data, size_t size, vc4_model** out);
+VC4_API int vc4_model_info_get(const vc4_model* m, vc4_model_info* out);
+VC4_API void vc4_model_free(vc4_model* m);
+
+/* Session::reset's device half: GPU::init_attention (gpu_attn.cpp:41-157)
+   with the KV axis (kv_bits 16 = q16 grid 1/2048, 8 = q8 grid 1/16) and
+   GPU::init_persistent (gpu_upload.cpp:196-220).  rope_cos / rope_sin are the
+   caller's tables, seq x head_dim/2 floats (session.cpp:188-202; see
+   vc4_rope_tables); NULL builds them from the container's theta.  A session
+   holds `slots` independent sequences (the reference has one). */
+VC4_API int vc4_session_create(vc4_model* m, int slots, int seq, int kv_bits,
+                       const float* rope_cos, const float* rope_sin, vc4_session** out);
+VC4_API void vc4_session_destroy(vc4_session* s);
+
+/* The rope tables exactly as Session::reset builds them (session.cpp:188-202). */
+VC4_API void vc4_rope_tables(float theta, int head_dim, int seq, const float* factors,
+                     float* cos_out, float* sin_out);
+
+/* Session::step (session.cpp:1797-1821) for one slot: run `token` at `pos`
+   through every layer; when logits is not NULL copy the vocab q16 logits
+   (as floats, value/256) to it.  Synchronous. */
+VC4_API int vc4_step(vc4_session* s, int slot, int token, int pos, float* logits);
+/* Session::step_greedy (session.cpp:1827-1842): same pass, returns the
+   first-maximum token (sampling.cpp:160-162). */
+VC4_API int vc4_step_greedy(vc4_session* s, int slot, int token, int pos, int* next_token);
+/* Batched decode (new for this tier; the reference has no multi-sequence
+   API): n sequences, each (slot, token, pos), host arrays.  next_tokens (n)
+   and logits (n*vocab floats) may be NULL.  Synchronous. */
+VC4_API int vc4_step_batch(vc4_session* s, int n, const int* slots, const int* tokens, const int* pos,
+                   int* next_tokens, float* logits);
+/* Device-resident form for benchmarking: the three int arrays live on the
+   device; the pass is enqueued on the session stream (replayed from a CUDA
+   graph) and returns without synchronising.  next_tokens (device, n) receives
+   the greedy tokens; when `advance` is nonzero tokens[i] becomes the greedy
+   token and pos[i] is incremented, so repeated calls decode autonomously. */
+VC4_API int vc4_step_batch_device(vc4_session* s, int n, const int* d_slots, int* d_tokens, int* d_pos,
+                          int* d_next_tokens, int advance);
+/* The session's CUDA stream (cudaStream_t), for event timing. */
+VC4_API void* vc4_session_stream(vc4_session* s);
+
+/* Prefill of a prompt on one slot: positions pos0 .. pos0+n-1 run in order
+   (the serial prompt loop, chat.cpp:245-297); the logits of the last position
+   are returned when logits is not NULL. */
+VC4_API int vc4_prefill(vc4_session* s, int slot, const int* tokens, int n, int pos0, float* logits);
+
+/* KV rows of one layer in the MMKV1 texel layout (the bytes
+   prefix_cache.cpp:59-67 reads with glReadPixels and 176-189 writes with
+   glTexSubImage2D): n rows of vc4_kv_row_bytes() each. */
+VC4_API int vc4_kv_row_bytes(const vc4_session* s);
+VC4_API int vc4_kv_read_rows(vc4_session* s, int slot, int layer, int n, void* host_out);
+VC4_API int vc4_kv_write_rows(vc4_session* s, int slot, int layer, int n, const void* host_in);
+
+/* Session::save_prefix_cache / load_prefix_cache (prefix_cache.cpp:25-207):
+   the MMKV1 file (version 2) plus its .json sidecar.  load validates the
+   header against the model and the KV axis and returns the token list. */
+VC4_API int vc4_save_prefix_cache(vc4_session* s, int slot, const char* path, const int* toks, int n,
+                          uint64_t system_fnv, uint64_t tools_fnv);
+VC4_API int vc4_load_prefix_cache(vc4_session* s, int slot, const char* path, int* toks_out, int cap,
+                          int* n_out);
+
+/* GPU::matvec_s (gpu_conv.cpp:271-287), the CPU path's matvec: x (host
+   floats, cols) is scaled by 2^k, quantised to q16, multiplied by one model
+   matrix and read back as floats.  which: 0 qkv, 1 wo, 2 w1, 3 w3, 4 w2,
+   5 router, 6 logits; expert selects an MoE expert. */
+VC4_API int vc4_matvec_s(vc4_model* m, int which, int layer, int expert, const float* x, float* out);
+
+/* draws()/syncs() (gpu.h:44-48): kernels launched and host syncs so far. */
+VC4_API int vc4_counters(const vc4_session* s, long long* launches, long long* syncs);
+/* Kernels one decode pass of n sequences launches. */
+VC4_API int vc4_launches_per_step(const vc4_session* s, int n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -16,6 +16,8 @@
 #include "vc4b200_internal.h"
 
 #include <cstdio>
+#include <map>
+#include <utility>
 
 namespace vc4 {
 namespace {
@@ -319,8 +321,9 @@ __host__ size_t smem_bytes(int nb, int stride, int gstride, int tmp_n) {
            (sizeof(int) * nb * gstride + 15) / 16 * 16 + 2 * (size_t)nb * stride + sizeof(int16_t) * (size_t)tmp_n;
 }
 
-inline int x_stride(const DMat& W) { return W.nchunks * cols_per_chunk(W.wtype); }
-inline int g_stride(const DMat& W) { return W.wtype == W_Q4 ? W.nchunks : 1; }
+__host__ __device__ inline int cpc_of(int wt) { return wt == W_Q8 ? 16 : wt == W_Q4 ? 32 : 64; }
+__host__ __device__ inline int x_stride(const DMat& W) { return W.nchunks * cpc_of(W.wtype); }
+__host__ __device__ inline int g_stride(const DMat& W) { return W.wtype == W_Q4 ? W.nchunks : 1; }
 
 // ---------------------------------------------------------------------------
 // Kernel parameter blocks
@@ -451,7 +454,8 @@ __device__ int route_of(const int16_t* xbf, const DMat& R, int D, int experts, R
 
 template <int WT, int NB>
 __global__ void __launch_bounds__(kThreads) k_gate(const DMat* mats, int i_w1, int i_w3, int i_router, int e_base,
-                                                   const float* rms_w, State s, Batch bt, Dims d, int layer, int b0) {
+                                                   const float* rms_w, State s, Batch bt, Dims d, int layer, int b0,
+                                                   int hs) {
     // MoE: blockIdx.y is the expert; the CTA serves the inputs routed to it.
     const int expert = blockIdx.y;
     const DMat& W1 = mats[d.experts ? e_base + expert * 4 + 0 : i_w1];
@@ -491,8 +495,7 @@ __global__ void __launch_bounds__(kThreads) k_gate(const DMat* mats, int i_w1, i
             const int g = mv_epi(t1 - corr, W1.rscale[row]);
             const int u = mv_epi(t3 - corr, W3.rscale[row]);
             float y = swiglu1(__fmul_rn((float)g, 1.0f / 256.0f), __fmul_rn((float)u, 1.0f / 256.0f));
-            const int hs = d.experts ? 0 : 0;
-            (void)hs;
+            if (hs > 0) y = __fmul_rn(y, ldexpf(1.0f, -hs));     // metadata key 15 store scale
             s.h[(size_t)slot * d.ffn + row] = (int16_t)q16s(y);
         }
     }
@@ -621,7 +624,7 @@ __global__ void __launch_bounds__(kThreads) k_attn(const float* q_norm, const fl
     float* kvv = qv + group * hd;                                // 2*hd (k, v)
     float* tile = kvv + 2 * hd;                                  // kTile*hp
     float* sc = tile + kTile * hp;                               // group*seq
-    double* pv = reinterpret_cast<double*>(sc + (((size_t)group * d.seq + 1) & ~(size_t)1));   // kWarps*group*hd
+    double* pv = reinterpret_cast<double*>(((uintptr_t)(sc + (size_t)group * d.seq) + 15) & ~(uintptr_t)15);
     const float* qkv = s.qkv + (size_t)slot * (d.dim + 2 * d.kv_dim);
     for (int i = threadIdx.x; i < group * hd; i += blockDim.x) qv[i] = qkv[g * group * hd + i];
     for (int i = threadIdx.x; i < hd; i += blockDim.x) {
@@ -685,7 +688,6 @@ __global__ void __launch_bounds__(kThreads) k_attn(const float* q_norm, const fl
     const int vofs = d.kv_bits == 16 ? 2 * d.kv_dim : d.kv_dim;   // V starts here in a row
     const float sq = __fsqrt_rn((float)hd);
     // scores: one thread per position, sequential fp32 dot (session.cpp:2031-2036)
-    float mxl = -1e30f;
     for (int t0 = 0; t0 <= pos; t0 += kTile) {
         const int nt = min(kTile, pos + 1 - t0);
         for (int e = threadIdx.x; e < nt * hd; e += blockDim.x) {
@@ -722,7 +724,6 @@ __global__ void __launch_bounds__(kThreads) k_attn(const float* q_norm, const fl
         for (int t = threadIdx.x; t <= pos; t += blockDim.x) S[t] = __fdiv_rn(S[t], fs);
         __syncthreads();
     }
-    (void)mxl;
     // P.V in double: warp w takes positions w, w+8, ..; lanes take dims.
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int nd = (hd + 31) / 32;
@@ -782,13 +783,46 @@ __global__ void __launch_bounds__(kThreads) k_raw(DMat W, const int16_t* xq, int
     }
 }
 
+// i16 matrix (the MoE router, shaders.cpp:1216-1230): one block per row.
+__global__ void __launch_bounds__(kThreads) k_raw_i16(DMat W, const int16_t* xq, int n, int32_t* out) {
+    __shared__ Red red;
+    const int row = blockIdx.x;
+    long long acc = 0;
+    for (int c = threadIdx.x; c < n; c += blockDim.x) acc += (long long)W.w16[(size_t)row * n + c] * xq[c];
+    acc = block_sum_i64(acc, red);
+    if (threadIdx.x == 0) out[row] = mv_epi(acc, W.rscale[row]);
+}
+
+// Greedy token of each sequence from its packed argmax key; optionally
+// advance the sequence (next token, position + 1).
+__global__ void k_finalize(State s, Batch bt, int* next, int* tokens, int* pos, int advance, const int* forced) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= bt.n) return;
+    const unsigned long long key = s.best[bt.slot[b]];
+    const int tok = (int)(0xFFFFFFFFu - (unsigned)(key & 0xFFFFFFFFull));
+    next[b] = tok;
+    if (advance) {
+        const int p = pos[b] + 1;
+        tokens[b] = forced ? forced[p < s.seq ? p : s.seq - 1] : tok;
+        pos[b] = p;
+    }
+}
+
 // ---------------------------------------------------------------------------
 // launch helpers
 // ---------------------------------------------------------------------------
 
+// Raise a kernel's dynamic shared memory limit once per size; repeated calls
+// (and calls during graph capture) are no-ops.
 template <typename K>
 void set_smem(K kernel, size_t bytes) {
-    if (bytes > 48 * 1024) cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    static std::map<std::pair<const void*, int>, size_t> done;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    size_t& have = done[{(const void*)kernel, dev}];
+    if (bytes <= 48 * 1024 || bytes <= have) return;
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    have = bytes;
 }
 
 constexpr int kNB = 4;   // inputs per CTA for the batched matvecs
@@ -824,7 +858,8 @@ void gate_t(const DModel& m, const State& s, const Batch& bt, int layer, cudaStr
     for (int b0 = 0; b0 < bt.n; b0 += kNB)
         k_gate<WT, kNB><<<grid, kThreads, sm, st>>>(m.d_mats, d.experts ? 0 : m.w1[layer], d.experts ? 0 : m.w3[layer],
                                                      d.experts ? m.router[layer] : 0, ebase,
-                                                     m.d_rms_ffn + (size_t)layer * d.dim, s, bt, d, layer, b0);
+                                                     m.d_rms_ffn + (size_t)layer * d.dim, s, bt, d, layer, b0,
+                                                     layer < (int)m.h.hid_scale.size() ? (int)m.h.hid_scale[layer] : 0);
 }
 
 template <int WT>
@@ -885,20 +920,29 @@ void launch_attention(const DModel& m, const State& s, const Batch& b, int layer
     Dims d = dims_of(m, s);
     const int group = d.heads / d.kv_heads, hd = d.head_dim;
     const size_t sm = 128 + sizeof(float) * ((size_t)group * hd + 2 * hd + (size_t)kTile * (hd + 1) +
-                                             (((size_t)group * d.seq + 1) & ~(size_t)1)) +
-                      sizeof(double) * (size_t)kWarps * group * hd + 64;
+                                             (size_t)group * d.seq) +
+                      16 + sizeof(double) * (size_t)kWarps * group * hd;
     set_smem(k_attn, sm);
     k_attn<<<dim3(d.kv_heads, b.n), kThreads, sm, st>>>(m.d_q_norm, m.d_k_norm, s, b, d, layer);
 }
 
 void launch_matvec_raw(const DModel& m, int mat, const int16_t* xq, int n, int32_t* out, cudaStream_t st) {
     const DMat& W = m.mats[mat];
+    if (W.wtype == W_I16) { k_raw_i16<<<W.rows, kThreads, 0, st>>>(W, xq, n, out); return; }
     const size_t sm = smem_bytes(1, x_stride(W), g_stride(W), 0);
     if (W.wtype == W_Q8) { set_smem(k_raw<W_Q8>, sm); k_raw<W_Q8><<<W.rblocks, kThreads, sm, st>>>(W, xq, n, out); }
     else if (W.wtype == W_Q4) { set_smem(k_raw<W_Q4>, sm); k_raw<W_Q4><<<W.rblocks, kThreads, sm, st>>>(W, xq, n, out); }
     else { set_smem(k_raw<W_T3>, sm); k_raw<W_T3><<<W.rblocks, kThreads, sm, st>>>(W, xq, n, out); }
 }
 
-int kernel_launches_per_step(const DModel& m) { return 5 * m.h.layers + 1; }
+void launch_finalize(const State& s, const Batch& b, int* next, int* tokens, int* pos, int advance,
+                     const int* forced, cudaStream_t st) {
+    k_finalize<<<(b.n + 127) / 128, 128, 0, st>>>(s, b, next, tokens, pos, advance, forced);
+}
+
+int kernel_launches_per_step(const DModel& m, int n) {
+    const int g = (n + kNB - 1) / kNB;
+    return m.h.layers * (4 * g + 1) + g + 1;
+}
 
 }  // namespace vc4

@@ -86,11 +86,6 @@ struct DMat {
     size_t bytes() const { return (size_t)rblocks * nchunks * 512 + (q4p ? (size_t)rblocks * nchunks * 128 : 0); }
 };
 
-struct DLayer {
-    DMat qkv, wo, w1, w3, w2a, w2b, router;   // w2b empty when the FFN is one chunk
-    DMat* ew1 = nullptr;                      // MoE: per-expert arrays (device copies of DMat)
-};
-
 struct DModel {
     HModel h;                        // dims and host copies of small tensors (weights dropped)
     int ffn_width = 0, ffn_chunk = 0;
@@ -98,7 +93,8 @@ struct DModel {
     int wtype = W_Q8;
     std::vector<DMat> mats;          // every matrix, owning
     std::vector<int> qkv, wo, w1, w3, w2a, w2b, router;   // per layer: index into mats
-    std::vector<int> e_w1, e_w3, e_w2a, e_w2b;            // [layer*experts + e]
+    std::vector<int> e_w1, e_w3, e_w2a, e_w2b;            // [layer*experts + e]; the four
+                                                          // matrices of an expert are consecutive
     int emb_mat = -1, logits_mat = -1;
     float* d_emb_scale = nullptr;
     float *d_rms_att = nullptr, *d_rms_ffn = nullptr, *d_rms_final = nullptr;
@@ -106,9 +102,10 @@ struct DModel {
     DMat* d_mats = nullptr;          // device array mirror of `mats` (for kernels that pick experts)
     size_t weight_bytes = 0;
     int device = 0;
+    std::vector<void*> allocs;     // every device allocation of the model
 };
 
-std::string upload_model(const HModel& h, DModel& d);
+std::string upload_model(HModel&& h, DModel& d);
 void free_model(DModel& d);
 
 // ---- per-launch parameter blocks -------------------------------------------------
@@ -148,7 +145,12 @@ void launch_logits(const DModel& m, const State& s, const Batch& b, cudaStream_t
 // A bare matvec of one model matrix over q16 inputs (the CPU-path entry,
 // GPU::matvec_s): xq are already scaled ints, out receives clamped q16 ints.
 void launch_matvec_raw(const DModel& m, int mat, const int16_t* xq, int n, int32_t* out, cudaStream_t st);
+// Greedy token from the packed argmax key; with `advance` the batch's token
+// becomes that token and its position moves on by one.
+// `forced` (indexed by position) replaces the greedy token during a prefill.
+void launch_finalize(const State& s, const Batch& b, int* next, int* tokens, int* pos, int advance,
+                     const int* forced, cudaStream_t st);
 
-int kernel_launches_per_step(const DModel& m);
+int kernel_launches_per_step(const DModel& m, int n);
 
 }  // namespace vc4
