@@ -604,6 +604,7 @@ __global__ void __launch_bounds__(kThreads) k_logits(DMat W, const float* rms_w,
 // ---------------------------------------------------------------------------
 
 constexpr int kTile = 128;   // positions per staged K/V tile
+constexpr int kRedBytes = (int)((sizeof(Red) + 15) / 16 * 16);
 
 __device__ __forceinline__ float kv_decode(const uint8_t* row, int i, int kv_bits) {
     if (kv_bits == 16) {
@@ -620,7 +621,7 @@ __global__ void __launch_bounds__(kThreads) k_attn(const float* q_norm, const fl
     const int hd = d.head_dim, group = d.heads / d.kv_heads, half = hd / 2;
     const int hp = hd + 1;                     // padded tile stride (floats)
     Red* red = reinterpret_cast<Red*>(smem);
-    float* qv = reinterpret_cast<float*>(smem + 128);          // group*hd
+    float* qv = reinterpret_cast<float*>(smem + kRedBytes);    // group*hd
     float* kvv = qv + group * hd;                                // 2*hd (k, v)
     float* tile = kvv + 2 * hd;                                  // kTile*hp
     float* sc = tile + kTile * hp;                               // group*seq
@@ -919,7 +920,7 @@ void launch_logits(const DModel& m, const State& s, const Batch& b, cudaStream_t
 void launch_attention(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st) {
     Dims d = dims_of(m, s);
     const int group = d.heads / d.kv_heads, hd = d.head_dim;
-    const size_t sm = 128 + sizeof(float) * ((size_t)group * hd + 2 * hd + (size_t)kTile * (hd + 1) +
+    const size_t sm = kRedBytes + sizeof(float) * ((size_t)group * hd + 2 * hd + (size_t)kTile * (hd + 1) +
                                              (size_t)group * d.seq) +
                       16 + sizeof(double) * (size_t)kWarps * group * hd;
     set_smem(k_attn, sm);
