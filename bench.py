@@ -1,0 +1,389 @@
+#!/usr/bin/env python
+"""Decode benchmark of the B200 quantized decode path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c1] [--impl ours|reference]
+
+One step = one greedy decode pass of every sequence of the configuration's
+batch (batch 1 for the default workload).  The default workload is BASELINE's
+MiniMind3-64M shaped, q4, batch 1, KV q16, SEQ 256, a 128-token
+seeded prompt (prefilled, untimed) then greedy decode.  Weights and prompts are
+seeded synthetic data of that shape, packed into an MMCF container byte-equal
+to the reference packer's output (sha256 checked against
+tests/golden/golden.json).
+
+`value` times K device-resident decode steps (inputs already in HBM, one CUDA
+graph replay each, L2 flushed between steps), `e2e` times K steps through the
+public API with host buffers (token/position in, greedy token out).  For N > 1
+every rank runs its own replica ("replicas only": the batch-1 path does not
+shard) and the time is the max over ranks.  `--impl reference` times the
+reference arithmetic on the host cores instead: the CPU restatement in
+oracle/ (the reference has no CPU engine; its GL path cannot run here).
+"""
+from __future__ import annotations
+
+import argparse
+import hashlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "vc4-gles2-inference_b200")
+for _p in (PKG, os.path.join(ROOT, "oracle")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "decode tokens/s per GPU and per box (1/2/4/8)"
+KV_NAME = {16: "q16", 8: "q8"}
+OPS = ["qkv", "attention", "wo", "ffn_gate", "ffn_down", "logits"]
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="c1")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="bounded CPU baseline sample")
+    return ap.parse_args()
+
+
+def model_path(cfg) -> str:
+    """The configuration's container, written once per host and verified
+    against the reference packer's sha256."""
+    from vc4b200 import mmcf_writer
+    d = os.path.join(tempfile.gettempdir(), "vc4b200_models")
+    os.makedirs(d, exist_ok=True)
+    path = os.path.join(d, "%s_%d.mmcf" % (cfg.key, cfg.seed))
+    want = None
+    try:
+        with open(os.path.join(ROOT, "tests", "golden", "golden.json")) as f:
+            want = json.load(f)["containers"].get(cfg.key, {}).get("sha256")
+    except OSError:
+        pass
+    if os.path.exists(path):
+        return path
+    data = mmcf_writer.pack_config(cfg)
+    if want and hashlib.sha256(data).hexdigest() != want:
+        raise SystemExit("container for %s does not match the reference packer's bytes" % cfg.key)
+    tmp = path + ".%d.tmp" % os.getpid()
+    with open(tmp, "wb") as f:
+        f.write(data)
+    os.replace(tmp, path)
+    return path
+
+
+def workload_desc(cfg) -> str:
+    s = cfg.shape
+    return ("%s: %s %s, batch %d, KV %s, SEQ %d, %d-token seeded prompt then greedy decode"
+            % (cfg.key, s.name, cfg.quant, cfg.batch, KV_NAME[cfg.kv_bits], cfg.seq, cfg.prompt))
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+
+class Clocks:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "--query-gpu=" + self.Q, "--format=csv,noheader,nounits",
+                                       "-lms", "200", "-i", str(device)], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self) -> dict:
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+        self.f.flush()
+        self.f.seek(0)
+        rows = [l.split(",") for l in self.f.read().splitlines() if l.strip()]
+        os.unlink(self.f.name)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+                for i, n in enumerate(names):
+                    if r[5 + i].strip().lower() == "active":
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                continue
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing (one process per GPU, no data-path collective)
+# ---------------------------------------------------------------------------
+
+class Dist:
+    def __init__(self, want: int):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+        if self.world > 1:
+            import datetime
+            import torch
+            import torch.distributed as dist
+            torch.cuda.set_device(self.local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", self.local))
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg:
+            self.pg.barrier()
+
+    def max(self, v: float) -> float:
+        if not self.pg:
+            return v
+        import torch
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# the reference arithmetic on the host cores (oracle/)
+# ---------------------------------------------------------------------------
+
+def cpu_decode_rate(cfg, path, steps: int, seconds: float, threads: int) -> dict:
+    """Greedy decode through the CPU restatement: prompt prefilled (untimed),
+    then up to `steps` decode passes or `seconds` of decode, whichever first."""
+    os.environ["OMP_NUM_THREADS"] = str(threads)
+    import oracle
+    from vc4b200 import synth
+    om = oracle.Model(path)
+    seqs = max(1, min(cfg.batch, 2))
+    tokens_done, t_total = 0, 0.0
+    for si in range(seqs):
+        prompt = synth.prompt_tokens(cfg, si)
+        s = oracle.Session(om, cfg.kv_bits)
+        for p, t in enumerate(prompt[:-1]):
+            s.step(t, p, want_logits=False)
+        tok, pos = prompt[-1], len(prompt) - 1
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            lg = s.step(tok, pos)
+            tok = oracle.argmax(lg)
+            pos += 1
+            tokens_done += 1
+            if pos >= cfg.seq or time.perf_counter() - t0 > seconds / seqs:
+                break
+        t_total += time.perf_counter() - t0
+        s.close()
+    return {"value": tokens_done / t_total, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": "%d greedy decode steps of %d sequence(s) after a %d-token prompt (prompt untimed), "
+                      "oracle/ C restatement, OpenMP over matrix rows" % (tokens_done, seqs, cfg.prompt)}
+
+
+def run_reference(args, cfg, dist):
+    if dist.rank != 0:
+        return
+    path = model_path(cfg)
+    threads = os.cpu_count() or 1
+    r = cpu_decode_rate(cfg, path, max(1, args.steps + args.warmup), 10 * args.cpu_seconds, threads)
+    line = {"metric": METRIC, "value": r["value"], "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000.0 / r["value"] * cfg.batch, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int64 (exact integer dot), f32/f64 epilogues",
+            "data": "synthetic (seeded weights and prompts of the configuration's shape)",
+            "config": {"workload": workload_desc(cfg), "impl_note": "reference arithmetic on host cores"},
+            "impl": "reference", "cpu_baseline": r,
+            "e2e": {"value": r["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# the B200 path
+# ---------------------------------------------------------------------------
+
+def run_ours(args, cfg, dist):
+    import numpy as np
+    import torch
+    import vc4b200
+    from vc4b200 import synth
+
+    dev = dist.local
+    torch.cuda.set_device(dev)
+    path = model_path(cfg)
+    gpu = vc4b200.GPU(dev)
+    model = vc4b200.Model(gpu, path)
+    B = cfg.batch
+    sess = vc4b200.Session(model, slots=B, seq=cfg.seq, kv=KV_NAME[cfg.kv_bits])
+    info = model.info
+    prompts = [synth.prompt_tokens(cfg, dist.rank * B + b) for b in range(B)]
+    t0 = time.perf_counter()
+    for b in range(B):
+        sess.prefill(prompts[b][:-1], 0, slot=b, want_logits=False)
+    prefill_s = time.perf_counter() - t0
+    P = cfg.prompt
+    stream = torch.cuda.ExternalStream(sess.stream())
+    d_slots = torch.arange(B, dtype=torch.int32, device="cuda")
+    d_tok = torch.tensor([p[-1] for p in prompts], dtype=torch.int32, device="cuda")
+    d_pos = torch.full((B,), P - 1, dtype=torch.int32, device="cuda")
+    d_next = torch.zeros(B, dtype=torch.int32, device="cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()
+    pos_now = [P - 1]
+
+    def wrap_positions():
+        # positions cycle within [P-1, seq): restart from the prompt's end
+        if pos_now[0] >= cfg.seq:
+            with torch.cuda.stream(stream):
+                d_tok.copy_(torch.tensor([p[-1] for p in prompts], dtype=torch.int32))
+                d_pos.fill_(P - 1)
+            pos_now[0] = P - 1
+
+    def step():
+        wrap_positions()
+        sess.step_batch_device(B, d_slots.data_ptr(), d_tok.data_ptr(), d_pos.data_ptr(), d_next.data_ptr(), True)
+        pos_now[0] += 1
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    l0, _ = sess.counters()
+    clocks = Clocks(dev)
+    dist.barrier()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for i in range(args.steps):
+            flush.fill_(i & 0xFF)                 # L2 flush between steps (outside the events)
+            ev[i][0].record(stream)
+            step()
+            ev[i][1].record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    clk = clocks.stop()
+    l1, _ = sess.counters()
+    ms = sum(a.elapsed_time(b) for a, b in ev)
+    ms_max = dist.max(ms)
+    tokens = B * args.steps * dist.world
+    value = tokens / (ms_max / 1000.0)
+
+    # e2e: the public API with host buffers, greedy token read back each step
+    import ctypes as C
+    slots_h = np.arange(B, dtype=np.int32)
+    tok_h = np.array([p[-1] for p in prompts], np.int32)
+    pos_h = np.full(B, P - 1, np.int32)
+    torch.cuda.synchronize()
+    e2e_s = 0.0
+    for i in range(args.steps):
+        if pos_h[0] >= cfg.seq:
+            tok_h[:] = [p[-1] for p in prompts]
+            pos_h[:] = P - 1
+        flush.fill_(i & 0xFF)
+        torch.cuda.synchronize()
+        t = time.perf_counter()
+        if B == 1:
+            nxt = np.array([sess.step_greedy(int(tok_h[0]), int(pos_h[0]))], np.int32)
+        else:
+            nxt = sess.step_batch(slots_h, tok_h, pos_h)
+        e2e_s += time.perf_counter() - t
+        tok_h, pos_h = nxt.astype(np.int32), pos_h + 1
+    e2e_s = dist.max(e2e_s)
+    e2e = {"value": tokens / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": 12 * B, "d2h_bytes_per_step": 4 * B}
+
+    # live per-op timing (replay probe, cold L2) for the roofline
+    L = info.layers
+    prof_pos = [min(int(pos_h[0]), cfg.seq - 1)] * B
+    op_ms, op_bytes = {}, {}
+    for op in range(6):
+        avg = C.c_double()
+        byt = C.c_double()
+        pos_arr = np.array(prof_pos, np.int32)
+        rc = vc4b200.lib().vc4_profile_op(sess._h, op, L - 1, B, vc4b200.engine._p(slots_h),
+                                          vc4b200.engine._p(tok_h), vc4b200.engine._p(pos_arr), 20, 1,
+                                          C.byref(avg))
+        if rc:
+            raise RuntimeError(vc4b200.lib().vc4_last_error().decode())
+        vc4b200.lib().vc4_op_bytes(sess._h, op, L - 1, B, vc4b200.engine._p(pos_arr), C.byref(byt))
+        op_ms[OPS[op]] = avg.value
+        op_bytes[OPS[op]] = byt.value
+    per_step = {k: op_ms[k] * (1 if k == "logits" else L) for k in OPS}
+    dom = max(per_step, key=per_step.get)
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        pass
+    hbm = float(peaks.get("hbm_gbs") or 6650.0)
+    achieved = op_bytes[dom] / (op_ms[dom] / 1000.0) / 1e9
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic_%s.txt" % cfg.key)) as f:
+            for line in f:
+                if line.startswith(dom + " "):
+                    traffic = float(line.split()[1])
+    except OSError:
+        pass
+    step_bytes = sum(op_bytes[k] * (1 if k == "logits" else L) for k in OPS)
+    roofline = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                "frac": achieved / hbm, "traffic": traffic,
+                "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)" if peaks else "fallback 6650 GB/s",
+                "bytes_per_launch": op_bytes[dom], "ms_per_launch": op_ms[dom],
+                "step_bytes": step_bytes, "step_frac": step_bytes / (ms / args.steps / 1000.0) / 1e9 / hbm,
+                "per_op_ms": op_ms, "per_op_bytes": op_bytes}
+
+    cpu = None
+    if dist.world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_decode_rate(cfg, path, args.steps, args.cpu_seconds, os.cpu_count() or 1)
+
+    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": dist.world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "int64 (exact dp4a integer dot), f32/f64 epilogues",
+            "data": "synthetic (seeded weights and prompts of the configuration's shape)",
+            "config": {"workload": workload_desc(cfg), "batch_per_gpu": B, "seq": cfg.seq, "quant": cfg.quant,
+                       "kv": KV_NAME[cfg.kv_bits], "parallelism": "dp%d replicas" % dist.world,
+                       "l2": "flushed (256 MiB write) between timed steps", "prefill_s": prefill_s},
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk, "gpu_launches": l1 - l0}
+    if dist.rank == 0:
+        print(json.dumps(line), flush=True)
+    sess.close()
+    model.close()
+    gpu.close()
+
+
+def main():
+    args = parse()
+    from vc4b200 import synth
+    cfg = dict(synth.CONFIGS, **synth.TINY_CONFIGS)[args.config]
+    dist = Dist(args.gpus)
+    try:
+        if args.impl == "reference":
+            run_reference(args, cfg, dist)
+        else:
+            run_ours(args, cfg, dist)
+    finally:
+        dist.close()
+
+
+if __name__ == "__main__":
+    main()

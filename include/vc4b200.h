@@ -129,6 +129,21 @@ VC4_API int vc4_load_prefix_cache(vc4_session* s, int slot, const char* path, in
    5 router, 6 logits; expert selects an MoE expert. */
 VC4_API int vc4_matvec_s(vc4_model* m, int which, int layer, int expert, const float* x, float* out);
 
+/* Replay probe (the reference's MATVEC_DUP / ATTN_DUP, session.cpp:15-48 and
+   gpu_attn.cpp:20-39): run one op of the decode pass `reps` times for the
+   batch (slots, tokens, pos; host arrays) on the session stream, timing each
+   launch with CUDA events.  op: 0 qkv, 1 attention, 2 wo, 3 ffn gate,
+   4 ffn down, 5 logits.  With flush != 0 a 256 MiB buffer is written between
+   launches (outside the timed interval) so every launch starts from a cold L2.
+   Every op rewrites the same outputs from unchanged inputs, so the state after
+   the probe is the state before it.  avg_ms receives the mean launch time. */
+VC4_API int vc4_profile_op(vc4_session* s, int op, int layer, int n, const int* slots, const int* tokens,
+                           const int* pos, int reps, int flush, double* avg_ms);
+/* Algorithmic bytes one launch of `op` moves for n sequences at the given
+   positions: weights (with scale planes) + KV rows read and written +
+   activations in and out. */
+VC4_API int vc4_op_bytes(const vc4_session* s, int op, int layer, int n, const int* pos, double* bytes);
+
 /* draws()/syncs() (gpu.h:44-48): kernels launched and host syncs so far. */
 VC4_API int vc4_counters(const vc4_session* s, long long* launches, long long* syncs);
 /* Kernels one decode pass of n sequences launches. */

@@ -755,3 +755,111 @@ extern "C" int vc4_load_prefix_cache(vc4_session* s, int slot, const char* path,
     *n_out = (int)n;
     return VC4_OK;
 }
+
+// ---------------------------------------------------------------------------
+// replay probe
+// ---------------------------------------------------------------------------
+
+namespace {
+
+void launch_op(vc4_session* s, int op, int layer, const Batch& b, cudaStream_t st) {
+    const DModel& m = s->m->d;
+    switch (op) {
+        case 0: launch_embed_qkv(m, s->st, b, layer, st); break;
+        case 1: launch_attention(m, s->st, b, layer, st); break;
+        case 2: launch_wo(m, s->st, b, layer, st); break;
+        case 3: launch_ffn_gate(m, s->st, b, layer, st); break;
+        case 4: launch_ffn_down(m, s->st, b, layer, st); break;
+        default: launch_logits(m, s->st, b, st); break;
+    }
+}
+
+}  // namespace
+
+extern "C" int vc4_profile_op(vc4_session* s, int op, int layer, int n, const int* slots, const int* tokens,
+                              const int* pos, int reps, int flush, double* avg_ms) {
+    if (op < 0 || op > 5 || layer < 0 || layer >= s->m->d.h.layers || n <= 0 || n > s->slots || reps <= 0)
+        return fail(VC4_EINVAL, "profile_op: bad arguments");
+    for (int i = 0; i < n; ++i)
+        if (int e = check_slot_pos(s, slots[i], pos[i])) return e;
+    CK(cudaSetDevice(s->m->d.device));
+    static thread_local void* scratch = nullptr;
+    const size_t kFlush = (size_t)256 << 20;
+    if (flush && !scratch) CK(cudaMalloc(&scratch, kFlush));
+    int* hp = s->h_pin;
+    for (int i = 0; i < n; ++i) { hp[i] = slots[i]; hp[n + i] = tokens[i]; hp[2 * n + i] = pos[i]; }
+    int* dcall = s->d_slot;
+    CK(cudaMemcpyAsync(dcall, hp, sizeof(int) * 3 * n, cudaMemcpyHostToDevice, s->stream));
+    Batch b;
+    b.n = n; b.slot = dcall; b.token = dcall + n; b.pos = dcall + 2 * n;
+    cudaEvent_t e0, e1;
+    CK(cudaEventCreate(&e0));
+    CK(cudaEventCreate(&e1));
+    double total = 0.0;
+    launch_op(s, op, layer, b, s->stream);   // warm: attributes, instruction cache
+    for (int r = 0; r < reps; ++r) {
+        if (flush) CK(cudaMemsetAsync(scratch, r & 0xFF, kFlush, s->stream));
+        CK(cudaEventRecord(e0, s->stream));
+        launch_op(s, op, layer, b, s->stream);
+        CK(cudaEventRecord(e1, s->stream));
+        CK(cudaEventSynchronize(e1));
+        float ms = 0.0f;
+        CK(cudaEventElapsedTime(&ms, e0, e1));
+        total += ms;
+    }
+    CK(cudaGetLastError());
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    *avg_ms = total / reps;
+    return VC4_OK;
+}
+
+extern "C" int vc4_op_bytes(const vc4_session* s, int op, int layer, int n, const int* pos, double* bytes) {
+    const DModel& m = s->m->d;
+    const HModel& h = m.h;
+    if (op < 0 || op > 5 || layer < 0 || layer >= h.layers || n <= 0) return fail(VC4_EINVAL, "op_bytes: bad arguments");
+    auto wbytes = [&](int idx) -> double {
+        if (idx < 0) return 0.0;
+        const DMat& w = m.mats[idx];
+        if (w.wtype == W_I16) return 2.0 * w.rows * w.cols;
+        const double per = w.wtype == W_Q8 ? 1.0 : w.wtype == W_Q4 ? 0.5 : 0.25;
+        return per * w.rows * w.cols + (w.wtype == W_Q4 ? 4.0 * w.rows * (w.cols / 32) : 0.0) + 4.0 * w.rows;
+    };
+    const double D = h.dim, Q = h.dim + 2 * h.kv_dim, F = m.ffn_width;
+    double b = 0.0;
+    switch (op) {
+        case 0: b = wbytes(m.qkv[layer]) + n * (2 * D + 4 * Q); break;
+        case 1: {
+            double kv = 0.0;
+            for (int i = 0; i < n; ++i) kv += (double)(pos[i] + 1) * s->st.row_bytes;
+            b = kv + n * (4 * Q + 2 * D + s->st.row_bytes);
+            break;
+        }
+        case 2: b = wbytes(m.wo[layer]) + n * (2 * D + 2 * D + 2 * D); break;
+        case 3: {
+            if (h.experts) {   // every expert's gate/up the batch touches: at most min(n, E)
+                const int touched = std::min(n, h.experts);
+                const int e0 = m.e_w1[(size_t)layer * h.experts];
+                b = touched * (wbytes(e0) + wbytes(e0 + 1)) + wbytes(m.router[layer]);
+            } else {
+                b = wbytes(m.w1[layer]) + wbytes(m.w3[layer]);
+            }
+            b += n * (2 * D + 2 * F);
+            break;
+        }
+        case 4: {
+            if (h.experts) {
+                const int touched = std::min(n, h.experts);
+                const int e0 = m.e_w1[(size_t)layer * h.experts];
+                b = touched * (wbytes(e0 + 2) + (m.ffn_chunked ? wbytes(e0 + 3) : 0.0));
+            } else {
+                b = wbytes(m.w2a[layer]) + wbytes(m.w2b[layer]);
+            }
+            b += n * (2 * F + 4 * D);
+            break;
+        }
+        default: b = wbytes(m.logits_mat) + n * (2 * D + 4.0 * h.vocab); break;
+    }
+    *bytes = b;
+    return VC4_OK;
+}
