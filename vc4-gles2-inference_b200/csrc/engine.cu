@@ -112,6 +112,7 @@ std::string relay(const HMat& h, int c0, int c1, DMat& d, std::vector<void*>& al
     const int ncols = c1 - c0;
     if (h.wtype == W_Q4 && (c0 % 32 || ncols % 32)) return "q4 slice is not group aligned";
     d.nchunks = (ncols + cpc - 1) / cpc;
+    if (d.nchunks > matvec_max_chunks()) return "matrix too wide for the matvec kernel (" + std::to_string(ncols) + " columns)";
     const size_t nbody = (size_t)d.rblocks * d.nchunks * 32 * 16;
     std::vector<uint8_t> body(nbody, 0);
     std::vector<int32_t> q4p;
@@ -407,6 +408,8 @@ int vc4_session_create(vc4_model* m, int slots, int seq, int kv_bits, const floa
     if (kv_bits != 16 && kv_bits != 8) return fail(VC4_EINVAL, "kv_bits must be 16 (q16) or 8 (q8)");
     if (kv_bits == 8 && (h.kv_dim % 4 || h.head_dim % 4)) return fail(VC4_EINVAL, "q8 KV needs kv_dim and head_dim divisible by 4");
     if (h.heads / h.kv_heads > 8 || h.head_dim > 128) return fail(VC4_EINVAL, "attention group above 8 or head_dim above 128");
+    if (!attention_fits(seq, h.head_dim, kv_bits, h.kv_dim))
+        return fail(VC4_EINVAL, "sequence length / head shape beyond the attention kernel's staging limits");
     CK(cudaSetDevice(m->d.device));
     vc4_session* s = new vc4_session();
     s->m = m; s->slots = slots; s->stream = m->g->stream;

@@ -15,6 +15,8 @@
 // reproduces it bit for bit.  Build with --fmad=false.
 #include "vc4b200_internal.h"
 
+#include <cooperative_groups.h>
+
 #include <cstdio>
 #include <map>
 #include <utility>
@@ -114,25 +116,6 @@ __device__ int block_max_i32(int v, Red& r) {
     for (int w = 1; w < kWarps; ++w) t = max(t, r.i32[w]);
     return t;
 }
-__device__ float block_max_f32(float v, Red& r) {
-    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    __syncthreads();
-    if ((threadIdx.x & 31) == 0) r.f32[threadIdx.x >> 5] = v;
-    __syncthreads();
-    float t = r.f32[0];
-    for (int w = 1; w < kWarps; ++w) t = fmaxf(t, r.f32[w]);
-    return t;
-}
-__device__ double block_sum_f64(double v, Red& r) {
-    for (int o = 16; o; o >>= 1) v = __dadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
-    __syncthreads();
-    if ((threadIdx.x & 31) == 0) r.f64[threadIdx.x >> 5] = v;
-    __syncthreads();
-    double t = 0.0;
-    for (int w = 0; w < kWarps; ++w) t = __dadd_rn(t, r.f64[w]);
-    return t;
-}
-
 // ---------------------------------------------------------------------------
 // Input staging: q16 ints -> (optionally 2^k scaled) ints split into lo/hi bytes
 // ---------------------------------------------------------------------------
@@ -210,20 +193,56 @@ __device__ void rmsnorm_q16(const int16_t* x, const float* w, int D, float eps, 
 
 // ---------------------------------------------------------------------------
 // Matvec core: one 32-row block of one matrix over nb staged inputs.
-// Warp w takes chunks w, w+8, ...; each lane owns one row.  Returns the
-// warp's partial exact sums.
+// Warp w owns chunks w, w+8, w+16, ...; each lane owns one row.  The chunks a
+// warp needs are loaded into registers first (mv_prefetch), before the kernel
+// waits on its predecessor, so the DRAM latency of the weights overlaps the
+// previous kernel; mv_compute then returns the warp's exact partial sums.
 // ---------------------------------------------------------------------------
 
-template <int WT, int NB>
-__device__ __forceinline__ void mv_block(const DMat& W, int blk, const XStage& xs, int nb, long long (&S)[NB]) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int nch = W.nchunks;
+// Programmatic dependent launch: let the next kernel start its weight
+// prefetch now; wait for the previous kernel's results before touching them.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+__device__ __forceinline__ int4 ld_weights(const int4* p) {
+    int4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.s32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+
+template <int MAXC>
+struct WRegs {
+    int4 w[MAXC];
+    int sp[MAXC];   // q4: packed (s16 | m16 << 16) of the chunk's scale group
+};
+
+template <int WT, int MAXC>
+__device__ __forceinline__ void mv_prefetch(const DMat& W, int blk, WRegs<MAXC>& R) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nch = W.nchunks;
+    const int4* body = reinterpret_cast<const int4*>(W.body) + (size_t)blk * nch * 32 + lane;
+#pragma unroll
+    for (int k = 0; k < MAXC; ++k) {
+        const int j = warp + k * kWarps;
+        if (j < nch) {
+            R.w[k] = ld_weights(body + (size_t)j * 32);
+            if (WT == W_Q4) R.sp[k] = __ldg(W.q4p + ((size_t)blk * nch + j) * 32 + lane);
+        }
+    }
+}
+
+template <int WT, int NB, int MAXC>
+__device__ __forceinline__ void mv_compute(const DMat& W, const WRegs<MAXC>& R, const XStage& xs, int nb,
+                                           long long (&S)[NB]) {
+    const int warp = threadIdx.x >> 5, nch = W.nchunks;
     int alo[NB], ahi[NB];
 #pragma unroll
     for (int b = 0; b < NB; ++b) { alo[b] = 0; ahi[b] = 0; S[b] = 0; }
-    const int4* body = reinterpret_cast<const int4*>(W.body) + (size_t)blk * nch * 32 + lane;
-    for (int j = warp; j < nch; j += kWarps) {
-        const int4 w = __ldg(body + (size_t)j * 32);
+#pragma unroll
+    for (int k = 0; k < MAXC; ++k) {
+        const int j = warp + k * kWarps;
+        if (j >= nch) break;
+        const int4 w = R.w[k];
         if (WT == W_Q8) {
 #pragma unroll
             for (int b = 0; b < NB; ++b) {
@@ -254,8 +273,7 @@ __device__ __forceinline__ void mv_block(const DMat& W, int blk, const XStage& x
                 }
             }
         } else {  // W_Q4: chunk j is scale group j
-            const int sp = __ldg(W.q4p + ((size_t)blk * nch + j) * 32 + lane);
-            const long long s16 = (short)(sp & 0xFFFF), m16 = (short)(sp >> 16);
+            const long long s16 = (short)(R.sp[k] & 0xFFFF), m16 = (short)(R.sp[k] >> 16);
             const unsigned wd[4] = {(unsigned)w.x, (unsigned)w.y, (unsigned)w.z, (unsigned)w.w};
 #pragma unroll
             for (int b = 0; b < NB; ++b) {
@@ -299,12 +317,12 @@ __device__ __forceinline__ long long reduce_warps(const long long (&S)[NB], int 
 }
 
 struct SmemLayout {
-    // dynamic shared memory: [Red][red i64 kWarps*NB*32][gsum][lo][hi][scratch int16]
     static __device__ char* base() { extern __shared__ __align__(16) char smem[]; return smem; }
 };
 
+// dynamic shared memory: [Red][partials kWarps*NB*32][gsum][lo][hi][scratch]
 template <int NB>
-__device__ void carve(int stride, int gstride, XStage& xs, Red*& red, long long*& part, int16_t*& tmp, int tmp_n) {
+__device__ void carve(int stride, int gstride, XStage& xs, Red*& red, long long*& part, int16_t*& tmp) {
     char* p = SmemLayout::base();
     red = reinterpret_cast<Red*>(p); p += (sizeof(Red) + 15) / 16 * 16;
     part = reinterpret_cast<long long*>(p); p += sizeof(long long) * kWarps * NB * 32;
@@ -312,7 +330,6 @@ __device__ void carve(int stride, int gstride, XStage& xs, Red*& red, long long*
     xs.lo = reinterpret_cast<uint8_t*>(p); p += (size_t)NB * stride;
     xs.hi = reinterpret_cast<int8_t*>(p); p += (size_t)NB * stride;
     tmp = reinterpret_cast<int16_t*>(p);
-    (void)tmp_n;
     xs.stride = stride; xs.gstride = gstride;
 }
 
@@ -348,19 +365,23 @@ Dims dims_of(const DModel& m, const State& s) {
 // qkv: [embedding] + RMSNorm + matvec_s(qkv)
 // ---------------------------------------------------------------------------
 
-template <int WT, int NB>
+template <int WT, int NB, int MAXC>
 __global__ void __launch_bounds__(kThreads) k_qkv(DMat W, DMat E, const float* emb_scale, const float* rms_w,
                                                   State s, Batch bt, Dims d, int layer, int b0) {
+    WRegs<MAXC> R;
+    mv_prefetch<WT, MAXC>(W, blockIdx.x, R);
+    pdl_launch_dependents();
+    pdl_wait();
     XStage xs; Red* red; long long* part; int16_t* tmp;
-    carve<NB>(x_stride(W), g_stride(W), xs, red, part, tmp, NB * d.dim);
+    carve<NB>(x_stride(W), g_stride(W), xs, red, part, tmp);
     const int nb = min(NB, bt.n - b0);
     for (int b = 0; b < nb; ++b) {
         const int slot = bt.slot[b0 + b];
         int16_t* x = s.x + (size_t)slot * d.dim;
         int16_t* xin = tmp + (size_t)b * d.dim;
         if (layer == 0) {
-            // embedding (session.cpp:342-371): q16(level * row scale); rows are
-            // read from the blocked q8 layout of the embedding matrix.
+            // embedding (session.cpp:342-371): q16(level * row scale); the row
+            // is read from the blocked q8 layout of the embedding matrix.
             const int tok = bt.token[b0 + b];
             const float es = emb_scale[tok];
             const int8_t* eb = reinterpret_cast<const int8_t*>(E.body) + ((size_t)(tok / 32) * E.nchunks * 32 + (tok % 32)) * 16;
@@ -380,7 +401,7 @@ __global__ void __launch_bounds__(kThreads) k_qkv(DMat W, DMat E, const float* e
         stage_one<WT>(xs, b, xin, d.dim, xs.k[b], *red);
     }
     long long S[NB];
-    mv_block<WT, NB>(W, blockIdx.x, xs, nb, S);
+    mv_compute<WT, NB, MAXC>(W, R, xs, nb, S);
     const long long tot = reduce_warps<NB>(S, nb, part);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (warp < nb) {
@@ -398,10 +419,14 @@ __global__ void __launch_bounds__(kThreads) k_qkv(DMat W, DMat E, const float* e
 // wo: matvec_s(wo, att) + add_q16 residual -> x1
 // ---------------------------------------------------------------------------
 
-template <int WT, int NB>
+template <int WT, int NB, int MAXC>
 __global__ void __launch_bounds__(kThreads) k_wo(DMat W, State s, Batch bt, Dims d, int b0) {
+    WRegs<MAXC> R;
+    mv_prefetch<WT, MAXC>(W, blockIdx.x, R);
+    pdl_launch_dependents();
+    pdl_wait();
     XStage xs; Red* red; long long* part; int16_t* tmp;
-    carve<NB>(x_stride(W), g_stride(W), xs, red, part, tmp, 0);
+    carve<NB>(x_stride(W), g_stride(W), xs, red, part, tmp);
     const int nb = min(NB, bt.n - b0);
     for (int b = 0; b < nb; ++b) {
         const int16_t* a = s.att + (size_t)bt.slot[b0 + b] * d.dim;
@@ -409,7 +434,7 @@ __global__ void __launch_bounds__(kThreads) k_wo(DMat W, State s, Batch bt, Dims
         stage_one<WT>(xs, b, a, d.dim, xs.k[b], *red);
     }
     long long S[NB];
-    mv_block<WT, NB>(W, blockIdx.x, xs, nb, S);
+    mv_compute<WT, NB, MAXC>(W, R, xs, nb, S);
     const long long tot = reduce_warps<NB>(S, nb, part);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (warp < nb) {
@@ -431,7 +456,7 @@ __global__ void __launch_bounds__(kThreads) k_wo(DMat W, State s, Batch bt, Dims
 
 // MoE route of one q16 input (session.cpp:1523-1536 + pick_expert 110-115):
 // matvec_s over the i16 router, first maximum.
-__device__ int route_of(const int16_t* xbf, const DMat& R, int D, int experts, Red& r, int* scratch) {
+__device__ int route_of(const int16_t* xbf, const DMat& R, int D, int experts, Red& r) {
     const int k = scale_exponent(xbf, D, r);
     const float sk = ldexpf(1.0f, k);
     int best = 0;
@@ -448,20 +473,28 @@ __device__ int route_of(const int16_t* xbf, const DMat& R, int D, int experts, R
         const float g = __fmul_rn(__fmul_rn((float)v, 1.0f / 256.0f), ldexpf(1.0f, -k));
         if (e == 0 || g > bestv) { best = e; bestv = g; }
     }
-    (void)scratch;
     return best;
 }
 
-template <int WT, int NB>
+// MoE: blockIdx.y is the expert and the CTA serves the inputs routed to it.
+// `early` prefetches the expert's weights before the routing is known (a
+// batch large enough that every expert is used); otherwise after it.
+template <int WT, int NB, int MAXC>
 __global__ void __launch_bounds__(kThreads) k_gate(const DMat* mats, int i_w1, int i_w3, int i_router, int e_base,
                                                    const float* rms_w, State s, Batch bt, Dims d, int layer, int b0,
-                                                   int hs) {
-    // MoE: blockIdx.y is the expert; the CTA serves the inputs routed to it.
+                                                   int hs, int early) {
     const int expert = blockIdx.y;
     const DMat& W1 = mats[d.experts ? e_base + expert * 4 + 0 : i_w1];
     const DMat& W3 = mats[d.experts ? e_base + expert * 4 + 1 : i_w3];
+    WRegs<MAXC> R1, R3;
+    if (early) {
+        mv_prefetch<WT, MAXC>(W1, blockIdx.x, R1);
+        mv_prefetch<WT, MAXC>(W3, blockIdx.x, R3);
+    }
+    pdl_launch_dependents();
+    pdl_wait();
     XStage xs; Red* red; long long* part; int16_t* tmp;
-    carve<NB>(x_stride(W1), g_stride(W1), xs, red, part, tmp, (NB + 1) * d.dim);
+    carve<NB>(x_stride(W1), g_stride(W1), xs, red, part, tmp);
     int* members = reinterpret_cast<int*>(tmp + (size_t)(NB + 1) * d.dim);   // batch indices served
     const int n_all = min(NB, bt.n - b0);
     int nb = 0;
@@ -470,7 +503,7 @@ __global__ void __launch_bounds__(kThreads) k_gate(const DMat* mats, int i_w1, i
         int16_t* xin = tmp + (size_t)nb * d.dim;
         rmsnorm_q16(s.x1 + (size_t)slot * d.dim, rms_w, d.dim, d.eps, xin, *red);
         if (d.experts) {
-            const int e = route_of(xin, mats[i_router], d.dim, d.experts, *red, nullptr);
+            const int e = route_of(xin, mats[i_router], d.dim, d.experts, *red);
             if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) s.route[(size_t)slot * d.layers + layer] = e;
             __syncthreads();
             if (e != expert) continue;
@@ -481,10 +514,14 @@ __global__ void __launch_bounds__(kThreads) k_gate(const DMat* mats, int i_w1, i
         ++nb;
     }
     if (nb == 0) return;
+    if (!early) {
+        mv_prefetch<WT, MAXC>(W1, blockIdx.x, R1);
+        mv_prefetch<WT, MAXC>(W3, blockIdx.x, R3);
+    }
     long long S1[NB], S3[NB];
-    mv_block<WT, NB>(W1, blockIdx.x, xs, nb, S1);
+    mv_compute<WT, NB, MAXC>(W1, R1, xs, nb, S1);
     const long long t1 = reduce_warps<NB>(S1, nb, part);
-    mv_block<WT, NB>(W3, blockIdx.x, xs, nb, S3);
+    mv_compute<WT, NB, MAXC>(W3, R3, xs, nb, S3);
     const long long t3 = reduce_warps<NB>(S3, nb, part);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (warp < nb) {
@@ -505,16 +542,22 @@ __global__ void __launch_bounds__(kThreads) k_gate(const DMat* mats, int i_w1, i
 // down: w2 (one or two column chunks) + residual -> x
 // ---------------------------------------------------------------------------
 
-template <int WT, int NB>
+template <int WT, int NB, int MAXC>
 __global__ void __launch_bounds__(kThreads) k_down(const DMat* mats, int i_w2a, int i_w2b, int e_base,
-                                                   State s, Batch bt, Dims d, int layer, int b0) {
+                                                   State s, Batch bt, Dims d, int layer, int b0, int early) {
     const int expert = blockIdx.y;
-    const DMat& Wa = mats[d.experts ? e_base + expert * 4 + 2 : i_w2a];
     const bool two = d.chunk < d.ffn;
+    const DMat& Wa = mats[d.experts ? e_base + expert * 4 + 2 : i_w2a];
     const DMat& Wb = mats[d.experts ? e_base + expert * 4 + 3 : (two ? i_w2b : i_w2a)];
+    WRegs<MAXC> Ra, Rb;
+    if (early) {
+        mv_prefetch<WT, MAXC>(Wa, blockIdx.x, Ra);
+        if (two) mv_prefetch<WT, MAXC>(Wb, blockIdx.x, Rb);
+    }
+    pdl_launch_dependents();
+    pdl_wait();
     XStage xa, xb; Red* red; long long* part; int16_t* tmp;
-    // stage A in the carved buffers, stage B right after them
-    carve<NB>(x_stride(Wa), g_stride(Wa), xa, red, part, tmp, 0);
+    carve<NB>(x_stride(Wa), g_stride(Wa), xa, red, part, tmp);
     xb = xa;
     const int sb = two ? x_stride(Wb) : 0;
     xb.stride = sb > 0 ? sb : 1;
@@ -537,12 +580,16 @@ __global__ void __launch_bounds__(kThreads) k_down(const DMat* mats, int i_w2a, 
     }
     __syncthreads();
     if (nb == 0) return;
+    if (!early) {
+        mv_prefetch<WT, MAXC>(Wa, blockIdx.x, Ra);
+        if (two) mv_prefetch<WT, MAXC>(Wb, blockIdx.x, Rb);
+    }
     long long Sa[NB], Sb[NB];
-    mv_block<WT, NB>(Wa, blockIdx.x, xa, nb, Sa);
+    mv_compute<WT, NB, MAXC>(Wa, Ra, xa, nb, Sa);
     const long long ta = reduce_warps<NB>(Sa, nb, part);
     long long tb = 0;
     if (two) {
-        mv_block<WT, NB>(Wb, blockIdx.x, xb, nb, Sb);
+        mv_compute<WT, NB, MAXC>(Wb, Rb, xb, nb, Sb);
         tb = reduce_warps<NB>(Sb, nb, part);
     }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -567,10 +614,14 @@ __global__ void __launch_bounds__(kThreads) k_down(const DMat* mats, int i_w2a, 
 // logits: RMSNorm(x) + logits matvec + first-max argmax
 // ---------------------------------------------------------------------------
 
-template <int WT, int NB>
+template <int WT, int NB, int MAXC>
 __global__ void __launch_bounds__(kThreads) k_logits(DMat W, const float* rms_w, State s, Batch bt, Dims d, int b0) {
+    WRegs<MAXC> R;
+    mv_prefetch<WT, MAXC>(W, blockIdx.x, R);
+    pdl_launch_dependents();
+    pdl_wait();
     XStage xs; Red* red; long long* part; int16_t* tmp;
-    carve<NB>(x_stride(W), g_stride(W), xs, red, part, tmp, NB * d.dim);
+    carve<NB>(x_stride(W), g_stride(W), xs, red, part, tmp);
     const int nb = min(NB, bt.n - b0);
     for (int b = 0; b < nb; ++b) {
         int16_t* xin = tmp + (size_t)b * d.dim;
@@ -579,7 +630,7 @@ __global__ void __launch_bounds__(kThreads) k_logits(DMat W, const float* rms_w,
         stage_one<WT>(xs, b, xin, d.dim, 0, *red);
     }
     long long S[NB];
-    mv_block<WT, NB>(W, blockIdx.x, xs, nb, S);
+    mv_compute<WT, NB, MAXC>(W, R, xs, nb, S);
     const long long tot = reduce_warps<NB>(S, nb, part);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (warp < nb) {
@@ -603,59 +654,131 @@ __global__ void __launch_bounds__(kThreads) k_logits(DMat W, const float* rms_w,
 // attention: qk-norm + RoPE + KV append (packed codec) + attention
 // ---------------------------------------------------------------------------
 
-constexpr int kTile = 128;   // positions per staged K/V tile
+// Attention for one (KV head, sequence) runs on a cluster of kAttnCtas CTAs.
+// The positions 0..pos are split into kAttnCtas contiguous ranges; each CTA
+// stages its K/V rows (decoded to float) in shared memory with one burst of
+// loads, computes its scores, and the cluster combines the softmax maximum, the
+// double-precision denominator and the double-precision P.V partials through
+// distributed shared memory in rank order.  The arithmetic is the reference's
+// (session.cpp:1989-2050): sequential fp32 q.k per position, global max,
+// exp(s - max), p = e / sum, out = sum p*v.
+constexpr int kAttnCtas = 8;
 constexpr int kRedBytes = (int)((sizeof(Red) + 15) / 16 * 16);
 
-__device__ __forceinline__ float kv_decode(const uint8_t* row, int i, int kv_bits) {
+__device__ __forceinline__ void decode8(const uint4 v, int kv_bits, float* out) {
+    // 16 bytes of a packed row: 8 q16 values (big-endian) or 16 q8 values.
+    const unsigned w[4] = {v.x, v.y, v.z, v.w};
     if (kv_bits == 16) {
-        const int q = (int)(short)(((unsigned)row[2 * i] << 8) | row[2 * i + 1]);
-        return __fdiv_rn((float)q, 2048.0f);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const unsigned x = w[k];
+            const int a = (int)(short)(((x & 0xFFu) << 8) | ((x >> 8) & 0xFFu));
+            const int b = (int)(short)((((x >> 16) & 0xFFu) << 8) | (x >> 24));
+            out[2 * k] = __fmul_rn((float)a, 1.0f / 2048.0f);
+            out[2 * k + 1] = __fmul_rn((float)b, 1.0f / 2048.0f);
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                out[4 * k + j] = __fmul_rn((float)(signed char)((w[k] >> (8 * j)) & 0xFFu), 1.0f / 16.0f);
     }
-    return __fdiv_rn((float)(signed char)row[i], 16.0f);
 }
 
-__global__ void __launch_bounds__(kThreads) k_attn(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int layer) {
+struct AttnSmem {
+    // carved from dynamic shared memory
+    Red* red;
+    float* q;        // group*hd
+    float* kv;       // 2*hd  (new k, v)
+    float* kt;       // rows*hp
+    float* vt;       // rows*hp
+    float* sc;       // group*rows
+    float* mx;       // group          (cluster-visible)
+    double* sum;     // group          (cluster-visible)
+    double* pv;      // group*hd       (cluster-visible)
+};
+
+__global__ void __cluster_dims__(kAttnCtas, 1, 1) __launch_bounds__(kThreads)
+k_attn(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int layer, int max_rows) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
     extern __shared__ __align__(16) char smem[];
-    const int g = blockIdx.x, b = blockIdx.y;
+    const int rank = (int)cluster.block_rank();
+    const int g = blockIdx.x / kAttnCtas, b = blockIdx.y;
     const int slot = bt.slot[b], pos = bt.pos[b];
-    const int hd = d.head_dim, group = d.heads / d.kv_heads, half = hd / 2;
-    const int hp = hd + 1;                     // padded tile stride (floats)
-    Red* red = reinterpret_cast<Red*>(smem);
-    float* qv = reinterpret_cast<float*>(smem + kRedBytes);    // group*hd
-    float* kvv = qv + group * hd;                                // 2*hd (k, v)
-    float* tile = kvv + 2 * hd;                                  // kTile*hp
-    float* sc = tile + kTile * hp;                               // group*seq
-    double* pv = reinterpret_cast<double*>(((uintptr_t)(sc + (size_t)group * d.seq) + 15) & ~(uintptr_t)15);
-    const float* qkv = s.qkv + (size_t)slot * (d.dim + 2 * d.kv_dim);
-    for (int i = threadIdx.x; i < group * hd; i += blockDim.x) qv[i] = qkv[g * group * hd + i];
-    for (int i = threadIdx.x; i < hd; i += blockDim.x) {
-        kvv[i] = qkv[d.dim + g * hd + i];
-        kvv[hd + i] = qkv[d.dim + d.kv_dim + g * hd + i];
+    const int hd = d.head_dim, group = d.heads / d.kv_heads, half = hd / 2, hp = hd + 1;
+    const int len = pos + 1;
+    const int per = (len + kAttnCtas - 1) / kAttnCtas;
+    const int t0 = min(len, rank * per), t1 = min(len, t0 + per), nt = t1 - t0;
+    AttnSmem sm;
+    {
+        char* p = smem;
+        sm.red = reinterpret_cast<Red*>(p); p += kRedBytes;
+        sm.pv = reinterpret_cast<double*>(p); p += sizeof(double) * ((group * hd + 1) & ~1);
+        sm.sum = reinterpret_cast<double*>(p); p += sizeof(double) * 8;
+        sm.mx = reinterpret_cast<float*>(p); p += sizeof(float) * 8;
+        sm.q = reinterpret_cast<float*>(p); p += sizeof(float) * group * hd;
+        sm.kv = reinterpret_cast<float*>(p); p += sizeof(float) * 2 * hd;
+        sm.kt = reinterpret_cast<float*>(p); p += sizeof(float) * (size_t)max_rows * hp;
+        sm.vt = reinterpret_cast<float*>(p); p += sizeof(float) * (size_t)max_rows * hp;
+        sm.sc = reinterpret_cast<float*>(p);
     }
-    __syncthreads();
-    // qk-norm (session.cpp:1950-1961): the squares of one head share a
-    // power-of-two grid, so the double sum is exact in any order.
-    if (d.qk_norm) {
-        for (int hh = 0; hh <= group; ++hh) {
-            float* v = hh < group ? qv + hh * hd : kvv;
-            const float* w = (hh < group ? q_norm : k_norm) + (size_t)layer * hd;
-            double acc = 0.0;
-            for (int i = threadIdx.x; i < hd; i += blockDim.x) acc = __dadd_rn(acc, __dmul_rn((double)v[i], (double)v[i]));
-            acc = block_sum_f64(acc, *red);
-            const float ss = __double2float_rn(acc);
-            const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)hd), 1e-6f)));
-            __syncthreads();
-            for (int i = threadIdx.x; i < hd; i += blockDim.x) v[i] = __fmul_rn(w[i], __fmul_rn(r, v[i]));
-            __syncthreads();
+    uint8_t* kvbase = s.kv + ((size_t)slot * d.layers + layer) * d.seq * d.row_bytes;
+    const int vofs = d.kv_bits == 16 ? 2 * d.kv_dim : d.kv_dim;
+    const int hbytes = d.kv_bits == 16 ? 2 * hd : hd;          // bytes of one head's K (or V) in a row
+    const int vpr = hbytes / 16;                               // 16-byte vectors per head row
+    const int vals = d.kv_bits == 16 ? 8 : 16;                 // values per vector
+    // 1. issue the loads of this CTA's cached K/V rows (all but `pos`)
+    constexpr int kMaxVec = 16;
+    uint4 buf[kMaxVec];
+    const int nvec = 2 * nt * vpr;
+    int nmine = 0;
+#pragma unroll
+    for (int k = 0; k < kMaxVec; ++k) {
+        const int v = threadIdx.x + k * kThreads;
+        if (v < nvec) {
+            const int which = v / (nt * vpr), r = (v / vpr) % nt, c = v % vpr;
+            const int t = t0 + r;
+            if (t != pos) {
+                const uint8_t* src = kvbase + (size_t)t * d.row_bytes + (which ? vofs : 0) + g * hbytes + c * 16;
+                buf[k] = *reinterpret_cast<const uint4*>(src);
+            }
+            nmine = k + 1;
         }
     }
-    // RoPE (session.cpp:1963-1987) with the host-built cos/sin tables.
+    pdl_launch_dependents();
+    pdl_wait();
+    // 2. q heads and the new k, v; qk-norm (exact double sum of squares), RoPE
+    const float* qkv = s.qkv + (size_t)slot * (d.dim + 2 * d.kv_dim);
+    for (int i = threadIdx.x; i < group * hd; i += blockDim.x) sm.q[i] = qkv[g * group * hd + i];
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) {
+        sm.kv[i] = qkv[d.dim + g * hd + i];
+        sm.kv[hd + i] = qkv[d.dim + d.kv_dim + g * hd + i];
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (d.qk_norm) {
+        // one warp per vector: heads 0..group-1 of q, then k
+        for (int hh = warp; hh <= group; hh += kWarps) {
+            float* v = hh < group ? sm.q + hh * hd : sm.kv;
+            double acc = 0.0;
+            for (int i = lane; i < hd; i += 32) acc = __dadd_rn(acc, __dmul_rn((double)v[i], (double)v[i]));
+            for (int o = 16; o; o >>= 1) acc = __dadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+            const float ss = __double2float_rn(acc);
+            const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)hd), 1e-6f)));
+            const float* w = (hh < group ? q_norm : k_norm) + (size_t)layer * hd;
+            __syncwarp();
+            for (int i = lane; i < hd; i += 32) v[i] = __fmul_rn(w[i], __fmul_rn(r, v[i]));
+        }
+        __syncthreads();
+    }
     {
         const float* cs = s.rope_cos + (size_t)pos * half;
         const float* sn = s.rope_sin + (size_t)pos * half;
         for (int t = threadIdx.x; t < (group + 1) * half; t += blockDim.x) {
             const int hh = t / half, i = t % half;
-            float* o = hh < group ? qv + hh * hd : kvv;
+            float* o = hh < group ? sm.q + hh * hd : sm.kv;
             const int ia = d.rope_half ? i : 2 * i, ib = d.rope_half ? i + half : 2 * i + 1;
             const float a = o[ia], bb = o[ib], c = cs[i], sv = sn[i];
             o[ia] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(bb, sv));
@@ -663,120 +786,126 @@ __global__ void __launch_bounds__(kThreads) k_attn(const float* q_norm, const fl
         }
     }
     __syncthreads();
-    // KV append: the packed codec (shaders_attn.cpp:141-159), this head's slice.
-    uint8_t* kvbase = s.kv + ((size_t)slot * d.layers + layer) * d.seq * d.row_bytes;
-    {
+    // 3. the CTA holding `pos` encodes the new row (shaders_attn.cpp:141-159),
+    //    writes it to the cache and keeps the decoded values for its tile.
+    if (pos >= t0 && pos < t1) {
         uint8_t* row = kvbase + (size_t)pos * d.row_bytes;
-        for (int i = threadIdx.x; i < hd; i += blockDim.x) {
-            const int c = g * hd + i;
-            for (int w = 0; w < 2; ++w) {
-                const float v = kvv[w * hd + i];
-                if (d.kv_bits == 16) {
-                    float q = floorf(__fadd_rn(__fmul_rn(v, 2048.0f), 0.5f));
-                    q = q < -32768.0f ? -32768.0f : q > 32767.0f ? 32767.0f : q;
-                    const unsigned u = (unsigned)(int)q & 0xFFFFu;
-                    uint8_t* p = row + (size_t)w * 2 * d.kv_dim + 2 * c;
-                    p[0] = (uint8_t)(u >> 8); p[1] = (uint8_t)u;
-                } else {
-                    float q = floorf(__fadd_rn(__fmul_rn(v, 16.0f), 0.5f));
-                    q = q < -128.0f ? -128.0f : q > 127.0f ? 127.0f : q;
-                    row[(size_t)w * d.kv_dim + c] = (uint8_t)(int)q;
-                }
+        for (int e = threadIdx.x; e < 2 * hd; e += blockDim.x) {
+            const int w = e / hd, i = e % hd, c = g * hd + i;
+            const float v = sm.kv[w * hd + i];
+            float dec;
+            if (d.kv_bits == 16) {
+                float q = floorf(__fadd_rn(__fmul_rn(v, 2048.0f), 0.5f));
+                q = q < -32768.0f ? -32768.0f : q > 32767.0f ? 32767.0f : q;
+                const unsigned u = (unsigned)(int)q & 0xFFFFu;
+                uint8_t* p = row + (size_t)w * 2 * d.kv_dim + 2 * c;
+                p[0] = (uint8_t)(u >> 8); p[1] = (uint8_t)u;
+                dec = __fmul_rn(q, 1.0f / 2048.0f);
+            } else {
+                float q = floorf(__fadd_rn(__fmul_rn(v, 16.0f), 0.5f));
+                q = q < -128.0f ? -128.0f : q > 127.0f ? 127.0f : q;
+                row[(size_t)w * d.kv_dim + c] = (uint8_t)(int)q;
+                dec = __fmul_rn(q, 1.0f / 16.0f);
             }
+            (w ? sm.vt : sm.kt)[(pos - t0) * hp + i] = dec;
         }
     }
+    // 4. land the loaded rows in the tiles
+#pragma unroll
+    for (int k = 0; k < kMaxVec; ++k) {
+        if (k >= nmine) break;
+        const int v = threadIdx.x + k * kThreads;
+        const int which = v / (nt * vpr), r = (v / vpr) % nt, c = v % vpr;
+        if (t0 + r == pos) continue;
+        float f[16];
+        decode8(buf[k], d.kv_bits, f);
+        float* dst = (which ? sm.vt : sm.kt) + r * hp + c * vals;
+        for (int j = 0; j < vals; ++j) dst[j] = f[j];
+    }
     __syncthreads();
-    const int vofs = d.kv_bits == 16 ? 2 * d.kv_dim : d.kv_dim;   // V starts here in a row
+    // 5. scores: one thread per (position, head), sequential fp32 dot
     const float sq = __fsqrt_rn((float)hd);
-    // scores: one thread per position, sequential fp32 dot (session.cpp:2031-2036)
-    for (int t0 = 0; t0 <= pos; t0 += kTile) {
-        const int nt = min(kTile, pos + 1 - t0);
-        for (int e = threadIdx.x; e < nt * hd; e += blockDim.x) {
-            const int t = e / hd, i = e % hd;
-            tile[t * hp + i] = kv_decode(kvbase + (size_t)(t0 + t) * d.row_bytes, g * hd + i, d.kv_bits);
-        }
-        __syncthreads();
-        for (int t = threadIdx.x; t < nt; t += blockDim.x) {
-            const float* kr = tile + t * hp;
-            for (int hh = 0; hh < group; ++hh) {
-                const float* q = qv + hh * hd;
-                float acc = 0.0f;
-                for (int i = 0; i < hd; ++i) acc = __fadd_rn(acc, __fmul_rn(q[i], kr[i]));
-                acc = __fdiv_rn(acc, sq);
-                sc[(size_t)hh * d.seq + t0 + t] = acc;
-            }
-        }
-        __syncthreads();
+    float lmax[8];
+    for (int hh = 0; hh < 8; ++hh) lmax[hh] = -1e30f;
+    for (int e = threadIdx.x; e < nt * group; e += blockDim.x) {
+        const int r = e / group, hh = e % group;
+        const float* kr = sm.kt + r * hp;
+        const float* q = sm.q + hh * hd;
+        float acc = 0.0f;
+        for (int i = 0; i < hd; ++i) acc = __fadd_rn(acc, __fmul_rn(q[i], kr[i]));
+        acc = __fdiv_rn(acc, sq);
+        sm.sc[hh * max_rows + r] = acc;
     }
-    // softmax per head: max, exp, double sum, divide (session.cpp:2037-2040)
-    for (int hh = 0; hh < group; ++hh) {
-        float* S = sc + (size_t)hh * d.seq;
+    __syncthreads();
+    // 6. cluster max per head
+    for (int hh = warp; hh < group; hh += kWarps) {
         float m = -1e30f;
-        for (int t = threadIdx.x; t <= pos; t += blockDim.x) m = fmaxf(m, S[t]);
-        m = block_max_f32(m, *red);
-        double sum = 0.0;
-        for (int t = threadIdx.x; t <= pos; t += blockDim.x) {
-            const float e = vexp(__fsub_rn(S[t], m));
-            S[t] = e;
-            sum = __dadd_rn(sum, (double)e);
-        }
-        sum = block_sum_f64(sum, *red);
-        const float fs = __double2float_rn(sum);
-        for (int t = threadIdx.x; t <= pos; t += blockDim.x) S[t] = __fdiv_rn(S[t], fs);
-        __syncthreads();
+        for (int r = lane; r < nt; r += 32) m = fmaxf(m, sm.sc[hh * max_rows + r]);
+        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (lane == 0) sm.mx[hh] = m;
     }
-    // P.V in double: warp w takes positions w, w+8, ..; lanes take dims.
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int nd = (hd + 31) / 32;
-    double acc[8 * 4];   // group <= 8, hd <= 128
-    for (int a = 0; a < group * nd; ++a) acc[a] = 0.0;
-    for (int t0 = 0; t0 <= pos; t0 += kTile) {
-        const int nt = min(kTile, pos + 1 - t0);
-        __syncthreads();
-        for (int e = threadIdx.x; e < nt * hd; e += blockDim.x) {
-            const int t = e / hd, i = e % hd;
-            tile[t * hp + i] = kv_decode(kvbase + (size_t)(t0 + t) * d.row_bytes + vofs - (d.kv_bits == 16 ? 0 : 0),
-                                         g * hd + i, d.kv_bits);
-        }
-        __syncthreads();
-        for (int t = warp; t < nt; t += kWarps) {
-            const float* vr = tile + t * hp;
-            for (int hh = 0; hh < group; ++hh) {
-                const double p = (double)sc[(size_t)hh * d.seq + t0 + t];
-                for (int m = 0; m < nd; ++m) {
-                    const int i = lane + 32 * m;
-                    if (i < hd) acc[hh * nd + m] = __dadd_rn(acc[hh * nd + m], __dmul_rn(p, (double)vr[i]));
-                }
-            }
+    cluster.sync();
+    for (int hh = 0; hh < group; ++hh) {
+        float m = -1e30f;
+        for (int c = 0; c < kAttnCtas; ++c) m = fmaxf(m, *cluster.map_shared_rank(sm.mx + hh, c));
+        lmax[hh] = m;
+    }
+    // 7. exp and the double denominator, cluster-combined in rank order
+    for (int e = threadIdx.x; e < nt * group; e += blockDim.x) {
+        const int r = e / group, hh = e % group;
+        float* p = sm.sc + hh * max_rows + r;
+        *p = vexp(__fsub_rn(*p, lmax[hh]));
+    }
+    __syncthreads();
+    for (int hh = warp; hh < group; hh += kWarps) {
+        double a = 0.0;
+        for (int r = lane; r < nt; r += 32) a = __dadd_rn(a, (double)sm.sc[hh * max_rows + r]);
+        for (int o = 16; o; o >>= 1) a = __dadd_rn(a, __shfl_xor_sync(0xffffffffu, a, o));
+        if (lane == 0) sm.sum[hh] = a;
+    }
+    cluster.sync();
+    for (int hh = 0; hh < group; ++hh) {
+        double a = 0.0;
+        for (int c = 0; c < kAttnCtas; ++c) a = __dadd_rn(a, *cluster.map_shared_rank(sm.sum + hh, c));
+        const float fs = __double2float_rn(a);
+        for (int r = threadIdx.x; r < nt; r += blockDim.x) {
+            float* p = sm.sc + hh * max_rows + r;
+            *p = __fdiv_rn(*p, fs);
         }
     }
     __syncthreads();
-    for (int hh = 0; hh < group; ++hh)
-        for (int m = 0; m < nd; ++m) {
-            const int i = lane + 32 * m;
-            if (i < hd) pv[((size_t)warp * group + hh) * hd + i] = acc[hh * nd + m];
-        }
-    __syncthreads();
+    // 8. P.V partials in double over this CTA's positions
     for (int e = threadIdx.x; e < group * hd; e += blockDim.x) {
-        double t = 0.0;
-        for (int w = 0; w < kWarps; ++w) t = __dadd_rn(t, pv[(size_t)w * group * hd + e]);
-        const float o = __double2float_rn(t);
-        s.att[(size_t)slot * d.dim + g * group * hd + e] = (int16_t)q16h(o);
+        const int hh = e / hd, i = e % hd;
+        const float* p = sm.sc + hh * max_rows;
+        double a = 0.0;
+        for (int r = 0; r < nt; ++r) a = __fma_rn((double)p[r], (double)sm.vt[r * hp + i], a);
+        sm.pv[e] = a;
     }
+    cluster.sync();
+    // 9. combine across the cluster in rank order; CTA c writes outputs e = c mod kAttnCtas
+    for (int e = rank + kAttnCtas * threadIdx.x; e < group * hd; e += kAttnCtas * blockDim.x) {
+        double a = 0.0;
+        for (int c = 0; c < kAttnCtas; ++c) a = __dadd_rn(a, *cluster.map_shared_rank(sm.pv + e, c));
+        s.att[(size_t)slot * d.dim + g * group * hd + e] = (int16_t)q16h(__double2float_rn(a));
+    }
+    cluster.sync();   // no CTA leaves while its shared memory may still be read
 }
 
 // ---------------------------------------------------------------------------
 // bare matvec (CPU-path entry)
 // ---------------------------------------------------------------------------
 
-template <int WT>
+template <int WT, int MAXC>
 __global__ void __launch_bounds__(kThreads) k_raw(DMat W, const int16_t* xq, int n, int32_t* out) {
+    WRegs<MAXC> R;
+    mv_prefetch<WT, MAXC>(W, blockIdx.x, R);
     XStage xs; Red* red; long long* part; int16_t* tmp;
-    carve<1>(x_stride(W), g_stride(W), xs, red, part, tmp, 0);
+    carve<1>(x_stride(W), g_stride(W), xs, red, part, tmp);
     xs.k[0] = 0;
     stage_one<WT>(xs, 0, xq, n, 0, *red);
     long long S[1];
-    mv_block<WT, 1>(W, blockIdx.x, xs, 1, S);
+    mv_compute<WT, 1, MAXC>(W, R, xs, 1, S);
     const long long tot = reduce_warps<1>(S, 1, part);
     if (threadIdx.x < 32) {
         const int row = blockIdx.x * 32 + threadIdx.x;
@@ -797,6 +926,7 @@ __global__ void __launch_bounds__(kThreads) k_raw_i16(DMat W, const int16_t* xq,
 // Greedy token of each sequence from its packed argmax key; optionally
 // advance the sequence (next token, position + 1).
 __global__ void k_finalize(State s, Batch bt, int* next, int* tokens, int* pos, int advance, const int* forced) {
+    pdl_wait();
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= bt.n) return;
     const unsigned long long key = s.best[bt.slot[b]];
@@ -826,114 +956,151 @@ void set_smem(K kernel, size_t bytes) {
     have = bytes;
 }
 
+// Every decode kernel is launched as a programmatic dependent of the one
+// before it (griddepcontrol in the kernels), inside the captured graph too.
+template <typename... KArgs, typename... Args>
+void launch_pdl(void (*kernel)(KArgs...), dim3 grid, size_t smem, cudaStream_t st, Args... args) {
+    set_smem(kernel, smem);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 constexpr int kNB = 4;   // inputs per CTA for the batched matvecs
 
-template <int WT>
-void qkv_t(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
-    const DMat& W = m.mats[m.qkv[layer]];
-    const DMat& E = m.mats[m.emb_mat];
-    Dims d = dims_of(m, s);
-    const size_t sm = smem_bytes(kNB, x_stride(W), g_stride(W), kNB * d.dim);
-    set_smem(k_qkv<WT, kNB>, sm);
-    for (int b0 = 0; b0 < bt.n; b0 += kNB)
-        k_qkv<WT, kNB><<<W.rblocks, kThreads, sm, st>>>(W, E, m.d_emb_scale, m.d_rms_att + (size_t)layer * d.dim, s, bt, d, layer, b0);
+// Registers per warp for a matrix: the smallest of 4/8/12/20 chunks that
+// covers nchunks/8 (upload refuses a matrix above 160 chunks).
+inline int maxc_for(int nch) {
+    const int per = (nch + kWarps - 1) / kWarps;
+    return per <= 4 ? 4 : per <= 8 ? 8 : per <= 12 ? 12 : 20;
 }
 
-template <int WT>
-void wo_t(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
-    const DMat& W = m.mats[m.wo[layer]];
-    Dims d = dims_of(m, s);
-    const size_t sm = smem_bytes(kNB, x_stride(W), g_stride(W), 0);
-    set_smem(k_wo<WT, kNB>, sm);
-    for (int b0 = 0; b0 < bt.n; b0 += kNB) k_wo<WT, kNB><<<W.rblocks, kThreads, sm, st>>>(W, s, bt, d, b0);
-}
+#define VC4_MAXC(M, F, ...)                                          \
+    do {                                                             \
+        if ((M) == 4) F<4>(__VA_ARGS__);                             \
+        else if ((M) == 8) F<8>(__VA_ARGS__);                        \
+        else if ((M) == 12) F<12>(__VA_ARGS__);                      \
+        else F<20>(__VA_ARGS__);                                     \
+    } while (0)
 
 template <int WT>
-void gate_t(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
-    Dims d = dims_of(m, s);
-    const int ebase = d.experts ? m.e_w1[(size_t)layer * d.experts] : 0;
-    const DMat& W1 = m.mats[d.experts ? ebase : m.w1[layer]];
-    const size_t sm = smem_bytes(kNB, x_stride(W1), g_stride(W1), (kNB + 1) * d.dim) + 64;
-    set_smem(k_gate<WT, kNB>, sm);
-    dim3 grid(W1.rblocks, d.experts ? d.experts : 1);
-    for (int b0 = 0; b0 < bt.n; b0 += kNB)
-        k_gate<WT, kNB><<<grid, kThreads, sm, st>>>(m.d_mats, d.experts ? 0 : m.w1[layer], d.experts ? 0 : m.w3[layer],
-                                                     d.experts ? m.router[layer] : 0, ebase,
-                                                     m.d_rms_ffn + (size_t)layer * d.dim, s, bt, d, layer, b0,
-                                                     layer < (int)m.h.hid_scale.size() ? (int)m.h.hid_scale[layer] : 0);
-}
-
-template <int WT>
-void down_t(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
-    Dims d = dims_of(m, s);
-    const int ebase = d.experts ? m.e_w1[(size_t)layer * d.experts] : 0;
-    const DMat& Wa = m.mats[d.experts ? ebase + 2 : m.w2a[layer]];
-    const bool two = m.ffn_chunked;
-    const DMat& Wb = m.mats[d.experts ? ebase + 3 : (two ? m.w2b[layer] : m.w2a[layer])];
-    const size_t sm = smem_bytes(kNB, x_stride(Wa), g_stride(Wa), 0) +
-                      (two ? 2 * (size_t)kNB * x_stride(Wb) + sizeof(int) * kNB * g_stride(Wb) : 16) + 256;
-    set_smem(k_down<WT, kNB>, sm);
-    dim3 grid(Wa.rblocks, d.experts ? d.experts : 1);
-    for (int b0 = 0; b0 < bt.n; b0 += kNB)
-        k_down<WT, kNB><<<grid, kThreads, sm, st>>>(m.d_mats, d.experts ? 0 : m.w2a[layer],
-                                                     d.experts ? 0 : (two ? m.w2b[layer] : m.w2a[layer]), ebase, s, bt, d,
-                                                     layer, b0);
-}
-
-template <int WT>
-void logits_t(const DModel& m, const State& s, const Batch& bt, cudaStream_t st) {
-    const DMat& W = m.mats[m.logits_mat];
-    Dims d = dims_of(m, s);
-    const size_t sm = smem_bytes(kNB, x_stride(W), g_stride(W), kNB * d.dim);
-    set_smem(k_logits<WT, kNB>, sm);
-    for (int b0 = 0; b0 < bt.n; b0 += kNB)
-        k_logits<WT, kNB><<<W.rblocks, kThreads, sm, st>>>(W, m.d_rms_final, s, bt, d, b0);
-}
+struct Ops {
+    template <int MAXC>
+    static void qkv(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
+        const DMat& W = m.mats[m.qkv[layer]];
+        const DMat& E = m.mats[m.emb_mat];
+        Dims d = dims_of(m, s);
+        const size_t sm = smem_bytes(kNB, x_stride(W), g_stride(W), kNB * d.dim);
+        for (int b0 = 0; b0 < bt.n; b0 += kNB)
+            launch_pdl(k_qkv<WT, kNB, MAXC>, dim3(W.rblocks), sm, st, W, E, m.d_emb_scale,
+                       (const float*)(m.d_rms_att + (size_t)layer * d.dim), s, bt, d, layer, b0);
+    }
+    template <int MAXC>
+    static void wo(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
+        const DMat& W = m.mats[m.wo[layer]];
+        Dims d = dims_of(m, s);
+        const size_t sm = smem_bytes(kNB, x_stride(W), g_stride(W), 0);
+        for (int b0 = 0; b0 < bt.n; b0 += kNB) launch_pdl(k_wo<WT, kNB, MAXC>, dim3(W.rblocks), sm, st, W, s, bt, d, b0);
+    }
+    template <int MAXC>
+    static void gate(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
+        Dims d = dims_of(m, s);
+        const int ebase = d.experts ? m.e_w1[(size_t)layer * d.experts] : 0;
+        const DMat& W1 = m.mats[d.experts ? ebase : m.w1[layer]];
+        const size_t sm = smem_bytes(kNB, x_stride(W1), g_stride(W1), (kNB + 1) * d.dim) + 64;
+        const dim3 grid(W1.rblocks, d.experts ? d.experts : 1);
+        const int hs = layer < (int)m.h.hid_scale.size() ? (int)m.h.hid_scale[layer] : 0;
+        const int early = d.experts == 0 || bt.n >= 2 * d.experts;
+        for (int b0 = 0; b0 < bt.n; b0 += kNB)
+            launch_pdl(k_gate<WT, kNB, MAXC>, grid, sm, st, (const DMat*)m.d_mats, d.experts ? 0 : m.w1[layer],
+                       d.experts ? 0 : m.w3[layer], d.experts ? m.router[layer] : 0, ebase,
+                       (const float*)(m.d_rms_ffn + (size_t)layer * d.dim), s, bt, d, layer, b0, hs, early);
+    }
+    template <int MAXC>
+    static void down(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
+        Dims d = dims_of(m, s);
+        const int ebase = d.experts ? m.e_w1[(size_t)layer * d.experts] : 0;
+        const DMat& Wa = m.mats[d.experts ? ebase + 2 : m.w2a[layer]];
+        const bool two = m.ffn_chunked;
+        const DMat& Wb = m.mats[d.experts ? ebase + 3 : (two ? m.w2b[layer] : m.w2a[layer])];
+        const size_t sm = smem_bytes(kNB, x_stride(Wa), g_stride(Wa), 0) +
+                          (two ? 2 * (size_t)kNB * x_stride(Wb) + sizeof(int) * kNB * g_stride(Wb) : 16) + 256;
+        const dim3 grid(Wa.rblocks, d.experts ? d.experts : 1);
+        const int early = d.experts == 0 || bt.n >= 2 * d.experts;
+        for (int b0 = 0; b0 < bt.n; b0 += kNB)
+            launch_pdl(k_down<WT, kNB, MAXC>, grid, sm, st, (const DMat*)m.d_mats, d.experts ? 0 : m.w2a[layer],
+                       d.experts ? 0 : (two ? m.w2b[layer] : m.w2a[layer]), ebase, s, bt, d, layer, b0, early);
+    }
+    template <int MAXC>
+    static void logits(const DModel& m, const State& s, const Batch& bt, cudaStream_t st) {
+        const DMat& W = m.mats[m.logits_mat];
+        Dims d = dims_of(m, s);
+        const size_t sm = smem_bytes(kNB, x_stride(W), g_stride(W), kNB * d.dim);
+        for (int b0 = 0; b0 < bt.n; b0 += kNB)
+            launch_pdl(k_logits<WT, kNB, MAXC>, dim3(W.rblocks), sm, st, W,
+                       (const float*)m.d_rms_final, s, bt, d, b0);
+    }
+    template <int MAXC>
+    static void raw(const DMat& W, const int16_t* xq, int n, int32_t* out, cudaStream_t st) {
+        const size_t sm = smem_bytes(1, x_stride(W), g_stride(W), 0);
+        set_smem(k_raw<WT, MAXC>, sm);
+        k_raw<WT, MAXC><<<W.rblocks, kThreads, sm, st>>>(W, xq, n, out);
+    }
+};
 
 }  // namespace
 
-#define VC4_DISPATCH(WT, FN, ...)                          \
-    do {                                                   \
-        if ((WT) == W_Q8) FN<W_Q8>(__VA_ARGS__);           \
-        else if ((WT) == W_Q4) FN<W_Q4>(__VA_ARGS__);      \
-        else FN<W_T3>(__VA_ARGS__);                        \
+#define VC4_DISPATCH(WT, M, FN, ...)                                   \
+    do {                                                               \
+        if ((WT) == W_Q8) VC4_MAXC(M, Ops<W_Q8>::FN, __VA_ARGS__);     \
+        else if ((WT) == W_Q4) VC4_MAXC(M, Ops<W_Q4>::FN, __VA_ARGS__); \
+        else VC4_MAXC(M, Ops<W_T3>::FN, __VA_ARGS__);                  \
     } while (0)
 
 void launch_embed_qkv(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st) {
-    VC4_DISPATCH(m.mats[m.qkv[layer]].wtype, qkv_t, m, s, b, layer, st);
+    const DMat& W = m.mats[m.qkv[layer]];
+    VC4_DISPATCH(W.wtype, maxc_for(W.nchunks), qkv, m, s, b, layer, st);
 }
 void launch_wo(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st) {
-    VC4_DISPATCH(m.mats[m.wo[layer]].wtype, wo_t, m, s, b, layer, st);
+    const DMat& W = m.mats[m.wo[layer]];
+    VC4_DISPATCH(W.wtype, maxc_for(W.nchunks), wo, m, s, b, layer, st);
 }
 void launch_ffn_gate(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st) {
-    const int wt = m.h.experts ? m.mats[m.e_w1[(size_t)layer * m.h.experts]].wtype : m.mats[m.w1[layer]].wtype;
-    VC4_DISPATCH(wt, gate_t, m, s, b, layer, st);
+    const DMat& W = m.h.experts ? m.mats[m.e_w1[(size_t)layer * m.h.experts]] : m.mats[m.w1[layer]];
+    VC4_DISPATCH(W.wtype, maxc_for(W.nchunks), gate, m, s, b, layer, st);
 }
 void launch_ffn_down(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st) {
-    const int wt = m.h.experts ? m.mats[m.e_w1[(size_t)layer * m.h.experts] + 2].wtype : m.mats[m.w2a[layer]].wtype;
-    VC4_DISPATCH(wt, down_t, m, s, b, layer, st);
+    const DMat& W = m.h.experts ? m.mats[m.e_w1[(size_t)layer * m.h.experts] + 2] : m.mats[m.w2a[layer]];
+    VC4_DISPATCH(W.wtype, maxc_for(W.nchunks), down, m, s, b, layer, st);
 }
 void launch_logits(const DModel& m, const State& s, const Batch& b, cudaStream_t st) {
-    logits_t<W_Q8>(m, s, b, st);
+    const DMat& W = m.mats[m.logits_mat];
+    VC4_MAXC(maxc_for(W.nchunks), Ops<W_Q8>::logits, m, s, b, st);
 }
 
 void launch_attention(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st) {
     Dims d = dims_of(m, s);
     const int group = d.heads / d.kv_heads, hd = d.head_dim;
-    const size_t sm = kRedBytes + sizeof(float) * ((size_t)group * hd + 2 * hd + (size_t)kTile * (hd + 1) +
-                                             (size_t)group * d.seq) +
-                      16 + sizeof(double) * (size_t)kWarps * group * hd;
-    set_smem(k_attn, sm);
-    k_attn<<<dim3(d.kv_heads, b.n), kThreads, sm, st>>>(m.d_q_norm, m.d_k_norm, s, b, d, layer);
+    const int max_rows = (d.seq + kAttnCtas - 1) / kAttnCtas;
+    const size_t sm = kRedBytes + sizeof(double) * (((size_t)group * hd + 1) & ~(size_t)1) + 8 * 8 + 8 * 4 +
+                      sizeof(float) * ((size_t)group * hd + 2 * hd + 2 * (size_t)max_rows * (hd + 1) +
+                                       (size_t)group * max_rows);
+    launch_pdl(k_attn, dim3(d.kv_heads * kAttnCtas, b.n), sm, st, (const float*)m.d_q_norm,
+               (const float*)m.d_k_norm, s, b, d, layer, max_rows);
 }
 
 void launch_matvec_raw(const DModel& m, int mat, const int16_t* xq, int n, int32_t* out, cudaStream_t st) {
     const DMat& W = m.mats[mat];
     if (W.wtype == W_I16) { k_raw_i16<<<W.rows, kThreads, 0, st>>>(W, xq, n, out); return; }
-    const size_t sm = smem_bytes(1, x_stride(W), g_stride(W), 0);
-    if (W.wtype == W_Q8) { set_smem(k_raw<W_Q8>, sm); k_raw<W_Q8><<<W.rblocks, kThreads, sm, st>>>(W, xq, n, out); }
-    else if (W.wtype == W_Q4) { set_smem(k_raw<W_Q4>, sm); k_raw<W_Q4><<<W.rblocks, kThreads, sm, st>>>(W, xq, n, out); }
-    else { set_smem(k_raw<W_T3>, sm); k_raw<W_T3><<<W.rblocks, kThreads, sm, st>>>(W, xq, n, out); }
+    VC4_DISPATCH(W.wtype, maxc_for(W.nchunks), raw, W, xq, n, out, st);
 }
 
 void launch_finalize(const State& s, const Batch& b, int* next, int* tokens, int* pos, int advance,
@@ -945,5 +1112,14 @@ int kernel_launches_per_step(const DModel& m, int n) {
     const int g = (n + kNB - 1) / kNB;
     return m.h.layers * (4 * g + 1) + g + 1;
 }
+
+bool attention_fits(int seq, int head_dim, int kv_bits, int kv_dim) {
+    const int hbytes = kv_bits == 16 ? 2 * head_dim : head_dim;
+    if (hbytes % 16 || kv_dim % 16) return false;
+    const int max_rows = (seq + kAttnCtas - 1) / kAttnCtas;
+    return 2 * max_rows * (hbytes / 16) <= 16 * kThreads;
+}
+
+int matvec_max_chunks() { return 20 * kWarps; }
 
 }  // namespace vc4

@@ -152,5 +152,8 @@ void launch_finalize(const State& s, const Batch& b, int* next, int* tokens, int
                      const int* forced, cudaStream_t st);
 
 int kernel_launches_per_step(const DModel& m, int n);
+// Shape limits of the kernels (checked at upload / session creation).
+bool attention_fits(int seq, int head_dim, int kv_bits, int kv_dim);
+int matvec_max_chunks();
 
 }  // namespace vc4
