@@ -80,6 +80,12 @@ def model_path(cfg) -> str:
     return path
 
 
+def sequence_ids(rank: int, batch: int) -> list:
+    """The seeded sequences a rank decodes: rank r owns r*B .. r*B+B-1, so
+    ranks never share a sequence and the job's work grows with the ranks."""
+    return [rank * batch + b for b in range(batch)]
+
+
 def workload_desc(cfg) -> str:
     s = cfg.shape
     return ("%s: %s %s, batch %d, KV %s, SEQ %d, %d-token seeded prompt then greedy decode"
@@ -135,18 +141,25 @@ class Clocks:
 # ---------------------------------------------------------------------------
 
 class Dist:
-    def __init__(self, want: int):
+    """torchrun plumbing: rank/world from the environment, a process group
+    used only for barriers and the max-over-ranks time (no data-path
+    collective: every rank decodes its own sequences)."""
+
+    def __init__(self, backend: str = "nccl", timeout_s: int = 120):
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
         self.rank = int(os.environ.get("RANK", "0"))
         self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.backend = backend
         self.pg = None
         if self.world > 1:
             import datetime
             import torch
             import torch.distributed as dist
-            torch.cuda.set_device(self.local)
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                    device_id=torch.device("cuda", self.local))
+            kw = {}
+            if backend == "nccl":
+                torch.cuda.set_device(self.local)
+                kw["device_id"] = torch.device("cuda", self.local)
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout_s), **kw)
             self.pg = dist
 
     def barrier(self):
@@ -154,11 +167,17 @@ class Dist:
             self.pg.barrier()
 
     def max(self, v: float) -> float:
+        return self._reduce(v, "max")
+
+    def sum(self, v: float) -> float:
+        return self._reduce(v, "sum")
+
+    def _reduce(self, v: float, how: str) -> float:
         if not self.pg:
             return v
         import torch
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
-        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        t = torch.tensor([v], dtype=torch.float64, device="cuda" if self.backend == "nccl" else "cpu")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX if how == "max" else self.pg.ReduceOp.SUM)
         return float(t.item())
 
     def close(self):
@@ -234,7 +253,7 @@ def run_ours(args, cfg, dist):
     B = cfg.batch
     sess = vc4b200.Session(model, slots=B, seq=cfg.seq, kv=KV_NAME[cfg.kv_bits])
     info = model.info
-    prompts = [synth.prompt_tokens(cfg, dist.rank * B + b) for b in range(B)]
+    prompts = [synth.prompt_tokens(cfg, i) for i in sequence_ids(dist.rank, B)]
     t0 = time.perf_counter()
     for b in range(B):
         sess.prefill(prompts[b][:-1], 0, slot=b, want_logits=False)
@@ -283,7 +302,7 @@ def run_ours(args, cfg, dist):
     l1, _ = sess.counters()
     ms = sum(a.elapsed_time(b) for a, b in ev)
     ms_max = dist.max(ms)
-    tokens = B * args.steps * dist.world
+    tokens = dist.sum(B * args.steps)
     value = tokens / (ms_max / 1000.0)
 
     # e2e: the public API with host buffers, greedy token read back each step
@@ -375,7 +394,7 @@ def main():
     args = parse()
     from vc4b200 import synth
     cfg = dict(synth.CONFIGS, **synth.TINY_CONFIGS)[args.config]
-    dist = Dist(args.gpus)
+    dist = Dist()
     try:
         if args.impl == "reference":
             run_reference(args, cfg, dist)

@@ -65,6 +65,11 @@ VC4_API int vc4_gpu_sync(vc4_gpu* g);
 VC4_API int vc4_model_load(vc4_gpu* g, const char* mmcf_path, vc4_model** out);
 VC4_API int vc4_model_load_bytes(vc4_gpu* g, const void* data, size_t size, vc4_model** out);
 VC4_API int vc4_model_info_get(const vc4_model* m, vc4_model_info* out);
+/* Model::probe (model.h:209-216): parse and validate a container on the host
+   without touching a GPU (this build validates every tensor record, not only
+   the header and metadata); fills info, or returns VC4_EFORMAT / VC4_EIO with
+   the reader's message. */
+VC4_API int vc4_model_probe(const char* mmcf_path, vc4_model_info* out);
 VC4_API void vc4_model_free(vc4_model* m);
 
 /* Session::reset's device half: GPU::init_attention (gpu_attn.cpp:41-157)

@@ -66,6 +66,11 @@ def lib():
         L.orc_model_mat_levels.argtypes = [vp, ip, ip, ip, vp]
         L.orc_model_mat_rowscale16.argtypes = [vp, ip, ip, ip, vp]
         L.orc_model_mat_q4params.argtypes = [vp, ip, ip, ip, vp, vp]
+        L.orc_model_mat_plane.argtypes = [vp, ip, ip, ip, vp]
+        L.orc_model_emb.argtypes = [vp, vp]
+        L.orc_model_vec.argtypes = [vp, ip, vp]
+        L.orc_fnv1a64.restype = C.c_uint64
+        L.orc_fnv1a64.argtypes = [vp, C.c_uint64]
         _lib = L
     return _lib
 
@@ -118,6 +123,24 @@ class Model:
         m16 = np.empty(r * (c // 32), np.int16)
         lib().orc_model_mat_q4params(self._h, which, layer, expert, _ptr(s16), _ptr(m16))
         return s16.reshape(r, -1), m16.reshape(r, -1)
+
+    def mat_plane(self, which, layer=0, expert=0):
+        r, _, _, _ = self.mat_shape(which, layer, expert)
+        out = np.empty(r, np.float32)
+        return out if lib().orc_model_mat_plane(self._h, which, layer, expert, _ptr(out)) == 1 else None
+
+    def emb(self):
+        n = lib().orc_model_emb(self._h, None)
+        out = np.empty(n, np.int8)
+        lib().orc_model_emb(self._h, _ptr(out))
+        return out
+
+    def vec(self, which: int):
+        n = lib().orc_model_vec(self._h, which, None)
+        out = np.empty(max(n, 0), np.float32)
+        if n > 0:
+            lib().orc_model_vec(self._h, which, _ptr(out))
+        return out
 
     def matvec(self, which, layer, expert, xq: np.ndarray):
         r, _, _, _ = self.mat_shape(which, layer, expert)
@@ -189,6 +212,12 @@ def generate(model: Model, kv_bits: int, prompt, steps: int, literal: bool = Fal
         toks.append(tok)
         logs.append(lg)
     return toks, np.stack(logs), s
+
+
+def fnv64(a: np.ndarray) -> str:
+    """FNV-1a/64 of an array's bytes, as 16 hex digits."""
+    a = np.ascontiguousarray(a)
+    return "%016x" % lib().orc_fnv1a64(_ptr(a), a.nbytes)
 
 
 def expf(x: float) -> float:

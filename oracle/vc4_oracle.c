@@ -1013,3 +1013,39 @@ int orc_model_mat_q4params(const orc_model* m, int which, int layer, int expert,
     memcpy(m16, w->m16, sizeof(int16_t) * (size_t)w->rows * w->groups);
     return ORC_OK;
 }
+
+int orc_model_mat_plane(const orc_model* m, int which, int layer, int expert, float* plane) {
+    const omat* w = pick(m, which, layer, expert);
+    if (!w || !w->plane) return 0;
+    memcpy(plane, w->plane, sizeof(float) * (size_t)w->rows);
+    return 1;
+}
+
+int orc_model_emb(const orc_model* m, int8_t* out) {
+    const int n = m->in.vocab * m->in.dim;
+    if (out) memcpy(out, m->emb, (size_t)n);
+    return n;
+}
+
+int orc_model_vec(const orc_model* m, int which, float* out) {
+    const orc_info* in = &m->in;
+    const float* src = NULL;
+    int n = 0;
+    switch (which) {
+        case 0: src = m->emb_scale; n = in->vocab; break;
+        case 1: src = m->rms_att; n = in->layers * in->dim; break;
+        case 2: src = m->rms_ffn; n = in->layers * in->dim; break;
+        case 3: src = m->rms_final; n = in->dim; break;
+        case 4: src = m->q_norm; n = m->q_norm ? in->layers * in->head_dim : 0; break;
+        case 5: src = m->k_norm; n = m->k_norm ? in->layers * in->head_dim : 0; break;
+        default: return -1;
+    }
+    if (out && src) memcpy(out, src, sizeof(float) * (size_t)n);
+    return n;
+}
+
+uint64_t orc_fnv1a64(const uint8_t* p, uint64_t n) {
+    uint64_t h = 1469598103934665603ull;
+    for (uint64_t i = 0; i < n; ++i) { h ^= p[i]; h *= 1099511628211ull; }
+    return h;
+}

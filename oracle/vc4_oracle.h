@@ -94,6 +94,15 @@ int orc_model_mat_rowscale16(const orc_model* m, int which, int layer, int exper
                              uint16_t* p16 /* rows, or returns 0 if none */);
 int orc_model_mat_q4params(const orc_model* m, int which, int layer, int expert,
                            int16_t* s16, int16_t* m16);
+/* The container's f32 row plane of a matrix (returns 1, or 0 if it has none). */
+int orc_model_mat_plane(const orc_model* m, int which, int layer, int expert, float* plane);
+/* Embedding levels (vocab*dim) and the model's f32 vectors:
+   which 0 emb_scale, 1 rms_att, 2 rms_ffn, 3 rms_final, 4 q_norm, 5 k_norm.
+   Returns the element count (out may be NULL to query it). */
+int orc_model_emb(const orc_model* m, int8_t* out);
+int orc_model_vec(const orc_model* m, int which, float* out);
+/* 64-bit FNV-1a of a byte string (the digest the golden summaries carry). */
+uint64_t orc_fnv1a64(const uint8_t* p, uint64_t n);
 
 #ifdef __cplusplus
 }

@@ -379,6 +379,21 @@ int vc4_model_info_get(const vc4_model* m, vc4_model_info* o) {
     return VC4_OK;
 }
 
+int vc4_model_probe(const char* path, vc4_model_info* o) {
+    HModel h;
+    const std::string e = load_mmcf(path, h);
+    if (!e.empty()) return fail(e.rfind("cannot", 0) == 0 || e.rfind("short", 0) == 0 ? VC4_EIO : VC4_EFORMAT, e);
+    memset(o, 0, sizeof(*o));
+    o->dim = h.dim; o->hidden = h.hidden; o->layers = h.layers; o->heads = h.heads; o->kv_heads = h.kv_heads;
+    o->vocab = h.vocab; o->seq = h.seq; o->head_dim = h.head_dim; o->kv_dim = h.kv_dim;
+    o->experts = h.experts; o->moe_hidden = h.moe_hidden; o->ffn_width = h.ffn_width();
+    o->ffn_chunked = o->ffn_width > 2048; o->ffn_chunk = o->ffn_chunked ? (o->ffn_width + 1) / 2 : o->ffn_width;
+    o->qk_norm = h.qk_norm; o->rope_half = h.rope_half; o->head_dedup = h.head_dedup; o->wtype = h.wo[0].wtype;
+    o->rope_theta = h.rope_theta; o->rms_eps = h.rms_eps;
+    o->source_size = h.source_size; o->source_mtime = h.source_mtime;
+    return VC4_OK;
+}
+
 void vc4_model_free(vc4_model* m) {
     if (!m) return;
     cudaSetDevice(m->d.device);

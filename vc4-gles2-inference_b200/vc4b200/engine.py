@@ -46,6 +46,10 @@ _PROTOS = {
     "vc4_model_load_bytes": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.POINTER(C.c_void_p)]),
     "vc4_model_info_get": (C.c_int, [C.c_void_p, C.POINTER(ModelInfo)]),
     "vc4_model_free": (None, [C.c_void_p]),
+    "vc4_model_probe": (C.c_int, [C.c_char_p, C.POINTER(ModelInfo)]),
+    "vc4_profile_op": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                 C.c_int, C.c_int, C.POINTER(C.c_double)]),
+    "vc4_op_bytes": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.POINTER(C.c_double)]),
     "vc4_session_create": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
                                      C.POINTER(C.c_void_p)]),
     "vc4_session_destroy": (None, [C.c_void_p]),
@@ -102,6 +106,13 @@ def rope_tables(theta: float, head_dim: int, seq: int, factors=None):
     f = None if factors is None else np.ascontiguousarray(factors, np.float32)
     lib().vc4_rope_tables(theta, head_dim, seq, _p(f) if f is not None else None, _p(c), _p(s))
     return c.reshape(seq, half), s.reshape(seq, half)
+
+
+def probe(path: str) -> ModelInfo:
+    """Model::probe: validate a container on the host (no GPU needed)."""
+    info = ModelInfo()
+    _check(lib().vc4_model_probe(path.encode(), C.byref(info)))
+    return info
 
 
 class GPU:
