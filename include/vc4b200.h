@@ -149,6 +149,22 @@ VC4_API int vc4_profile_op(vc4_session* s, int op, int layer, int n, const int* 
    activations in and out. */
 VC4_API int vc4_op_bytes(const vc4_session* s, int op, int layer, int n, const int* pos, double* bytes);
 
+/* No counterpart in the reference.  vc4_matvec_s for callers that cannot
+   allocate device memory: a host whose device memory belongs to its own pool,
+   or a thread that must not risk the device synchronisation an allocation can
+   cause.  d_x (cols floats) and d_out (rows floats) are the caller's device
+   buffers; the scaled input and the integer results live in one static device
+   array of at most 16384 columns and 81920 rows, resident on every GPU that
+   uses the library until the process exits.  Larger matrices return
+   VC4_EINVAL.  Nothing is allocated or freed.  The work is queued on `stream`
+   (NULL: the model's stream) and the call returns without waiting.  The first
+   call on a device looks up the array's device address (cudaGetSymbolAddress)
+   and caches it, so make that first call before any stream capture.  Every
+   call shares the one array, so calls whose work can overlap on the GPU race:
+   keep them on one stream. */
+VC4_API int vc4_matvec_s_noalloc(vc4_model* m, int which, int layer, int expert, const float* d_x,
+                                 float* d_out, void* stream);
+
 /* draws()/syncs() (gpu.h:44-48): kernels launched and host syncs so far. */
 VC4_API int vc4_counters(const vc4_session* s, long long* launches, long long* syncs);
 /* Kernels one decode pass of n sequences launches. */

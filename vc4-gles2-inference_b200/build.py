@@ -22,7 +22,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-std=c++17", "-O3", "-lineinfo", "--fmad=false", "-I" + INCLUDE, "-I" + CSRC,
          "-Xcompiler", "-fPIC,-ffp-contract=off,-fvisibility=hidden", "-diag-suppress", "177"]
-SOURCES = ["kernels.cu", "engine.cu", "mmcf.cpp"]
+SOURCES = ["kernels.cu", "engine.cu", "noalloc.cu", "mmcf.cpp"]
 HEADERS = ["vc4b200_internal.h"]
 
 

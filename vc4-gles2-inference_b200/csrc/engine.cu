@@ -881,3 +881,45 @@ extern "C" int vc4_op_bytes(const vc4_session* s, int op, int layer, int n, cons
     *bytes = b;
     return VC4_OK;
 }
+
+// ---------------------------------------------------------------------------
+// internal accessors for other translation units of the library
+// ---------------------------------------------------------------------------
+
+namespace vc4 {
+
+int set_error(int code, const char* msg) { return fail(code, msg); }
+
+const DModel& model_of(const vc4_model* m) { return m->d; }
+
+cudaStream_t model_stream(const vc4_model* m) { return m->g->stream; }
+
+// The device matrix `which` of `layer` (and `expert`) names, as vc4_matvec_s
+// resolves it; returns VC4_OK and the index into DModel::mats.
+int lookup_matrix(const vc4_model* m, int which, int layer, int expert, int* idx) {
+    const DModel& d = m->d;
+    const HModel& h = d.h;
+    *idx = -1;
+    if (which != 6 && (layer < 0 || layer >= h.layers)) return fail(VC4_EINVAL, "layer out of range");
+    const bool moe = h.experts > 0;
+    if (moe && (which == 2 || which == 3 || which == 4)) {
+        if (expert < 0 || expert >= h.experts) return fail(VC4_EINVAL, "expert out of range");
+        *idx = d.e_w1[(size_t)layer * h.experts + expert] + (which == 2 ? 0 : which == 3 ? 1 : 2);
+    } else {
+        switch (which) {
+            case 0: *idx = d.qkv[layer]; break;
+            case 1: *idx = d.wo[layer]; break;
+            case 2: *idx = d.w1[layer]; break;
+            case 3: *idx = d.w3[layer]; break;
+            case 4: *idx = d.w2a[layer]; break;
+            case 5: *idx = moe ? d.router[layer] : -1; break;
+            case 6: *idx = d.logits_mat; break;
+            default: break;
+        }
+    }
+    if (*idx < 0) return fail(VC4_EINVAL, "no such matrix");
+    if (which == 4 && d.ffn_chunked) return fail(VC4_EINVAL, "w2 of a chunked FFN is two matrices; the CPU path never draws it whole");
+    return VC4_OK;
+}
+
+}  // namespace vc4

@@ -156,4 +156,12 @@ int kernel_launches_per_step(const DModel& m, int n);
 bool attention_fits(int seq, int head_dim, int kv_bits, int kv_dim);
 int matvec_max_chunks();
 
+// Accessors engine.cu gives the library's other translation units.
+}  // namespace vc4
+struct vc4_model;
+namespace vc4 {
+int set_error(int code, const char* msg);
+const DModel& model_of(const vc4_model* m);
+cudaStream_t model_stream(const vc4_model* m);
+int lookup_matrix(const vc4_model* m, int which, int layer, int expert, int* idx);
 }  // namespace vc4

@@ -69,6 +69,8 @@ _PROTOS = {
     "vc4_load_prefix_cache": (C.c_int, [C.c_void_p, C.c_int, C.c_char_p, C.c_void_p, C.c_int,
                                         C.POINTER(C.c_int)]),
     "vc4_matvec_s": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
+    "vc4_matvec_s_noalloc": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
+                                       C.c_void_p]),
     "vc4_counters": (C.c_int, [C.c_void_p, C.POINTER(C.c_longlong), C.POINTER(C.c_longlong)]),
     "vc4_launches_per_step": (C.c_int, [C.c_void_p, C.c_int]),
 }
