@@ -112,7 +112,8 @@ std::string relay(const HMat& h, int c0, int c1, DMat& d, std::vector<void*>& al
     const int ncols = c1 - c0;
     if (h.wtype == W_Q4 && (c0 % 32 || ncols % 32)) return "q4 slice is not group aligned";
     d.nchunks = (ncols + cpc - 1) / cpc;
-    if (d.nchunks > matvec_max_chunks()) return "matrix too wide for the matvec kernel (" + std::to_string(ncols) + " columns)";
+    if (d.nchunks > matvec_max_chunks() || d.nchunks * cpc > max_input_cols())
+        return "matrix too wide for the matvec kernel (" + std::to_string(ncols) + " columns)";
     const size_t nbody = (size_t)d.rblocks * d.nchunks * 32 * 16;
     std::vector<uint8_t> body(nbody, 0);
     std::vector<int32_t> q4p;
@@ -272,11 +273,20 @@ void enqueue_pass(vc4_session* s, const PassArgs& a, cudaStream_t st) {
         launch_ffn_gate(m, s->st, b, l, st);
         launch_ffn_down(m, s->st, b, l, st);
     }
-    launch_logits(m, s->st, b, st);
-    launch_finalize(s->st, b, a.next, a.tokens, a.pos, a.advance, a.forced, st);
+    launch_logits(m, s->st, b, a.next, a.tokens, a.pos, a.advance, a.forced, st);
 }
 
 }  // namespace
+
+// The kernels' self-check word (shared-memory reservation), read after the
+// eager first run of every pass shape.
+static int check_kernel_word(vc4_session* s) {
+    int w = 0;
+    CK(cudaStreamSynchronize(s->stream));
+    CK(cudaMemcpy(&w, s->st.err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (w) return fail(VC4_ECUDA, "a kernel found its shared-memory reservation too small (needs " + std::to_string(w) + " bytes)");
+    return VC4_OK;
+}
 
 // One decode pass: the first call of a shape runs eagerly (kernel attributes
 // are set, errors surface) and captures a graph; later calls replay it.
@@ -289,6 +299,7 @@ static int run_pass(vc4_session* s, const PassArgs& a) {
     } else {
         enqueue_pass(s, a, s->stream);
         CK(cudaGetLastError());
+        if (int e = check_kernel_word(s)) return e;
         cudaGraph_t g = nullptr;
         CK(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
         enqueue_pass(s, a, s->stream);
@@ -423,6 +434,8 @@ int vc4_session_create(vc4_model* m, int slots, int seq, int kv_bits, const floa
     if (kv_bits != 16 && kv_bits != 8) return fail(VC4_EINVAL, "kv_bits must be 16 (q16) or 8 (q8)");
     if (kv_bits == 8 && (h.kv_dim % 4 || h.head_dim % 4)) return fail(VC4_EINVAL, "q8 KV needs kv_dim and head_dim divisible by 4");
     if (h.heads / h.kv_heads > 8 || h.head_dim > 128) return fail(VC4_EINVAL, "attention group above 8 or head_dim above 128");
+    if (h.dim > max_input_cols() || m->d.ffn_width > max_input_cols())
+        return fail(VC4_EINVAL, "model width beyond the kernels' staging limit");
     if (!attention_fits(seq, h.head_dim, kv_bits, h.kv_dim))
         return fail(VC4_EINVAL, "sequence length / head shape beyond the attention kernel's staging limits");
     CK(cudaSetDevice(m->d.device));
@@ -445,7 +458,7 @@ int vc4_session_create(vc4_model* m, int slots, int seq, int kv_bits, const floa
               alloc((void**)&st.rope_cos, (size_t)seq * (h.head_dim / 2) * 4) &&
               alloc((void**)&st.rope_sin, (size_t)seq * (h.head_dim / 2) * 4) &&
               alloc((void**)&s->d_slot, (size_t)(3 * slots + 1) * 4) && alloc((void**)&s->d_next, (size_t)slots * 4) &&
-              alloc((void**)&s->d_pos, (size_t)seq * 4 + 16);
+              alloc((void**)&s->d_pos, (size_t)seq * 4 + 16) && alloc((void**)&st.done, 16) && alloc((void**)&st.err, 16);
     if (!ok) { vc4_session_destroy(s); return fail(VC4_ECUDA, "session allocation failed (slots*seq too large?)"); }
     s->d_tok = s->d_slot + slots;
     if (cudaMallocHost((void**)&s->h_pin, (size_t)(4 * slots + 16) * 4) != cudaSuccess ||
@@ -479,7 +492,7 @@ void vc4_session_destroy(vc4_session* s) {
     State& st = s->st;
     for (void* p : {(void*)st.x, (void*)st.x1, (void*)st.qkv, (void*)st.att, (void*)st.h, (void*)st.logits,
                     (void*)st.best, (void*)st.next, (void*)st.route, (void*)st.kv, (void*)st.rope_cos,
-                    (void*)st.rope_sin, (void*)s->d_slot, (void*)s->d_next, (void*)s->d_pos})
+                    (void*)st.rope_sin, (void*)s->d_slot, (void*)s->d_next, (void*)s->d_pos, (void*)st.done, (void*)st.err})
         if (p) cudaFree(p);
     if (s->h_pin) cudaFreeHost(s->h_pin);
     if (s->h_logits) cudaFreeHost(s->h_logits);
@@ -516,7 +529,7 @@ static int host_step(vc4_session* s, int n, const int* slots, const int* tokens,
     CK(cudaMemcpyAsync(hp + 3 * n, s->d_next, sizeof(int) * n, cudaMemcpyDeviceToHost, s->stream));
     if (logits)
         for (int i = 0; i < n; ++i)
-            CK(cudaMemcpyAsync(s->h_logits + (size_t)i * V, s->st.logits + (size_t)slots[i] * V, sizeof(int32_t) * V,
+            CK(cudaMemcpyAsync(s->h_logits + (size_t)i * V, s->st.logits + (size_t)i * V, sizeof(int32_t) * V,
                                cudaMemcpyDeviceToHost, s->stream));
     CK(cudaStreamSynchronize(s->stream));
     s->syncs++;
@@ -568,7 +581,7 @@ int vc4_prefill(vc4_session* s, int slot, const int* tokens, int n, int pos0, fl
     PassArgs a{1, dcall, dcall + 1, dcall + 2, s->d_next, 1, dprompt};
     for (int i = 0; i < n; ++i)
         if (int e = run_pass(s, a)) return e;
-    if (logits) CK(cudaMemcpyAsync(s->h_logits, s->st.logits + (size_t)slot * V, sizeof(int32_t) * V,
+    if (logits) CK(cudaMemcpyAsync(s->h_logits, s->st.logits, sizeof(int32_t) * V,
                                    cudaMemcpyDeviceToHost, s->stream));
     CK(cudaStreamSynchronize(s->stream));
     s->syncs++;
@@ -788,7 +801,7 @@ void launch_op(vc4_session* s, int op, int layer, const Batch& b, cudaStream_t s
         case 2: launch_wo(m, s->st, b, layer, st); break;
         case 3: launch_ffn_gate(m, s->st, b, layer, st); break;
         case 4: launch_ffn_down(m, s->st, b, layer, st); break;
-        default: launch_logits(m, s->st, b, st); break;
+        default: launch_logits(m, s->st, b, s->d_next, nullptr, nullptr, 0, nullptr, st); break;
     }
 }
 
@@ -828,6 +841,7 @@ extern "C" int vc4_profile_op(vc4_session* s, int op, int layer, int n, const in
     CK(cudaGetLastError());
     cudaEventDestroy(e0);
     cudaEventDestroy(e1);
+    if (int e = check_kernel_word(s)) return e;
     *avg_ms = total / reps;
     return VC4_OK;
 }

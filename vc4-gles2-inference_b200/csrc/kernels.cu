@@ -120,6 +120,8 @@ __device__ int block_max_i32(int v, Red& r) {
 // Input staging: q16 ints -> (optionally 2^k scaled) ints split into lo/hi bytes
 // ---------------------------------------------------------------------------
 
+constexpr int kPer = 16;   // vector elements per thread: inputs of up to 16*256 = 4096 columns
+
 struct XStage {
     uint8_t* lo;       // [nb][stride]
     int8_t* hi;        // [nb][stride]
@@ -128,6 +130,47 @@ struct XStage {
     int gstride;
     int k[8];          // per input: power-of-two input scale (matvec_s)
 };
+
+// Copy n int16 from global to shared memory with every load issued before the
+// first store (one DRAM round trip); 16-byte vectors when aligned.
+__device__ __forceinline__ void load_vec(const int16_t* __restrict__ g, int n, int16_t* sm) {
+    if ((n & 7) == 0 && (((uintptr_t)g | (uintptr_t)sm) & 15) == 0) {
+        const int nv = n >> 3;
+        uint4 t[2];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int v = threadIdx.x + i * blockDim.x;
+            if (v < nv) t[i] = __ldcg(reinterpret_cast<const uint4*>(g) + v);
+        }
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int v = threadIdx.x + i * blockDim.x;
+            if (v < nv) reinterpret_cast<uint4*>(sm)[v] = t[i];
+        }
+        return;
+    }
+    int16_t t[kPer];
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+        const int c = threadIdx.x + i * blockDim.x;
+        t[i] = c < n ? __ldcg(g + c) : (int16_t)0;
+    }
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+        const int c = threadIdx.x + i * blockDim.x;
+        if (c < n) sm[c] = t[i];
+    }
+}
+
+// This thread's elements c = threadIdx.x + i*blockDim.x of a float vector,
+// loaded into registers (the per-layer norm weights, prefetched early).
+__device__ __forceinline__ void load_f32_regs(const float* __restrict__ g, int n, float (&r)[kPer]) {
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+        const int c = threadIdx.x + i * blockDim.x;
+        r[i] = c < n ? __ldg(g + c) : 0.0f;
+    }
+}
 
 // matvec_s scaling exponent of a q16 vector (gpu_conv.cpp:271-287):
 // max|x| = f*2^e with f in [0.5, 1) gives k = 6 - e.
@@ -142,7 +185,9 @@ __device__ int scale_exponent(const int16_t* v, int n, Red& r) {
 }
 
 // Stage one input: x'[c] = v[c]*2^k (k >= 0: exact shift; k < 0: x_pack's
-// round-half-even), zero-padded to `stride`; group sums for q4 / total for t3.
+// round-half-even), zero-padded to `stride`; q4 group sums by warp shuffles
+// (a warp covers one 32-column group per iteration), the t3 total by a block
+// reduction.  v is in shared memory.  Ends with a barrier.
 template <int WT>
 __device__ void stage_one(XStage& xs, int b, const int16_t* v, int n, int k, Red& r) {
     uint8_t* lo = xs.lo + (size_t)b * xs.stride;
@@ -157,6 +202,11 @@ __device__ void stage_one(XStage& xs, int b, const int16_t* v, int n, int k, Red
         }
         lo[c] = (uint8_t)(q & 0xFF);
         hi[c] = (int8_t)(q >> 8);
+        if (WT == W_Q4) {
+            int g = q;
+            for (int o = 16; o; o >>= 1) g += __shfl_xor_sync(0xffffffffu, g, o);
+            if ((threadIdx.x & 31) == 0) xs.gsum[b * xs.gstride + (c >> 5)] = g;
+        }
         tot += q;
     }
     if (WT == W_T3) {
@@ -164,29 +214,25 @@ __device__ void stage_one(XStage& xs, int b, const int16_t* v, int n, int k, Red
         if (threadIdx.x == 0) xs.gsum[b * xs.gstride] = (int)t;
     }
     __syncthreads();
-    if (WT == W_Q4) {
-        const int ng = xs.stride / 32;
-        for (int g = threadIdx.x; g < ng; g += blockDim.x) {
-            int s = 0;
-            for (int j = 0; j < 32; ++j) s += (int)lo[g * 32 + j] + 256 * (int)hi[g * 32 + j];
-            xs.gsum[b * xs.gstride + g] = s;
-        }
-    }
-    __syncthreads();
 }
 
 // RMSNorm of a q16 vector into q16 ints (session.cpp:1932-1948 with the exact
-// integer sum of squares rounded once).
-__device__ void rmsnorm_q16(const int16_t* x, const float* w, int D, float eps, int16_t* out, Red& r) {
+// integer sum of squares rounded once).  x and out are shared memory; w holds
+// this thread's norm weights (load_f32_regs).
+__device__ void rmsnorm_q16(const int16_t* x, const float (&w)[kPer], int D, float eps, int16_t* out, Red& r) {
     long long ss = 0;
     for (int c = threadIdx.x; c < D; c += blockDim.x) { const long long a = x[c]; ss += a * a; }
     ss = block_sum_i64(ss, r);
     const float s1 = __fmul_rn(__ll2float_rn(ss), 1.0f / 65536.0f);
     const float s2 = __fdiv_rn(s1, (float)D);
     const float rr = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(s2, eps)));
-    for (int c = threadIdx.x; c < D; c += blockDim.x) {
-        const float xv = __fmul_rn((float)x[c], 1.0f / 256.0f);
-        out[c] = (int16_t)q16h(__fmul_rn(w[c], __fmul_rn(rr, xv)));
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+        const int c = threadIdx.x + i * blockDim.x;
+        if (c < D) {
+            const float xv = __fmul_rn((float)x[c], 1.0f / 256.0f);
+            out[c] = (int16_t)q16h(__fmul_rn(w[i], __fmul_rn(rr, xv)));
+        }
     }
     __syncthreads();
 }
@@ -215,6 +261,7 @@ template <int MAXC>
 struct WRegs {
     int4 w[MAXC];
     int sp[MAXC];   // q4: packed (s16 | m16 << 16) of the chunk's scale group
+    float rs;       // the epilogue scale of this lane's row
 };
 
 template <int WT, int MAXC>
@@ -229,6 +276,7 @@ __device__ __forceinline__ void mv_prefetch(const DMat& W, int blk, WRegs<MAXC>&
             if (WT == W_Q4) R.sp[k] = __ldg(W.q4p + ((size_t)blk * nch + j) * 32 + lane);
         }
     }
+    R.rs = __ldg(W.rscale + (size_t)blk * 32 + lane);
 }
 
 template <int WT, int NB, int MAXC>
@@ -320,6 +368,18 @@ struct SmemLayout {
     static __device__ char* base() { extern __shared__ __align__(16) char smem[]; return smem; }
 };
 
+// Self-check before any shared-memory use: the launch must have reserved at
+// least `need` bytes of dynamic shared memory.  A short launch records the
+// shortfall in the session's error word and the block returns without
+// touching shared memory (the host turns the word into an error).
+__device__ __forceinline__ bool smem_ok(size_t need, int* err) {
+    unsigned have;
+    asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(have));
+    if ((size_t)have >= need) return true;
+    if (threadIdx.x == 0) atomicMax(err, (int)need);
+    return false;
+}
+
 // dynamic shared memory: [Red][partials kWarps*NB*32][gsum][lo][hi][scratch]
 template <int NB>
 __device__ void carve(int stride, int gstride, XStage& xs, Red*& red, long long*& part, int16_t*& tmp) {
@@ -333,7 +393,7 @@ __device__ void carve(int stride, int gstride, XStage& xs, Red*& red, long long*
     xs.stride = stride; xs.gstride = gstride;
 }
 
-__host__ size_t smem_bytes(int nb, int stride, int gstride, int tmp_n) {
+__host__ __device__ size_t smem_bytes(int nb, int stride, int gstride, int tmp_n) {
     return (sizeof(Red) + 15) / 16 * 16 + sizeof(long long) * kWarps * nb * 32 +
            (sizeof(int) * nb * gstride + 15) / 16 * 16 + 2 * (size_t)nb * stride + sizeof(int16_t) * (size_t)tmp_n;
 }
@@ -362,27 +422,44 @@ Dims dims_of(const DModel& m, const State& s) {
 }
 
 // ---------------------------------------------------------------------------
+// Per-pass activations are indexed by the batch position b; only the KV cache
+// is indexed by the sequence's slot.  Every kernel issues its weight, scale
+// and norm-weight loads before griddepcontrol.wait and needs one dependent
+// round trip for its activations afterwards.
+// ---------------------------------------------------------------------------
+
+// Two matrices a kernel reads by value, per expert for MoE (blockIdx.y).
+struct MatSet {
+    DMat a[8];
+    DMat b[8];
+    DMat router;
+};
+
+// ---------------------------------------------------------------------------
 // qkv: [embedding] + RMSNorm + matvec_s(qkv)
 // ---------------------------------------------------------------------------
 
 template <int WT, int NB, int MAXC>
 __global__ void __launch_bounds__(kThreads) k_qkv(DMat W, DMat E, const float* emb_scale, const float* rms_w,
                                                   State s, Batch bt, Dims d, int layer, int b0) {
+    if (!smem_ok(smem_bytes(NB, x_stride(W), g_stride(W), NB * d.dim), s.err)) return;
     WRegs<MAXC> R;
     mv_prefetch<WT, MAXC>(W, blockIdx.x, R);
+    float nw[kPer];
+    load_f32_regs(rms_w, d.dim, nw);
     pdl_launch_dependents();
     pdl_wait();
     XStage xs; Red* red; long long* part; int16_t* tmp;
     carve<NB>(x_stride(W), g_stride(W), xs, red, part, tmp);
     const int nb = min(NB, bt.n - b0);
     for (int b = 0; b < nb; ++b) {
-        const int slot = bt.slot[b0 + b];
-        int16_t* x = s.x + (size_t)slot * d.dim;
+        const int bi = b0 + b;
+        int16_t* x = s.x + (size_t)bi * d.dim;
         int16_t* xin = tmp + (size_t)b * d.dim;
         if (layer == 0) {
             // embedding (session.cpp:342-371): q16(level * row scale); the row
             // is read from the blocked q8 layout of the embedding matrix.
-            const int tok = bt.token[b0 + b];
+            const int tok = bt.token[bi];
             const float es = emb_scale[tok];
             const int8_t* eb = reinterpret_cast<const int8_t*>(E.body) + ((size_t)(tok / 32) * E.nchunks * 32 + (tok % 32)) * 16;
             for (int c = threadIdx.x; c < d.dim; c += blockDim.x) {
@@ -391,12 +468,12 @@ __global__ void __launch_bounds__(kThreads) k_qkv(DMat W, DMat E, const float* e
                 xin[c] = q;
                 if (blockIdx.x == 0) x[c] = q;
             }
-            if (blockIdx.x == 0 && threadIdx.x == 0) s.best[slot] = 0ull;
+            if (blockIdx.x == 0 && threadIdx.x == 0) s.best[bi] = 0ull;
         } else {
-            for (int c = threadIdx.x; c < d.dim; c += blockDim.x) xin[c] = x[c];
+            load_vec(x, d.dim, xin);
         }
         __syncthreads();
-        rmsnorm_q16(xin, rms_w, d.dim, d.eps, xin, *red);
+        rmsnorm_q16(xin, nw, d.dim, d.eps, xin, *red);
         xs.k[b] = scale_exponent(xin, d.dim, *red);
         stage_one<WT>(xs, b, xin, d.dim, xs.k[b], *red);
     }
@@ -408,9 +485,9 @@ __global__ void __launch_bounds__(kThreads) k_qkv(DMat W, DMat E, const float* e
         const int row = blockIdx.x * 32 + lane;
         if (row < W.rows) {
             const long long St = WT == W_T3 ? tot - xs.gsum[warp * xs.gstride] : tot;
-            const int v = mv_epi(St, W.rscale[row]);
+            const int v = mv_epi(St, R.rs);
             const float out = __fmul_rn(__fmul_rn((float)v, 1.0f / 256.0f), ldexpf(1.0f, -xs.k[warp]));
-            s.qkv[(size_t)bt.slot[b0 + warp] * (d.dim + 2 * d.kv_dim) + row] = out;
+            s.qkv[(size_t)(b0 + warp) * (d.dim + 2 * d.kv_dim) + row] = out;
         }
     }
 }
@@ -421,6 +498,7 @@ __global__ void __launch_bounds__(kThreads) k_qkv(DMat W, DMat E, const float* e
 
 template <int WT, int NB, int MAXC>
 __global__ void __launch_bounds__(kThreads) k_wo(DMat W, State s, Batch bt, Dims d, int b0) {
+    if (!smem_ok(smem_bytes(NB, x_stride(W), g_stride(W), NB * d.dim), s.err)) return;
     WRegs<MAXC> R;
     mv_prefetch<WT, MAXC>(W, blockIdx.x, R);
     pdl_launch_dependents();
@@ -428,25 +506,26 @@ __global__ void __launch_bounds__(kThreads) k_wo(DMat W, State s, Batch bt, Dims
     XStage xs; Red* red; long long* part; int16_t* tmp;
     carve<NB>(x_stride(W), g_stride(W), xs, red, part, tmp);
     const int nb = min(NB, bt.n - b0);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row = blockIdx.x * 32 + lane;
+    // the residual this thread's epilogue adds, fetched with the inputs
+    const int xres = (warp < nb && row < W.rows) ? (int)__ldcg(s.x + (size_t)(b0 + warp) * d.dim + row) : 0;
+    for (int b = 0; b < nb; ++b) load_vec(s.att + (size_t)(b0 + b) * d.dim, d.dim, tmp + (size_t)b * d.dim);
+    __syncthreads();
     for (int b = 0; b < nb; ++b) {
-        const int16_t* a = s.att + (size_t)bt.slot[b0 + b] * d.dim;
+        const int16_t* a = tmp + (size_t)b * d.dim;
         xs.k[b] = scale_exponent(a, d.dim, *red);
         stage_one<WT>(xs, b, a, d.dim, xs.k[b], *red);
     }
     long long S[NB];
     mv_compute<WT, NB, MAXC>(W, R, xs, nb, S);
     const long long tot = reduce_warps<NB>(S, nb, part);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (warp < nb) {
-        const int row = blockIdx.x * 32 + lane;
-        if (row < W.rows) {
-            const int slot = bt.slot[b0 + warp];
-            const long long St = WT == W_T3 ? tot - xs.gsum[warp * xs.gstride] : tot;
-            const int v = mv_epi(St, W.rscale[row]);
-            const float wo = __fmul_rn(__fmul_rn((float)v, 1.0f / 256.0f), ldexpf(1.0f, -xs.k[warp]));
-            const float xr = __fmul_rn((float)s.x[(size_t)slot * d.dim + row], 1.0f / 256.0f);
-            s.x1[(size_t)slot * d.dim + row] = (int16_t)q16h(__fadd_rn(xr, wo));
-        }
+    if (warp < nb && row < W.rows) {
+        const long long St = WT == W_T3 ? tot - xs.gsum[warp * xs.gstride] : tot;
+        const int v = mv_epi(St, R.rs);
+        const float wo = __fmul_rn(__fmul_rn((float)v, 1.0f / 256.0f), ldexpf(1.0f, -xs.k[warp]));
+        const float xr = __fmul_rn((float)xres, 1.0f / 256.0f);
+        s.x1[(size_t)(b0 + warp) * d.dim + row] = (int16_t)q16h(__fadd_rn(xr, wo));
     }
 }
 
@@ -476,35 +555,38 @@ __device__ int route_of(const int16_t* xbf, const DMat& R, int D, int experts, R
     return best;
 }
 
-// MoE: blockIdx.y is the expert and the CTA serves the inputs routed to it.
-// `early` prefetches the expert's weights before the routing is known (a
-// batch large enough that every expert is used); otherwise after it.
+// blockIdx.y is the expert (0 for a dense FFN); an MoE CTA serves the inputs
+// routed to its expert.  `early` prefetches the expert's weights before the
+// routing is known (a batch that uses every expert), otherwise after it.
 template <int WT, int NB, int MAXC>
-__global__ void __launch_bounds__(kThreads) k_gate(const DMat* mats, int i_w1, int i_w3, int i_router, int e_base,
-                                                   const float* rms_w, State s, Batch bt, Dims d, int layer, int b0,
-                                                   int hs, int early) {
+__global__ void __launch_bounds__(kThreads) k_gate(MatSet M, const float* rms_w, State s, Batch bt, Dims d,
+                                                   int layer, int b0, int hs, int early) {
     const int expert = blockIdx.y;
-    const DMat& W1 = mats[d.experts ? e_base + expert * 4 + 0 : i_w1];
-    const DMat& W3 = mats[d.experts ? e_base + expert * 4 + 1 : i_w3];
+    const DMat& W1 = M.a[expert];
+    const DMat& W3 = M.b[expert];
+    if (!smem_ok(smem_bytes(NB, x_stride(W1), g_stride(W1), (NB + 1) * d.dim) + 64, s.err)) return;
     WRegs<MAXC> R1, R3;
     if (early) {
         mv_prefetch<WT, MAXC>(W1, blockIdx.x, R1);
         mv_prefetch<WT, MAXC>(W3, blockIdx.x, R3);
     }
+    float nw[kPer];
+    load_f32_regs(rms_w, d.dim, nw);
     pdl_launch_dependents();
     pdl_wait();
     XStage xs; Red* red; long long* part; int16_t* tmp;
     carve<NB>(x_stride(W1), g_stride(W1), xs, red, part, tmp);
     int* members = reinterpret_cast<int*>(tmp + (size_t)(NB + 1) * d.dim);   // batch indices served
     const int n_all = min(NB, bt.n - b0);
+    for (int b = 0; b < n_all; ++b) load_vec(s.x1 + (size_t)(b0 + b) * d.dim, d.dim, tmp + (size_t)b * d.dim);
+    __syncthreads();
     int nb = 0;
     for (int b = 0; b < n_all; ++b) {
-        const int slot = bt.slot[b0 + b];
-        int16_t* xin = tmp + (size_t)nb * d.dim;
-        rmsnorm_q16(s.x1 + (size_t)slot * d.dim, rms_w, d.dim, d.eps, xin, *red);
+        int16_t* xin = tmp + (size_t)b * d.dim;
+        rmsnorm_q16(xin, nw, d.dim, d.eps, xin, *red);
         if (d.experts) {
-            const int e = route_of(xin, mats[i_router], d.dim, d.experts, *red);
-            if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) s.route[(size_t)slot * d.layers + layer] = e;
+            const int e = route_of(xin, M.router, d.dim, d.experts, *red);
+            if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) s.route[(size_t)(b0 + b) * d.layers + layer] = e;
             __syncthreads();
             if (e != expert) continue;
         }
@@ -527,13 +609,13 @@ __global__ void __launch_bounds__(kThreads) k_gate(const DMat* mats, int i_w1, i
     if (warp < nb) {
         const int row = blockIdx.x * 32 + lane;
         if (row < W1.rows) {
-            const int slot = bt.slot[b0 + members[warp]];
+            const int bi = b0 + members[warp];
             const int corr = WT == W_T3 ? xs.gsum[warp * xs.gstride] : 0;
-            const int g = mv_epi(t1 - corr, W1.rscale[row]);
-            const int u = mv_epi(t3 - corr, W3.rscale[row]);
+            const int g = mv_epi(t1 - corr, R1.rs);
+            const int u = mv_epi(t3 - corr, R3.rs);
             float y = swiglu1(__fmul_rn((float)g, 1.0f / 256.0f), __fmul_rn((float)u, 1.0f / 256.0f));
             if (hs > 0) y = __fmul_rn(y, ldexpf(1.0f, -hs));     // metadata key 15 store scale
-            s.h[(size_t)slot * d.ffn + row] = (int16_t)q16s(y);
+            s.h[(size_t)bi * d.ffn + row] = (int16_t)q16s(y);
         }
     }
 }
@@ -543,12 +625,14 @@ __global__ void __launch_bounds__(kThreads) k_gate(const DMat* mats, int i_w1, i
 // ---------------------------------------------------------------------------
 
 template <int WT, int NB, int MAXC>
-__global__ void __launch_bounds__(kThreads) k_down(const DMat* mats, int i_w2a, int i_w2b, int e_base,
-                                                   State s, Batch bt, Dims d, int layer, int b0, int early) {
+__global__ void __launch_bounds__(kThreads) k_down(MatSet M, State s, Batch bt, Dims d, int layer, int b0, int early) {
     const int expert = blockIdx.y;
     const bool two = d.chunk < d.ffn;
-    const DMat& Wa = mats[d.experts ? e_base + expert * 4 + 2 : i_w2a];
-    const DMat& Wb = mats[d.experts ? e_base + expert * 4 + 3 : (two ? i_w2b : i_w2a)];
+    const DMat& Wa = M.a[expert];
+    const DMat& Wb = M.b[expert];
+    if (!smem_ok(smem_bytes(NB, x_stride(Wa), g_stride(Wa), 0) + 2 * (size_t)NB * (two ? x_stride(Wb) : 16) +
+                     sizeof(int) * NB * g_stride(Wb) + 256 + sizeof(int16_t) * (size_t)NB * d.ffn, s.err))
+        return;
     WRegs<MAXC> Ra, Rb;
     if (early) {
         mv_prefetch<WT, MAXC>(Wa, blockIdx.x, Ra);
@@ -560,26 +644,32 @@ __global__ void __launch_bounds__(kThreads) k_down(const DMat* mats, int i_w2a, 
     carve<NB>(x_stride(Wa), g_stride(Wa), xa, red, part, tmp);
     xb = xa;
     const int sb = two ? x_stride(Wb) : 0;
-    xb.stride = sb > 0 ? sb : 1;
+    xb.stride = sb > 0 ? sb : 16;
     xb.gstride = g_stride(Wb);
     xb.gsum = reinterpret_cast<int*>(tmp);
     xb.lo = reinterpret_cast<uint8_t*>(xb.gsum + NB * xb.gstride + 4);
     xb.lo = reinterpret_cast<uint8_t*>(((uintptr_t)xb.lo + 15) & ~(uintptr_t)15);
     xb.hi = reinterpret_cast<int8_t*>(xb.lo + (size_t)NB * xb.stride);
     int* members = reinterpret_cast<int*>(xb.hi + (size_t)NB * xb.stride);
+    int16_t* hbuf = reinterpret_cast<int16_t*>(((uintptr_t)(members + NB) + 15) & ~(uintptr_t)15);   // [nb][ffn]
     const int n_all = min(NB, bt.n - b0);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row = blockIdx.x * 32 + lane;
     int nb = 0;
     for (int b = 0; b < n_all; ++b) {
-        const int slot = bt.slot[b0 + b];
-        if (d.experts && s.route[(size_t)slot * d.layers + layer] != expert) continue;
-        const int16_t* h = s.h + (size_t)slot * d.ffn;
+        if (d.experts && __ldcg(s.route + (size_t)(b0 + b) * d.layers + layer) != expert) continue;
         if (threadIdx.x == 0) members[nb] = b;
-        stage_one<WT>(xa, nb, h, d.chunk, 0, *red);
-        if (two) stage_one<WT>(xb, nb, h + d.chunk, d.ffn - d.chunk, 0, *red);
+        load_vec(s.h + (size_t)(b0 + b) * d.ffn, d.ffn, hbuf + (size_t)nb * d.ffn);
         ++nb;
     }
     __syncthreads();
     if (nb == 0) return;
+    const int xres = (warp < nb && row < Wa.rows) ? (int)__ldcg(s.x1 + (size_t)(b0 + members[warp]) * d.dim + row) : 0;
+    for (int b = 0; b < nb; ++b) {
+        const int16_t* h = hbuf + (size_t)b * d.ffn;
+        stage_one<WT>(xa, b, h, d.chunk, 0, *red);
+        if (two) stage_one<WT>(xb, b, h + d.chunk, d.ffn - d.chunk, 0, *red);
+    }
     if (!early) {
         mv_prefetch<WT, MAXC>(Wa, blockIdx.x, Ra);
         if (two) mv_prefetch<WT, MAXC>(Wb, blockIdx.x, Rb);
@@ -592,40 +682,51 @@ __global__ void __launch_bounds__(kThreads) k_down(const DMat* mats, int i_w2a, 
         mv_compute<WT, NB, MAXC>(Wb, Rb, xb, nb, Sb);
         tb = reduce_warps<NB>(Sb, nb, part);
     }
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (warp < nb) {
-        const int row = blockIdx.x * 32 + lane;
-        if (row < Wa.rows) {
-            const int slot = bt.slot[b0 + members[warp]];
-            const int va = mv_epi(WT == W_T3 ? ta - xa.gsum[warp * xa.gstride] : ta, Wa.rscale[row]);
-            float o2 = __fmul_rn((float)va, 1.0f / 256.0f);
-            if (two) {
-                const int vb = mv_epi(WT == W_T3 ? tb - xb.gsum[warp * xb.gstride] : tb, Wb.rscale[row]);
-                // add_q16 of the two chunk outputs (session.cpp:2052-2067)
-                o2 = __fmul_rn((float)q16h(__fadd_rn(o2, __fmul_rn((float)vb, 1.0f / 256.0f))), 1.0f / 256.0f);
-            }
-            const float x1 = __fmul_rn((float)s.x1[(size_t)slot * d.dim + row], 1.0f / 256.0f);
-            s.x[(size_t)slot * d.dim + row] = (int16_t)q16h(__fadd_rn(x1, o2));
+    if (warp < nb && row < Wa.rows) {
+        const int bi = b0 + members[warp];
+        const int va = mv_epi(WT == W_T3 ? ta - xa.gsum[warp * xa.gstride] : ta, Ra.rs);
+        float o2 = __fmul_rn((float)va, 1.0f / 256.0f);
+        if (two) {
+            const int vb = mv_epi(WT == W_T3 ? tb - xb.gsum[warp * xb.gstride] : tb, Rb.rs);
+            // add_q16 of the two chunk outputs (session.cpp:2052-2067)
+            o2 = __fmul_rn((float)q16h(__fadd_rn(o2, __fmul_rn((float)vb, 1.0f / 256.0f))), 1.0f / 256.0f);
         }
+        const float x1 = __fmul_rn((float)xres, 1.0f / 256.0f);
+        s.x[(size_t)bi * d.dim + row] = (int16_t)q16h(__fadd_rn(x1, o2));
     }
 }
 
 // ---------------------------------------------------------------------------
-// logits: RMSNorm(x) + logits matvec + first-max argmax
+// logits: RMSNorm(x) + logits matvec + first-max argmax; the last CTA of the
+// launch turns the packed keys into greedy tokens (and advances the sequences)
 // ---------------------------------------------------------------------------
 
+struct Finalize {
+    int* next;          // greedy token per batch position
+    int* tokens;        // advance: becomes the greedy (or forced) token
+    int* pos;           // advance: + 1
+    const int* forced;  // prefill: token at each position
+    int advance;
+};
+
 template <int WT, int NB, int MAXC>
-__global__ void __launch_bounds__(kThreads) k_logits(DMat W, const float* rms_w, State s, Batch bt, Dims d, int b0) {
+__global__ void __launch_bounds__(kThreads) k_logits(DMat W, const float* rms_w, State s, Batch bt, Dims d, int b0,
+                                                     Finalize fz) {
+    if (!smem_ok(smem_bytes(NB, x_stride(W), g_stride(W), NB * d.dim), s.err)) return;
     WRegs<MAXC> R;
     mv_prefetch<WT, MAXC>(W, blockIdx.x, R);
+    float nw[kPer];
+    load_f32_regs(rms_w, d.dim, nw);
     pdl_launch_dependents();
     pdl_wait();
     XStage xs; Red* red; long long* part; int16_t* tmp;
     carve<NB>(x_stride(W), g_stride(W), xs, red, part, tmp);
     const int nb = min(NB, bt.n - b0);
+    for (int b = 0; b < nb; ++b) load_vec(s.x + (size_t)(b0 + b) * d.dim, d.dim, tmp + (size_t)b * d.dim);
+    __syncthreads();
     for (int b = 0; b < nb; ++b) {
         int16_t* xin = tmp + (size_t)b * d.dim;
-        rmsnorm_q16(s.x + (size_t)bt.slot[b0 + b] * d.dim, rms_w, d.dim, d.eps, xin, *red);
+        rmsnorm_q16(xin, nw, d.dim, d.eps, xin, *red);
         xs.k[b] = 0;
         stage_one<WT>(xs, b, xin, d.dim, 0, *red);
     }
@@ -635,24 +736,42 @@ __global__ void __launch_bounds__(kThreads) k_logits(DMat W, const float* rms_w,
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (warp < nb) {
         const int row = blockIdx.x * 32 + lane;
-        const int slot = bt.slot[b0 + warp];
+        const int bi = b0 + warp;
         unsigned long long key = 0ull;
         if (row < W.rows) {
-            const int v = mv_epi(tot, W.rscale[row]);
-            s.logits[(size_t)slot * d.vocab + row] = v;
+            const int v = mv_epi(tot, R.rs);
+            s.logits[(size_t)bi * d.vocab + row] = v;
             key = ((unsigned long long)(unsigned)(v + 32768) << 32) | (unsigned)(0xFFFFFFFFu - (unsigned)row);
         }
         for (int o = 16; o; o >>= 1) {
             const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, key, o);
             key = k2 > key ? k2 : key;
         }
-        if (lane == 0 && key) atomicMax(&s.best[slot], key);
+        if (lane == 0 && key) { atomicMax(&s.best[bi], key); __threadfence(); }
     }
+    // last CTA: greedy tokens for this launch's inputs
+    __shared__ int last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        last = atomicAdd(s.done, 1) == (int)gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    if (threadIdx.x < nb) {
+        const int bi = b0 + threadIdx.x;
+        const unsigned long long key = __ldcg(&s.best[bi]);
+        const int tok = (int)(0xFFFFFFFFu - (unsigned)(key & 0xFFFFFFFFull));
+        fz.next[bi] = tok;
+        if (fz.advance) {
+            const int p = fz.pos[bi] + 1;
+            fz.tokens[bi] = fz.forced ? fz.forced[p < s.seq ? p : s.seq - 1] : tok;
+            fz.pos[bi] = p;
+        }
+    }
+    if (threadIdx.x == 0) *s.done = 0;
 }
-
-// ---------------------------------------------------------------------------
-// attention: qk-norm + RoPE + KV append (packed codec) + attention
-// ---------------------------------------------------------------------------
 
 // Attention for one (KV head, sequence) runs on a cluster of kAttnCtas CTAs.
 // The positions 0..pos are split into kAttnCtas contiguous ranges; each CTA
@@ -664,6 +783,11 @@ __global__ void __launch_bounds__(kThreads) k_logits(DMat W, const float* rms_w,
 // exp(s - max), p = e / sum, out = sum p*v.
 constexpr int kAttnCtas = 8;
 constexpr int kRedBytes = (int)((sizeof(Red) + 15) / 16 * 16);
+
+__host__ __device__ inline size_t attn_smem_bytes(int group, int hd, int max_rows) {
+    return kRedBytes + sizeof(double) * (((size_t)group * hd + 1) & ~(size_t)1) + 8 * 8 + 8 * 4 +
+           sizeof(float) * ((size_t)group * hd + 2 * hd + 2 * (size_t)max_rows * (hd + 1) + (size_t)group * max_rows);
+}
 
 __device__ __forceinline__ void decode8(const uint4 v, int kv_bits, float* out) {
     // 16 bytes of a packed row: 8 q16 values (big-endian) or 16 q8 values.
@@ -708,6 +832,7 @@ k_attn(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int 
     const int g = blockIdx.x / kAttnCtas, b = blockIdx.y;
     const int slot = bt.slot[b], pos = bt.pos[b];
     const int hd = d.head_dim, group = d.heads / d.kv_heads, half = hd / 2, hp = hd + 1;
+    if (!smem_ok(attn_smem_bytes(group, hd, max_rows), s.err)) return;
     const int len = pos + 1;
     const int per = (len + kAttnCtas - 1) / kAttnCtas;
     const int t0 = min(len, rank * per), t1 = min(len, t0 + per), nt = t1 - t0;
@@ -750,7 +875,7 @@ k_attn(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int 
     pdl_launch_dependents();
     pdl_wait();
     // 2. q heads and the new k, v; qk-norm (exact double sum of squares), RoPE
-    const float* qkv = s.qkv + (size_t)slot * (d.dim + 2 * d.kv_dim);
+    const float* qkv = s.qkv + (size_t)b * (d.dim + 2 * d.kv_dim);
     for (int i = threadIdx.x; i < group * hd; i += blockDim.x) sm.q[i] = qkv[g * group * hd + i];
     for (int i = threadIdx.x; i < hd; i += blockDim.x) {
         sm.kv[i] = qkv[d.dim + g * hd + i];
@@ -887,7 +1012,7 @@ k_attn(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int 
     for (int e = rank + kAttnCtas * threadIdx.x; e < group * hd; e += kAttnCtas * blockDim.x) {
         double a = 0.0;
         for (int c = 0; c < kAttnCtas; ++c) a = __dadd_rn(a, *cluster.map_shared_rank(sm.pv + e, c));
-        s.att[(size_t)slot * d.dim + g * group * hd + e] = (int16_t)q16h(__double2float_rn(a));
+        s.att[(size_t)b * d.dim + g * group * hd + e] = (int16_t)q16h(__double2float_rn(a));
     }
     cluster.sync();   // no CTA leaves while its shared memory may still be read
 }
@@ -921,22 +1046,6 @@ __global__ void __launch_bounds__(kThreads) k_raw_i16(DMat W, const int16_t* xq,
     for (int c = threadIdx.x; c < n; c += blockDim.x) acc += (long long)W.w16[(size_t)row * n + c] * xq[c];
     acc = block_sum_i64(acc, red);
     if (threadIdx.x == 0) out[row] = mv_epi(acc, W.rscale[row]);
-}
-
-// Greedy token of each sequence from its packed argmax key; optionally
-// advance the sequence (next token, position + 1).
-__global__ void k_finalize(State s, Batch bt, int* next, int* tokens, int* pos, int advance, const int* forced) {
-    pdl_wait();
-    const int b = blockIdx.x * blockDim.x + threadIdx.x;
-    if (b >= bt.n) return;
-    const unsigned long long key = s.best[bt.slot[b]];
-    const int tok = (int)(0xFFFFFFFFu - (unsigned)(key & 0xFFFFFFFFull));
-    next[b] = tok;
-    if (advance) {
-        const int p = pos[b] + 1;
-        tokens[b] = forced ? forced[p < s.seq ? p : s.seq - 1] : tok;
-        pos[b] = p;
-    }
 }
 
 // ---------------------------------------------------------------------------
@@ -1007,46 +1116,62 @@ struct Ops {
     static void wo(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
         const DMat& W = m.mats[m.wo[layer]];
         Dims d = dims_of(m, s);
-        const size_t sm = smem_bytes(kNB, x_stride(W), g_stride(W), 0);
+        const size_t sm = smem_bytes(kNB, x_stride(W), g_stride(W), kNB * d.dim);
         for (int b0 = 0; b0 < bt.n; b0 += kNB) launch_pdl(k_wo<WT, kNB, MAXC>, dim3(W.rblocks), sm, st, W, s, bt, d, b0);
     }
     template <int MAXC>
     static void gate(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
         Dims d = dims_of(m, s);
-        const int ebase = d.experts ? m.e_w1[(size_t)layer * d.experts] : 0;
-        const DMat& W1 = m.mats[d.experts ? ebase : m.w1[layer]];
+        MatSet M;
+        if (d.experts) {
+            const int eb = m.e_w1[(size_t)layer * d.experts];
+            for (int e = 0; e < d.experts; ++e) { M.a[e] = m.mats[eb + 4 * e]; M.b[e] = m.mats[eb + 4 * e + 1]; }
+            M.router = m.mats[m.router[layer]];
+        } else {
+            M.a[0] = m.mats[m.w1[layer]];
+            M.b[0] = m.mats[m.w3[layer]];
+        }
+        const DMat& W1 = M.a[0];
         const size_t sm = smem_bytes(kNB, x_stride(W1), g_stride(W1), (kNB + 1) * d.dim) + 64;
         const dim3 grid(W1.rblocks, d.experts ? d.experts : 1);
         const int hs = layer < (int)m.h.hid_scale.size() ? (int)m.h.hid_scale[layer] : 0;
         const int early = d.experts == 0 || bt.n >= 2 * d.experts;
         for (int b0 = 0; b0 < bt.n; b0 += kNB)
-            launch_pdl(k_gate<WT, kNB, MAXC>, grid, sm, st, (const DMat*)m.d_mats, d.experts ? 0 : m.w1[layer],
-                       d.experts ? 0 : m.w3[layer], d.experts ? m.router[layer] : 0, ebase,
-                       (const float*)(m.d_rms_ffn + (size_t)layer * d.dim), s, bt, d, layer, b0, hs, early);
+            launch_pdl(k_gate<WT, kNB, MAXC>, grid, sm, st, M, (const float*)(m.d_rms_ffn + (size_t)layer * d.dim),
+                       s, bt, d, layer, b0, hs, early);
     }
     template <int MAXC>
     static void down(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
         Dims d = dims_of(m, s);
-        const int ebase = d.experts ? m.e_w1[(size_t)layer * d.experts] : 0;
-        const DMat& Wa = m.mats[d.experts ? ebase + 2 : m.w2a[layer]];
+        MatSet M;
         const bool two = m.ffn_chunked;
-        const DMat& Wb = m.mats[d.experts ? ebase + 3 : (two ? m.w2b[layer] : m.w2a[layer])];
+        if (d.experts) {
+            const int eb = m.e_w1[(size_t)layer * d.experts];
+            for (int e = 0; e < d.experts; ++e) {
+                M.a[e] = m.mats[eb + 4 * e + 2];
+                M.b[e] = two ? m.mats[eb + 4 * e + 3] : m.mats[eb + 4 * e + 2];
+            }
+        } else {
+            M.a[0] = m.mats[m.w2a[layer]];
+            M.b[0] = two ? m.mats[m.w2b[layer]] : m.mats[m.w2a[layer]];
+        }
+        const DMat& Wa = M.a[0];
+        const DMat& Wb = M.b[0];
         const size_t sm = smem_bytes(kNB, x_stride(Wa), g_stride(Wa), 0) +
-                          (two ? 2 * (size_t)kNB * x_stride(Wb) + sizeof(int) * kNB * g_stride(Wb) : 16) + 256;
+                          2 * (size_t)kNB * (two ? x_stride(Wb) : 16) + sizeof(int) * kNB * g_stride(Wb) + 256 +
+                          sizeof(int16_t) * (size_t)kNB * d.ffn;
         const dim3 grid(Wa.rblocks, d.experts ? d.experts : 1);
         const int early = d.experts == 0 || bt.n >= 2 * d.experts;
         for (int b0 = 0; b0 < bt.n; b0 += kNB)
-            launch_pdl(k_down<WT, kNB, MAXC>, grid, sm, st, (const DMat*)m.d_mats, d.experts ? 0 : m.w2a[layer],
-                       d.experts ? 0 : (two ? m.w2b[layer] : m.w2a[layer]), ebase, s, bt, d, layer, b0, early);
+            launch_pdl(k_down<WT, kNB, MAXC>, grid, sm, st, M, s, bt, d, layer, b0, early);
     }
     template <int MAXC>
-    static void logits(const DModel& m, const State& s, const Batch& bt, cudaStream_t st) {
+    static void logits(const DModel& m, const State& s, const Batch& bt, const Finalize& fz, cudaStream_t st) {
         const DMat& W = m.mats[m.logits_mat];
         Dims d = dims_of(m, s);
         const size_t sm = smem_bytes(kNB, x_stride(W), g_stride(W), kNB * d.dim);
         for (int b0 = 0; b0 < bt.n; b0 += kNB)
-            launch_pdl(k_logits<WT, kNB, MAXC>, dim3(W.rblocks), sm, st, W,
-                       (const float*)m.d_rms_final, s, bt, d, b0);
+            launch_pdl(k_logits<WT, kNB, MAXC>, dim3(W.rblocks), sm, st, W, (const float*)m.d_rms_final, s, bt, d, b0, fz);
     }
     template <int MAXC>
     static void raw(const DMat& W, const int16_t* xq, int n, int32_t* out, cudaStream_t st) {
@@ -1081,18 +1206,18 @@ void launch_ffn_down(const DModel& m, const State& s, const Batch& b, int layer,
     const DMat& W = m.h.experts ? m.mats[m.e_w1[(size_t)layer * m.h.experts] + 2] : m.mats[m.w2a[layer]];
     VC4_DISPATCH(W.wtype, maxc_for(W.nchunks), down, m, s, b, layer, st);
 }
-void launch_logits(const DModel& m, const State& s, const Batch& b, cudaStream_t st) {
+void launch_logits(const DModel& m, const State& s, const Batch& b, int* next, int* tokens, int* pos, int advance,
+                   const int* forced, cudaStream_t st) {
     const DMat& W = m.mats[m.logits_mat];
-    VC4_MAXC(maxc_for(W.nchunks), Ops<W_Q8>::logits, m, s, b, st);
+    Finalize fz{next, tokens, pos, forced, advance};
+    VC4_MAXC(maxc_for(W.nchunks), Ops<W_Q8>::logits, m, s, b, fz, st);
 }
 
 void launch_attention(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st) {
     Dims d = dims_of(m, s);
     const int group = d.heads / d.kv_heads, hd = d.head_dim;
     const int max_rows = (d.seq + kAttnCtas - 1) / kAttnCtas;
-    const size_t sm = kRedBytes + sizeof(double) * (((size_t)group * hd + 1) & ~(size_t)1) + 8 * 8 + 8 * 4 +
-                      sizeof(float) * ((size_t)group * hd + 2 * hd + 2 * (size_t)max_rows * (hd + 1) +
-                                       (size_t)group * max_rows);
+    const size_t sm = attn_smem_bytes(group, hd, max_rows);
     launch_pdl(k_attn, dim3(d.kv_heads * kAttnCtas, b.n), sm, st, (const float*)m.d_q_norm,
                (const float*)m.d_k_norm, s, b, d, layer, max_rows);
 }
@@ -1103,15 +1228,12 @@ void launch_matvec_raw(const DModel& m, int mat, const int16_t* xq, int n, int32
     VC4_DISPATCH(W.wtype, maxc_for(W.nchunks), raw, W, xq, n, out, st);
 }
 
-void launch_finalize(const State& s, const Batch& b, int* next, int* tokens, int* pos, int advance,
-                     const int* forced, cudaStream_t st) {
-    k_finalize<<<(b.n + 127) / 128, 128, 0, st>>>(s, b, next, tokens, pos, advance, forced);
-}
-
 int kernel_launches_per_step(const DModel& m, int n) {
     const int g = (n + kNB - 1) / kNB;
-    return m.h.layers * (4 * g + 1) + g + 1;
+    return m.h.layers * (4 * g + 1) + g;
 }
+
+int max_input_cols() { return kPer * kThreads; }
 
 bool attention_fits(int seq, int head_dim, int kv_bits, int kv_dim) {
     const int hbytes = kv_bits == 16 ? 2 * head_dim : head_dim;

@@ -120,6 +120,8 @@ struct Batch {
 };
 
 struct State {                      // per-slot activations, [slot][...]
+    // Activations are transient within a pass and indexed by batch position;
+    // the KV cache is indexed by the sequence's slot.
     int16_t* x = nullptr;            // residual, q16 ints [slots][dim]
     int16_t* x1 = nullptr;           // residual after attention
     float* qkv = nullptr;            // matvec_s output [slots][dim+2kv]
@@ -133,6 +135,8 @@ struct State {                      // per-slot activations, [slot][...]
     int kv_bits = 16, row_bytes = 0, seq = 0, slots = 0;
     float* rope_cos = nullptr;       // [seq][head_dim/2]
     float* rope_sin = nullptr;
+    int* done = nullptr;             // CTA arrival counter of the logits kernel (reset by its last CTA)
+    int* err = nullptr;              // kernel self-check word: nonzero = a launch reserved too little shared memory
 };
 
 // Kernel launchers (kernels.cu).  All enqueue on `st`; none synchronises.
@@ -141,20 +145,19 @@ void launch_attention(const DModel& m, const State& s, const Batch& b, int layer
 void launch_wo(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st);
 void launch_ffn_gate(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st);
 void launch_ffn_down(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st);
-void launch_logits(const DModel& m, const State& s, const Batch& b, cudaStream_t st);
+// Logits + first-max argmax; the launch's last CTA writes the greedy tokens to
+// `next` and, with `advance`, moves each sequence on (token, position + 1);
+// `forced` (indexed by position) replaces the greedy token during a prefill.
+void launch_logits(const DModel& m, const State& s, const Batch& b, int* next, int* tokens, int* pos, int advance,
+                   const int* forced, cudaStream_t st);
 // A bare matvec of one model matrix over q16 inputs (the CPU-path entry,
 // GPU::matvec_s): xq are already scaled ints, out receives clamped q16 ints.
 void launch_matvec_raw(const DModel& m, int mat, const int16_t* xq, int n, int32_t* out, cudaStream_t st);
-// Greedy token from the packed argmax key; with `advance` the batch's token
-// becomes that token and its position moves on by one.
-// `forced` (indexed by position) replaces the greedy token during a prefill.
-void launch_finalize(const State& s, const Batch& b, int* next, int* tokens, int* pos, int advance,
-                     const int* forced, cudaStream_t st);
-
 int kernel_launches_per_step(const DModel& m, int n);
 // Shape limits of the kernels (checked at upload / session creation).
 bool attention_fits(int seq, int head_dim, int kv_bits, int kv_dim);
 int matvec_max_chunks();
+int max_input_cols();
 
 // Accessors engine.cu gives the library's other translation units.
 }  // namespace vc4
