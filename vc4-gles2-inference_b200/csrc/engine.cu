@@ -436,7 +436,7 @@ int vc4_session_create(vc4_model* m, int slots, int seq, int kv_bits, const floa
     if (h.heads / h.kv_heads > 8 || h.head_dim > 128) return fail(VC4_EINVAL, "attention group above 8 or head_dim above 128");
     if (h.dim > max_input_cols() || m->d.ffn_width > max_input_cols())
         return fail(VC4_EINVAL, "model width beyond the kernels' staging limit");
-    if (!attention_fits(seq, h.head_dim, kv_bits, h.kv_dim))
+    if (!attention_fits(seq, h.head_dim, kv_bits, h.kv_dim, h.heads / h.kv_heads))
         return fail(VC4_EINVAL, "sequence length / head shape beyond the attention kernel's staging limits");
     CK(cudaSetDevice(m->d.device));
     vc4_session* s = new vc4_session();

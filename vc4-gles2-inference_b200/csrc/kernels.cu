@@ -19,12 +19,14 @@
 
 #include <cstdio>
 #include <map>
+#include <mutex>
 #include <utility>
 
 namespace vc4 {
 namespace {
 
 constexpr int kThreads = kWarps * 32;
+constexpr size_t kMaxDynSmem = 227 * 1024;   // opt-in dynamic shared memory per CTA on sm_100
 
 // ---------------------------------------------------------------------------
 // Exact arithmetic helpers (each mirrors one step of the oracle)
@@ -773,248 +775,322 @@ __global__ void __launch_bounds__(kThreads) k_logits(DMat W, const float* rms_w,
     if (threadIdx.x == 0) *s.done = 0;
 }
 
-// Attention for one (KV head, sequence) runs on a cluster of kAttnCtas CTAs.
-// The positions 0..pos are split into kAttnCtas contiguous ranges; each CTA
-// stages its K/V rows (decoded to float) in shared memory with one burst of
-// loads, computes its scores, and the cluster combines the softmax maximum, the
-// double-precision denominator and the double-precision P.V partials through
-// distributed shared memory in rank order.  The arithmetic is the reference's
-// (session.cpp:1989-2050): sequential fp32 q.k per position, global max,
-// exp(s - max), p = e / sum, out = sum p*v.
+// Attention for one (KV head, sequence) runs on a cluster of kAttnCtas CTAs
+// with a single cluster barrier:
+//  - before the grid-dependency wait every CTA stages the cache rows it needs
+//    (cp.async) and decodes them to fp32 in shared memory: the K rows of its
+//    contiguous share of positions 0..pos, and a slice of V columns for every
+//    position;
+//  - after the wait each CTA rebuilds the normalised, rotated q heads and the
+//    new k (identical in every CTA), encodes the new cache row (written by the
+//    CTA whose share holds `pos`), computes the scores of its positions and
+//    stores them into every CTA of the cluster (distributed shared memory);
+//  - after the barrier each CTA holds all scores, runs the softmax for all
+//    positions itself (the same order in every CTA) and computes P.V for its
+//    own V columns, so no partial results cross CTAs.
+// The arithmetic is the reference's (session.cpp:1989-2050): sequential fp32
+// q.k per position, global max, exp(s - max), p = e / sum (the sum in double,
+// rounded once), out = sum p*v in double.
 constexpr int kAttnCtas = 8;
-constexpr int kRedBytes = (int)((sizeof(Red) + 15) / 16 * 16);
 
-__host__ __device__ inline size_t attn_smem_bytes(int group, int hd, int max_rows) {
-    return kRedBytes + sizeof(double) * (((size_t)group * hd + 1) & ~(size_t)1) + 8 * 8 + 8 * 4 +
-           sizeof(float) * ((size_t)group * hd + 2 * hd + 2 * (size_t)max_rows * (hd + 1) + (size_t)group * max_rows);
-}
-
-__device__ __forceinline__ void decode8(const uint4 v, int kv_bits, float* out) {
-    // 16 bytes of a packed row: 8 q16 values (big-endian) or 16 q8 values.
-    const unsigned w[4] = {v.x, v.y, v.z, v.w};
-    if (kv_bits == 16) {
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const unsigned x = w[k];
-            const int a = (int)(short)(((x & 0xFFu) << 8) | ((x >> 8) & 0xFFu));
-            const int b = (int)(short)((((x >> 16) & 0xFFu) << 8) | (x >> 24));
-            out[2 * k] = __fmul_rn((float)a, 1.0f / 2048.0f);
-            out[2 * k + 1] = __fmul_rn((float)b, 1.0f / 2048.0f);
-        }
-    } else {
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-                out[4 * k + j] = __fmul_rn((float)(signed char)((w[k] >> (8 * j)) & 0xFFu), 1.0f / 16.0f);
-    }
-}
+__host__ __device__ inline int attn_vs(int hd) { return (((hd + kAttnCtas - 1) / kAttnCtas) + 3) & ~3; }
+__host__ __device__ inline int attn_rows(int seq) { return (seq + kAttnCtas - 1) / kAttnCtas; }
+__host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~(size_t)15; }
 
 struct AttnSmem {
-    // carved from dynamic shared memory
-    Red* red;
-    float* q;        // group*hd
-    float* kv;       // 2*hd  (new k, v)
-    float* kt;       // rows*hp
-    float* vt;       // rows*hp
-    float* sc;       // group*rows
-    float* mx;       // group          (cluster-visible)
-    double* sum;     // group          (cluster-visible)
-    double* pv;      // group*hd       (cluster-visible)
+    uint8_t* kraw;   // attn_rows(seq) x hbytes: K rows of this CTA's positions (cache bytes)
+    uint8_t* vraw;   // seq x vs*kvb: this CTA's V columns of every position (cache bytes)
+    double* pv;      // max(kThreads, group*vs): P.V partials
+    double* redd;    // kWarps: softmax sums per warp
+    float* kt;       // attn_rows(seq) x (hd + 4): decoded K rows
+    float* vt;       // seq x vs: decoded V columns
+    float* q;        // (group + 1) x hd: q heads, then the new k
+    float* vn;       // hd: the new v
+    float* rc;       // hd/2: RoPE cos at pos
+    float* rsn;      // hd/2: RoPE sin at pos
+    float* wq;       // hd: q_norm weights of the layer
+    float* wk;       // hd: k_norm weights of the layer
+    float* redf;     // kWarps: softmax maxima per warp
+    float* sc;       // group x seq: scores, then probabilities (cluster-written)
 };
 
+__host__ __device__ inline size_t attn_carve(int group, int hd, int seq, int kv_bits, char* base, AttnSmem* sm) {
+    const int kvb = kv_bits / 8, vs = attn_vs(hd), rows = attn_rows(seq);
+    const int npv = group * vs > kThreads ? group * vs : kThreads;
+    size_t o = 0;
+    const size_t kraw = o; o = align16(o + (size_t)rows * hd * kvb);
+    const size_t vraw = o; o = align16(o + (size_t)seq * vs * kvb);
+    const size_t pv = o;   o = align16(o + sizeof(double) * npv);
+    const size_t redd = o; o = align16(o + sizeof(double) * kWarps);
+    const size_t kt = o;   o = align16(o + sizeof(float) * (size_t)rows * (hd + 4));
+    const size_t vt = o;   o = align16(o + sizeof(float) * (size_t)seq * vs);
+    const size_t q = o;    o = align16(o + sizeof(float) * (size_t)(group + 1) * hd);
+    const size_t vn = o;   o += sizeof(float) * hd;
+    const size_t rc = o;   o += sizeof(float) * (hd / 2);
+    const size_t rsn = o;  o += sizeof(float) * (hd / 2);
+    const size_t wq = o;   o += sizeof(float) * hd;
+    const size_t wk = o;   o += sizeof(float) * hd;
+    const size_t redf = o; o += sizeof(float) * kWarps;
+    const size_t sc = o;   o += sizeof(float) * (size_t)group * seq;
+    if (sm) {
+        sm->kraw = reinterpret_cast<uint8_t*>(base + kraw);
+        sm->vraw = reinterpret_cast<uint8_t*>(base + vraw);
+        sm->pv = reinterpret_cast<double*>(base + pv);
+        sm->redd = reinterpret_cast<double*>(base + redd);
+        sm->kt = reinterpret_cast<float*>(base + kt);
+        sm->vt = reinterpret_cast<float*>(base + vt);
+        sm->q = reinterpret_cast<float*>(base + q);
+        sm->vn = reinterpret_cast<float*>(base + vn);
+        sm->rc = reinterpret_cast<float*>(base + rc);
+        sm->rsn = reinterpret_cast<float*>(base + rsn);
+        sm->wq = reinterpret_cast<float*>(base + wq);
+        sm->wk = reinterpret_cast<float*>(base + wk);
+        sm->redf = reinterpret_cast<float*>(base + redf);
+        sm->sc = reinterpret_cast<float*>(base + sc);
+    }
+    return align16(o);
+}
+__host__ __device__ inline size_t attn_smem_bytes(int group, int hd, int seq, int kv_bits) {
+    return attn_carve(group, hd, seq, kv_bits, nullptr, nullptr);
+}
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(d), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// The values of one 32-bit word of a packed cache row: two q16 big-endian
+// values on the 1/2048 grid, or four q8 two's-complement values on the 1/16
+// grid (shaders_attn.cpp:141-159).  Returns the number of values.
+__device__ __forceinline__ int kv_word(unsigned w, int kvb, float* out) {
+    if (kvb == 2) {
+        out[0] = __fmul_rn((float)(short)(((w & 0xFFu) << 8) | ((w >> 8) & 0xFFu)), 1.0f / 2048.0f);
+        out[1] = __fmul_rn((float)(short)((((w >> 16) & 0xFFu) << 8) | (w >> 24)), 1.0f / 2048.0f);
+        return 2;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) out[j] = __fmul_rn((float)(signed char)((w >> (8 * j)) & 0xFFu), 1.0f / 16.0f);
+    return 4;
+}
+// The packed bytes of one value (the inverse of kv_word), as the low bits of a word.
+__device__ __forceinline__ unsigned kv_encode(float x, int kvb, float* dec) {
+    if (kvb == 2) {
+        float q = floorf(__fadd_rn(__fmul_rn(x, 2048.0f), 0.5f));
+        q = q < -32768.0f ? -32768.0f : q > 32767.0f ? 32767.0f : q;
+        *dec = __fmul_rn(q, 1.0f / 2048.0f);
+        const unsigned u = (unsigned)(int)q & 0xFFFFu;
+        return (u >> 8) | ((u & 0xFFu) << 8);           // big-endian byte order in memory
+    }
+    float q = floorf(__fadd_rn(__fmul_rn(x, 16.0f), 0.5f));
+    q = q < -128.0f ? -128.0f : q > 127.0f ? 127.0f : q;
+    *dec = __fmul_rn(q, 1.0f / 16.0f);
+    return (unsigned)(int)q & 0xFFu;
+}
+
 __global__ void __cluster_dims__(kAttnCtas, 1, 1) __launch_bounds__(kThreads)
-k_attn(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int layer, int max_rows) {
+k_attn(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int layer) {
     namespace cg = cooperative_groups;
     cg::cluster_group cluster = cg::this_cluster();
     extern __shared__ __align__(16) char smem[];
+    const int hd = d.head_dim, group = d.heads / d.kv_heads, half = hd / 2, hp = hd + 4;
+    if (!smem_ok(attn_smem_bytes(group, hd, d.seq, d.kv_bits), s.err)) return;
+    AttnSmem sm;
+    attn_carve(group, hd, d.seq, d.kv_bits, smem, &sm);
     const int rank = (int)cluster.block_rank();
     const int g = blockIdx.x / kAttnCtas, b = blockIdx.y;
-    const int slot = bt.slot[b], pos = bt.pos[b];
-    const int hd = d.head_dim, group = d.heads / d.kv_heads, half = hd / 2, hp = hd + 1;
-    if (!smem_ok(attn_smem_bytes(group, hd, max_rows), s.err)) return;
-    const int len = pos + 1;
+    const int slot = bt.slot[b], pos = bt.pos[b], len = pos + 1;
     const int per = (len + kAttnCtas - 1) / kAttnCtas;
     const int t0 = min(len, rank * per), t1 = min(len, t0 + per), nt = t1 - t0;
-    AttnSmem sm;
-    {
-        char* p = smem;
-        sm.red = reinterpret_cast<Red*>(p); p += kRedBytes;
-        sm.pv = reinterpret_cast<double*>(p); p += sizeof(double) * ((group * hd + 1) & ~1);
-        sm.sum = reinterpret_cast<double*>(p); p += sizeof(double) * 8;
-        sm.mx = reinterpret_cast<float*>(p); p += sizeof(float) * 8;
-        sm.q = reinterpret_cast<float*>(p); p += sizeof(float) * group * hd;
-        sm.kv = reinterpret_cast<float*>(p); p += sizeof(float) * 2 * hd;
-        sm.kt = reinterpret_cast<float*>(p); p += sizeof(float) * (size_t)max_rows * hp;
-        sm.vt = reinterpret_cast<float*>(p); p += sizeof(float) * (size_t)max_rows * hp;
-        sm.sc = reinterpret_cast<float*>(p);
-    }
+    const int kvb = d.kv_bits / 8, hbytes = hd * kvb, vofs = d.kv_dim * kvb;
+    const int vs = attn_vs(hd), c0 = min(hd, rank * vs), c1 = min(hd, c0 + vs), nc = c1 - c0;
+    const int vrow = vs * kvb;                    // staged bytes per position of the V slice
+    const int vpw = 4 / kvb;                      // values per 32-bit word
     uint8_t* kvbase = s.kv + ((size_t)slot * d.layers + layer) * d.seq * d.row_bytes;
-    const int vofs = d.kv_bits == 16 ? 2 * d.kv_dim : d.kv_dim;
-    const int hbytes = d.kv_bits == 16 ? 2 * hd : hd;          // bytes of one head's K (or V) in a row
-    const int vpr = hbytes / 16;                               // 16-byte vectors per head row
-    const int vals = d.kv_bits == 16 ? 8 : 16;                 // values per vector
-    // 1. issue the loads of this CTA's cached K/V rows (all but `pos`)
-    constexpr int kMaxVec = 16;
-    uint4 buf[kMaxVec];
-    const int nvec = 2 * nt * vpr;
-    int nmine = 0;
-#pragma unroll
-    for (int k = 0; k < kMaxVec; ++k) {
-        const int v = threadIdx.x + k * kThreads;
-        if (v < nvec) {
-            const int which = v / (nt * vpr), r = (v / vpr) % nt, c = v % vpr;
-            const int t = t0 + r;
-            if (t != pos) {
-                const uint8_t* src = kvbase + (size_t)t * d.row_bytes + (which ? vofs : 0) + g * hbytes + c * 16;
-                buf[k] = *reinterpret_cast<const uint4*>(src);
-            }
-            nmine = k + 1;
+
+    // 1. stage and decode the cached rows (every position but `pos`, which
+    //    this step writes), the RoPE row and the norm weights
+    const int kvec = hbytes / 16;
+    for (int v = threadIdx.x; v < nt * kvec; v += kThreads) {
+        const int r = v / kvec, c = v % kvec, t = t0 + r;
+        if (t != pos) cp_async16(sm.kraw + r * hbytes + c * 16, kvbase + (size_t)t * d.row_bytes + g * hbytes + c * 16);
+    }
+    const int vw = nc * kvb / 4;                  // words per position of the V slice
+    for (int v = threadIdx.x; v < pos * vw; v += kThreads) {
+        const int t = v / vw, c = v % vw;
+        cp_async4(sm.vraw + (size_t)t * vrow + c * 4,
+                  kvbase + (size_t)t * d.row_bytes + vofs + g * hbytes + c0 * kvb + c * 4);
+    }
+    for (int i = threadIdx.x; i < half; i += kThreads) {
+        sm.rc[i] = s.rope_cos[(size_t)pos * half + i];
+        sm.rsn[i] = s.rope_sin[(size_t)pos * half + i];
+    }
+    if (d.qk_norm)
+        for (int i = threadIdx.x; i < hd; i += kThreads) {
+            sm.wq[i] = q_norm[(size_t)layer * hd + i];
+            sm.wk[i] = k_norm[(size_t)layer * hd + i];
         }
+    cp_async_wait_all();
+    __syncthreads();
+    const int kw = hbytes / 4;
+    for (int v = threadIdx.x; v < nt * kw; v += kThreads) {
+        const int r = v / kw, c = v % kw;
+        if (t0 + r == pos) continue;
+        float f[4];
+        const int n = kv_word(reinterpret_cast<const unsigned*>(sm.kraw + r * hbytes)[c], kvb, f);
+        for (int j = 0; j < n; ++j) sm.kt[r * hp + c * n + j] = f[j];
+    }
+    for (int v = threadIdx.x; v < pos * vw; v += kThreads) {
+        const int t = v / vw, c = v % vw;
+        float f[4];
+        const int n = kv_word(reinterpret_cast<const unsigned*>(sm.vraw + (size_t)t * vrow)[c], kvb, f);
+        for (int j = 0; j < n; ++j) sm.vt[(size_t)t * vs + c * n + j] = f[j];
     }
     pdl_launch_dependents();
     pdl_wait();
-    // 2. q heads and the new k, v; qk-norm (exact double sum of squares), RoPE
+
+    // 2. q heads, new k, new v from the qkv matvec; qk-norm (exact double sum
+    //    of squares) and RoPE, one warp per vector
     const float* qkv = s.qkv + (size_t)b * (d.dim + 2 * d.kv_dim);
-    for (int i = threadIdx.x; i < group * hd; i += blockDim.x) sm.q[i] = qkv[g * group * hd + i];
-    for (int i = threadIdx.x; i < hd; i += blockDim.x) {
-        sm.kv[i] = qkv[d.dim + g * hd + i];
-        sm.kv[hd + i] = qkv[d.dim + d.kv_dim + g * hd + i];
+    for (int i = threadIdx.x; i < group * hd; i += kThreads) sm.q[i] = qkv[g * group * hd + i];
+    for (int i = threadIdx.x; i < hd; i += kThreads) {
+        sm.q[group * hd + i] = qkv[d.dim + g * hd + i];
+        sm.vn[i] = qkv[d.dim + d.kv_dim + g * hd + i];
     }
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (d.qk_norm) {
-        // one warp per vector: heads 0..group-1 of q, then k
-        for (int hh = warp; hh <= group; hh += kWarps) {
-            float* v = hh < group ? sm.q + hh * hd : sm.kv;
+    for (int hh = warp; hh <= group; hh += kWarps) {
+        float* v = sm.q + hh * hd;
+        if (d.qk_norm) {
             double acc = 0.0;
             for (int i = lane; i < hd; i += 32) acc = __dadd_rn(acc, __dmul_rn((double)v[i], (double)v[i]));
             for (int o = 16; o; o >>= 1) acc = __dadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
             const float ss = __double2float_rn(acc);
             const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)hd), 1e-6f)));
-            const float* w = (hh < group ? q_norm : k_norm) + (size_t)layer * hd;
-            __syncwarp();
+            const float* w = hh < group ? sm.wq : sm.wk;
             for (int i = lane; i < hd; i += 32) v[i] = __fmul_rn(w[i], __fmul_rn(r, v[i]));
+            __syncwarp();
         }
-        __syncthreads();
-    }
-    {
-        const float* cs = s.rope_cos + (size_t)pos * half;
-        const float* sn = s.rope_sin + (size_t)pos * half;
-        for (int t = threadIdx.x; t < (group + 1) * half; t += blockDim.x) {
-            const int hh = t / half, i = t % half;
-            float* o = hh < group ? sm.q + hh * hd : sm.kv;
+        for (int i = lane; i < half; i += 32) {
             const int ia = d.rope_half ? i : 2 * i, ib = d.rope_half ? i + half : 2 * i + 1;
-            const float a = o[ia], bb = o[ib], c = cs[i], sv = sn[i];
-            o[ia] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(bb, sv));
-            o[ib] = __fadd_rn(__fmul_rn(a, sv), __fmul_rn(bb, c));
+            const float a = v[ia], bb = v[ib], c = sm.rc[i], sv = sm.rsn[i];
+            v[ia] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(bb, sv));
+            v[ib] = __fadd_rn(__fmul_rn(a, sv), __fmul_rn(bb, c));
         }
     }
     __syncthreads();
-    // 3. the CTA holding `pos` encodes the new row (shaders_attn.cpp:141-159),
-    //    writes it to the cache and keeps the decoded values for its tile.
-    if (pos >= t0 && pos < t1) {
-        uint8_t* row = kvbase + (size_t)pos * d.row_bytes;
-        for (int e = threadIdx.x; e < 2 * hd; e += blockDim.x) {
-            const int w = e / hd, i = e % hd, c = g * hd + i;
-            const float v = sm.kv[w * hd + i];
-            float dec;
-            if (d.kv_bits == 16) {
-                float q = floorf(__fadd_rn(__fmul_rn(v, 2048.0f), 0.5f));
-                q = q < -32768.0f ? -32768.0f : q > 32767.0f ? 32767.0f : q;
-                const unsigned u = (unsigned)(int)q & 0xFFFFu;
-                uint8_t* p = row + (size_t)w * 2 * d.kv_dim + 2 * c;
-                p[0] = (uint8_t)(u >> 8); p[1] = (uint8_t)u;
-                dec = __fmul_rn(q, 1.0f / 2048.0f);
-            } else {
-                float q = floorf(__fadd_rn(__fmul_rn(v, 16.0f), 0.5f));
-                q = q < -128.0f ? -128.0f : q > 127.0f ? 127.0f : q;
-                row[(size_t)w * d.kv_dim + c] = (uint8_t)(int)q;
-                dec = __fmul_rn(q, 1.0f / 16.0f);
-            }
-            (w ? sm.vt : sm.kt)[(pos - t0) * hp + i] = dec;
+
+    // 3. encode the new row one 32-bit word at a time (shaders_attn.cpp:141-159);
+    //    every CTA encodes it identically, the one whose share holds `pos`
+    //    writes it to the cache
+    const bool owner = pos >= t0 && pos < t1;
+    uint8_t* row = kvbase + (size_t)pos * d.row_bytes;
+    for (int e = threadIdx.x; e < 2 * kw; e += kThreads) {
+        const int w = e / kw, c = e % kw, i0 = c * vpw;
+        const float* src = w ? sm.vn : sm.q + group * hd;
+        unsigned word = 0;
+        float dec[4];
+        for (int j = 0; j < vpw; ++j) word |= kv_encode(src[i0 + j], kvb, &dec[j]) << (8 * kvb * j);
+        if (owner) *reinterpret_cast<unsigned*>(row + (w ? vofs : 0) + g * hbytes + c * 4) = word;
+        for (int j = 0; j < vpw; ++j) {
+            const int i = i0 + j;
+            if (!w && owner) sm.kt[(pos - t0) * hp + i] = dec[j];
+            if (w && i >= c0 && i < c1) sm.vt[(size_t)pos * vs + i - c0] = dec[j];
         }
     }
-    // 4. land the loaded rows in the tiles
-#pragma unroll
-    for (int k = 0; k < kMaxVec; ++k) {
-        if (k >= nmine) break;
-        const int v = threadIdx.x + k * kThreads;
-        const int which = v / (nt * vpr), r = (v / vpr) % nt, c = v % vpr;
-        if (t0 + r == pos) continue;
-        float f[16];
-        decode8(buf[k], d.kv_bits, f);
-        float* dst = (which ? sm.vt : sm.kt) + r * hp + c * vals;
-        for (int j = 0; j < vals; ++j) dst[j] = f[j];
-    }
     __syncthreads();
-    // 5. scores: one thread per (position, head), sequential fp32 dot
+
+    // 4. scores of this CTA's positions: sequential fp32 dot, / sqrt(hd);
+    //    stored into every CTA of the cluster
     const float sq = __fsqrt_rn((float)hd);
-    float lmax[8];
-    for (int hh = 0; hh < 8; ++hh) lmax[hh] = -1e30f;
-    for (int e = threadIdx.x; e < nt * group; e += blockDim.x) {
+    for (int e = threadIdx.x; e < nt * group; e += kThreads) {
         const int r = e / group, hh = e % group;
-        const float* kr = sm.kt + r * hp;
-        const float* q = sm.q + hh * hd;
+        const float4* kr = reinterpret_cast<const float4*>(sm.kt + r * hp);
+        const float4* qh = reinterpret_cast<const float4*>(sm.q + hh * hd);
         float acc = 0.0f;
-        for (int i = 0; i < hd; ++i) acc = __fadd_rn(acc, __fmul_rn(q[i], kr[i]));
+#pragma unroll 4
+        for (int i = 0; i < hd / 4; ++i) {
+            const float4 k4 = kr[i], q4 = qh[i];
+            acc = __fadd_rn(acc, __fmul_rn(q4.x, k4.x));
+            acc = __fadd_rn(acc, __fmul_rn(q4.y, k4.y));
+            acc = __fadd_rn(acc, __fmul_rn(q4.z, k4.z));
+            acc = __fadd_rn(acc, __fmul_rn(q4.w, k4.w));
+        }
         acc = __fdiv_rn(acc, sq);
-        sm.sc[hh * max_rows + r] = acc;
+        float* dst = sm.sc + hh * d.seq + t0 + r;
+#pragma unroll
+        for (int c = 0; c < kAttnCtas; ++c) *cluster.map_shared_rank(dst, c) = acc;
     }
-    __syncthreads();
-    // 6. cluster max per head
-    for (int hh = warp; hh < group; hh += kWarps) {
-        float m = -1e30f;
-        for (int r = lane; r < nt; r += 32) m = fmaxf(m, sm.sc[hh * max_rows + r]);
-        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        if (lane == 0) sm.mx[hh] = m;
-    }
-    cluster.sync();
-    for (int hh = 0; hh < group; ++hh) {
-        float m = -1e30f;
-        for (int c = 0; c < kAttnCtas; ++c) m = fmaxf(m, *cluster.map_shared_rank(sm.mx + hh, c));
-        lmax[hh] = m;
-    }
-    // 7. exp and the double denominator, cluster-combined in rank order
-    for (int e = threadIdx.x; e < nt * group; e += blockDim.x) {
-        const int r = e / group, hh = e % group;
-        float* p = sm.sc + hh * max_rows + r;
-        *p = vexp(__fsub_rn(*p, lmax[hh]));
-    }
-    __syncthreads();
-    for (int hh = warp; hh < group; hh += kWarps) {
-        double a = 0.0;
-        for (int r = lane; r < nt; r += 32) a = __dadd_rn(a, (double)sm.sc[hh * max_rows + r]);
-        for (int o = 16; o; o >>= 1) a = __dadd_rn(a, __shfl_xor_sync(0xffffffffu, a, o));
-        if (lane == 0) sm.sum[hh] = a;
-    }
-    cluster.sync();
-    for (int hh = 0; hh < group; ++hh) {
-        double a = 0.0;
-        for (int c = 0; c < kAttnCtas; ++c) a = __dadd_rn(a, *cluster.map_shared_rank(sm.sum + hh, c));
-        const float fs = __double2float_rn(a);
-        for (int r = threadIdx.x; r < nt; r += blockDim.x) {
-            float* p = sm.sc + hh * max_rows + r;
-            *p = __fdiv_rn(*p, fs);
+    cluster.sync();   // the last access to another CTA's shared memory
+
+    // 5. softmax over all positions: kWarps / group warps per head (one when
+    //    the group is larger), reductions through shared memory in warp order
+    {
+        const int wph = group >= kWarps ? 1 : kWarps / group;
+        const int hpr = kWarps / wph;             // heads per round
+        const int hw = warp / wph, sub = warp % wph, step = wph * 32;
+        for (int h0 = 0; h0 < group; h0 += hpr) {
+            const int hh = h0 + hw;
+            const bool act = hw < hpr && hh < group;
+            float* p = sm.sc + (act ? hh : 0) * d.seq;
+            float m = -1e30f;
+            if (act)
+                for (int t = sub * 32 + lane; t < len; t += step) m = fmaxf(m, p[t]);
+            for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            if (lane == 0) sm.redf[warp] = m;
+            __syncthreads();
+            double a = 0.0;
+            if (act) {
+                m = sm.redf[hw * wph];
+                for (int k = 1; k < wph; ++k) m = fmaxf(m, sm.redf[hw * wph + k]);
+#pragma unroll 4
+                for (int t = sub * 32 + lane; t < len; t += step) {
+                    const float ev = vexp(__fsub_rn(p[t], m));
+                    p[t] = ev;
+                    a = __dadd_rn(a, (double)ev);
+                }
+            }
+            for (int o = 16; o; o >>= 1) a = __dadd_rn(a, __shfl_xor_sync(0xffffffffu, a, o));
+            if (lane == 0) sm.redd[warp] = a;
+            __syncthreads();
+            if (act) {
+                double tot = sm.redd[hw * wph];
+                for (int k = 1; k < wph; ++k) tot = __dadd_rn(tot, sm.redd[hw * wph + k]);
+                const float fs = __double2float_rn(tot);
+#pragma unroll 4
+                for (int t = sub * 32 + lane; t < len; t += step) p[t] = __fdiv_rn(p[t], fs);
+            }
         }
     }
     __syncthreads();
-    // 8. P.V partials in double over this CTA's positions
-    for (int e = threadIdx.x; e < group * hd; e += blockDim.x) {
-        const int hh = e / hd, i = e % hd;
-        const float* p = sm.sc + hh * max_rows;
+
+    // 6. P.V for this CTA's V columns: each output's positions split into ks
+    //    contiguous ranges, partial sums in double combined in range order
+    const int nout = group * nc;
+    if (nout == 0) return;
+    const int ks = nout >= kThreads ? 1 : min(32, kThreads / nout);
+    const int chunk = (len + ks - 1) / ks;
+    for (int e = threadIdx.x; e < nout * ks; e += kThreads) {
+        const int o = e / ks, j = e % ks, hh = o / nc, i = o % nc;
+        const int ta = min(len, j * chunk), tb = min(len, ta + chunk);
+        const float* p = sm.sc + hh * d.seq;
+        const float* vc = sm.vt + i;
         double a = 0.0;
-        for (int r = 0; r < nt; ++r) a = __fma_rn((double)p[r], (double)sm.vt[r * hp + i], a);
+#pragma unroll 4
+        for (int t = ta; t < tb; ++t) a = __fma_rn((double)p[t], (double)vc[(size_t)t * vs], a);
         sm.pv[e] = a;
     }
-    cluster.sync();
-    // 9. combine across the cluster in rank order; CTA c writes outputs e = c mod kAttnCtas
-    for (int e = rank + kAttnCtas * threadIdx.x; e < group * hd; e += kAttnCtas * blockDim.x) {
+    __syncthreads();
+    for (int o = threadIdx.x; o < nout; o += kThreads) {
         double a = 0.0;
-        for (int c = 0; c < kAttnCtas; ++c) a = __dadd_rn(a, *cluster.map_shared_rank(sm.pv + e, c));
-        s.att[(size_t)b * d.dim + g * group * hd + e] = (int16_t)q16h(__double2float_rn(a));
+        for (int j = 0; j < ks; ++j) a = __dadd_rn(a, sm.pv[o * ks + j]);
+        const int hh = o / nc, i = o % nc;
+        s.att[(size_t)b * d.dim + (size_t)(g * group + hh) * hd + c0 + i] = (int16_t)q16h(__double2float_rn(a));
     }
-    cluster.sync();   // no CTA leaves while its shared memory may still be read
 }
 
 // ---------------------------------------------------------------------------
@@ -1057,6 +1133,8 @@ __global__ void __launch_bounds__(kThreads) k_raw_i16(DMat W, const int16_t* xq,
 template <typename K>
 void set_smem(K kernel, size_t bytes) {
     static std::map<std::pair<const void*, int>, size_t> done;
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lk(mu);
     int dev = 0;
     cudaGetDevice(&dev);
     size_t& have = done[{(const void*)kernel, dev}];
@@ -1215,11 +1293,9 @@ void launch_logits(const DModel& m, const State& s, const Batch& b, int* next, i
 
 void launch_attention(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st) {
     Dims d = dims_of(m, s);
-    const int group = d.heads / d.kv_heads, hd = d.head_dim;
-    const int max_rows = (d.seq + kAttnCtas - 1) / kAttnCtas;
-    const size_t sm = attn_smem_bytes(group, hd, max_rows);
+    const size_t sm = attn_smem_bytes(d.heads / d.kv_heads, d.head_dim, d.seq, d.kv_bits);
     launch_pdl(k_attn, dim3(d.kv_heads * kAttnCtas, b.n), sm, st, (const float*)m.d_q_norm,
-               (const float*)m.d_k_norm, s, b, d, layer, max_rows);
+               (const float*)m.d_k_norm, s, b, d, layer);
 }
 
 void launch_matvec_raw(const DModel& m, int mat, const int16_t* xq, int n, int32_t* out, cudaStream_t st) {
@@ -1235,11 +1311,10 @@ int kernel_launches_per_step(const DModel& m, int n) {
 
 int max_input_cols() { return kPer * kThreads; }
 
-bool attention_fits(int seq, int head_dim, int kv_bits, int kv_dim) {
-    const int hbytes = kv_bits == 16 ? 2 * head_dim : head_dim;
-    if (hbytes % 16 || kv_dim % 16) return false;
-    const int max_rows = (seq + kAttnCtas - 1) / kAttnCtas;
-    return 2 * max_rows * (hbytes / 16) <= 16 * kThreads;
+bool attention_fits(int seq, int head_dim, int kv_bits, int kv_dim, int group) {
+    const int hbytes = head_dim * (kv_bits / 8);
+    if (hbytes % 16 || kv_dim % 16 || head_dim % 4) return false;
+    return attn_smem_bytes(group, head_dim, seq, kv_bits) <= kMaxDynSmem;
 }
 
 int matvec_max_chunks() { return 20 * kWarps; }

@@ -155,7 +155,7 @@ void launch_logits(const DModel& m, const State& s, const Batch& b, int* next, i
 void launch_matvec_raw(const DModel& m, int mat, const int16_t* xq, int n, int32_t* out, cudaStream_t st);
 int kernel_launches_per_step(const DModel& m, int n);
 // Shape limits of the kernels (checked at upload / session creation).
-bool attention_fits(int seq, int head_dim, int kv_bits, int kv_dim);
+bool attention_fits(int seq, int head_dim, int kv_bits, int kv_dim, int group);
 int matvec_max_chunks();
 int max_input_cols();
 
