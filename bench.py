@@ -97,11 +97,32 @@ def workload_desc(cfg) -> str:
 # ---------------------------------------------------------------------------
 
 class Clocks:
+    """SM clock and throttle reasons sampled while the timed region runs.
+
+    NVML is polled from a thread every couple of milliseconds, so even a timed
+    region of a few tens of milliseconds gets samples; nvidia-smi's 200 ms
+    loop is the fallback when the NVML binding is missing."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event reason bits
+    BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+            "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80}
 
     def __init__(self, device: int):
+        self.sm, self.mx, self.reasons, self.p, self.nv = [], None, set(), None, None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = self._handle(pynvml, device)
+            self.mx = float(pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM))
+            self.run = True
+            self.t = threading.Thread(target=self._poll, daemon=True)
+            self.t.start()
+            return
+        except Exception:
+            self.nv = None
         self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         try:
             self.p = subprocess.Popen(["nvidia-smi", "--query-gpu=" + self.Q, "--format=csv,noheader,nounits",
@@ -109,7 +130,38 @@ class Clocks:
         except OSError:
             self.p = None
 
+    @staticmethod
+    def _handle(nv, device):
+        try:
+            import torch
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            return nv.nvmlDeviceGetHandleByUUID(("GPU-" + uuid).encode())
+        except Exception:
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+            idx = int(vis.split(",")[device]) if vis and vis.split(",")[device].isdigit() else device
+            return nv.nvmlDeviceGetHandleByIndex(idx)
+
+    def _poll(self):
+        nv = self.nv
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while self.run:
+            try:
+                self.sm.append(float(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)))
+                bits = get_reasons(self.h)
+                for n, b in self.BITS.items():
+                    if bits & b:
+                        self.reasons.add(n)
+            except Exception:
+                pass
+            time.sleep(0.002)
+
     def stop(self) -> dict:
+        if self.nv is not None:
+            self.run = False
+            self.t.join(timeout=5)
+            return {"sm_mhz": statistics.median(self.sm) if self.sm else None, "sm_max_mhz": self.mx,
+                    "reasons": sorted(self.reasons), "samples": len(self.sm), "source": "nvml"}
         if self.p is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.p.terminate()
@@ -133,7 +185,7 @@ class Clocks:
             except (ValueError, IndexError):
                 continue
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvidia-smi"}
 
 
 # ---------------------------------------------------------------------------

@@ -284,7 +284,9 @@ static int check_kernel_word(vc4_session* s) {
     int w = 0;
     CK(cudaStreamSynchronize(s->stream));
     CK(cudaMemcpy(&w, s->st.err, sizeof(int), cudaMemcpyDeviceToHost));
-    if (w) return fail(VC4_ECUDA, "a kernel found its shared-memory reservation too small (needs " + std::to_string(w) + " bytes)");
+    if (w > 0) return fail(VC4_ECUDA, "a kernel found its shared-memory reservation too small (needs " + std::to_string(w) + " bytes)");
+    if (w == -2) return fail(VC4_ECUDA, "a kernel's bulk copy did not complete within its time limit");
+    if (w) return fail(VC4_ECUDA, "kernel self-check failed (code " + std::to_string(w) + ")");
     return VC4_OK;
 }
 
@@ -350,6 +352,7 @@ static int finish_load(vc4_gpu* g, HModel&& h, vc4_model** out) {
     vc4_model* m = new vc4_model();
     m->g = g;
     m->d.device = g->device;
+    cudaDeviceGetAttribute(&m->d.num_sms, cudaDevAttrMultiProcessorCount, g->device);
     const std::string e = upload_model(std::move(h), m->d);
     if (!e.empty()) {
         free_model(m->d);

@@ -27,6 +27,7 @@ namespace {
 
 constexpr int kThreads = kWarps * 32;
 constexpr size_t kMaxDynSmem = 227 * 1024;   // opt-in dynamic shared memory per CTA on sm_100
+__host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~(size_t)15; }
 
 // ---------------------------------------------------------------------------
 // Exact arithmetic helpers (each mirrors one step of the oracle)
@@ -259,6 +260,55 @@ __device__ __forceinline__ int4 ld_weights(const int4* p) {
     return v;
 }
 
+
+// ---------------------------------------------------------------------------
+// Bulk copies (cp.async.bulk, the 1-D TMA) into shared memory, completed on
+// mbarriers.  Waits are bounded by the global timer.
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ unsigned smem_addr(const void* p) { return (unsigned)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void mbar_init(unsigned long long* bar, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+// Makes mbarrier initialisation visible to the asynchronous (bulk-copy) proxy.
+__device__ __forceinline__ void mbar_fence_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void mbar_expect_tx(unsigned long long* bar, unsigned bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+// Orders this thread's earlier generic-proxy shared-memory accesses before
+// later bulk copies into the same memory.
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// global -> shared, `bytes` a multiple of 16, both addresses 16-byte aligned.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, unsigned long long* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(unsigned long long* bar, unsigned parity) {
+    unsigned ok;
+    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+                 : "=r"(ok) : "r"(smem_addr(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
+// Waits for phase `parity` of `bar`; false if it has not completed within
+// `limit_ns` (the caller then reports an error instead of waiting for ever).
+__device__ __forceinline__ bool mbar_wait(unsigned long long* bar, unsigned parity,
+                                          unsigned long long limit_ns = 100000000ull) {
+    if (mbar_try(bar, parity)) return true;
+    const unsigned long long t0 = global_ns();
+    while (!mbar_try(bar, parity))
+        if (global_ns() - t0 > limit_ns) return false;
+    return true;
+}
+
+// Error word values besides shared-memory shortfalls (which record the bytes needed).
+constexpr int kErrCopyTimeout = -2;
+constexpr int kStreamStages = 4;   // ring depth of the streaming kernels
+
 template <int MAXC>
 struct WRegs {
     int4 w[MAXC];
@@ -281,7 +331,8 @@ __device__ __forceinline__ void mv_prefetch(const DMat& W, int blk, WRegs<MAXC>&
     R.rs = __ldg(W.rscale + (size_t)blk * 32 + lane);
 }
 
-template <int WT, int NB, int MAXC>
+// OWN: the staged input holds only this warp's chunks, slot k for chunk j.
+template <int WT, int NB, int MAXC, bool OWN = false>
 __device__ __forceinline__ void mv_compute(const DMat& W, const WRegs<MAXC>& R, const XStage& xs, int nb,
                                            long long (&S)[NB]) {
     const int warp = threadIdx.x >> 5, nch = W.nchunks;
@@ -293,12 +344,13 @@ __device__ __forceinline__ void mv_compute(const DMat& W, const WRegs<MAXC>& R, 
         const int j = warp + k * kWarps;
         if (j >= nch) break;
         const int4 w = R.w[k];
+        const int xi = OWN ? k : j;   // staged chunk index
         if (WT == W_Q8) {
 #pragma unroll
             for (int b = 0; b < NB; ++b) {
                 if (b >= nb) break;
-                const uint4 L = *reinterpret_cast<const uint4*>(xs.lo + (size_t)b * xs.stride + j * 16);
-                const uint4 H = *reinterpret_cast<const uint4*>(xs.hi + (size_t)b * xs.stride + j * 16);
+                const uint4 L = *reinterpret_cast<const uint4*>(xs.lo + (size_t)b * xs.stride + xi * 16);
+                const uint4 H = *reinterpret_cast<const uint4*>(xs.hi + (size_t)b * xs.stride + xi * 16);
                 alo[b] = dp4a_su(w.x, L.x, alo[b]); alo[b] = dp4a_su(w.y, L.y, alo[b]);
                 alo[b] = dp4a_su(w.z, L.z, alo[b]); alo[b] = dp4a_su(w.w, L.w, alo[b]);
                 ahi[b] = dp4a_ss(w.x, (int)H.x, ahi[b]); ahi[b] = dp4a_ss(w.y, (int)H.y, ahi[b]);
@@ -309,8 +361,8 @@ __device__ __forceinline__ void mv_compute(const DMat& W, const WRegs<MAXC>& R, 
 #pragma unroll
             for (int b = 0; b < NB; ++b) {
                 if (b >= nb) break;
-                const uint4* L4 = reinterpret_cast<const uint4*>(xs.lo + (size_t)b * xs.stride + j * 64);
-                const uint4* H4 = reinterpret_cast<const uint4*>(xs.hi + (size_t)b * xs.stride + j * 64);
+                const uint4* L4 = reinterpret_cast<const uint4*>(xs.lo + (size_t)b * xs.stride + xi * 64);
+                const uint4* H4 = reinterpret_cast<const uint4*>(xs.hi + (size_t)b * xs.stride + xi * 64);
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
                     const uint4 L = L4[q], H = H4[q];
@@ -328,8 +380,8 @@ __device__ __forceinline__ void mv_compute(const DMat& W, const WRegs<MAXC>& R, 
 #pragma unroll
             for (int b = 0; b < NB; ++b) {
                 if (b >= nb) break;
-                const uint4* L4 = reinterpret_cast<const uint4*>(xs.lo + (size_t)b * xs.stride + j * 32);
-                const uint4* H4 = reinterpret_cast<const uint4*>(xs.hi + (size_t)b * xs.stride + j * 32);
+                const uint4* L4 = reinterpret_cast<const uint4*>(xs.lo + (size_t)b * xs.stride + xi * 32);
+                const uint4* H4 = reinterpret_cast<const uint4*>(xs.hi + (size_t)b * xs.stride + xi * 32);
                 const uint4 L0 = L4[0], L1 = L4[1], H0 = H4[0], H1 = H4[1];
                 const unsigned l[8] = {L0.x, L0.y, L0.z, L0.w, L1.x, L1.y, L1.z, L1.w};
                 const unsigned h[8] = {H0.x, H0.y, H0.z, H0.w, H1.x, H1.y, H1.z, H1.w};
@@ -341,7 +393,7 @@ __device__ __forceinline__ void mv_compute(const DMat& W, const WRegs<MAXC>& R, 
                     nhi = dp4a_us(n0, (int)h[2 * q], nhi); nhi = dp4a_us(n1, (int)h[2 * q + 1], nhi);
                 }
                 const long long N = (long long)nlo + 256LL * nhi;
-                S[b] += s16 * N + m16 * (long long)xs.gsum[b * xs.gstride + j];
+                S[b] += s16 * N + m16 * (long long)xs.gsum[b * xs.gstride + xi];
             }
         }
     }
@@ -438,57 +490,204 @@ struct MatSet {
 };
 
 // ---------------------------------------------------------------------------
-// qkv: [embedding] + RMSNorm + matvec_s(qkv)
+// Warp-staged matvec kernels.  Warp w of a CTA computes the dot products of
+// the column chunks j = w, w + kWarps, ... (its slots k = 0, 1, ...), so it
+// only reads the input bytes of those chunks.  Every warp prepares them
+// itself from the whole input vector in shared memory: the RMSNorm sum of
+// squares, the power-of-two input scale (from the maximum over all columns)
+// and the t3 column total are warp reductions, identical in every warp, and
+// the bytes of x' = x*2^k for the warp's own chunks go to its own slice.  A
+// kernel therefore has two block barriers: after its inputs land in shared
+// memory, and for the cross-warp sum of the dot products.
+// ---------------------------------------------------------------------------
+
+struct WStage {     // one warp's slice of staged input bytes
+    uint8_t* lo;    // [nb][wst]
+    int8_t* hi;     // [nb][wst]
+    int* gsum;      // q4: [nb][gst] chunk sums; t3: [nb] totals (gsum[b*gst])
+    int wst, gst;
+};
+
+__host__ __device__ inline int own_slots(int nch) { return (nch + kWarps - 1) / kWarps; }
+__host__ __device__ inline size_t wstage_bytes(const DMat& W, int nb) {
+    const int own = own_slots(W.nchunks), cpc = cpc_of(W.wtype), gst = W.wtype == W_Q4 ? own : 1;
+    return align16((size_t)2 * nb * own * cpc) + align16(sizeof(int) * (size_t)nb * gst);
+}
+__device__ __forceinline__ WStage wstage_at(const DMat& W, int nb, char* base) {
+    WStage w;
+    const int own = own_slots(W.nchunks);
+    char* p = base + (size_t)(threadIdx.x >> 5) * wstage_bytes(W, nb);
+    w.wst = own * cpc_of(W.wtype);
+    w.gst = W.wtype == W_Q4 ? own : 1;
+    w.lo = reinterpret_cast<uint8_t*>(p);
+    w.hi = reinterpret_cast<int8_t*>(p + (size_t)nb * w.wst);
+    w.gsum = reinterpret_cast<int*>(p + align16((size_t)2 * nb * w.wst));
+    return w;
+}
+__device__ __forceinline__ XStage xstage_of(const WStage& w) {
+    XStage x;
+    x.lo = w.lo; x.hi = w.hi; x.stride = w.wst; x.gsum = w.gsum; x.gstride = w.gst;
+    return x;
+}
+
+// Dynamic shared memory of the warp-staged kernels.
+struct MvLayout {
+    size_t part, x, nw, ws, extra, total;
+};
+__host__ __device__ inline MvLayout mv_layout(size_t ws_per_warp, int nb, int nvals, int nnw, size_t extra) {
+    MvLayout L;
+    size_t o = 0;
+    L.part = o;  o = align16(o + sizeof(long long) * 2 * kWarps * (size_t)nb * 32);
+    L.x = o;     o = align16(o + sizeof(int16_t) * (size_t)nvals);
+    L.nw = o;    o = align16(o + sizeof(float) * (size_t)nnw);
+    L.ws = o;    o = align16(o + kWarps * ws_per_warp);
+    L.extra = o; o = align16(o + extra);
+    L.total = o;
+    return L;
+}
+
+__device__ __forceinline__ long long warp_sum_i64(long long v) {
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+// matvec_s input scale: k = 6 - e for max|x| = f*2^e (gpu_conv.cpp:271-287), 0 for a zero vector.
+__device__ __forceinline__ int exp_from_max(int mx) {
+    if (mx == 0) return 0;
+    int e = 0;
+    frexpf(__fmul_rn((float)mx, 1.0f / 256.0f), &e);
+    return 6 - e;
+}
+// 1/sqrt(mean(x^2) + eps) of a q16 vector from its exact integer sum of squares
+// (session.cpp:1932-1948, the sum rounded once).
+__device__ __forceinline__ float rms_rr(long long ss, int D, float eps) {
+    const float s1 = __fmul_rn(__ll2float_rn(ss), 1.0f / 65536.0f);
+    const float s2 = __fdiv_rn(s1, (float)D);
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(s2, eps)));
+}
+__device__ __forceinline__ int xnorm(int a, float w, float rr) {
+    return q16h(__fmul_rn(w, __fmul_rn(rr, __fmul_rn((float)a, 1.0f / 256.0f))));
+}
+__device__ __forceinline__ int xscale(int a, int k, float sk) {
+    return k >= 0 ? (a << k) : __float2int_rn(__fmul_rn((float)a, sk));
+}
+__device__ __forceinline__ long long warp_sumsq(const int16_t* x, int D) {
+    long long ss = 0;
+    for (int c = (threadIdx.x & 31); c < D; c += 32) { const int a = x[c]; ss += a * a; }
+    return warp_sum_i64(ss);
+}
+
+// x'[c] = value(c)*2^k into the warp's slice for the columns of its own
+// chunks (zero past D); q4: the sum of each chunk; t3: the total over all D
+// columns.  Ends with the slice written by this warp (caller: __syncwarp).
+template <int WT, typename F>
+__device__ __forceinline__ void warp_stage(const WStage& ws, int b, int nch, int D, int k, F value) {
+    constexpr int cpc = WT == W_Q8 ? 16 : WT == W_Q4 ? 32 : 64;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const float sk = ldexpf(1.0f, k);
+    uint8_t* lo = ws.lo + (size_t)b * ws.wst;
+    int8_t* hi = ws.hi + (size_t)b * ws.wst;
+    for (int e = lane; e < ws.wst; e += 32) {
+        const int slot = e / cpc, j = warp + slot * kWarps, c = j * cpc + e % cpc;
+        const int q = (j < nch && c < D) ? xscale(value(c), k, sk) : 0;
+        lo[e] = (uint8_t)(q & 0xFF);
+        hi[e] = (int8_t)(q >> 8);
+        if (WT == W_Q4) {   // wst is a multiple of 32: every lane is here, one chunk per pass
+            const int gs = __reduce_add_sync(0xffffffffu, q);
+            if (lane == 0) ws.gsum[b * ws.gst + slot] = gs;
+        }
+    }
+    if (WT == W_T3) {
+        int t = 0;
+        for (int c = lane; c < D; c += 32) t += xscale(value(c), k, sk);
+        t = __reduce_add_sync(0xffffffffu, t);
+        if (lane == 0) ws.gsum[b * ws.gst] = t;
+    }
+}
+
+// Cross-warp sum of V partial dot products per (input, row) with one block
+// barrier; on return warps b < nb hold the totals of input b, row `lane`.
+// The partial buffer is not reused afterwards.
+template <int NB, int V>
+__device__ __forceinline__ void reduce_once(const long long (&S)[V][NB], int nb, long long* red,
+                                            long long (&out)[V]) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int v = 0; v < V; ++v)
+#pragma unroll
+        for (int b = 0; b < NB; ++b) red[((warp * V + v) * NB + b) * 32 + lane] = S[v][b];
+    __syncthreads();
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+        long long t = 0;
+        if (warp < nb)
+            for (int w = 0; w < kWarps; ++w) t += red[((w * V + v) * NB + warp) * 32 + lane];
+        out[v] = t;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// qkv: embedding (layer 0) or x, RMSNorm, matvec_s(qkv) -> fp32 qkv
 // ---------------------------------------------------------------------------
 
 template <int WT, int NB, int MAXC>
 __global__ void __launch_bounds__(kThreads) k_qkv(DMat W, DMat E, const float* emb_scale, const float* rms_w,
                                                   State s, Batch bt, Dims d, int layer, int b0) {
-    if (!smem_ok(smem_bytes(NB, x_stride(W), g_stride(W), NB * d.dim), s.err)) return;
+    const MvLayout L = mv_layout(wstage_bytes(W, NB), NB, NB * d.dim, d.dim, 0);
+    if (!smem_ok(L.total, s.err)) return;
+    char* sm = SmemLayout::base();
     WRegs<MAXC> R;
     mv_prefetch<WT, MAXC>(W, blockIdx.x, R);
-    float nw[kPer];
-    load_f32_regs(rms_w, d.dim, nw);
+    float* nws = reinterpret_cast<float*>(sm + L.nw);
+    for (int c = threadIdx.x; c < d.dim; c += kThreads) nws[c] = __ldg(rms_w + c);
     pdl_launch_dependents();
     pdl_wait();
-    XStage xs; Red* red; long long* part; int16_t* tmp;
-    carve<NB>(x_stride(W), g_stride(W), xs, red, part, tmp);
+    int16_t* xv = reinterpret_cast<int16_t*>(sm + L.x);
     const int nb = min(NB, bt.n - b0);
     for (int b = 0; b < nb; ++b) {
         const int bi = b0 + b;
-        int16_t* x = s.x + (size_t)bi * d.dim;
-        int16_t* xin = tmp + (size_t)b * d.dim;
+        int16_t* xin = xv + (size_t)b * d.dim;
         if (layer == 0) {
             // embedding (session.cpp:342-371): q16(level * row scale); the row
             // is read from the blocked q8 layout of the embedding matrix.
             const int tok = bt.token[bi];
             const float es = emb_scale[tok];
             const int8_t* eb = reinterpret_cast<const int8_t*>(E.body) + ((size_t)(tok / 32) * E.nchunks * 32 + (tok % 32)) * 16;
-            for (int c = threadIdx.x; c < d.dim; c += blockDim.x) {
-                const int lv = eb[(size_t)(c / 16) * 512 + (c % 16)];
-                const int16_t q = (int16_t)q16h(__fmul_rn((float)lv, es));
+            int16_t* x = s.x + (size_t)bi * d.dim;
+            for (int c = threadIdx.x; c < d.dim; c += kThreads) {
+                const int16_t q = (int16_t)q16h(__fmul_rn((float)eb[(size_t)(c / 16) * 512 + (c % 16)], es));
                 xin[c] = q;
                 if (blockIdx.x == 0) x[c] = q;
             }
             if (blockIdx.x == 0 && threadIdx.x == 0) s.best[bi] = 0ull;
         } else {
-            load_vec(x, d.dim, xin);
+            load_vec(s.x + (size_t)bi * d.dim, d.dim, xin);
         }
-        __syncthreads();
-        rmsnorm_q16(xin, nw, d.dim, d.eps, xin, *red);
-        xs.k[b] = scale_exponent(xin, d.dim, *red);
-        stage_one<WT>(xs, b, xin, d.dim, xs.k[b], *red);
     }
-    long long S[NB];
-    mv_compute<WT, NB, MAXC>(W, R, xs, nb, S);
-    const long long tot = reduce_warps<NB>(S, nb, part);
+    __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const WStage ws = wstage_at(W, NB, sm + L.ws);
+    int kw = 0;   // input scale of input `warp` (its epilogue)
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+        if (b >= nb) break;
+        const int16_t* x = xv + (size_t)b * d.dim;
+        const float rr = rms_rr(warp_sumsq(x, d.dim), d.dim, d.eps);
+        int mx = 0;
+        for (int c = lane; c < d.dim; c += 32) mx = max(mx, abs(xnorm(x[c], nws[c], rr)));
+        const int k = exp_from_max(__reduce_max_sync(0xffffffffu, mx));
+        if (b == warp) kw = k;
+        warp_stage<WT>(ws, b, W.nchunks, d.dim, k, [&](int c) { return xnorm(x[c], nws[c], rr); });
+    }
+    __syncwarp();
+    long long S[1][NB], tot[1];
+    mv_compute<WT, NB, MAXC, true>(W, R, xstage_of(ws), nb, S[0]);
+    reduce_once<NB, 1>(S, nb, reinterpret_cast<long long*>(sm + L.part), tot);
     if (warp < nb) {
         const int row = blockIdx.x * 32 + lane;
         if (row < W.rows) {
-            const long long St = WT == W_T3 ? tot - xs.gsum[warp * xs.gstride] : tot;
+            const long long St = WT == W_T3 ? tot[0] - ws.gsum[warp * ws.gst] : tot[0];
             const int v = mv_epi(St, R.rs);
-            const float out = __fmul_rn(__fmul_rn((float)v, 1.0f / 256.0f), ldexpf(1.0f, -xs.k[warp]));
+            const float out = __fmul_rn(__fmul_rn((float)v, 1.0f / 256.0f), ldexpf(1.0f, -kw));
             s.qkv[(size_t)(b0 + warp) * (d.dim + 2 * d.kv_dim) + row] = out;
         }
     }
@@ -500,121 +699,128 @@ __global__ void __launch_bounds__(kThreads) k_qkv(DMat W, DMat E, const float* e
 
 template <int WT, int NB, int MAXC>
 __global__ void __launch_bounds__(kThreads) k_wo(DMat W, State s, Batch bt, Dims d, int b0) {
-    if (!smem_ok(smem_bytes(NB, x_stride(W), g_stride(W), NB * d.dim), s.err)) return;
+    const MvLayout L = mv_layout(wstage_bytes(W, NB), NB, NB * d.dim, 0, 0);
+    if (!smem_ok(L.total, s.err)) return;
+    char* sm = SmemLayout::base();
     WRegs<MAXC> R;
     mv_prefetch<WT, MAXC>(W, blockIdx.x, R);
     pdl_launch_dependents();
     pdl_wait();
-    XStage xs; Red* red; long long* part; int16_t* tmp;
-    carve<NB>(x_stride(W), g_stride(W), xs, red, part, tmp);
     const int nb = min(NB, bt.n - b0);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row = blockIdx.x * 32 + lane;
     // the residual this thread's epilogue adds, fetched with the inputs
     const int xres = (warp < nb && row < W.rows) ? (int)__ldcg(s.x + (size_t)(b0 + warp) * d.dim + row) : 0;
-    for (int b = 0; b < nb; ++b) load_vec(s.att + (size_t)(b0 + b) * d.dim, d.dim, tmp + (size_t)b * d.dim);
+    int16_t* av = reinterpret_cast<int16_t*>(sm + L.x);
+    for (int b = 0; b < nb; ++b) load_vec(s.att + (size_t)(b0 + b) * d.dim, d.dim, av + (size_t)b * d.dim);
     __syncthreads();
-    for (int b = 0; b < nb; ++b) {
-        const int16_t* a = tmp + (size_t)b * d.dim;
-        xs.k[b] = scale_exponent(a, d.dim, *red);
-        stage_one<WT>(xs, b, a, d.dim, xs.k[b], *red);
+    const WStage ws = wstage_at(W, NB, sm + L.ws);
+    int kw = 0;
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+        if (b >= nb) break;
+        const int16_t* a = av + (size_t)b * d.dim;
+        int mx = 0;
+        for (int c = lane; c < d.dim; c += 32) mx = max(mx, abs((int)a[c]));
+        const int k = exp_from_max(__reduce_max_sync(0xffffffffu, mx));
+        if (b == warp) kw = k;
+        warp_stage<WT>(ws, b, W.nchunks, d.dim, k, [&](int c) { return (int)a[c]; });
     }
-    long long S[NB];
-    mv_compute<WT, NB, MAXC>(W, R, xs, nb, S);
-    const long long tot = reduce_warps<NB>(S, nb, part);
+    __syncwarp();
+    long long S[1][NB], tot[1];
+    mv_compute<WT, NB, MAXC, true>(W, R, xstage_of(ws), nb, S[0]);
+    reduce_once<NB, 1>(S, nb, reinterpret_cast<long long*>(sm + L.part), tot);
     if (warp < nb && row < W.rows) {
-        const long long St = WT == W_T3 ? tot - xs.gsum[warp * xs.gstride] : tot;
+        const long long St = WT == W_T3 ? tot[0] - ws.gsum[warp * ws.gst] : tot[0];
         const int v = mv_epi(St, R.rs);
-        const float wo = __fmul_rn(__fmul_rn((float)v, 1.0f / 256.0f), ldexpf(1.0f, -xs.k[warp]));
+        const float wo = __fmul_rn(__fmul_rn((float)v, 1.0f / 256.0f), ldexpf(1.0f, -kw));
         const float xr = __fmul_rn((float)xres, 1.0f / 256.0f);
         s.x1[(size_t)(b0 + warp) * d.dim + row] = (int16_t)q16h(__fadd_rn(xr, wo));
     }
 }
 
 // ---------------------------------------------------------------------------
-// gate: RMSNorm(x1) + [router] + w1/w3 + SwiGLU -> h
+// gate: RMSNorm(x1), optional MoE routing (top-1, shaders.cpp:1216-1230 and
+// session.cpp:110-115), w1/w3 matvecs and SwiGLU (q16 pair rounding,
+// shaders.cpp:116-136) -> h (the GPU FFN path the CPU session draws)
 // ---------------------------------------------------------------------------
 
-// MoE route of one q16 input (session.cpp:1523-1536 + pick_expert 110-115):
-// matvec_s over the i16 router, first maximum.
-__device__ int route_of(const int16_t* xbf, const DMat& R, int D, int experts, Red& r) {
-    const int k = scale_exponent(xbf, D, r);
-    const float sk = ldexpf(1.0f, k);
-    int best = 0;
-    float bestv = 0.0f;
-    for (int e = 0; e < experts; ++e) {
-        long long acc = 0;
-        for (int c = threadIdx.x; c < D; c += blockDim.x) {
-            const int a = xbf[c];
-            const int q = k >= 0 ? (a << k) : __float2int_rn(__fmul_rn((float)a, sk));
-            acc += (long long)R.w16[(size_t)e * D + c] * q;
-        }
-        acc = block_sum_i64(acc, r);
-        const int v = mv_epi(acc, R.rscale[e]);
-        const float g = __fmul_rn(__fmul_rn((float)v, 1.0f / 256.0f), ldexpf(1.0f, -k));
-        if (e == 0 || g > bestv) { best = e; bestv = g; }
-    }
-    return best;
-}
-
-// blockIdx.y is the expert (0 for a dense FFN); an MoE CTA serves the inputs
-// routed to its expert.  `early` prefetches the expert's weights before the
-// routing is known (a batch that uses every expert), otherwise after it.
 template <int WT, int NB, int MAXC>
 __global__ void __launch_bounds__(kThreads) k_gate(MatSet M, const float* rms_w, State s, Batch bt, Dims d,
                                                    int layer, int b0, int hs, int early) {
     const int expert = blockIdx.y;
     const DMat& W1 = M.a[expert];
     const DMat& W3 = M.b[expert];
-    if (!smem_ok(smem_bytes(NB, x_stride(W1), g_stride(W1), (NB + 1) * d.dim) + 64, s.err)) return;
+    const size_t rbytes = d.experts ? sizeof(int16_t) * (size_t)d.experts * d.dim : 0;
+    const MvLayout L = mv_layout(wstage_bytes(W1, NB), NB, NB * d.dim, d.dim, rbytes + 64);
+    if (!smem_ok(L.total, s.err)) return;
+    char* sm = SmemLayout::base();
     WRegs<MAXC> R1, R3;
     if (early) {
         mv_prefetch<WT, MAXC>(W1, blockIdx.x, R1);
         mv_prefetch<WT, MAXC>(W3, blockIdx.x, R3);
     }
-    float nw[kPer];
-    load_f32_regs(rms_w, d.dim, nw);
+    float* nws = reinterpret_cast<float*>(sm + L.nw);
+    for (int c = threadIdx.x; c < d.dim; c += kThreads) nws[c] = __ldg(rms_w + c);
+    int16_t* rw = reinterpret_cast<int16_t*>(sm + L.extra);             // router rows
+    int* members = reinterpret_cast<int*>(sm + L.extra + align16(rbytes));
+    for (int i = threadIdx.x; i < d.experts * d.dim; i += kThreads) rw[i] = M.router.w16[i];
     pdl_launch_dependents();
     pdl_wait();
-    XStage xs; Red* red; long long* part; int16_t* tmp;
-    carve<NB>(x_stride(W1), g_stride(W1), xs, red, part, tmp);
-    int* members = reinterpret_cast<int*>(tmp + (size_t)(NB + 1) * d.dim);   // batch indices served
+    int16_t* xv = reinterpret_cast<int16_t*>(sm + L.x);
     const int n_all = min(NB, bt.n - b0);
-    for (int b = 0; b < n_all; ++b) load_vec(s.x1 + (size_t)(b0 + b) * d.dim, d.dim, tmp + (size_t)b * d.dim);
+    for (int b = 0; b < n_all; ++b) load_vec(s.x1 + (size_t)(b0 + b) * d.dim, d.dim, xv + (size_t)b * d.dim);
     __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const WStage ws = wstage_at(W1, NB, sm + L.ws);
     int nb = 0;
-    for (int b = 0; b < n_all; ++b) {
-        int16_t* xin = tmp + (size_t)b * d.dim;
-        rmsnorm_q16(xin, nw, d.dim, d.eps, xin, *red);
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+        if (b >= n_all) break;
+        const int16_t* x = xv + (size_t)b * d.dim;
+        const float rr = rms_rr(warp_sumsq(x, d.dim), d.dim, d.eps);
         if (d.experts) {
-            const int e = route_of(xin, M.router, d.dim, d.experts, *red);
-            if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) s.route[(size_t)(b0 + b) * d.layers + layer] = e;
-            __syncthreads();
-            if (e != expert) continue;
+            // router: matvec_s over the normalised input, first maximum wins
+            int mx = 0;
+            for (int c = lane; c < d.dim; c += 32) mx = max(mx, abs(xnorm(x[c], nws[c], rr)));
+            const int k = exp_from_max(__reduce_max_sync(0xffffffffu, mx));
+            const float sk = ldexpf(1.0f, k);
+            int best = 0;
+            float bestv = 0.0f;
+            for (int e = 0; e < d.experts; ++e) {
+                long long acc = 0;
+                for (int c = lane; c < d.dim; c += 32)
+                    acc += (long long)rw[(size_t)e * d.dim + c] * xscale(xnorm(x[c], nws[c], rr), k, sk);
+                const int v = mv_epi(warp_sum_i64(acc), M.router.rscale[e]);
+                const float gv = __fmul_rn(__fmul_rn((float)v, 1.0f / 256.0f), ldexpf(1.0f, -k));
+                if (e == 0 || gv > bestv) { best = e; bestv = gv; }
+            }
+            if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0)
+                s.route[(size_t)(b0 + b) * d.layers + layer] = best;
+            if (best != expert) continue;
         }
         if (threadIdx.x == 0) members[nb] = b;
-        xs.k[nb] = 0;
-        stage_one<WT>(xs, nb, xin, d.dim, 0, *red);
+        warp_stage<WT>(ws, nb, W1.nchunks, d.dim, 0, [&](int c) { return xnorm(x[c], nws[c], rr); });
         ++nb;
     }
-    if (nb == 0) return;
+    if (nb == 0) return;   // the same in every warp: no input routed to this expert
     if (!early) {
         mv_prefetch<WT, MAXC>(W1, blockIdx.x, R1);
         mv_prefetch<WT, MAXC>(W3, blockIdx.x, R3);
     }
-    long long S1[NB], S3[NB];
-    mv_compute<WT, NB, MAXC>(W1, R1, xs, nb, S1);
-    const long long t1 = reduce_warps<NB>(S1, nb, part);
-    mv_compute<WT, NB, MAXC>(W3, R3, xs, nb, S3);
-    const long long t3 = reduce_warps<NB>(S3, nb, part);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncwarp();
+    long long S[2][NB], tot[2];
+    const XStage xs = xstage_of(ws);
+    mv_compute<WT, NB, MAXC, true>(W1, R1, xs, nb, S[0]);
+    mv_compute<WT, NB, MAXC, true>(W3, R3, xs, nb, S[1]);
+    reduce_once<NB, 2>(S, nb, reinterpret_cast<long long*>(sm + L.part), tot);
     if (warp < nb) {
         const int row = blockIdx.x * 32 + lane;
         if (row < W1.rows) {
             const int bi = b0 + members[warp];
-            const int corr = WT == W_T3 ? xs.gsum[warp * xs.gstride] : 0;
-            const int g = mv_epi(t1 - corr, R1.rs);
-            const int u = mv_epi(t3 - corr, R3.rs);
+            const int corr = WT == W_T3 ? ws.gsum[warp * ws.gst] : 0;
+            const int g = mv_epi(tot[0] - corr, R1.rs);
+            const int u = mv_epi(tot[1] - corr, R3.rs);
             float y = swiglu1(__fmul_rn((float)g, 1.0f / 256.0f), __fmul_rn((float)u, 1.0f / 256.0f));
             if (hs > 0) y = __fmul_rn(y, ldexpf(1.0f, -hs));     // metadata key 15 store scale
             s.h[(size_t)bi * d.ffn + row] = (int16_t)q16s(y);
@@ -632,9 +838,10 @@ __global__ void __launch_bounds__(kThreads) k_down(MatSet M, State s, Batch bt, 
     const bool two = d.chunk < d.ffn;
     const DMat& Wa = M.a[expert];
     const DMat& Wb = M.b[expert];
-    if (!smem_ok(smem_bytes(NB, x_stride(Wa), g_stride(Wa), 0) + 2 * (size_t)NB * (two ? x_stride(Wb) : 16) +
-                     sizeof(int) * NB * g_stride(Wb) + 256 + sizeof(int16_t) * (size_t)NB * d.ffn, s.err))
-        return;
+    const size_t wsa = wstage_bytes(Wa, NB), wsb = two ? wstage_bytes(Wb, NB) : 0;
+    const MvLayout L = mv_layout(wsa + wsb, NB, NB * d.ffn, 0, 64);
+    if (!smem_ok(L.total, s.err)) return;
+    char* sm = SmemLayout::base();
     WRegs<MAXC> Ra, Rb;
     if (early) {
         mv_prefetch<WT, MAXC>(Wa, blockIdx.x, Ra);
@@ -642,18 +849,8 @@ __global__ void __launch_bounds__(kThreads) k_down(MatSet M, State s, Batch bt, 
     }
     pdl_launch_dependents();
     pdl_wait();
-    XStage xa, xb; Red* red; long long* part; int16_t* tmp;
-    carve<NB>(x_stride(Wa), g_stride(Wa), xa, red, part, tmp);
-    xb = xa;
-    const int sb = two ? x_stride(Wb) : 0;
-    xb.stride = sb > 0 ? sb : 16;
-    xb.gstride = g_stride(Wb);
-    xb.gsum = reinterpret_cast<int*>(tmp);
-    xb.lo = reinterpret_cast<uint8_t*>(xb.gsum + NB * xb.gstride + 4);
-    xb.lo = reinterpret_cast<uint8_t*>(((uintptr_t)xb.lo + 15) & ~(uintptr_t)15);
-    xb.hi = reinterpret_cast<int8_t*>(xb.lo + (size_t)NB * xb.stride);
-    int* members = reinterpret_cast<int*>(xb.hi + (size_t)NB * xb.stride);
-    int16_t* hbuf = reinterpret_cast<int16_t*>(((uintptr_t)(members + NB) + 15) & ~(uintptr_t)15);   // [nb][ffn]
+    int* members = reinterpret_cast<int*>(sm + L.extra);
+    int16_t* hv = reinterpret_cast<int16_t*>(sm + L.x);
     const int n_all = min(NB, bt.n - b0);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row = blockIdx.x * 32 + lane;
@@ -661,35 +858,46 @@ __global__ void __launch_bounds__(kThreads) k_down(MatSet M, State s, Batch bt, 
     for (int b = 0; b < n_all; ++b) {
         if (d.experts && __ldcg(s.route + (size_t)(b0 + b) * d.layers + layer) != expert) continue;
         if (threadIdx.x == 0) members[nb] = b;
-        load_vec(s.h + (size_t)(b0 + b) * d.ffn, d.ffn, hbuf + (size_t)nb * d.ffn);
+        load_vec(s.h + (size_t)(b0 + b) * d.ffn, d.ffn, hv + (size_t)nb * d.ffn);
         ++nb;
     }
     __syncthreads();
     if (nb == 0) return;
     const int xres = (warp < nb && row < Wa.rows) ? (int)__ldcg(s.x1 + (size_t)(b0 + members[warp]) * d.dim + row) : 0;
-    for (int b = 0; b < nb; ++b) {
-        const int16_t* h = hbuf + (size_t)b * d.ffn;
-        stage_one<WT>(xa, b, h, d.chunk, 0, *red);
-        if (two) stage_one<WT>(xb, b, h + d.chunk, d.ffn - d.chunk, 0, *red);
+    char* wbase = sm + L.ws;
+    const WStage xa = wstage_at(Wa, NB, wbase);
+    WStage xb = xa;
+    if (two) {
+        // the second chunk's slices follow all first-chunk slices
+        xb = wstage_at(Wb, NB, wbase + kWarps * wsa);
+    }
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+        if (b >= nb) break;
+        const int16_t* h = hv + (size_t)b * d.ffn;
+        warp_stage<WT>(xa, b, Wa.nchunks, d.chunk, 0, [&](int c) { return (int)h[c]; });
+        if (two) warp_stage<WT>(xb, b, Wb.nchunks, d.ffn - d.chunk, 0, [&](int c) { return (int)h[d.chunk + c]; });
     }
     if (!early) {
         mv_prefetch<WT, MAXC>(Wa, blockIdx.x, Ra);
         if (two) mv_prefetch<WT, MAXC>(Wb, blockIdx.x, Rb);
     }
-    long long Sa[NB], Sb[NB];
-    mv_compute<WT, NB, MAXC>(Wa, Ra, xa, nb, Sa);
-    const long long ta = reduce_warps<NB>(Sa, nb, part);
-    long long tb = 0;
+    __syncwarp();
+    long long S[2][NB], tot[2];
+    mv_compute<WT, NB, MAXC, true>(Wa, Ra, xstage_of(xa), nb, S[0]);
     if (two) {
-        mv_compute<WT, NB, MAXC>(Wb, Rb, xb, nb, Sb);
-        tb = reduce_warps<NB>(Sb, nb, part);
+        mv_compute<WT, NB, MAXC, true>(Wb, Rb, xstage_of(xb), nb, S[1]);
+    } else {
+#pragma unroll
+        for (int b = 0; b < NB; ++b) S[1][b] = 0;
     }
+    reduce_once<NB, 2>(S, nb, reinterpret_cast<long long*>(sm + L.part), tot);
     if (warp < nb && row < Wa.rows) {
         const int bi = b0 + members[warp];
-        const int va = mv_epi(WT == W_T3 ? ta - xa.gsum[warp * xa.gstride] : ta, Ra.rs);
+        const int va = mv_epi(WT == W_T3 ? tot[0] - xa.gsum[warp * xa.gst] : tot[0], Ra.rs);
         float o2 = __fmul_rn((float)va, 1.0f / 256.0f);
         if (two) {
-            const int vb = mv_epi(WT == W_T3 ? tb - xb.gsum[warp * xb.gstride] : tb, Rb.rs);
+            const int vb = mv_epi(WT == W_T3 ? tot[1] - xb.gsum[warp * xb.gst] : tot[1], Rb.rs);
             // add_q16 of the two chunk outputs (session.cpp:2052-2067)
             o2 = __fmul_rn((float)q16h(__fadd_rn(o2, __fmul_rn((float)vb, 1.0f / 256.0f))), 1.0f / 256.0f);
         }
@@ -711,52 +919,25 @@ struct Finalize {
     int advance;
 };
 
-template <int WT, int NB, int MAXC>
-__global__ void __launch_bounds__(kThreads) k_logits(DMat W, const float* rms_w, State s, Batch bt, Dims d, int b0,
-                                                     Finalize fz) {
-    if (!smem_ok(smem_bytes(NB, x_stride(W), g_stride(W), NB * d.dim), s.err)) return;
-    WRegs<MAXC> R;
-    mv_prefetch<WT, MAXC>(W, blockIdx.x, R);
-    float nw[kPer];
-    load_f32_regs(rms_w, d.dim, nw);
-    pdl_launch_dependents();
-    pdl_wait();
-    XStage xs; Red* red; long long* part; int16_t* tmp;
-    carve<NB>(x_stride(W), g_stride(W), xs, red, part, tmp);
-    const int nb = min(NB, bt.n - b0);
-    for (int b = 0; b < nb; ++b) load_vec(s.x + (size_t)(b0 + b) * d.dim, d.dim, tmp + (size_t)b * d.dim);
-    __syncthreads();
-    for (int b = 0; b < nb; ++b) {
-        int16_t* xin = tmp + (size_t)b * d.dim;
-        rmsnorm_q16(xin, nw, d.dim, d.eps, xin, *red);
-        xs.k[b] = 0;
-        stage_one<WT>(xs, b, xin, d.dim, 0, *red);
-    }
-    long long S[NB];
-    mv_compute<WT, NB, MAXC>(W, R, xs, nb, S);
-    const long long tot = reduce_warps<NB>(S, nb, part);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (warp < nb) {
-        const int row = blockIdx.x * 32 + lane;
-        const int bi = b0 + warp;
-        unsigned long long key = 0ull;
-        if (row < W.rows) {
-            const int v = mv_epi(tot, R.rs);
-            s.logits[(size_t)bi * d.vocab + row] = v;
-            key = ((unsigned long long)(unsigned)(v + 32768) << 32) | (unsigned)(0xFFFFFFFFu - (unsigned)row);
-        }
-        for (int o = 16; o; o >>= 1) {
-            const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, key, o);
-            key = k2 > key ? k2 : key;
-        }
-        if (lane == 0 && key) { atomicMax(&s.best[bi], key); __threadfence(); }
-    }
-    // last CTA: greedy tokens for this launch's inputs
+// Logits and the greedy token.  The greedy token is the first maximum
+// (sampling.cpp:160-162), found by a packed-key atomicMax over all rows; the
+// last CTA to finish writes the next token (and advances position and token
+// for the device-resident decode loop).  Two kernels share that tail:
+//  - k_logits: one CTA per 32-row block, the columns split over the warps,
+//    for heads of up to a few hundred blocks (latency: every SM busy at once);
+//  - k_logits_wide: one warp per 32-row block (lanes are rows, each warp walks
+//    all column chunks, no cross-warp reduction), grid-stride over the blocks,
+//    several CTAs per SM, for heads of thousands of blocks (HBM streaming).
+__device__ __forceinline__ unsigned long long logit_key(int v, int row) {
+    return ((unsigned long long)(unsigned)(v + 32768) << 32) | (unsigned)(0xFFFFFFFFu - (unsigned)row);
+}
+
+__device__ __forceinline__ void logits_finish(State& s, int b0, int nb, const Finalize& fz) {
     __shared__ int last;
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence();
-        last = atomicAdd(s.done, 1) == (int)gridDim.x - 1;
+        last = atomicAdd(s.done, 1) == (int)(gridDim.x * gridDim.y) - 1;
     }
     __syncthreads();
     if (!last) return;
@@ -775,8 +956,197 @@ __global__ void __launch_bounds__(kThreads) k_logits(DMat W, const float* rms_w,
     if (threadIdx.x == 0) *s.done = 0;
 }
 
-// Attention for one (KV head, sequence) runs on a cluster of kAttnCtas CTAs
-// with a single cluster barrier:
+template <int NB>
+__device__ __forceinline__ void logits_stage_inputs(const DMat& W, const float (&nw)[kPer], State& s, const Dims& d,
+                                                    int b0, int nb, XStage& xs, Red*& red, int16_t*& tmp) {
+    long long* part;
+    carve<NB>(x_stride(W), g_stride(W), xs, red, part, tmp);
+    for (int b = 0; b < nb; ++b) load_vec(s.x + (size_t)(b0 + b) * d.dim, d.dim, tmp + (size_t)b * d.dim);
+    __syncthreads();
+    for (int b = 0; b < nb; ++b) {
+        int16_t* xin = tmp + (size_t)b * d.dim;
+        rmsnorm_q16(xin, nw, d.dim, d.eps, xin, *red);
+        xs.k[b] = 0;
+        stage_one<W_Q8>(xs, b, xin, d.dim, 0, *red);
+    }
+}
+
+template <int NB, int MAXC>
+__global__ void __launch_bounds__(kThreads) k_logits(DMat W, const float* rms_w, State s, Batch bt, Dims d, int b0,
+                                                     Finalize fz) {
+    const MvLayout L = mv_layout(wstage_bytes(W, NB), NB, NB * d.dim, d.dim, 0);
+    if (!smem_ok(L.total, s.err)) return;
+    char* sm = SmemLayout::base();
+    WRegs<MAXC> R;
+    mv_prefetch<W_Q8, MAXC>(W, blockIdx.x, R);
+    float* nws = reinterpret_cast<float*>(sm + L.nw);
+    for (int c = threadIdx.x; c < d.dim; c += kThreads) nws[c] = __ldg(rms_w + c);
+    pdl_launch_dependents();
+    pdl_wait();
+    int16_t* xv = reinterpret_cast<int16_t*>(sm + L.x);
+    const int nb = min(NB, bt.n - b0);
+    for (int b = 0; b < nb; ++b) load_vec(s.x + (size_t)(b0 + b) * d.dim, d.dim, xv + (size_t)b * d.dim);
+    __syncthreads();
+    const WStage ws = wstage_at(W, NB, sm + L.ws);
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+        if (b >= nb) break;
+        const int16_t* x = xv + (size_t)b * d.dim;
+        const float rr = rms_rr(warp_sumsq(x, d.dim), d.dim, d.eps);
+        warp_stage<W_Q8>(ws, b, W.nchunks, d.dim, 0, [&](int c) { return xnorm(x[c], nws[c], rr); });
+    }
+    __syncwarp();
+    long long S[1][NB], tot[1];
+    mv_compute<W_Q8, NB, MAXC, true>(W, R, xstage_of(ws), nb, S[0]);
+    reduce_once<NB, 1>(S, nb, reinterpret_cast<long long*>(sm + L.part), tot);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warp < nb) {
+        const int row = blockIdx.x * 32 + lane;
+        const int bi = b0 + warp;
+        unsigned long long key = 0ull;
+        if (row < W.rows) {
+            const int v = mv_epi(tot[0], R.rs);
+            s.logits[(size_t)bi * d.vocab + row] = v;
+            key = logit_key(v, row);
+        }
+        for (int o = 16; o; o >>= 1) {
+            const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, key, o);
+            key = k2 > key ? k2 : key;
+        }
+        if (lane == 0 && key) { atomicMax(&s.best[bi], key); __threadfence(); }
+    }
+    logits_finish(s, b0, nb, fz);
+}
+
+// One warp per 32-row block: lanes are rows, the warp walks every column
+// chunk of its blocks.  Each warp streams its weights through its own ring of
+// shared-memory stages filled by bulk copies (pieces of up to kWidePiece
+// 16-column chunks, 512 contiguous bytes per chunk), so the copies in flight
+// cost no registers; the first pieces are requested before the grid-dependency
+// wait.  Blocks are dealt to warps round-robin over the whole grid.
+constexpr int kWidePiece = 16;
+
+__host__ __device__ inline size_t wide_base(const DMat& W, int nb, int dim) {
+    return (smem_bytes(nb, x_stride(W), g_stride(W), nb * dim) + 127) & ~(size_t)127;
+}
+// Ring stages per warp that fit next to the input staging (0: none fit).
+__host__ __device__ inline int wide_stages(const DMat& W, int nb, int dim) {
+    const size_t base = wide_base(W, nb, dim);
+    if (base >= kMaxDynSmem) return 0;
+    const size_t per_warp = (kMaxDynSmem - base) / kWarps;
+    const size_t stage = (size_t)kWidePiece * 512 + 8;
+    const int st = (int)(per_warp / stage);
+    return st > 4 ? 4 : st;
+}
+__host__ __device__ inline size_t wide_smem(const DMat& W, int nb, int dim, int stages) {
+    return wide_base(W, nb, dim) + (size_t)kWarps * stages * ((size_t)kWidePiece * 512 + 8);
+}
+
+template <int NB>
+__global__ void __launch_bounds__(kThreads) k_logits_wide(DMat W, const float* rms_w, State s, Batch bt, Dims d,
+                                                         int b0, Finalize fz, int stages) {
+    if (!smem_ok(wide_smem(W, NB, d.dim, stages), s.err)) return;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nch = W.nchunks;
+    char* ring = SmemLayout::base() + wide_base(W, NB, d.dim) + (size_t)warp * stages * kWidePiece * 512;
+    unsigned long long* bar = reinterpret_cast<unsigned long long*>(
+        SmemLayout::base() + wide_base(W, NB, d.dim) + (size_t)kWarps * stages * kWidePiece * 512) + warp * stages;
+    const int ppb = (nch + kWidePiece - 1) / kWidePiece;             // pieces per block
+    const int stride = gridDim.x * kWarps;
+    const int first = blockIdx.x * kWarps + warp;
+    const int nblk = first < W.rblocks ? (W.rblocks - first + stride - 1) / stride : 0;
+    const int npieces = nblk * ppb;
+    auto issue = [&](int p) {
+        const int blk = first + (p / ppb) * stride, j0 = (p % ppb) * kWidePiece;
+        const unsigned bytes = (unsigned)min(kWidePiece, nch - j0) * 512u;
+        unsigned long long* b = &bar[p % stages];
+        mbar_expect_tx(b, bytes);
+        bulk_g2s(ring + (size_t)(p % stages) * kWidePiece * 512, W.body + ((size_t)blk * nch + j0) * 512, bytes, b);
+    };
+    if (lane == 0) {
+        for (int i = 0; i < stages; ++i) mbar_init(&bar[i], 1);
+        mbar_fence_init();
+        for (int p = 0; p < min(stages, npieces); ++p) issue(p);
+    }
+    float nw[kPer];
+    load_f32_regs(rms_w, d.dim, nw);
+    pdl_launch_dependents();
+    pdl_wait();
+    XStage xs; Red* red; int16_t* tmp;
+    const int nb = min(NB, bt.n - b0);
+    logits_stage_inputs<NB>(W, nw, s, d, b0, nb, xs, red, tmp);   // block-wide; publishes the mbarriers
+    unsigned long long best[NB];
+#pragma unroll
+    for (int b = 0; b < NB; ++b) best[b] = 0ull;
+    int alo[NB], ahi[NB];
+    float rs = 0.0f;
+    bool failed = false;
+    for (int p = 0; p < npieces; ++p) {
+        const int blk = first + (p / ppb) * stride, j0 = (p % ppb) * kWidePiece;
+        if (j0 == 0) {
+            rs = __ldg(W.rscale + (size_t)blk * 32 + lane);
+#pragma unroll
+            for (int b = 0; b < NB; ++b) { alo[b] = 0; ahi[b] = 0; }
+        }
+        if (!mbar_wait(&bar[p % stages], (unsigned)(p / stages) & 1u)) { failed = true; break; }
+        const int4* buf = reinterpret_cast<const int4*>(ring + (size_t)(p % stages) * kWidePiece * 512) + lane;
+        const int nu = min(kWidePiece, nch - j0);
+#pragma unroll 4
+        for (int u = 0; u < nu; ++u) {
+            const int4 w = buf[u * 32];
+            const int j = j0 + u;
+#pragma unroll
+            for (int b = 0; b < NB; ++b) {
+                if (b >= nb) break;
+                const uint4 L = *reinterpret_cast<const uint4*>(xs.lo + (size_t)b * xs.stride + j * 16);
+                const uint4 H = *reinterpret_cast<const uint4*>(xs.hi + (size_t)b * xs.stride + j * 16);
+                alo[b] = dp4a_su(w.x, L.x, alo[b]); alo[b] = dp4a_su(w.y, L.y, alo[b]);
+                alo[b] = dp4a_su(w.z, L.z, alo[b]); alo[b] = dp4a_su(w.w, L.w, alo[b]);
+                ahi[b] = dp4a_ss(w.x, (int)H.x, ahi[b]); ahi[b] = dp4a_ss(w.y, (int)H.y, ahi[b]);
+                ahi[b] = dp4a_ss(w.z, (int)H.z, ahi[b]); ahi[b] = dp4a_ss(w.w, (int)H.w, ahi[b]);
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && p + stages < npieces) {
+            fence_proxy_async();
+            issue(p + stages);
+        }
+        if (j0 + kWidePiece >= nch) {
+            const int row = blk * 32 + lane;
+#pragma unroll
+            for (int b = 0; b < NB; ++b) {
+                if (b >= nb || row >= W.rows) continue;
+                const int v = mv_epi((long long)alo[b] + 256LL * (long long)ahi[b], rs);
+                s.logits[(size_t)(b0 + b) * d.vocab + row] = v;
+                const unsigned long long key = logit_key(v, row);
+                best[b] = key > best[b] ? key : best[b];
+            }
+        }
+    }
+    if (failed) {
+        // a copy did not land in time: report it and wait (bounded) for this
+        // warp's copies still in flight before the shared memory is released
+        if (lane == 0) {
+            atomicExch(s.err, kErrCopyTimeout);
+            for (int p = 0; p < npieces; ++p) mbar_wait(&bar[p % stages], (unsigned)(p / stages) & 1u, 10000000ull);
+        }
+        __syncwarp();
+    }
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+        if (b >= nb) break;
+        unsigned long long kk = best[b];
+        for (int o = 16; o; o >>= 1) {
+            const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, kk, o);
+            kk = k2 > kk ? k2 : kk;
+        }
+        if (lane == 0 && kk) atomicMax(&s.best[b0 + b], kk);
+    }
+    logits_finish(s, b0, nb, fz);
+}
+
+// Attention for one (KV head, sequence) runs on group/hq clusters of kAttnCtas
+// CTAs, each cluster serving hq of the KV head's query heads, with a single
+// cluster barrier:
 //  - before the grid-dependency wait every CTA stages the cache rows it needs
 //    (cp.async) and decodes them to fp32 in shared memory: the K rows of its
 //    contiguous share of positions 0..pos, and a slice of V columns for every
@@ -795,7 +1165,6 @@ constexpr int kAttnCtas = 8;
 
 __host__ __device__ inline int attn_vs(int hd) { return (((hd + kAttnCtas - 1) / kAttnCtas) + 3) & ~3; }
 __host__ __device__ inline int attn_rows(int seq) { return (seq + kAttnCtas - 1) / kAttnCtas; }
-__host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~(size_t)15; }
 
 struct AttnSmem {
     uint8_t* kraw;   // attn_rows(seq) x hbytes: K rows of this CTA's positions (cache bytes)
@@ -893,16 +1262,18 @@ __device__ __forceinline__ unsigned kv_encode(float x, int kvb, float* dec) {
 }
 
 __global__ void __cluster_dims__(kAttnCtas, 1, 1) __launch_bounds__(kThreads)
-k_attn(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int layer) {
+k_attn(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int layer, int hq) {
     namespace cg = cooperative_groups;
     cg::cluster_group cluster = cg::this_cluster();
     extern __shared__ __align__(16) char smem[];
     const int hd = d.head_dim, group = d.heads / d.kv_heads, half = hd / 2, hp = hd + 4;
-    if (!smem_ok(attn_smem_bytes(group, hd, d.seq, d.kv_bits), s.err)) return;
+    if (!smem_ok(attn_smem_bytes(hq, hd, d.seq, d.kv_bits), s.err)) return;
     AttnSmem sm;
-    attn_carve(group, hd, d.seq, d.kv_bits, smem, &sm);
+    attn_carve(hq, hd, d.seq, d.kv_bits, smem, &sm);
     const int rank = (int)cluster.block_rank();
-    const int g = blockIdx.x / kAttnCtas, b = blockIdx.y;
+    // cluster (g, split) serves q heads split*hq .. split*hq + hq - 1 of KV head g
+    const int qsplit = group / hq, g = blockIdx.x / kAttnCtas / qsplit, split = blockIdx.x / kAttnCtas % qsplit;
+    const int h0 = split * hq, b = blockIdx.y;
     const int slot = bt.slot[b], pos = bt.pos[b], len = pos + 1;
     const int per = (len + kAttnCtas - 1) / kAttnCtas;
     const int t0 = min(len, rank * per), t1 = min(len, t0 + per), nt = t1 - t0;
@@ -956,14 +1327,14 @@ k_attn(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int 
     // 2. q heads, new k, new v from the qkv matvec; qk-norm (exact double sum
     //    of squares) and RoPE, one warp per vector
     const float* qkv = s.qkv + (size_t)b * (d.dim + 2 * d.kv_dim);
-    for (int i = threadIdx.x; i < group * hd; i += kThreads) sm.q[i] = qkv[g * group * hd + i];
+    for (int i = threadIdx.x; i < hq * hd; i += kThreads) sm.q[i] = qkv[(g * group + h0) * hd + i];
     for (int i = threadIdx.x; i < hd; i += kThreads) {
-        sm.q[group * hd + i] = qkv[d.dim + g * hd + i];
+        sm.q[hq * hd + i] = qkv[d.dim + g * hd + i];
         sm.vn[i] = qkv[d.dim + d.kv_dim + g * hd + i];
     }
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int hh = warp; hh <= group; hh += kWarps) {
+    for (int hh = warp; hh <= hq; hh += kWarps) {
         float* v = sm.q + hh * hd;
         if (d.qk_norm) {
             double acc = 0.0;
@@ -971,7 +1342,7 @@ k_attn(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int 
             for (int o = 16; o; o >>= 1) acc = __dadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
             const float ss = __double2float_rn(acc);
             const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)hd), 1e-6f)));
-            const float* w = hh < group ? sm.wq : sm.wk;
+            const float* w = hh < hq ? sm.wq : sm.wk;
             for (int i = lane; i < hd; i += 32) v[i] = __fmul_rn(w[i], __fmul_rn(r, v[i]));
             __syncwarp();
         }
@@ -986,16 +1357,17 @@ k_attn(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int 
 
     // 3. encode the new row one 32-bit word at a time (shaders_attn.cpp:141-159);
     //    every CTA encodes it identically, the one whose share holds `pos`
-    //    writes it to the cache
+    //    writes it to the cache (the first split of the KV head)
     const bool owner = pos >= t0 && pos < t1;
+    const bool writer = owner && split == 0;
     uint8_t* row = kvbase + (size_t)pos * d.row_bytes;
     for (int e = threadIdx.x; e < 2 * kw; e += kThreads) {
         const int w = e / kw, c = e % kw, i0 = c * vpw;
-        const float* src = w ? sm.vn : sm.q + group * hd;
+        const float* src = w ? sm.vn : sm.q + hq * hd;
         unsigned word = 0;
         float dec[4];
         for (int j = 0; j < vpw; ++j) word |= kv_encode(src[i0 + j], kvb, &dec[j]) << (8 * kvb * j);
-        if (owner) *reinterpret_cast<unsigned*>(row + (w ? vofs : 0) + g * hbytes + c * 4) = word;
+        if (writer) *reinterpret_cast<unsigned*>(row + (w ? vofs : 0) + g * hbytes + c * 4) = word;
         for (int j = 0; j < vpw; ++j) {
             const int i = i0 + j;
             if (!w && owner) sm.kt[(pos - t0) * hp + i] = dec[j];
@@ -1007,8 +1379,8 @@ k_attn(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int 
     // 4. scores of this CTA's positions: sequential fp32 dot, / sqrt(hd);
     //    stored into every CTA of the cluster
     const float sq = __fsqrt_rn((float)hd);
-    for (int e = threadIdx.x; e < nt * group; e += kThreads) {
-        const int r = e / group, hh = e % group;
+    for (int e = threadIdx.x; e < nt * hq; e += kThreads) {
+        const int r = e / hq, hh = e % hq;
         const float4* kr = reinterpret_cast<const float4*>(sm.kt + r * hp);
         const float4* qh = reinterpret_cast<const float4*>(sm.q + hh * hd);
         float acc = 0.0f;
@@ -1027,15 +1399,16 @@ k_attn(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int 
     }
     cluster.sync();   // the last access to another CTA's shared memory
 
-    // 5. softmax over all positions: kWarps / group warps per head (one when
-    //    the group is larger), reductions through shared memory in warp order
+    // 5. softmax over all positions: kWarps / hq warps per head (one when
+    //    a cluster serves more heads than warps), reductions through shared
+    //    memory in warp order
     {
-        const int wph = group >= kWarps ? 1 : kWarps / group;
+        const int wph = hq >= kWarps ? 1 : kWarps / hq;
         const int hpr = kWarps / wph;             // heads per round
         const int hw = warp / wph, sub = warp % wph, step = wph * 32;
-        for (int h0 = 0; h0 < group; h0 += hpr) {
-            const int hh = h0 + hw;
-            const bool act = hw < hpr && hh < group;
+        for (int r0 = 0; r0 < hq; r0 += hpr) {
+            const int hh = r0 + hw;
+            const bool act = hw < hpr && hh < hq;
             float* p = sm.sc + (act ? hh : 0) * d.seq;
             float m = -1e30f;
             if (act)
@@ -1070,7 +1443,7 @@ k_attn(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int 
 
     // 6. P.V for this CTA's V columns: each output's positions split into ks
     //    contiguous ranges, partial sums in double combined in range order
-    const int nout = group * nc;
+    const int nout = hq * nc;
     if (nout == 0) return;
     const int ks = nout >= kThreads ? 1 : min(32, kThreads / nout);
     const int chunk = (len + ks - 1) / ks;
@@ -1089,7 +1462,7 @@ k_attn(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int 
         double a = 0.0;
         for (int j = 0; j < ks; ++j) a = __dadd_rn(a, sm.pv[o * ks + j]);
         const int hh = o / nc, i = o % nc;
-        s.att[(size_t)b * d.dim + (size_t)(g * group + hh) * hd + c0 + i] = (int16_t)q16h(__double2float_rn(a));
+        s.att[(size_t)b * d.dim + (size_t)(g * group + h0 + hh) * hd + c0 + i] = (int16_t)q16h(__double2float_rn(a));
     }
 }
 
@@ -1180,25 +1553,25 @@ inline int maxc_for(int nch) {
 
 template <int WT>
 struct Ops {
-    template <int MAXC>
-    static void qkv(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
+    template <int NB, int MAXC>
+    static void qkv_nb(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
         const DMat& W = m.mats[m.qkv[layer]];
         const DMat& E = m.mats[m.emb_mat];
         Dims d = dims_of(m, s);
-        const size_t sm = smem_bytes(kNB, x_stride(W), g_stride(W), kNB * d.dim);
-        for (int b0 = 0; b0 < bt.n; b0 += kNB)
-            launch_pdl(k_qkv<WT, kNB, MAXC>, dim3(W.rblocks), sm, st, W, E, m.d_emb_scale,
+        const size_t sm = mv_layout(wstage_bytes(W, NB), NB, NB * d.dim, d.dim, 0).total;
+        for (int b0 = 0; b0 < bt.n; b0 += NB)
+            launch_pdl(k_qkv<WT, NB, MAXC>, dim3(W.rblocks), sm, st, W, E, m.d_emb_scale,
                        (const float*)(m.d_rms_att + (size_t)layer * d.dim), s, bt, d, layer, b0);
     }
-    template <int MAXC>
-    static void wo(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
+    template <int NB, int MAXC>
+    static void wo_nb(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
         const DMat& W = m.mats[m.wo[layer]];
         Dims d = dims_of(m, s);
-        const size_t sm = smem_bytes(kNB, x_stride(W), g_stride(W), kNB * d.dim);
-        for (int b0 = 0; b0 < bt.n; b0 += kNB) launch_pdl(k_wo<WT, kNB, MAXC>, dim3(W.rblocks), sm, st, W, s, bt, d, b0);
+        const size_t sm = mv_layout(wstage_bytes(W, NB), NB, NB * d.dim, 0, 0).total;
+        for (int b0 = 0; b0 < bt.n; b0 += NB) launch_pdl(k_wo<WT, NB, MAXC>, dim3(W.rblocks), sm, st, W, s, bt, d, b0);
     }
-    template <int MAXC>
-    static void gate(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
+    template <int NB, int MAXC>
+    static void gate_nb(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
         Dims d = dims_of(m, s);
         MatSet M;
         if (d.experts) {
@@ -1210,16 +1583,17 @@ struct Ops {
             M.b[0] = m.mats[m.w3[layer]];
         }
         const DMat& W1 = M.a[0];
-        const size_t sm = smem_bytes(kNB, x_stride(W1), g_stride(W1), (kNB + 1) * d.dim) + 64;
+        const size_t rbytes = d.experts ? sizeof(int16_t) * (size_t)d.experts * d.dim : 0;
+        const size_t sm = mv_layout(wstage_bytes(W1, NB), NB, NB * d.dim, d.dim, rbytes + 64).total;
         const dim3 grid(W1.rblocks, d.experts ? d.experts : 1);
         const int hs = layer < (int)m.h.hid_scale.size() ? (int)m.h.hid_scale[layer] : 0;
         const int early = d.experts == 0 || bt.n >= 2 * d.experts;
-        for (int b0 = 0; b0 < bt.n; b0 += kNB)
-            launch_pdl(k_gate<WT, kNB, MAXC>, grid, sm, st, M, (const float*)(m.d_rms_ffn + (size_t)layer * d.dim),
+        for (int b0 = 0; b0 < bt.n; b0 += NB)
+            launch_pdl(k_gate<WT, NB, MAXC>, grid, sm, st, M, (const float*)(m.d_rms_ffn + (size_t)layer * d.dim),
                        s, bt, d, layer, b0, hs, early);
     }
-    template <int MAXC>
-    static void down(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
+    template <int NB, int MAXC>
+    static void down_nb(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
         Dims d = dims_of(m, s);
         MatSet M;
         const bool two = m.ffn_chunked;
@@ -1235,21 +1609,56 @@ struct Ops {
         }
         const DMat& Wa = M.a[0];
         const DMat& Wb = M.b[0];
-        const size_t sm = smem_bytes(kNB, x_stride(Wa), g_stride(Wa), 0) +
-                          2 * (size_t)kNB * (two ? x_stride(Wb) : 16) + sizeof(int) * kNB * g_stride(Wb) + 256 +
-                          sizeof(int16_t) * (size_t)kNB * d.ffn;
+        const size_t sm =
+            mv_layout(wstage_bytes(Wa, NB) + (two ? wstage_bytes(Wb, NB) : 0), NB, NB * d.ffn, 0, 64).total;
         const dim3 grid(Wa.rblocks, d.experts ? d.experts : 1);
         const int early = d.experts == 0 || bt.n >= 2 * d.experts;
-        for (int b0 = 0; b0 < bt.n; b0 += kNB)
-            launch_pdl(k_down<WT, kNB, MAXC>, grid, sm, st, M, s, bt, d, layer, b0, early);
+        for (int b0 = 0; b0 < bt.n; b0 += NB)
+            launch_pdl(k_down<WT, NB, MAXC>, grid, sm, st, M, s, bt, d, layer, b0, early);
+    }
+    template <int NB, int MAXC>
+    static void logits_nb(const DModel& m, const State& s, const Batch& bt, const Finalize& fz, cudaStream_t st) {
+        const DMat& W = m.mats[m.logits_mat];
+        Dims d = dims_of(m, s);
+        const int nsm = std::max(1, m.num_sms);
+        const int stages = wide_stages(W, NB, d.dim);
+        if (W.rblocks > 2 * nsm && stages >= 2) {
+            const int grid = std::min((W.rblocks + kWarps - 1) / kWarps, nsm);
+            const size_t wsm = wide_smem(W, NB, d.dim, stages);
+            for (int b0 = 0; b0 < bt.n; b0 += NB)
+                launch_pdl(k_logits_wide<NB>, dim3(grid), wsm, st, W, (const float*)m.d_rms_final, s, bt, d, b0, fz,
+                           stages);
+        } else {
+            const size_t csm = mv_layout(wstage_bytes(W, NB), NB, NB * d.dim, d.dim, 0).total;
+            for (int b0 = 0; b0 < bt.n; b0 += NB)
+                launch_pdl(k_logits<NB, MAXC>, dim3(W.rblocks), csm, st, W, (const float*)m.d_rms_final, s, bt, d, b0,
+                           fz);
+        }
+    }
+    template <int MAXC>
+    static void qkv(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
+        if (bt.n == 1) qkv_nb<1, MAXC>(m, s, bt, layer, st);
+        else qkv_nb<kNB, MAXC>(m, s, bt, layer, st);
+    }
+    template <int MAXC>
+    static void wo(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
+        if (bt.n == 1) wo_nb<1, MAXC>(m, s, bt, layer, st);
+        else wo_nb<kNB, MAXC>(m, s, bt, layer, st);
+    }
+    template <int MAXC>
+    static void gate(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
+        if (bt.n == 1) gate_nb<1, MAXC>(m, s, bt, layer, st);
+        else gate_nb<kNB, MAXC>(m, s, bt, layer, st);
+    }
+    template <int MAXC>
+    static void down(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
+        if (bt.n == 1) down_nb<1, MAXC>(m, s, bt, layer, st);
+        else down_nb<kNB, MAXC>(m, s, bt, layer, st);
     }
     template <int MAXC>
     static void logits(const DModel& m, const State& s, const Batch& bt, const Finalize& fz, cudaStream_t st) {
-        const DMat& W = m.mats[m.logits_mat];
-        Dims d = dims_of(m, s);
-        const size_t sm = smem_bytes(kNB, x_stride(W), g_stride(W), kNB * d.dim);
-        for (int b0 = 0; b0 < bt.n; b0 += kNB)
-            launch_pdl(k_logits<WT, kNB, MAXC>, dim3(W.rblocks), sm, st, W, (const float*)m.d_rms_final, s, bt, d, b0, fz);
+        if (bt.n == 1) logits_nb<1, MAXC>(m, s, bt, fz, st);
+        else logits_nb<kNB, MAXC>(m, s, bt, fz, st);
     }
     template <int MAXC>
     static void raw(const DMat& W, const int16_t* xq, int n, int32_t* out, cudaStream_t st) {
@@ -1291,11 +1700,15 @@ void launch_logits(const DModel& m, const State& s, const Batch& b, int* next, i
     VC4_MAXC(maxc_for(W.nchunks), Ops<W_Q8>::logits, m, s, b, fz, st);
 }
 
+// q heads per cluster: two when the group divides by two, else one
+int attn_heads_per_cluster(int group) { return group % 2 == 0 ? 2 : 1; }
+
 void launch_attention(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st) {
     Dims d = dims_of(m, s);
-    const size_t sm = attn_smem_bytes(d.heads / d.kv_heads, d.head_dim, d.seq, d.kv_bits);
-    launch_pdl(k_attn, dim3(d.kv_heads * kAttnCtas, b.n), sm, st, (const float*)m.d_q_norm,
-               (const float*)m.d_k_norm, s, b, d, layer);
+    const int group = d.heads / d.kv_heads, hq = attn_heads_per_cluster(group);
+    const size_t sm = attn_smem_bytes(hq, d.head_dim, d.seq, d.kv_bits);
+    launch_pdl(k_attn, dim3(d.kv_heads * (group / hq) * kAttnCtas, b.n), sm, st, (const float*)m.d_q_norm,
+               (const float*)m.d_k_norm, s, b, d, layer, hq);
 }
 
 void launch_matvec_raw(const DModel& m, int mat, const int16_t* xq, int n, int32_t* out, cudaStream_t st) {
@@ -1314,7 +1727,7 @@ int max_input_cols() { return kPer * kThreads; }
 bool attention_fits(int seq, int head_dim, int kv_bits, int kv_dim, int group) {
     const int hbytes = head_dim * (kv_bits / 8);
     if (hbytes % 16 || kv_dim % 16 || head_dim % 4) return false;
-    return attn_smem_bytes(group, head_dim, seq, kv_bits) <= kMaxDynSmem;
+    return attn_smem_bytes(attn_heads_per_cluster(group), head_dim, seq, kv_bits) <= kMaxDynSmem;
 }
 
 int matvec_max_chunks() { return 20 * kWarps; }

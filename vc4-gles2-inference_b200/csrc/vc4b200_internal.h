@@ -102,6 +102,7 @@ struct DModel {
     DMat* d_mats = nullptr;          // device array mirror of `mats` (for kernels that pick experts)
     size_t weight_bytes = 0;
     int device = 0;
+    int num_sms = 0;                 // streaming multiprocessors of `device`
     std::vector<void*> allocs;     // every device allocation of the model
 };
 
