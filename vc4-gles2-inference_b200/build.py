@@ -8,6 +8,7 @@ vc4b200/_lib/libvc4b200.so.  Objects go to _build/ next to this file.
 """
 from __future__ import annotations
 
+import concurrent.futures
 import os
 import subprocess
 import sys
@@ -22,8 +23,8 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-std=c++17", "-O3", "-lineinfo", "--fmad=false", "-I" + INCLUDE, "-I" + CSRC,
          "-Xcompiler", "-fPIC,-ffp-contract=off,-fvisibility=hidden", "-diag-suppress", "177"]
-SOURCES = ["kernels.cu", "engine.cu", "noalloc.cu", "mmcf.cpp"]
-HEADERS = ["vc4b200_internal.h"]
+SOURCES = ["kernels.cu", "ops_q8.cu", "ops_q4.cu", "ops_t3.cu", "engine.cu", "noalloc.cu", "mmcf.cpp"]
+HEADERS = ["vc4b200_internal.h", "kernels.cuh", "ops_wt.inc"]
 
 
 def _newer(target: str, deps: list) -> bool:
@@ -37,7 +38,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
     os.makedirs(BUILD, exist_ok=True)
     os.makedirs(os.path.dirname(OUT), exist_ok=True)
     hdrs = [os.path.join(CSRC, h) for h in HEADERS] + [os.path.join(INCLUDE, "vc4b200.h")]
-    objs = []
+    objs, cmds = [], []
     for src in SOURCES:
         path = os.path.join(CSRC, src)
         obj = os.path.join(BUILD, src + ".o")
@@ -46,9 +47,14 @@ def build(force: bool = False, verbose: bool = False) -> str:
             cmd = [NVCC] + ARCH + FLAGS + ["-c", path, "-o", obj]
             if src.endswith(".cpp"):
                 cmd = [NVCC] + ARCH + FLAGS + ["-x", "c++", "-c", path, "-o", obj]
+            cmds.append(cmd)
+    # the translation units are independent: compile them side by side
+    with concurrent.futures.ThreadPoolExecutor(max_workers=max(1, min(len(cmds), os.cpu_count() or 1))) as ex:
+        for cmd in cmds:
             if verbose:
                 print(" ".join(cmd), flush=True)
-            subprocess.run(cmd, check=True)
+        for f in [ex.submit(subprocess.run, cmd, check=True) for cmd in cmds]:
+            f.result()
     if force or _newer(OUT, objs):
         cmd = [NVCC] + ARCH + ["-shared", "-o", OUT] + objs
         if verbose:

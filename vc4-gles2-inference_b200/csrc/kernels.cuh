@@ -1,0 +1,1693 @@
+// kernels.cuh -- sm_100a kernels of the quantized decode step (shared by the
+// translation units: kernels.cu holds the weight-type independent kernels and
+// the launch entry points, ops_q8.cu / ops_q4.cu / ops_t3.cu instantiate the
+// matvec kernels of one weight type each, so the three compile in parallel).
+//
+// One decode step of one layer is five kernels:
+//   qkv    embedding (layer 0) + RMSNorm + matvec_s(qkv)             -> qkv floats
+//   attn   qk-norm + RoPE + packed KV append + attention over the cache -> att (q16)
+//   wo     matvec_s(wo) + residual add                               -> x1 (q16)
+//   gate   RMSNorm + [MoE router] + w1/w3 matvecs + SwiGLU            -> h (q16)
+//   down   w2 (one or two column chunks) + residual add              -> x (q16)
+// and after the last layer `logits` (RMSNorm + logits matvec + first-max
+// argmax).  The arithmetic is the reference CPU layer loop's
+// (engine/src/session.cpp:373-556) with the shader arithmetic of the
+// matrices it draws; every weight x activation product is an exact integer
+// (dp4a on the 8-bit weights and the split lo/hi bytes of the q16 input), and
+// each float step is an explicitly rounded IEEE operation so the CPU oracle
+// reproduces it bit for bit.  Build with --fmad=false.
+#pragma once
+#include "vc4b200_internal.h"
+
+#include <cooperative_groups.h>
+
+#include <cstdio>
+#include <map>
+#include <mutex>
+#include <utility>
+
+namespace vc4 {
+namespace {
+
+constexpr int kThreads = kWarps * 32;
+constexpr size_t kMaxDynSmem = 227 * 1024;   // opt-in dynamic shared memory per CTA on sm_100
+__host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~(size_t)15; }
+
+// ---------------------------------------------------------------------------
+// Exact arithmetic helpers (each mirrors one step of the oracle)
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ int dp4a_su(int a, unsigned b, int c) {
+    int d; asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
+}
+__device__ __forceinline__ int dp4a_ss(int a, int b, int c) {
+    int d; asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
+}
+__device__ __forceinline__ int dp4a_uu(unsigned a, unsigned b, int c) {
+    int d; asm("dp4a.u32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
+}
+__device__ __forceinline__ int dp4a_us(unsigned a, int b, int c) {
+    int d; asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
+}
+
+// q16 host quantisation: lrintf(v*256) clamped (common.h:188-193).
+__device__ __forceinline__ int q16h(float v) {
+    const int q = __float2int_rn(__fmul_rn(v, 256.0f));
+    return q < -32768 ? -32768 : q > 32767 ? 32767 : q;
+}
+// q16 shader store: clamp(floor(v*256+0.5)) (xformat.cpp x_st2).
+__device__ __forceinline__ int q16s(float v) {
+    float f = floorf(__fadd_rn(__fmul_rn(v, 256.0f), 0.5f));
+    f = f < -32768.0f ? -32768.0f : f > 32767.0f ? 32767.0f : f;
+    return (int)f;
+}
+// Matvec epilogue: floor(S*sc + 0.5) clamped to the q16 rail.
+__device__ __forceinline__ int mv_epi(long long S, float sc) {
+    double v = floor(__dadd_rn(__dmul_rn(__ll2double_rn(S), (double)sc), 0.5));
+    v = v < -32768.0 ? -32768.0 : v > 32767.0 ? 32767.0 : v;
+    return (int)v;
+}
+// Portable exp: Cody-Waite reduction + degree-7 Taylor (same ops as orc_expf).
+__device__ __forceinline__ float vexp(float x) {
+    if (x != x) return x;
+    if (x > 88.72283935546875f) return __int_as_float(0x7f800000);
+    if (x < -103.97208404541016f) return 0.0f;
+    const float k = rintf(__fmul_rn(x, 1.44269502162933349609375f));
+    float r = __fmaf_rn(-k, 0.693145751953125f, x);
+    r = __fmaf_rn(-k, 1.428606765330187045037746429443359375e-06f, r);
+    float p = 1.98412698412698412698e-4f;
+    p = __fmaf_rn(p, r, 1.38888888888888888889e-3f);
+    p = __fmaf_rn(p, r, 8.33333333333333333333e-3f);
+    p = __fmaf_rn(p, r, 4.16666666666666666667e-2f);
+    p = __fmaf_rn(p, r, 1.66666666666666666667e-1f);
+    p = __fmaf_rn(p, r, 0.5f);
+    p = __fmaf_rn(p, r, 1.0f);
+    p = __fmaf_rn(p, r, 1.0f);
+    int ki = (int)k;
+    if (ki > 127) { p = __fmul_rn(p, 2.0f); ki -= 1; }
+    if (ki < -126) return __fmul_rn(__fmul_rn(p, __int_as_float((ki + 64 + 127) << 23)), __int_as_float((-64 + 127) << 23));
+    return __fmul_rn(p, __int_as_float((ki + 127) << 23));
+}
+// SiLU(g)*u in the shaders' order.
+__device__ __forceinline__ float swiglu1(float g, float u) {
+    const float den = __fadd_rn(1.0f, vexp(-g));
+    return __fmul_rn(__fdiv_rn(g, den), u);
+}
+
+// ---------------------------------------------------------------------------
+// Block reductions (256 threads)
+// ---------------------------------------------------------------------------
+
+struct Red {
+    long long i64[kWarps];
+    double f64[kWarps];
+    float f32[kWarps];
+    int i32[kWarps];
+};
+
+__device__ long long block_sum_i64(long long v, Red& r) {
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) r.i64[threadIdx.x >> 5] = v;
+    __syncthreads();
+    long long t = 0;
+    for (int w = 0; w < kWarps; ++w) t += r.i64[w];
+    return t;
+}
+__device__ int block_max_i32(int v, Red& r) {
+    for (int o = 16; o; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) r.i32[threadIdx.x >> 5] = v;
+    __syncthreads();
+    int t = r.i32[0];
+    for (int w = 1; w < kWarps; ++w) t = max(t, r.i32[w]);
+    return t;
+}
+// ---------------------------------------------------------------------------
+// Input staging: q16 ints -> (optionally 2^k scaled) ints split into lo/hi bytes
+// ---------------------------------------------------------------------------
+
+constexpr int kPer = 16;   // vector elements per thread: inputs of up to 16*256 = 4096 columns
+
+struct XStage {
+    uint8_t* lo;       // [nb][stride]
+    int8_t* hi;        // [nb][stride]
+    int stride;        // padded column count
+    int* gsum;         // q4: [nb][stride/32] group sums; t3: [nb] totals (in gsum[b*gstride])
+    int gstride;
+    int k[8];          // per input: power-of-two input scale (matvec_s)
+};
+
+// Copy n int16 from global to shared memory with every load issued before the
+// first store (one DRAM round trip); 16-byte vectors when aligned.
+__device__ __forceinline__ void load_vec(const int16_t* __restrict__ g, int n, int16_t* sm) {
+    if ((n & 7) == 0 && (((uintptr_t)g | (uintptr_t)sm) & 15) == 0) {
+        const int nv = n >> 3;
+        uint4 t[2];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int v = threadIdx.x + i * blockDim.x;
+            if (v < nv) t[i] = __ldcg(reinterpret_cast<const uint4*>(g) + v);
+        }
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int v = threadIdx.x + i * blockDim.x;
+            if (v < nv) reinterpret_cast<uint4*>(sm)[v] = t[i];
+        }
+        return;
+    }
+    int16_t t[kPer];
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+        const int c = threadIdx.x + i * blockDim.x;
+        t[i] = c < n ? __ldcg(g + c) : (int16_t)0;
+    }
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+        const int c = threadIdx.x + i * blockDim.x;
+        if (c < n) sm[c] = t[i];
+    }
+}
+
+// This thread's elements c = threadIdx.x + i*blockDim.x of a float vector,
+// loaded into registers (the per-layer norm weights, prefetched early).
+__device__ __forceinline__ void load_f32_regs(const float* __restrict__ g, int n, float (&r)[kPer]) {
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+        const int c = threadIdx.x + i * blockDim.x;
+        r[i] = c < n ? __ldg(g + c) : 0.0f;
+    }
+}
+
+// matvec_s scaling exponent of a q16 vector (gpu_conv.cpp:271-287):
+// max|x| = f*2^e with f in [0.5, 1) gives k = 6 - e.
+__device__ int scale_exponent(const int16_t* v, int n, Red& r) {
+    int mx = 0;
+    for (int c = threadIdx.x; c < n; c += blockDim.x) mx = max(mx, abs((int)v[c]));
+    mx = block_max_i32(mx, r);
+    if (mx == 0) return 0;
+    int e = 0;
+    frexpf(__fmul_rn((float)mx, 1.0f / 256.0f), &e);
+    return 6 - e;
+}
+
+// Stage one input: x'[c] = v[c]*2^k (k >= 0: exact shift; k < 0: x_pack's
+// round-half-even), zero-padded to `stride`; q4 group sums by warp shuffles
+// (a warp covers one 32-column group per iteration), the t3 total by a block
+// reduction.  v is in shared memory.  Ends with a barrier.
+template <int WT>
+__device__ void stage_one(XStage& xs, int b, const int16_t* v, int n, int k, Red& r) {
+    uint8_t* lo = xs.lo + (size_t)b * xs.stride;
+    int8_t* hi = xs.hi + (size_t)b * xs.stride;
+    const float sk = ldexpf(1.0f, k);
+    int tot = 0;
+    for (int c = threadIdx.x; c < xs.stride; c += blockDim.x) {
+        int q = 0;
+        if (c < n) {
+            const int a = v[c];
+            q = k >= 0 ? (a << k) : __float2int_rn(__fmul_rn((float)a, sk));
+        }
+        lo[c] = (uint8_t)(q & 0xFF);
+        hi[c] = (int8_t)(q >> 8);
+        if (WT == W_Q4) {
+            int g = q;
+            for (int o = 16; o; o >>= 1) g += __shfl_xor_sync(0xffffffffu, g, o);
+            if ((threadIdx.x & 31) == 0) xs.gsum[b * xs.gstride + (c >> 5)] = g;
+        }
+        tot += q;
+    }
+    if (WT == W_T3) {
+        const long long t = block_sum_i64(tot, r);
+        if (threadIdx.x == 0) xs.gsum[b * xs.gstride] = (int)t;
+    }
+    __syncthreads();
+}
+
+// RMSNorm of a q16 vector into q16 ints (session.cpp:1932-1948 with the exact
+// integer sum of squares rounded once).  x and out are shared memory; w holds
+// this thread's norm weights (load_f32_regs).
+__device__ void rmsnorm_q16(const int16_t* x, const float (&w)[kPer], int D, float eps, int16_t* out, Red& r) {
+    long long ss = 0;
+    for (int c = threadIdx.x; c < D; c += blockDim.x) { const long long a = x[c]; ss += a * a; }
+    ss = block_sum_i64(ss, r);
+    const float s1 = __fmul_rn(__ll2float_rn(ss), 1.0f / 65536.0f);
+    const float s2 = __fdiv_rn(s1, (float)D);
+    const float rr = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(s2, eps)));
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+        const int c = threadIdx.x + i * blockDim.x;
+        if (c < D) {
+            const float xv = __fmul_rn((float)x[c], 1.0f / 256.0f);
+            out[c] = (int16_t)q16h(__fmul_rn(w[i], __fmul_rn(rr, xv)));
+        }
+    }
+    __syncthreads();
+}
+
+// ---------------------------------------------------------------------------
+// Matvec core: one 32-row block of one matrix over nb staged inputs.
+// Warp w owns chunks w, w+8, w+16, ...; each lane owns one row.  The chunks a
+// warp needs are loaded into registers first (mv_prefetch), before the kernel
+// waits on its predecessor, so the DRAM latency of the weights overlaps the
+// previous kernel; mv_compute then returns the warp's exact partial sums.
+// ---------------------------------------------------------------------------
+
+// Programmatic dependent launch: let the next kernel start its weight
+// prefetch now; wait for the previous kernel's results before touching them.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+__device__ __forceinline__ int4 ld_weights(const int4* p) {
+    int4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.s32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+
+
+// ---------------------------------------------------------------------------
+// Bulk copies (cp.async.bulk, the 1-D TMA) into shared memory, completed on
+// mbarriers.  Waits are bounded by the global timer.
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ unsigned smem_addr(const void* p) { return (unsigned)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void mbar_init(unsigned long long* bar, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+// Makes mbarrier initialisation visible to the asynchronous (bulk-copy) proxy.
+__device__ __forceinline__ void mbar_fence_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void mbar_expect_tx(unsigned long long* bar, unsigned bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+// Orders this thread's earlier generic-proxy shared-memory accesses before
+// later bulk copies into the same memory.
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// global -> shared, `bytes` a multiple of 16, both addresses 16-byte aligned.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, unsigned long long* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(unsigned long long* bar, unsigned parity) {
+    unsigned ok;
+    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+                 : "=r"(ok) : "r"(smem_addr(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
+// Waits for phase `parity` of `bar`; false if it has not completed within
+// `limit_ns` (the caller then reports an error instead of waiting for ever).
+__device__ __forceinline__ bool mbar_wait(unsigned long long* bar, unsigned parity,
+                                          unsigned long long limit_ns = 100000000ull) {
+    if (mbar_try(bar, parity)) return true;
+    const unsigned long long t0 = global_ns();
+    while (!mbar_try(bar, parity))
+        if (global_ns() - t0 > limit_ns) return false;
+    return true;
+}
+
+// Error word values besides shared-memory shortfalls (which record the bytes needed).
+constexpr int kErrCopyTimeout = -2;
+constexpr int kStreamStages = 4;   // ring depth of the streaming kernels
+
+template <int MAXC>
+struct WRegs {
+    int4 w[MAXC];
+    int sp[MAXC];   // q4: packed (s16 | m16 << 16) of the chunk's scale group
+    float rs;       // the epilogue scale of this lane's row
+};
+
+template <int WT, int MAXC>
+__device__ __forceinline__ void mv_prefetch(const DMat& W, int blk, WRegs<MAXC>& R) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nch = W.nchunks;
+    const int4* body = reinterpret_cast<const int4*>(W.body) + (size_t)blk * nch * 32 + lane;
+#pragma unroll
+    for (int k = 0; k < MAXC; ++k) {
+        const int j = warp + k * kWarps;
+        if (j < nch) {
+            R.w[k] = ld_weights(body + (size_t)j * 32);
+            if (WT == W_Q4) R.sp[k] = __ldg(W.q4p + ((size_t)blk * nch + j) * 32 + lane);
+        }
+    }
+    R.rs = __ldg(W.rscale + (size_t)blk * 32 + lane);
+}
+
+// OWN: the staged input holds only this warp's chunks, slot k for chunk j.
+template <int WT, int NB, int MAXC, bool OWN = false>
+__device__ __forceinline__ void mv_compute(const DMat& W, const WRegs<MAXC>& R, const XStage& xs, int nb,
+                                           long long (&S)[NB]) {
+    const int warp = threadIdx.x >> 5, nch = W.nchunks;
+    int alo[NB], ahi[NB];
+#pragma unroll
+    for (int b = 0; b < NB; ++b) { alo[b] = 0; ahi[b] = 0; S[b] = 0; }
+#pragma unroll
+    for (int k = 0; k < MAXC; ++k) {
+        const int j = warp + k * kWarps;
+        if (j >= nch) break;
+        const int4 w = R.w[k];
+        const int xi = OWN ? k : j;   // staged chunk index
+        if (WT == W_Q8) {
+#pragma unroll
+            for (int b = 0; b < NB; ++b) {
+                if (b >= nb) break;
+                const uint4 L = *reinterpret_cast<const uint4*>(xs.lo + (size_t)b * xs.stride + xi * 16);
+                const uint4 H = *reinterpret_cast<const uint4*>(xs.hi + (size_t)b * xs.stride + xi * 16);
+                alo[b] = dp4a_su(w.x, L.x, alo[b]); alo[b] = dp4a_su(w.y, L.y, alo[b]);
+                alo[b] = dp4a_su(w.z, L.z, alo[b]); alo[b] = dp4a_su(w.w, L.w, alo[b]);
+                ahi[b] = dp4a_ss(w.x, (int)H.x, ahi[b]); ahi[b] = dp4a_ss(w.y, (int)H.y, ahi[b]);
+                ahi[b] = dp4a_ss(w.z, (int)H.z, ahi[b]); ahi[b] = dp4a_ss(w.w, (int)H.w, ahi[b]);
+            }
+        } else if (WT == W_T3) {
+            const unsigned wd[4] = {(unsigned)w.x, (unsigned)w.y, (unsigned)w.z, (unsigned)w.w};
+#pragma unroll
+            for (int b = 0; b < NB; ++b) {
+                if (b >= nb) break;
+                const uint4* L4 = reinterpret_cast<const uint4*>(xs.lo + (size_t)b * xs.stride + xi * 64);
+                const uint4* H4 = reinterpret_cast<const uint4*>(xs.hi + (size_t)b * xs.stride + xi * 64);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const uint4 L = L4[q], H = H4[q];
+                    const unsigned e0 = wd[q] & 0x03030303u, e1 = (wd[q] >> 2) & 0x03030303u;
+                    const unsigned e2 = (wd[q] >> 4) & 0x03030303u, e3 = (wd[q] >> 6) & 0x03030303u;
+                    alo[b] = dp4a_uu(e0, L.x, alo[b]); alo[b] = dp4a_uu(e1, L.y, alo[b]);
+                    alo[b] = dp4a_uu(e2, L.z, alo[b]); alo[b] = dp4a_uu(e3, L.w, alo[b]);
+                    ahi[b] = dp4a_us(e0, (int)H.x, ahi[b]); ahi[b] = dp4a_us(e1, (int)H.y, ahi[b]);
+                    ahi[b] = dp4a_us(e2, (int)H.z, ahi[b]); ahi[b] = dp4a_us(e3, (int)H.w, ahi[b]);
+                }
+            }
+        } else {  // W_Q4: chunk j is scale group j
+            const long long s16 = (short)(R.sp[k] & 0xFFFF), m16 = (short)(R.sp[k] >> 16);
+            const unsigned wd[4] = {(unsigned)w.x, (unsigned)w.y, (unsigned)w.z, (unsigned)w.w};
+#pragma unroll
+            for (int b = 0; b < NB; ++b) {
+                if (b >= nb) break;
+                const uint4* L4 = reinterpret_cast<const uint4*>(xs.lo + (size_t)b * xs.stride + xi * 32);
+                const uint4* H4 = reinterpret_cast<const uint4*>(xs.hi + (size_t)b * xs.stride + xi * 32);
+                const uint4 L0 = L4[0], L1 = L4[1], H0 = H4[0], H1 = H4[1];
+                const unsigned l[8] = {L0.x, L0.y, L0.z, L0.w, L1.x, L1.y, L1.z, L1.w};
+                const unsigned h[8] = {H0.x, H0.y, H0.z, H0.w, H1.x, H1.y, H1.z, H1.w};
+                int nlo = 0, nhi = 0;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const unsigned n0 = wd[q] & 0x0F0F0F0Fu, n1 = (wd[q] >> 4) & 0x0F0F0F0Fu;
+                    nlo = dp4a_uu(n0, l[2 * q], nlo); nlo = dp4a_uu(n1, l[2 * q + 1], nlo);
+                    nhi = dp4a_us(n0, (int)h[2 * q], nhi); nhi = dp4a_us(n1, (int)h[2 * q + 1], nhi);
+                }
+                const long long N = (long long)nlo + 256LL * nhi;
+                S[b] += s16 * N + m16 * (long long)xs.gsum[b * xs.gstride + xi];
+            }
+        }
+    }
+    if (WT != W_Q4) {
+#pragma unroll
+        for (int b = 0; b < NB; ++b) S[b] = (long long)alo[b] + 256LL * (long long)ahi[b];
+    }
+}
+
+// Cross-warp sum of the per-warp partials: on return every thread with
+// warp index b < nb holds the full sum of row (lane) for input b.
+template <int NB>
+__device__ __forceinline__ long long reduce_warps(const long long (&S)[NB], int nb, long long* red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int b = 0; b < NB; ++b) red[(warp * NB + b) * 32 + lane] = S[b];
+    __syncthreads();
+    long long t = 0;
+    if (warp < nb)
+        for (int w = 0; w < kWarps; ++w) t += red[(w * NB + warp) * 32 + lane];
+    __syncthreads();
+    return t;
+}
+
+struct SmemLayout {
+    static __device__ char* base() { extern __shared__ __align__(16) char smem[]; return smem; }
+};
+
+// Self-check before any shared-memory use: the launch must have reserved at
+// least `need` bytes of dynamic shared memory.  A short launch records the
+// shortfall in the session's error word and the block returns without
+// touching shared memory (the host turns the word into an error).
+__device__ __forceinline__ bool smem_ok(size_t need, int* err) {
+    unsigned have;
+    asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(have));
+    if ((size_t)have >= need) return true;
+    if (threadIdx.x == 0) atomicMax(err, (int)need);
+    return false;
+}
+
+// dynamic shared memory: [Red][partials kWarps*NB*32][gsum][lo][hi][scratch]
+template <int NB>
+__device__ void carve(int stride, int gstride, XStage& xs, Red*& red, long long*& part, int16_t*& tmp) {
+    char* p = SmemLayout::base();
+    red = reinterpret_cast<Red*>(p); p += (sizeof(Red) + 15) / 16 * 16;
+    part = reinterpret_cast<long long*>(p); p += sizeof(long long) * kWarps * NB * 32;
+    xs.gsum = reinterpret_cast<int*>(p); p += (sizeof(int) * NB * gstride + 15) / 16 * 16;
+    xs.lo = reinterpret_cast<uint8_t*>(p); p += (size_t)NB * stride;
+    xs.hi = reinterpret_cast<int8_t*>(p); p += (size_t)NB * stride;
+    tmp = reinterpret_cast<int16_t*>(p);
+    xs.stride = stride; xs.gstride = gstride;
+}
+
+__host__ __device__ size_t smem_bytes(int nb, int stride, int gstride, int tmp_n) {
+    return (sizeof(Red) + 15) / 16 * 16 + sizeof(long long) * kWarps * nb * 32 +
+           (sizeof(int) * nb * gstride + 15) / 16 * 16 + 2 * (size_t)nb * stride + sizeof(int16_t) * (size_t)tmp_n;
+}
+
+__host__ __device__ inline int cpc_of(int wt) { return wt == W_Q8 ? 16 : wt == W_Q4 ? 32 : 64; }
+__host__ __device__ inline int x_stride(const DMat& W) { return W.nchunks * cpc_of(W.wtype); }
+__host__ __device__ inline int g_stride(const DMat& W) { return W.wtype == W_Q4 ? W.nchunks : 1; }
+
+// ---------------------------------------------------------------------------
+// Kernel parameter blocks
+// ---------------------------------------------------------------------------
+
+struct Dims {
+    int dim, kv_dim, heads, kv_heads, head_dim, layers, vocab, ffn, chunk, experts, seq, row_bytes, kv_bits;
+    int rope_half, qk_norm;
+    float eps;
+};
+
+Dims dims_of(const DModel& m, const State& s) {
+    Dims d;
+    d.dim = m.h.dim; d.kv_dim = m.h.kv_dim; d.heads = m.h.heads; d.kv_heads = m.h.kv_heads;
+    d.head_dim = m.h.head_dim; d.layers = m.h.layers; d.vocab = m.h.vocab; d.ffn = m.ffn_width;
+    d.chunk = m.ffn_chunk; d.experts = m.h.experts; d.seq = s.seq; d.row_bytes = s.row_bytes;
+    d.kv_bits = s.kv_bits; d.rope_half = m.h.rope_half; d.qk_norm = m.h.qk_norm; d.eps = m.h.rms_eps;
+    return d;
+}
+
+// ---------------------------------------------------------------------------
+// Per-pass activations are indexed by the batch position b; only the KV cache
+// is indexed by the sequence's slot.  Every kernel issues its weight, scale
+// and norm-weight loads before griddepcontrol.wait and needs one dependent
+// round trip for its activations afterwards.
+// ---------------------------------------------------------------------------
+
+// Two matrices a kernel reads by value, per expert for MoE (blockIdx.y).
+struct MatSet {
+    DMat a[8];
+    DMat b[8];
+    DMat router;
+};
+
+// ---------------------------------------------------------------------------
+// Warp-staged matvec kernels.  Warp w of a CTA computes the dot products of
+// the column chunks j = w, w + kWarps, ... (its slots k = 0, 1, ...), so it
+// only reads the input bytes of those chunks.  Every warp prepares them
+// itself from the whole input vector in shared memory: the RMSNorm sum of
+// squares, the power-of-two input scale (from the maximum over all columns)
+// and the t3 column total are warp reductions, identical in every warp, and
+// the bytes of x' = x*2^k for the warp's own chunks go to its own slice.  A
+// kernel therefore has two block barriers: after its inputs land in shared
+// memory, and for the cross-warp sum of the dot products.
+// ---------------------------------------------------------------------------
+
+struct WStage {     // one warp's slice of staged input bytes
+    uint8_t* lo;    // [nb][wst]
+    int8_t* hi;     // [nb][wst]
+    int* gsum;      // q4: [nb][gst] chunk sums; t3: [nb] totals (gsum[b*gst])
+    int wst, gst;
+};
+
+__host__ __device__ inline int own_slots(int nch) { return (nch + kWarps - 1) / kWarps; }
+__host__ __device__ inline size_t wstage_bytes(const DMat& W, int nb) {
+    const int own = own_slots(W.nchunks), cpc = cpc_of(W.wtype), gst = W.wtype == W_Q4 ? own : 1;
+    return align16((size_t)2 * nb * own * cpc) + align16(sizeof(int) * (size_t)nb * gst);
+}
+__device__ __forceinline__ WStage wstage_at(const DMat& W, int nb, char* base) {
+    WStage w;
+    const int own = own_slots(W.nchunks);
+    char* p = base + (size_t)(threadIdx.x >> 5) * wstage_bytes(W, nb);
+    w.wst = own * cpc_of(W.wtype);
+    w.gst = W.wtype == W_Q4 ? own : 1;
+    w.lo = reinterpret_cast<uint8_t*>(p);
+    w.hi = reinterpret_cast<int8_t*>(p + (size_t)nb * w.wst);
+    w.gsum = reinterpret_cast<int*>(p + align16((size_t)2 * nb * w.wst));
+    return w;
+}
+__device__ __forceinline__ XStage xstage_of(const WStage& w) {
+    XStage x;
+    x.lo = w.lo; x.hi = w.hi; x.stride = w.wst; x.gsum = w.gsum; x.gstride = w.gst;
+    return x;
+}
+
+// Dynamic shared memory of the warp-staged kernels.
+struct MvLayout {
+    size_t part, x, nw, ws, extra, total;
+};
+__host__ __device__ inline MvLayout mv_layout(size_t ws_per_warp, int nb, int nvals, int nnw, size_t extra) {
+    MvLayout L;
+    size_t o = 0;
+    L.part = o;  o = align16(o + sizeof(long long) * 2 * kWarps * (size_t)nb * 32);
+    L.x = o;     o = align16(o + sizeof(int16_t) * (size_t)nvals);
+    L.nw = o;    o = align16(o + sizeof(float) * (size_t)nnw);
+    L.ws = o;    o = align16(o + kWarps * ws_per_warp);
+    L.extra = o; o = align16(o + extra);
+    L.total = o;
+    return L;
+}
+
+__device__ __forceinline__ long long warp_sum_i64(long long v) {
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+// matvec_s input scale: k = 6 - e for max|x| = f*2^e (gpu_conv.cpp:271-287), 0 for a zero vector.
+__device__ __forceinline__ int exp_from_max(int mx) {
+    if (mx == 0) return 0;
+    int e = 0;
+    frexpf(__fmul_rn((float)mx, 1.0f / 256.0f), &e);
+    return 6 - e;
+}
+// 1/sqrt(mean(x^2) + eps) of a q16 vector from its exact integer sum of squares
+// (session.cpp:1932-1948, the sum rounded once).
+__device__ __forceinline__ float rms_rr(long long ss, int D, float eps) {
+    const float s1 = __fmul_rn(__ll2float_rn(ss), 1.0f / 65536.0f);
+    const float s2 = __fdiv_rn(s1, (float)D);
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(s2, eps)));
+}
+__device__ __forceinline__ int xnorm(int a, float w, float rr) {
+    return q16h(__fmul_rn(w, __fmul_rn(rr, __fmul_rn((float)a, 1.0f / 256.0f))));
+}
+__device__ __forceinline__ int xscale(int a, int k, float sk) {
+    return k >= 0 ? (a << k) : __float2int_rn(__fmul_rn((float)a, sk));
+}
+__device__ __forceinline__ long long warp_sumsq(const int16_t* x, int D) {
+    long long ss = 0;
+    for (int c = (threadIdx.x & 31); c < D; c += 32) { const int a = x[c]; ss += a * a; }
+    return warp_sum_i64(ss);
+}
+
+// x'[c] = value(c)*2^k into the warp's slice for the columns of its own
+// chunks (zero past D); q4: the sum of each chunk; t3: the total over all D
+// columns.  Ends with the slice written by this warp (caller: __syncwarp).
+template <int WT, typename F>
+__device__ __forceinline__ void warp_stage(const WStage& ws, int b, int nch, int D, int k, F value) {
+    constexpr int cpc = WT == W_Q8 ? 16 : WT == W_Q4 ? 32 : 64;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const float sk = ldexpf(1.0f, k);
+    uint8_t* lo = ws.lo + (size_t)b * ws.wst;
+    int8_t* hi = ws.hi + (size_t)b * ws.wst;
+    for (int e = lane; e < ws.wst; e += 32) {
+        const int slot = e / cpc, j = warp + slot * kWarps, c = j * cpc + e % cpc;
+        const int q = (j < nch && c < D) ? xscale(value(c), k, sk) : 0;
+        lo[e] = (uint8_t)(q & 0xFF);
+        hi[e] = (int8_t)(q >> 8);
+        if (WT == W_Q4) {   // wst is a multiple of 32: every lane is here, one chunk per pass
+            const int gs = __reduce_add_sync(0xffffffffu, q);
+            if (lane == 0) ws.gsum[b * ws.gst + slot] = gs;
+        }
+    }
+    if (WT == W_T3) {
+        int t = 0;
+        for (int c = lane; c < D; c += 32) t += xscale(value(c), k, sk);
+        t = __reduce_add_sync(0xffffffffu, t);
+        if (lane == 0) ws.gsum[b * ws.gst] = t;
+    }
+}
+
+// Cross-warp sum of V partial dot products per (input, row) with one block
+// barrier; on return warps b < nb hold the totals of input b, row `lane`.
+// The partial buffer is not reused afterwards.
+template <int NB, int V>
+__device__ __forceinline__ void reduce_once(const long long (&S)[V][NB], int nb, long long* red,
+                                            long long (&out)[V]) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int v = 0; v < V; ++v)
+#pragma unroll
+        for (int b = 0; b < NB; ++b) red[((warp * V + v) * NB + b) * 32 + lane] = S[v][b];
+    __syncthreads();
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+        long long t = 0;
+        if (warp < nb)
+            for (int w = 0; w < kWarps; ++w) t += red[((w * V + v) * NB + warp) * 32 + lane];
+        out[v] = t;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// qkv: embedding (layer 0) or x, RMSNorm, matvec_s(qkv) -> fp32 qkv
+// ---------------------------------------------------------------------------
+
+template <int WT, int NB, int MAXC>
+__global__ void __launch_bounds__(kThreads) k_qkv(DMat W, DMat E, const float* emb_scale, const float* rms_w,
+                                                  State s, Batch bt, Dims d, int layer, int b0) {
+    const MvLayout L = mv_layout(wstage_bytes(W, NB), NB, NB * d.dim, d.dim, 0);
+    if (!smem_ok(L.total, s.err)) return;
+    char* sm = SmemLayout::base();
+    WRegs<MAXC> R;
+    mv_prefetch<WT, MAXC>(W, blockIdx.x, R);
+    float* nws = reinterpret_cast<float*>(sm + L.nw);
+    for (int c = threadIdx.x; c < d.dim; c += kThreads) nws[c] = __ldg(rms_w + c);
+    pdl_launch_dependents();
+    pdl_wait();
+    int16_t* xv = reinterpret_cast<int16_t*>(sm + L.x);
+    const int nb = min(NB, bt.n - b0);
+    for (int b = 0; b < nb; ++b) {
+        const int bi = b0 + b;
+        int16_t* xin = xv + (size_t)b * d.dim;
+        if (layer == 0) {
+            // embedding (session.cpp:342-371): q16(level * row scale); the row
+            // is read from the blocked q8 layout of the embedding matrix.
+            const int tok = bt.token[bi];
+            const float es = emb_scale[tok];
+            const int8_t* eb = reinterpret_cast<const int8_t*>(E.body) + ((size_t)(tok / 32) * E.nchunks * 32 + (tok % 32)) * 16;
+            int16_t* x = s.x + (size_t)bi * d.dim;
+            for (int c = threadIdx.x; c < d.dim; c += kThreads) {
+                const int16_t q = (int16_t)q16h(__fmul_rn((float)eb[(size_t)(c / 16) * 512 + (c % 16)], es));
+                xin[c] = q;
+                if (blockIdx.x == 0) x[c] = q;
+            }
+            if (blockIdx.x == 0 && threadIdx.x == 0) s.best[bi] = 0ull;
+        } else {
+            load_vec(s.x + (size_t)bi * d.dim, d.dim, xin);
+        }
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const WStage ws = wstage_at(W, NB, sm + L.ws);
+    int kw = 0;   // input scale of input `warp` (its epilogue)
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+        if (b >= nb) break;
+        const int16_t* x = xv + (size_t)b * d.dim;
+        const float rr = rms_rr(warp_sumsq(x, d.dim), d.dim, d.eps);
+        int mx = 0;
+        for (int c = lane; c < d.dim; c += 32) mx = max(mx, abs(xnorm(x[c], nws[c], rr)));
+        const int k = exp_from_max(__reduce_max_sync(0xffffffffu, mx));
+        if (b == warp) kw = k;
+        warp_stage<WT>(ws, b, W.nchunks, d.dim, k, [&](int c) { return xnorm(x[c], nws[c], rr); });
+    }
+    __syncwarp();
+    long long S[1][NB], tot[1];
+    mv_compute<WT, NB, MAXC, true>(W, R, xstage_of(ws), nb, S[0]);
+    reduce_once<NB, 1>(S, nb, reinterpret_cast<long long*>(sm + L.part), tot);
+    if (warp < nb) {
+        const int row = blockIdx.x * 32 + lane;
+        if (row < W.rows) {
+            const long long St = WT == W_T3 ? tot[0] - ws.gsum[warp * ws.gst] : tot[0];
+            const int v = mv_epi(St, R.rs);
+            const float out = __fmul_rn(__fmul_rn((float)v, 1.0f / 256.0f), ldexpf(1.0f, -kw));
+            s.qkv[(size_t)(b0 + warp) * (d.dim + 2 * d.kv_dim) + row] = out;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// wo: matvec_s(wo, att) + add_q16 residual -> x1
+// ---------------------------------------------------------------------------
+
+template <int WT, int NB, int MAXC>
+__global__ void __launch_bounds__(kThreads) k_wo(DMat W, State s, Batch bt, Dims d, int b0) {
+    const MvLayout L = mv_layout(wstage_bytes(W, NB), NB, NB * d.dim, 0, 0);
+    if (!smem_ok(L.total, s.err)) return;
+    char* sm = SmemLayout::base();
+    WRegs<MAXC> R;
+    mv_prefetch<WT, MAXC>(W, blockIdx.x, R);
+    pdl_launch_dependents();
+    pdl_wait();
+    const int nb = min(NB, bt.n - b0);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row = blockIdx.x * 32 + lane;
+    // the residual this thread's epilogue adds, fetched with the inputs
+    const int xres = (warp < nb && row < W.rows) ? (int)__ldcg(s.x + (size_t)(b0 + warp) * d.dim + row) : 0;
+    int16_t* av = reinterpret_cast<int16_t*>(sm + L.x);
+    for (int b = 0; b < nb; ++b) load_vec(s.att + (size_t)(b0 + b) * d.dim, d.dim, av + (size_t)b * d.dim);
+    __syncthreads();
+    const WStage ws = wstage_at(W, NB, sm + L.ws);
+    int kw = 0;
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+        if (b >= nb) break;
+        const int16_t* a = av + (size_t)b * d.dim;
+        int mx = 0;
+        for (int c = lane; c < d.dim; c += 32) mx = max(mx, abs((int)a[c]));
+        const int k = exp_from_max(__reduce_max_sync(0xffffffffu, mx));
+        if (b == warp) kw = k;
+        warp_stage<WT>(ws, b, W.nchunks, d.dim, k, [&](int c) { return (int)a[c]; });
+    }
+    __syncwarp();
+    long long S[1][NB], tot[1];
+    mv_compute<WT, NB, MAXC, true>(W, R, xstage_of(ws), nb, S[0]);
+    reduce_once<NB, 1>(S, nb, reinterpret_cast<long long*>(sm + L.part), tot);
+    if (warp < nb && row < W.rows) {
+        const long long St = WT == W_T3 ? tot[0] - ws.gsum[warp * ws.gst] : tot[0];
+        const int v = mv_epi(St, R.rs);
+        const float wo = __fmul_rn(__fmul_rn((float)v, 1.0f / 256.0f), ldexpf(1.0f, -kw));
+        const float xr = __fmul_rn((float)xres, 1.0f / 256.0f);
+        s.x1[(size_t)(b0 + warp) * d.dim + row] = (int16_t)q16h(__fadd_rn(xr, wo));
+    }
+}
+
+// ---------------------------------------------------------------------------
+// gate: RMSNorm(x1), optional MoE routing (top-1, shaders.cpp:1216-1230 and
+// session.cpp:110-115), w1/w3 matvecs and SwiGLU (q16 pair rounding,
+// shaders.cpp:116-136) -> h (the GPU FFN path the CPU session draws)
+// ---------------------------------------------------------------------------
+
+template <int WT, int NB, int MAXC>
+__global__ void __launch_bounds__(kThreads) k_gate(MatSet M, const float* rms_w, State s, Batch bt, Dims d,
+                                                   int layer, int b0, int hs, int early) {
+    const int expert = blockIdx.y;
+    const DMat& W1 = M.a[expert];
+    const DMat& W3 = M.b[expert];
+    const size_t rbytes = d.experts ? sizeof(int16_t) * (size_t)d.experts * d.dim : 0;
+    const MvLayout L = mv_layout(wstage_bytes(W1, NB), NB, NB * d.dim, d.dim, rbytes + 64);
+    if (!smem_ok(L.total, s.err)) return;
+    char* sm = SmemLayout::base();
+    WRegs<MAXC> R1, R3;
+    if (early) {
+        mv_prefetch<WT, MAXC>(W1, blockIdx.x, R1);
+        mv_prefetch<WT, MAXC>(W3, blockIdx.x, R3);
+    }
+    float* nws = reinterpret_cast<float*>(sm + L.nw);
+    for (int c = threadIdx.x; c < d.dim; c += kThreads) nws[c] = __ldg(rms_w + c);
+    int16_t* rw = reinterpret_cast<int16_t*>(sm + L.extra);             // router rows
+    int* members = reinterpret_cast<int*>(sm + L.extra + align16(rbytes));
+    for (int i = threadIdx.x; i < d.experts * d.dim; i += kThreads) rw[i] = M.router.w16[i];
+    pdl_launch_dependents();
+    pdl_wait();
+    int16_t* xv = reinterpret_cast<int16_t*>(sm + L.x);
+    const int n_all = min(NB, bt.n - b0);
+    for (int b = 0; b < n_all; ++b) load_vec(s.x1 + (size_t)(b0 + b) * d.dim, d.dim, xv + (size_t)b * d.dim);
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const WStage ws = wstage_at(W1, NB, sm + L.ws);
+    int nb = 0;
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+        if (b >= n_all) break;
+        const int16_t* x = xv + (size_t)b * d.dim;
+        const float rr = rms_rr(warp_sumsq(x, d.dim), d.dim, d.eps);
+        if (d.experts) {
+            // router: matvec_s over the normalised input, first maximum wins
+            int mx = 0;
+            for (int c = lane; c < d.dim; c += 32) mx = max(mx, abs(xnorm(x[c], nws[c], rr)));
+            const int k = exp_from_max(__reduce_max_sync(0xffffffffu, mx));
+            const float sk = ldexpf(1.0f, k);
+            int best = 0;
+            float bestv = 0.0f;
+            for (int e = 0; e < d.experts; ++e) {
+                long long acc = 0;
+                for (int c = lane; c < d.dim; c += 32)
+                    acc += (long long)rw[(size_t)e * d.dim + c] * xscale(xnorm(x[c], nws[c], rr), k, sk);
+                const int v = mv_epi(warp_sum_i64(acc), M.router.rscale[e]);
+                const float gv = __fmul_rn(__fmul_rn((float)v, 1.0f / 256.0f), ldexpf(1.0f, -k));
+                if (e == 0 || gv > bestv) { best = e; bestv = gv; }
+            }
+            if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0)
+                s.route[(size_t)(b0 + b) * d.layers + layer] = best;
+            if (best != expert) continue;
+        }
+        if (threadIdx.x == 0) members[nb] = b;
+        warp_stage<WT>(ws, nb, W1.nchunks, d.dim, 0, [&](int c) { return xnorm(x[c], nws[c], rr); });
+        ++nb;
+    }
+    if (nb == 0) return;   // the same in every warp: no input routed to this expert
+    if (!early) {
+        mv_prefetch<WT, MAXC>(W1, blockIdx.x, R1);
+        mv_prefetch<WT, MAXC>(W3, blockIdx.x, R3);
+    }
+    __syncwarp();
+    long long S[2][NB], tot[2];
+    const XStage xs = xstage_of(ws);
+    mv_compute<WT, NB, MAXC, true>(W1, R1, xs, nb, S[0]);
+    mv_compute<WT, NB, MAXC, true>(W3, R3, xs, nb, S[1]);
+    reduce_once<NB, 2>(S, nb, reinterpret_cast<long long*>(sm + L.part), tot);
+    if (warp < nb) {
+        const int row = blockIdx.x * 32 + lane;
+        if (row < W1.rows) {
+            const int bi = b0 + members[warp];
+            const int corr = WT == W_T3 ? ws.gsum[warp * ws.gst] : 0;
+            const int g = mv_epi(tot[0] - corr, R1.rs);
+            const int u = mv_epi(tot[1] - corr, R3.rs);
+            float y = swiglu1(__fmul_rn((float)g, 1.0f / 256.0f), __fmul_rn((float)u, 1.0f / 256.0f));
+            if (hs > 0) y = __fmul_rn(y, ldexpf(1.0f, -hs));     // metadata key 15 store scale
+            s.h[(size_t)bi * d.ffn + row] = (int16_t)q16s(y);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// down: w2 (one or two column chunks) + residual -> x
+// ---------------------------------------------------------------------------
+
+template <int WT, int NB, int MAXC>
+__global__ void __launch_bounds__(kThreads) k_down(MatSet M, State s, Batch bt, Dims d, int layer, int b0, int early) {
+    const int expert = blockIdx.y;
+    const bool two = d.chunk < d.ffn;
+    const DMat& Wa = M.a[expert];
+    const DMat& Wb = M.b[expert];
+    const size_t wsa = wstage_bytes(Wa, NB), wsb = two ? wstage_bytes(Wb, NB) : 0;
+    const MvLayout L = mv_layout(wsa + wsb, NB, NB * d.ffn, 0, 64);
+    if (!smem_ok(L.total, s.err)) return;
+    char* sm = SmemLayout::base();
+    WRegs<MAXC> Ra, Rb;
+    if (early) {
+        mv_prefetch<WT, MAXC>(Wa, blockIdx.x, Ra);
+        if (two) mv_prefetch<WT, MAXC>(Wb, blockIdx.x, Rb);
+    }
+    pdl_launch_dependents();
+    pdl_wait();
+    int* members = reinterpret_cast<int*>(sm + L.extra);
+    int16_t* hv = reinterpret_cast<int16_t*>(sm + L.x);
+    const int n_all = min(NB, bt.n - b0);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row = blockIdx.x * 32 + lane;
+    int nb = 0;
+    for (int b = 0; b < n_all; ++b) {
+        if (d.experts && __ldcg(s.route + (size_t)(b0 + b) * d.layers + layer) != expert) continue;
+        if (threadIdx.x == 0) members[nb] = b;
+        load_vec(s.h + (size_t)(b0 + b) * d.ffn, d.ffn, hv + (size_t)nb * d.ffn);
+        ++nb;
+    }
+    __syncthreads();
+    if (nb == 0) return;
+    const int xres = (warp < nb && row < Wa.rows) ? (int)__ldcg(s.x1 + (size_t)(b0 + members[warp]) * d.dim + row) : 0;
+    char* wbase = sm + L.ws;
+    const WStage xa = wstage_at(Wa, NB, wbase);
+    WStage xb = xa;
+    if (two) {
+        // the second chunk's slices follow all first-chunk slices
+        xb = wstage_at(Wb, NB, wbase + kWarps * wsa);
+    }
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+        if (b >= nb) break;
+        const int16_t* h = hv + (size_t)b * d.ffn;
+        warp_stage<WT>(xa, b, Wa.nchunks, d.chunk, 0, [&](int c) { return (int)h[c]; });
+        if (two) warp_stage<WT>(xb, b, Wb.nchunks, d.ffn - d.chunk, 0, [&](int c) { return (int)h[d.chunk + c]; });
+    }
+    if (!early) {
+        mv_prefetch<WT, MAXC>(Wa, blockIdx.x, Ra);
+        if (two) mv_prefetch<WT, MAXC>(Wb, blockIdx.x, Rb);
+    }
+    __syncwarp();
+    long long S[2][NB], tot[2];
+    mv_compute<WT, NB, MAXC, true>(Wa, Ra, xstage_of(xa), nb, S[0]);
+    if (two) {
+        mv_compute<WT, NB, MAXC, true>(Wb, Rb, xstage_of(xb), nb, S[1]);
+    } else {
+#pragma unroll
+        for (int b = 0; b < NB; ++b) S[1][b] = 0;
+    }
+    reduce_once<NB, 2>(S, nb, reinterpret_cast<long long*>(sm + L.part), tot);
+    if (warp < nb && row < Wa.rows) {
+        const int bi = b0 + members[warp];
+        const int va = mv_epi(WT == W_T3 ? tot[0] - xa.gsum[warp * xa.gst] : tot[0], Ra.rs);
+        float o2 = __fmul_rn((float)va, 1.0f / 256.0f);
+        if (two) {
+            const int vb = mv_epi(WT == W_T3 ? tot[1] - xb.gsum[warp * xb.gst] : tot[1], Rb.rs);
+            // add_q16 of the two chunk outputs (session.cpp:2052-2067)
+            o2 = __fmul_rn((float)q16h(__fadd_rn(o2, __fmul_rn((float)vb, 1.0f / 256.0f))), 1.0f / 256.0f);
+        }
+        const float x1 = __fmul_rn((float)xres, 1.0f / 256.0f);
+        s.x[(size_t)bi * d.dim + row] = (int16_t)q16h(__fadd_rn(x1, o2));
+    }
+}
+
+// ---------------------------------------------------------------------------
+// logits: RMSNorm(x) + logits matvec + first-max argmax; the last CTA of the
+// launch turns the packed keys into greedy tokens (and advances the sequences)
+// ---------------------------------------------------------------------------
+
+struct Finalize {
+    int* next;          // greedy token per batch position
+    int* tokens;        // advance: becomes the greedy (or forced) token
+    int* pos;           // advance: + 1
+    const int* forced;  // prefill: token at each position
+    int advance;
+};
+
+// Logits and the greedy token.  The greedy token is the first maximum
+// (sampling.cpp:160-162), found by a packed-key atomicMax over all rows; the
+// last CTA to finish writes the next token (and advances position and token
+// for the device-resident decode loop).  Two kernels share that tail:
+//  - k_logits: one CTA per 32-row block, the columns split over the warps,
+//    for heads of up to a few hundred blocks (latency: every SM busy at once);
+//  - k_logits_wide: one warp per 32-row block (lanes are rows, each warp walks
+//    all column chunks, no cross-warp reduction), grid-stride over the blocks,
+//    several CTAs per SM, for heads of thousands of blocks (HBM streaming).
+__device__ __forceinline__ unsigned long long logit_key(int v, int row) {
+    return ((unsigned long long)(unsigned)(v + 32768) << 32) | (unsigned)(0xFFFFFFFFu - (unsigned)row);
+}
+
+__device__ __forceinline__ void logits_finish(State& s, int b0, int nb, const Finalize& fz) {
+    __shared__ int last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        last = atomicAdd(s.done, 1) == (int)(gridDim.x * gridDim.y) - 1;
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    if (threadIdx.x < nb) {
+        const int bi = b0 + threadIdx.x;
+        const unsigned long long key = __ldcg(&s.best[bi]);
+        const int tok = (int)(0xFFFFFFFFu - (unsigned)(key & 0xFFFFFFFFull));
+        fz.next[bi] = tok;
+        if (fz.advance) {
+            const int p = fz.pos[bi] + 1;
+            fz.tokens[bi] = fz.forced ? fz.forced[p < s.seq ? p : s.seq - 1] : tok;
+            fz.pos[bi] = p;
+        }
+    }
+    if (threadIdx.x == 0) *s.done = 0;
+}
+
+template <int NB>
+__device__ __forceinline__ void logits_stage_inputs(const DMat& W, const float (&nw)[kPer], State& s, const Dims& d,
+                                                    int b0, int nb, XStage& xs, Red*& red, int16_t*& tmp) {
+    long long* part;
+    carve<NB>(x_stride(W), g_stride(W), xs, red, part, tmp);
+    for (int b = 0; b < nb; ++b) load_vec(s.x + (size_t)(b0 + b) * d.dim, d.dim, tmp + (size_t)b * d.dim);
+    __syncthreads();
+    for (int b = 0; b < nb; ++b) {
+        int16_t* xin = tmp + (size_t)b * d.dim;
+        rmsnorm_q16(xin, nw, d.dim, d.eps, xin, *red);
+        xs.k[b] = 0;
+        stage_one<W_Q8>(xs, b, xin, d.dim, 0, *red);
+    }
+}
+
+template <int NB, int MAXC>
+__global__ void __launch_bounds__(kThreads) k_logits(DMat W, const float* rms_w, State s, Batch bt, Dims d, int b0,
+                                                     Finalize fz) {
+    const MvLayout L = mv_layout(wstage_bytes(W, NB), NB, NB * d.dim, d.dim, 0);
+    if (!smem_ok(L.total, s.err)) return;
+    char* sm = SmemLayout::base();
+    WRegs<MAXC> R;
+    mv_prefetch<W_Q8, MAXC>(W, blockIdx.x, R);
+    float* nws = reinterpret_cast<float*>(sm + L.nw);
+    for (int c = threadIdx.x; c < d.dim; c += kThreads) nws[c] = __ldg(rms_w + c);
+    pdl_launch_dependents();
+    pdl_wait();
+    int16_t* xv = reinterpret_cast<int16_t*>(sm + L.x);
+    const int nb = min(NB, bt.n - b0);
+    for (int b = 0; b < nb; ++b) load_vec(s.x + (size_t)(b0 + b) * d.dim, d.dim, xv + (size_t)b * d.dim);
+    __syncthreads();
+    const WStage ws = wstage_at(W, NB, sm + L.ws);
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+        if (b >= nb) break;
+        const int16_t* x = xv + (size_t)b * d.dim;
+        const float rr = rms_rr(warp_sumsq(x, d.dim), d.dim, d.eps);
+        warp_stage<W_Q8>(ws, b, W.nchunks, d.dim, 0, [&](int c) { return xnorm(x[c], nws[c], rr); });
+    }
+    __syncwarp();
+    long long S[1][NB], tot[1];
+    mv_compute<W_Q8, NB, MAXC, true>(W, R, xstage_of(ws), nb, S[0]);
+    reduce_once<NB, 1>(S, nb, reinterpret_cast<long long*>(sm + L.part), tot);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warp < nb) {
+        const int row = blockIdx.x * 32 + lane;
+        const int bi = b0 + warp;
+        unsigned long long key = 0ull;
+        if (row < W.rows) {
+            const int v = mv_epi(tot[0], R.rs);
+            s.logits[(size_t)bi * d.vocab + row] = v;
+            key = logit_key(v, row);
+        }
+        for (int o = 16; o; o >>= 1) {
+            const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, key, o);
+            key = k2 > key ? k2 : key;
+        }
+        if (lane == 0 && key) { atomicMax(&s.best[bi], key); __threadfence(); }
+    }
+    logits_finish(s, b0, nb, fz);
+}
+
+// One warp per 32-row block: lanes are rows, the warp walks every column
+// chunk of its blocks.  Each warp streams its weights through its own ring of
+// shared-memory stages filled by bulk copies (pieces of up to kWidePiece
+// 16-column chunks, 512 contiguous bytes per chunk), so the copies in flight
+// cost no registers; the first pieces are requested before the grid-dependency
+// wait.  Blocks are dealt to warps round-robin over the whole grid.
+constexpr int kWidePiece = 16;
+
+__host__ __device__ inline size_t wide_base(const DMat& W, int nb, int dim) {
+    return (smem_bytes(nb, x_stride(W), g_stride(W), nb * dim) + 127) & ~(size_t)127;
+}
+// Ring stages per warp that fit next to the input staging (0: none fit).
+__host__ __device__ inline int wide_stages(const DMat& W, int nb, int dim) {
+    const size_t base = wide_base(W, nb, dim);
+    if (base >= kMaxDynSmem) return 0;
+    const size_t per_warp = (kMaxDynSmem - base) / kWarps;
+    const size_t stage = (size_t)kWidePiece * 512 + 8;
+    const int st = (int)(per_warp / stage);
+    return st > 4 ? 4 : st;
+}
+__host__ __device__ inline size_t wide_smem(const DMat& W, int nb, int dim, int stages) {
+    return wide_base(W, nb, dim) + (size_t)kWarps * stages * ((size_t)kWidePiece * 512 + 8);
+}
+
+template <int NB>
+__global__ void __launch_bounds__(kThreads) k_logits_wide(DMat W, const float* rms_w, State s, Batch bt, Dims d,
+                                                         int b0, Finalize fz, int stages) {
+    if (!smem_ok(wide_smem(W, NB, d.dim, stages), s.err)) return;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nch = W.nchunks;
+    char* ring = SmemLayout::base() + wide_base(W, NB, d.dim) + (size_t)warp * stages * kWidePiece * 512;
+    unsigned long long* bar = reinterpret_cast<unsigned long long*>(
+        SmemLayout::base() + wide_base(W, NB, d.dim) + (size_t)kWarps * stages * kWidePiece * 512) + warp * stages;
+    const int ppb = (nch + kWidePiece - 1) / kWidePiece;             // pieces per block
+    const int stride = gridDim.x * kWarps;
+    const int first = blockIdx.x * kWarps + warp;
+    const int nblk = first < W.rblocks ? (W.rblocks - first + stride - 1) / stride : 0;
+    const int npieces = nblk * ppb;
+    auto issue = [&](int p) {
+        const int blk = first + (p / ppb) * stride, j0 = (p % ppb) * kWidePiece;
+        const unsigned bytes = (unsigned)min(kWidePiece, nch - j0) * 512u;
+        unsigned long long* b = &bar[p % stages];
+        mbar_expect_tx(b, bytes);
+        bulk_g2s(ring + (size_t)(p % stages) * kWidePiece * 512, W.body + ((size_t)blk * nch + j0) * 512, bytes, b);
+    };
+    if (lane == 0) {
+        for (int i = 0; i < stages; ++i) mbar_init(&bar[i], 1);
+        mbar_fence_init();
+        for (int p = 0; p < min(stages, npieces); ++p) issue(p);
+    }
+    float nw[kPer];
+    load_f32_regs(rms_w, d.dim, nw);
+    pdl_launch_dependents();
+    pdl_wait();
+    XStage xs; Red* red; int16_t* tmp;
+    const int nb = min(NB, bt.n - b0);
+    logits_stage_inputs<NB>(W, nw, s, d, b0, nb, xs, red, tmp);   // block-wide; publishes the mbarriers
+    unsigned long long best[NB];
+#pragma unroll
+    for (int b = 0; b < NB; ++b) best[b] = 0ull;
+    int alo[NB], ahi[NB];
+    float rs = 0.0f;
+    bool failed = false;
+    for (int p = 0; p < npieces; ++p) {
+        const int blk = first + (p / ppb) * stride, j0 = (p % ppb) * kWidePiece;
+        if (j0 == 0) {
+            rs = __ldg(W.rscale + (size_t)blk * 32 + lane);
+#pragma unroll
+            for (int b = 0; b < NB; ++b) { alo[b] = 0; ahi[b] = 0; }
+        }
+        if (!mbar_wait(&bar[p % stages], (unsigned)(p / stages) & 1u)) { failed = true; break; }
+        const int4* buf = reinterpret_cast<const int4*>(ring + (size_t)(p % stages) * kWidePiece * 512) + lane;
+        const int nu = min(kWidePiece, nch - j0);
+#pragma unroll 4
+        for (int u = 0; u < nu; ++u) {
+            const int4 w = buf[u * 32];
+            const int j = j0 + u;
+#pragma unroll
+            for (int b = 0; b < NB; ++b) {
+                if (b >= nb) break;
+                const uint4 L = *reinterpret_cast<const uint4*>(xs.lo + (size_t)b * xs.stride + j * 16);
+                const uint4 H = *reinterpret_cast<const uint4*>(xs.hi + (size_t)b * xs.stride + j * 16);
+                alo[b] = dp4a_su(w.x, L.x, alo[b]); alo[b] = dp4a_su(w.y, L.y, alo[b]);
+                alo[b] = dp4a_su(w.z, L.z, alo[b]); alo[b] = dp4a_su(w.w, L.w, alo[b]);
+                ahi[b] = dp4a_ss(w.x, (int)H.x, ahi[b]); ahi[b] = dp4a_ss(w.y, (int)H.y, ahi[b]);
+                ahi[b] = dp4a_ss(w.z, (int)H.z, ahi[b]); ahi[b] = dp4a_ss(w.w, (int)H.w, ahi[b]);
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && p + stages < npieces) {
+            fence_proxy_async();
+            issue(p + stages);
+        }
+        if (j0 + kWidePiece >= nch) {
+            const int row = blk * 32 + lane;
+#pragma unroll
+            for (int b = 0; b < NB; ++b) {
+                if (b >= nb || row >= W.rows) continue;
+                const int v = mv_epi((long long)alo[b] + 256LL * (long long)ahi[b], rs);
+                s.logits[(size_t)(b0 + b) * d.vocab + row] = v;
+                const unsigned long long key = logit_key(v, row);
+                best[b] = key > best[b] ? key : best[b];
+            }
+        }
+    }
+    if (failed) {
+        // a copy did not land in time: report it and wait (bounded) for this
+        // warp's copies still in flight before the shared memory is released
+        if (lane == 0) {
+            atomicExch(s.err, kErrCopyTimeout);
+            for (int p = 0; p < npieces; ++p) mbar_wait(&bar[p % stages], (unsigned)(p / stages) & 1u, 10000000ull);
+        }
+        __syncwarp();
+    }
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+        if (b >= nb) break;
+        unsigned long long kk = best[b];
+        for (int o = 16; o; o >>= 1) {
+            const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, kk, o);
+            kk = k2 > kk ? k2 : kk;
+        }
+        if (lane == 0 && kk) atomicMax(&s.best[b0 + b], kk);
+    }
+    logits_finish(s, b0, nb, fz);
+}
+
+#ifdef VC4_COMMON_TU
+// Attention for one (KV head, sequence) runs on group/hq clusters of kAttnCtas
+// CTAs, each cluster serving hq of the KV head's query heads, with a single
+// cluster barrier:
+//  - before the grid-dependency wait every CTA stages the cache rows it needs
+//    (cp.async) and decodes them to fp32 in shared memory: the K rows of its
+//    contiguous share of positions 0..pos, and a slice of V columns for every
+//    position;
+//  - after the wait each CTA rebuilds the normalised, rotated q heads and the
+//    new k (identical in every CTA), encodes the new cache row (written by the
+//    CTA whose share holds `pos`), computes the scores of its positions and
+//    stores them into every CTA of the cluster (distributed shared memory);
+//  - after the barrier each CTA holds all scores, runs the softmax for all
+//    positions itself (the same order in every CTA) and computes P.V for its
+//    own V columns, so no partial results cross CTAs.
+// The arithmetic is the reference's (session.cpp:1989-2050): sequential fp32
+// q.k per position, global max, exp(s - max), p = e / sum (the sum in double,
+// rounded once), out = sum p*v in double.
+constexpr int kAttnCtas = 8;
+
+__host__ __device__ inline int attn_vs(int hd) { return (((hd + kAttnCtas - 1) / kAttnCtas) + 3) & ~3; }
+__host__ __device__ inline int attn_rows(int seq) { return (seq + kAttnCtas - 1) / kAttnCtas; }
+
+struct AttnSmem {
+    uint8_t* kraw;   // attn_rows(seq) x hbytes: K rows of this CTA's positions (cache bytes)
+    uint8_t* vraw;   // seq x vs*kvb: this CTA's V columns of every position (cache bytes)
+    double* pv;      // max(kThreads, group*vs): P.V partials
+    double* redd;    // kWarps: softmax sums per warp
+    float* kt;       // attn_rows(seq) x (hd + 4): decoded K rows
+    float* vt;       // seq x vs: decoded V columns
+    float* q;        // (group + 1) x hd: q heads, then the new k
+    float* vn;       // hd: the new v
+    float* rc;       // hd/2: RoPE cos at pos
+    float* rsn;      // hd/2: RoPE sin at pos
+    float* wq;       // hd: q_norm weights of the layer
+    float* wk;       // hd: k_norm weights of the layer
+    float* redf;     // kWarps: softmax maxima per warp
+    float* sc;       // group x seq: scores, then probabilities (cluster-written)
+};
+
+__host__ __device__ inline size_t attn_carve(int group, int hd, int seq, int kv_bits, char* base, AttnSmem* sm) {
+    const int kvb = kv_bits / 8, vs = attn_vs(hd), rows = attn_rows(seq);
+    const int npv = group * vs > kThreads ? group * vs : kThreads;
+    size_t o = 0;
+    const size_t kraw = o; o = align16(o + (size_t)rows * hd * kvb);
+    const size_t vraw = o; o = align16(o + (size_t)seq * vs * kvb);
+    const size_t pv = o;   o = align16(o + sizeof(double) * npv);
+    const size_t redd = o; o = align16(o + sizeof(double) * kWarps);
+    const size_t kt = o;   o = align16(o + sizeof(float) * (size_t)rows * (hd + 4));
+    const size_t vt = o;   o = align16(o + sizeof(float) * (size_t)seq * vs);
+    const size_t q = o;    o = align16(o + sizeof(float) * (size_t)(group + 1) * hd);
+    const size_t vn = o;   o += sizeof(float) * hd;
+    const size_t rc = o;   o += sizeof(float) * (hd / 2);
+    const size_t rsn = o;  o += sizeof(float) * (hd / 2);
+    const size_t wq = o;   o += sizeof(float) * hd;
+    const size_t wk = o;   o += sizeof(float) * hd;
+    const size_t redf = o; o += sizeof(float) * kWarps;
+    const size_t sc = o;   o += sizeof(float) * (size_t)group * seq;
+    if (sm) {
+        sm->kraw = reinterpret_cast<uint8_t*>(base + kraw);
+        sm->vraw = reinterpret_cast<uint8_t*>(base + vraw);
+        sm->pv = reinterpret_cast<double*>(base + pv);
+        sm->redd = reinterpret_cast<double*>(base + redd);
+        sm->kt = reinterpret_cast<float*>(base + kt);
+        sm->vt = reinterpret_cast<float*>(base + vt);
+        sm->q = reinterpret_cast<float*>(base + q);
+        sm->vn = reinterpret_cast<float*>(base + vn);
+        sm->rc = reinterpret_cast<float*>(base + rc);
+        sm->rsn = reinterpret_cast<float*>(base + rsn);
+        sm->wq = reinterpret_cast<float*>(base + wq);
+        sm->wk = reinterpret_cast<float*>(base + wk);
+        sm->redf = reinterpret_cast<float*>(base + redf);
+        sm->sc = reinterpret_cast<float*>(base + sc);
+    }
+    return align16(o);
+}
+__host__ __device__ inline size_t attn_smem_bytes(int group, int hd, int seq, int kv_bits) {
+    return attn_carve(group, hd, seq, kv_bits, nullptr, nullptr);
+}
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(d), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// The values of one 32-bit word of a packed cache row: two q16 big-endian
+// values on the 1/2048 grid, or four q8 two's-complement values on the 1/16
+// grid (shaders_attn.cpp:141-159).  Returns the number of values.
+__device__ __forceinline__ int kv_word(unsigned w, int kvb, float* out) {
+    if (kvb == 2) {
+        out[0] = __fmul_rn((float)(short)(((w & 0xFFu) << 8) | ((w >> 8) & 0xFFu)), 1.0f / 2048.0f);
+        out[1] = __fmul_rn((float)(short)((((w >> 16) & 0xFFu) << 8) | (w >> 24)), 1.0f / 2048.0f);
+        return 2;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) out[j] = __fmul_rn((float)(signed char)((w >> (8 * j)) & 0xFFu), 1.0f / 16.0f);
+    return 4;
+}
+// The packed bytes of one value (the inverse of kv_word), as the low bits of a word.
+__device__ __forceinline__ unsigned kv_encode(float x, int kvb, float* dec) {
+    if (kvb == 2) {
+        float q = floorf(__fadd_rn(__fmul_rn(x, 2048.0f), 0.5f));
+        q = q < -32768.0f ? -32768.0f : q > 32767.0f ? 32767.0f : q;
+        *dec = __fmul_rn(q, 1.0f / 2048.0f);
+        const unsigned u = (unsigned)(int)q & 0xFFFFu;
+        return (u >> 8) | ((u & 0xFFu) << 8);           // big-endian byte order in memory
+    }
+    float q = floorf(__fadd_rn(__fmul_rn(x, 16.0f), 0.5f));
+    q = q < -128.0f ? -128.0f : q > 127.0f ? 127.0f : q;
+    *dec = __fmul_rn(q, 1.0f / 16.0f);
+    return (unsigned)(int)q & 0xFFu;
+}
+
+__global__ void __cluster_dims__(kAttnCtas, 1, 1) __launch_bounds__(kThreads)
+k_attn(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int layer, int hq) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    extern __shared__ __align__(16) char smem[];
+    const int hd = d.head_dim, group = d.heads / d.kv_heads, half = hd / 2, hp = hd + 4;
+    if (!smem_ok(attn_smem_bytes(hq, hd, d.seq, d.kv_bits), s.err)) return;
+    AttnSmem sm;
+    attn_carve(hq, hd, d.seq, d.kv_bits, smem, &sm);
+    const int rank = (int)cluster.block_rank();
+    // cluster (g, split) serves q heads split*hq .. split*hq + hq - 1 of KV head g
+    const int qsplit = group / hq, g = blockIdx.x / kAttnCtas / qsplit, split = blockIdx.x / kAttnCtas % qsplit;
+    const int h0 = split * hq, b = blockIdx.y;
+    const int slot = bt.slot[b], pos = bt.pos[b], len = pos + 1;
+    const int per = (len + kAttnCtas - 1) / kAttnCtas;
+    const int t0 = min(len, rank * per), t1 = min(len, t0 + per), nt = t1 - t0;
+    const int kvb = d.kv_bits / 8, hbytes = hd * kvb, vofs = d.kv_dim * kvb;
+    const int vs = attn_vs(hd), c0 = min(hd, rank * vs), c1 = min(hd, c0 + vs), nc = c1 - c0;
+    const int vrow = vs * kvb;                    // staged bytes per position of the V slice
+    const int vpw = 4 / kvb;                      // values per 32-bit word
+    uint8_t* kvbase = s.kv + ((size_t)slot * d.layers + layer) * d.seq * d.row_bytes;
+
+    // 1. stage and decode the cached rows (every position but `pos`, which
+    //    this step writes), the RoPE row and the norm weights
+    const int kvec = hbytes / 16;
+    for (int v = threadIdx.x; v < nt * kvec; v += kThreads) {
+        const int r = v / kvec, c = v % kvec, t = t0 + r;
+        if (t != pos) cp_async16(sm.kraw + r * hbytes + c * 16, kvbase + (size_t)t * d.row_bytes + g * hbytes + c * 16);
+    }
+    const int vw = nc * kvb / 4;                  // words per position of the V slice
+    for (int v = threadIdx.x; v < pos * vw; v += kThreads) {
+        const int t = v / vw, c = v % vw;
+        cp_async4(sm.vraw + (size_t)t * vrow + c * 4,
+                  kvbase + (size_t)t * d.row_bytes + vofs + g * hbytes + c0 * kvb + c * 4);
+    }
+    for (int i = threadIdx.x; i < half; i += kThreads) {
+        sm.rc[i] = s.rope_cos[(size_t)pos * half + i];
+        sm.rsn[i] = s.rope_sin[(size_t)pos * half + i];
+    }
+    if (d.qk_norm)
+        for (int i = threadIdx.x; i < hd; i += kThreads) {
+            sm.wq[i] = q_norm[(size_t)layer * hd + i];
+            sm.wk[i] = k_norm[(size_t)layer * hd + i];
+        }
+    cp_async_wait_all();
+    __syncthreads();
+    const int kw = hbytes / 4;
+    for (int v = threadIdx.x; v < nt * kw; v += kThreads) {
+        const int r = v / kw, c = v % kw;
+        if (t0 + r == pos) continue;
+        float f[4];
+        const int n = kv_word(reinterpret_cast<const unsigned*>(sm.kraw + r * hbytes)[c], kvb, f);
+        for (int j = 0; j < n; ++j) sm.kt[r * hp + c * n + j] = f[j];
+    }
+    for (int v = threadIdx.x; v < pos * vw; v += kThreads) {
+        const int t = v / vw, c = v % vw;
+        float f[4];
+        const int n = kv_word(reinterpret_cast<const unsigned*>(sm.vraw + (size_t)t * vrow)[c], kvb, f);
+        for (int j = 0; j < n; ++j) sm.vt[(size_t)t * vs + c * n + j] = f[j];
+    }
+    pdl_launch_dependents();
+    pdl_wait();
+
+    // 2. q heads, new k, new v from the qkv matvec; qk-norm (exact double sum
+    //    of squares) and RoPE, one warp per vector
+    const float* qkv = s.qkv + (size_t)b * (d.dim + 2 * d.kv_dim);
+    for (int i = threadIdx.x; i < hq * hd; i += kThreads) sm.q[i] = qkv[(g * group + h0) * hd + i];
+    for (int i = threadIdx.x; i < hd; i += kThreads) {
+        sm.q[hq * hd + i] = qkv[d.dim + g * hd + i];
+        sm.vn[i] = qkv[d.dim + d.kv_dim + g * hd + i];
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int hh = warp; hh <= hq; hh += kWarps) {
+        float* v = sm.q + hh * hd;
+        if (d.qk_norm) {
+            double acc = 0.0;
+            for (int i = lane; i < hd; i += 32) acc = __dadd_rn(acc, __dmul_rn((double)v[i], (double)v[i]));
+            for (int o = 16; o; o >>= 1) acc = __dadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+            const float ss = __double2float_rn(acc);
+            const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)hd), 1e-6f)));
+            const float* w = hh < hq ? sm.wq : sm.wk;
+            for (int i = lane; i < hd; i += 32) v[i] = __fmul_rn(w[i], __fmul_rn(r, v[i]));
+            __syncwarp();
+        }
+        for (int i = lane; i < half; i += 32) {
+            const int ia = d.rope_half ? i : 2 * i, ib = d.rope_half ? i + half : 2 * i + 1;
+            const float a = v[ia], bb = v[ib], c = sm.rc[i], sv = sm.rsn[i];
+            v[ia] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(bb, sv));
+            v[ib] = __fadd_rn(__fmul_rn(a, sv), __fmul_rn(bb, c));
+        }
+    }
+    __syncthreads();
+
+    // 3. encode the new row one 32-bit word at a time (shaders_attn.cpp:141-159);
+    //    every CTA encodes it identically, the one whose share holds `pos`
+    //    writes it to the cache (the first split of the KV head)
+    const bool owner = pos >= t0 && pos < t1;
+    const bool writer = owner && split == 0;
+    uint8_t* row = kvbase + (size_t)pos * d.row_bytes;
+    for (int e = threadIdx.x; e < 2 * kw; e += kThreads) {
+        const int w = e / kw, c = e % kw, i0 = c * vpw;
+        const float* src = w ? sm.vn : sm.q + hq * hd;
+        unsigned word = 0;
+        float dec[4];
+        for (int j = 0; j < vpw; ++j) word |= kv_encode(src[i0 + j], kvb, &dec[j]) << (8 * kvb * j);
+        if (writer) *reinterpret_cast<unsigned*>(row + (w ? vofs : 0) + g * hbytes + c * 4) = word;
+        for (int j = 0; j < vpw; ++j) {
+            const int i = i0 + j;
+            if (!w && owner) sm.kt[(pos - t0) * hp + i] = dec[j];
+            if (w && i >= c0 && i < c1) sm.vt[(size_t)pos * vs + i - c0] = dec[j];
+        }
+    }
+    __syncthreads();
+
+    // 4. scores of this CTA's positions: sequential fp32 dot, / sqrt(hd);
+    //    stored into every CTA of the cluster
+    const float sq = __fsqrt_rn((float)hd);
+    for (int e = threadIdx.x; e < nt * hq; e += kThreads) {
+        const int r = e / hq, hh = e % hq;
+        const float4* kr = reinterpret_cast<const float4*>(sm.kt + r * hp);
+        const float4* qh = reinterpret_cast<const float4*>(sm.q + hh * hd);
+        float acc = 0.0f;
+#pragma unroll 4
+        for (int i = 0; i < hd / 4; ++i) {
+            const float4 k4 = kr[i], q4 = qh[i];
+            acc = __fadd_rn(acc, __fmul_rn(q4.x, k4.x));
+            acc = __fadd_rn(acc, __fmul_rn(q4.y, k4.y));
+            acc = __fadd_rn(acc, __fmul_rn(q4.z, k4.z));
+            acc = __fadd_rn(acc, __fmul_rn(q4.w, k4.w));
+        }
+        acc = __fdiv_rn(acc, sq);
+        float* dst = sm.sc + hh * d.seq + t0 + r;
+#pragma unroll
+        for (int c = 0; c < kAttnCtas; ++c) *cluster.map_shared_rank(dst, c) = acc;
+    }
+    cluster.sync();   // the last access to another CTA's shared memory
+
+    // 5. softmax over all positions: kWarps / hq warps per head (one when
+    //    a cluster serves more heads than warps), reductions through shared
+    //    memory in warp order
+    {
+        const int wph = hq >= kWarps ? 1 : kWarps / hq;
+        const int hpr = kWarps / wph;             // heads per round
+        const int hw = warp / wph, sub = warp % wph, step = wph * 32;
+        for (int r0 = 0; r0 < hq; r0 += hpr) {
+            const int hh = r0 + hw;
+            const bool act = hw < hpr && hh < hq;
+            float* p = sm.sc + (act ? hh : 0) * d.seq;
+            float m = -1e30f;
+            if (act)
+                for (int t = sub * 32 + lane; t < len; t += step) m = fmaxf(m, p[t]);
+            for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            if (lane == 0) sm.redf[warp] = m;
+            __syncthreads();
+            double a = 0.0;
+            if (act) {
+                m = sm.redf[hw * wph];
+                for (int k = 1; k < wph; ++k) m = fmaxf(m, sm.redf[hw * wph + k]);
+#pragma unroll 4
+                for (int t = sub * 32 + lane; t < len; t += step) {
+                    const float ev = vexp(__fsub_rn(p[t], m));
+                    p[t] = ev;
+                    a = __dadd_rn(a, (double)ev);
+                }
+            }
+            for (int o = 16; o; o >>= 1) a = __dadd_rn(a, __shfl_xor_sync(0xffffffffu, a, o));
+            if (lane == 0) sm.redd[warp] = a;
+            __syncthreads();
+            if (act) {
+                double tot = sm.redd[hw * wph];
+                for (int k = 1; k < wph; ++k) tot = __dadd_rn(tot, sm.redd[hw * wph + k]);
+                const float fs = __double2float_rn(tot);
+#pragma unroll 4
+                for (int t = sub * 32 + lane; t < len; t += step) p[t] = __fdiv_rn(p[t], fs);
+            }
+        }
+    }
+    __syncthreads();
+
+    // 6. P.V for this CTA's V columns: each output's positions split into ks
+    //    contiguous ranges, partial sums in double combined in range order
+    const int nout = hq * nc;
+    if (nout == 0) return;
+    const int ks = nout >= kThreads ? 1 : min(32, kThreads / nout);
+    const int chunk = (len + ks - 1) / ks;
+    for (int e = threadIdx.x; e < nout * ks; e += kThreads) {
+        const int o = e / ks, j = e % ks, hh = o / nc, i = o % nc;
+        const int ta = min(len, j * chunk), tb = min(len, ta + chunk);
+        const float* p = sm.sc + hh * d.seq;
+        const float* vc = sm.vt + i;
+        double a = 0.0;
+#pragma unroll 4
+        for (int t = ta; t < tb; ++t) a = __fma_rn((double)p[t], (double)vc[(size_t)t * vs], a);
+        sm.pv[e] = a;
+    }
+    __syncthreads();
+    for (int o = threadIdx.x; o < nout; o += kThreads) {
+        double a = 0.0;
+        for (int j = 0; j < ks; ++j) a = __dadd_rn(a, sm.pv[o * ks + j]);
+        const int hh = o / nc, i = o % nc;
+        s.att[(size_t)b * d.dim + (size_t)(g * group + h0 + hh) * hd + c0 + i] = (int16_t)q16h(__double2float_rn(a));
+    }
+}
+
+#endif  // VC4_COMMON_TU
+
+// ---------------------------------------------------------------------------
+// bare matvec (CPU-path entry)
+// ---------------------------------------------------------------------------
+
+template <int WT, int MAXC>
+__global__ void __launch_bounds__(kThreads) k_raw(DMat W, const int16_t* xq, int n, int32_t* out) {
+    WRegs<MAXC> R;
+    mv_prefetch<WT, MAXC>(W, blockIdx.x, R);
+    XStage xs; Red* red; long long* part; int16_t* tmp;
+    carve<1>(x_stride(W), g_stride(W), xs, red, part, tmp);
+    xs.k[0] = 0;
+    stage_one<WT>(xs, 0, xq, n, 0, *red);
+    long long S[1];
+    mv_compute<WT, 1, MAXC>(W, R, xs, 1, S);
+    const long long tot = reduce_warps<1>(S, 1, part);
+    if (threadIdx.x < 32) {
+        const int row = blockIdx.x * 32 + threadIdx.x;
+        if (row < W.rows) out[row] = mv_epi(WT == W_T3 ? tot - xs.gsum[0] : tot, W.rscale[row]);
+    }
+}
+
+#ifdef VC4_COMMON_TU
+// i16 matrix (the MoE router, shaders.cpp:1216-1230): one block per row.
+__global__ void __launch_bounds__(kThreads) k_raw_i16(DMat W, const int16_t* xq, int n, int32_t* out) {
+    __shared__ Red red;
+    const int row = blockIdx.x;
+    long long acc = 0;
+    for (int c = threadIdx.x; c < n; c += blockDim.x) acc += (long long)W.w16[(size_t)row * n + c] * xq[c];
+    acc = block_sum_i64(acc, red);
+    if (threadIdx.x == 0) out[row] = mv_epi(acc, W.rscale[row]);
+}
+#endif  // VC4_COMMON_TU
+
+// ---------------------------------------------------------------------------
+// launch helpers
+// ---------------------------------------------------------------------------
+
+// Raise a kernel's dynamic shared memory limit once per size; repeated calls
+// (and calls during graph capture) are no-ops.
+template <typename K>
+void set_smem(K kernel, size_t bytes) {
+    static std::map<std::pair<const void*, int>, size_t> done;
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lk(mu);
+    int dev = 0;
+    cudaGetDevice(&dev);
+    size_t& have = done[{(const void*)kernel, dev}];
+    if (bytes <= 48 * 1024 || bytes <= have) return;
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    have = bytes;
+}
+
+// Every decode kernel is launched as a programmatic dependent of the one
+// before it (griddepcontrol in the kernels), inside the captured graph too.
+template <typename... KArgs, typename... Args>
+void launch_pdl(void (*kernel)(KArgs...), dim3 grid, size_t smem, cudaStream_t st, Args... args) {
+    set_smem(kernel, smem);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+constexpr int kNB = 4;   // inputs per CTA for the batched matvecs
+
+// Registers per warp for a matrix: the smallest of 4/8/12/20 chunks that
+// covers nchunks/8 (upload refuses a matrix above 160 chunks).
+inline int maxc_for(int nch) {
+    const int per = (nch + kWarps - 1) / kWarps;
+    return per <= 4 ? 4 : per <= 8 ? 8 : per <= 12 ? 12 : 20;
+}
+
+#define VC4_MAXC(M, F, ...)                                          \
+    do {                                                             \
+        if ((M) == 4) F<4>(__VA_ARGS__);                             \
+        else if ((M) == 8) F<8>(__VA_ARGS__);                        \
+        else if ((M) == 12) F<12>(__VA_ARGS__);                      \
+        else F<20>(__VA_ARGS__);                                     \
+    } while (0)
+
+template <int WT>
+struct Ops {
+    template <int NB, int MAXC>
+    static void qkv_nb(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
+        const DMat& W = m.mats[m.qkv[layer]];
+        const DMat& E = m.mats[m.emb_mat];
+        Dims d = dims_of(m, s);
+        const size_t sm = mv_layout(wstage_bytes(W, NB), NB, NB * d.dim, d.dim, 0).total;
+        for (int b0 = 0; b0 < bt.n; b0 += NB)
+            launch_pdl(k_qkv<WT, NB, MAXC>, dim3(W.rblocks), sm, st, W, E, m.d_emb_scale,
+                       (const float*)(m.d_rms_att + (size_t)layer * d.dim), s, bt, d, layer, b0);
+    }
+    template <int NB, int MAXC>
+    static void wo_nb(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
+        const DMat& W = m.mats[m.wo[layer]];
+        Dims d = dims_of(m, s);
+        const size_t sm = mv_layout(wstage_bytes(W, NB), NB, NB * d.dim, 0, 0).total;
+        for (int b0 = 0; b0 < bt.n; b0 += NB) launch_pdl(k_wo<WT, NB, MAXC>, dim3(W.rblocks), sm, st, W, s, bt, d, b0);
+    }
+    template <int NB, int MAXC>
+    static void gate_nb(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
+        Dims d = dims_of(m, s);
+        MatSet M;
+        if (d.experts) {
+            const int eb = m.e_w1[(size_t)layer * d.experts];
+            for (int e = 0; e < d.experts; ++e) { M.a[e] = m.mats[eb + 4 * e]; M.b[e] = m.mats[eb + 4 * e + 1]; }
+            M.router = m.mats[m.router[layer]];
+        } else {
+            M.a[0] = m.mats[m.w1[layer]];
+            M.b[0] = m.mats[m.w3[layer]];
+        }
+        const DMat& W1 = M.a[0];
+        const size_t rbytes = d.experts ? sizeof(int16_t) * (size_t)d.experts * d.dim : 0;
+        const size_t sm = mv_layout(wstage_bytes(W1, NB), NB, NB * d.dim, d.dim, rbytes + 64).total;
+        const dim3 grid(W1.rblocks, d.experts ? d.experts : 1);
+        const int hs = layer < (int)m.h.hid_scale.size() ? (int)m.h.hid_scale[layer] : 0;
+        const int early = d.experts == 0 || bt.n >= 2 * d.experts;
+        for (int b0 = 0; b0 < bt.n; b0 += NB)
+            launch_pdl(k_gate<WT, NB, MAXC>, grid, sm, st, M, (const float*)(m.d_rms_ffn + (size_t)layer * d.dim),
+                       s, bt, d, layer, b0, hs, early);
+    }
+    template <int NB, int MAXC>
+    static void down_nb(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
+        Dims d = dims_of(m, s);
+        MatSet M;
+        const bool two = m.ffn_chunked;
+        if (d.experts) {
+            const int eb = m.e_w1[(size_t)layer * d.experts];
+            for (int e = 0; e < d.experts; ++e) {
+                M.a[e] = m.mats[eb + 4 * e + 2];
+                M.b[e] = two ? m.mats[eb + 4 * e + 3] : m.mats[eb + 4 * e + 2];
+            }
+        } else {
+            M.a[0] = m.mats[m.w2a[layer]];
+            M.b[0] = two ? m.mats[m.w2b[layer]] : m.mats[m.w2a[layer]];
+        }
+        const DMat& Wa = M.a[0];
+        const DMat& Wb = M.b[0];
+        const size_t sm =
+            mv_layout(wstage_bytes(Wa, NB) + (two ? wstage_bytes(Wb, NB) : 0), NB, NB * d.ffn, 0, 64).total;
+        const dim3 grid(Wa.rblocks, d.experts ? d.experts : 1);
+        const int early = d.experts == 0 || bt.n >= 2 * d.experts;
+        for (int b0 = 0; b0 < bt.n; b0 += NB)
+            launch_pdl(k_down<WT, NB, MAXC>, grid, sm, st, M, s, bt, d, layer, b0, early);
+    }
+    template <int NB, int MAXC>
+    static void logits_nb(const DModel& m, const State& s, const Batch& bt, const Finalize& fz, cudaStream_t st) {
+        const DMat& W = m.mats[m.logits_mat];
+        Dims d = dims_of(m, s);
+        const int nsm = std::max(1, m.num_sms);
+        const int stages = wide_stages(W, NB, d.dim);
+        if (W.rblocks > 2 * nsm && stages >= 2) {
+            const int grid = std::min((W.rblocks + kWarps - 1) / kWarps, nsm);
+            const size_t wsm = wide_smem(W, NB, d.dim, stages);
+            for (int b0 = 0; b0 < bt.n; b0 += NB)
+                launch_pdl(k_logits_wide<NB>, dim3(grid), wsm, st, W, (const float*)m.d_rms_final, s, bt, d, b0, fz,
+                           stages);
+        } else {
+            const size_t csm = mv_layout(wstage_bytes(W, NB), NB, NB * d.dim, d.dim, 0).total;
+            for (int b0 = 0; b0 < bt.n; b0 += NB)
+                launch_pdl(k_logits<NB, MAXC>, dim3(W.rblocks), csm, st, W, (const float*)m.d_rms_final, s, bt, d, b0,
+                           fz);
+        }
+    }
+    template <int MAXC>
+    static void qkv(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
+        if (bt.n == 1) qkv_nb<1, MAXC>(m, s, bt, layer, st);
+        else qkv_nb<kNB, MAXC>(m, s, bt, layer, st);
+    }
+    template <int MAXC>
+    static void wo(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
+        if (bt.n == 1) wo_nb<1, MAXC>(m, s, bt, layer, st);
+        else wo_nb<kNB, MAXC>(m, s, bt, layer, st);
+    }
+    template <int MAXC>
+    static void gate(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
+        if (bt.n == 1) gate_nb<1, MAXC>(m, s, bt, layer, st);
+        else gate_nb<kNB, MAXC>(m, s, bt, layer, st);
+    }
+    template <int MAXC>
+    static void down(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
+        if (bt.n == 1) down_nb<1, MAXC>(m, s, bt, layer, st);
+        else down_nb<kNB, MAXC>(m, s, bt, layer, st);
+    }
+    template <int MAXC>
+    static void logits(const DModel& m, const State& s, const Batch& bt, const Finalize& fz, cudaStream_t st) {
+        if (bt.n == 1) logits_nb<1, MAXC>(m, s, bt, fz, st);
+        else logits_nb<kNB, MAXC>(m, s, bt, fz, st);
+    }
+    template <int MAXC>
+    static void raw(const DMat& W, const int16_t* xq, int n, int32_t* out, cudaStream_t st) {
+        const size_t sm = smem_bytes(1, x_stride(W), g_stride(W), 0);
+        set_smem(k_raw<WT, MAXC>, sm);
+        k_raw<WT, MAXC><<<W.rblocks, kThreads, sm, st>>>(W, xq, n, out);
+    }
+};
+
+}  // namespace
+
+// Per-weight-type launch entry points (ops_q8.cu, ops_q4.cu, ops_t3.cu).
+#define VC4_OPS_DECL(SUF)                                                                       \
+    void qkv_##SUF(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st);  \
+    void wo_##SUF(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st);   \
+    void gate_##SUF(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st); \
+    void down_##SUF(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st); \
+    void raw_##SUF(const DMat& W, const int16_t* xq, int n, int32_t* out, cudaStream_t st);
+VC4_OPS_DECL(q8)
+VC4_OPS_DECL(q4)
+VC4_OPS_DECL(t3)
+
+}  // namespace vc4
