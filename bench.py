@@ -40,7 +40,7 @@ for _p in (PKG, os.path.join(ROOT, "oracle")):
 
 METRIC = "decode tokens/s per GPU and per box (1/2/4/8)"
 KV_NAME = {16: "q16", 8: "q8"}
-OPS = ["qkv", "attention", "wo", "ffn_gate", "ffn_down", "logits"]
+OPS = ["qkv", "attention", "wo", "ffn", None, "logits"]   # op 4 (w2) runs inside op 3
 
 
 def parse():
@@ -385,6 +385,8 @@ def run_ours(args, cfg, dist):
     prof_pos = [min(int(pos_h[0]), cfg.seq - 1)] * B
     op_ms, op_bytes = {}, {}
     for op in range(6):
+        if OPS[op] is None:
+            continue
         avg = C.c_double()
         byt = C.c_double()
         pos_arr = np.array(prof_pos, np.int32)
@@ -396,7 +398,7 @@ def run_ours(args, cfg, dist):
         vc4b200.lib().vc4_op_bytes(sess._h, op, L - 1, B, vc4b200.engine._p(pos_arr), C.byref(byt))
         op_ms[OPS[op]] = avg.value
         op_bytes[OPS[op]] = byt.value
-    per_step = {k: op_ms[k] * (1 if k == "logits" else L) for k in OPS}
+    per_step = {k: op_ms[k] * (1 if k == "logits" else L) for k in op_ms}
     dom = max(per_step, key=per_step.get)
     peaks = {}
     try:
@@ -414,7 +416,7 @@ def run_ours(args, cfg, dist):
                     traffic = float(line.split()[1])
     except OSError:
         pass
-    step_bytes = sum(op_bytes[k] * (1 if k == "logits" else L) for k in OPS)
+    step_bytes = sum(op_bytes[k] * (1 if k == "logits" else L) for k in op_bytes)
     roofline = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm, "unit": "GB/s",
                 "frac": achieved / hbm, "traffic": traffic,
                 "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)" if peaks else "fallback 6650 GB/s",

@@ -137,11 +137,13 @@ VC4_API int vc4_matvec_s(vc4_model* m, int which, int layer, int expert, const f
 /* Replay probe (the reference's MATVEC_DUP / ATTN_DUP, session.cpp:15-48 and
    gpu_attn.cpp:20-39): run one op of the decode pass `reps` times for the
    batch (slots, tokens, pos; host arrays) on the session stream, timing each
-   launch with CUDA events.  op: 0 qkv, 1 attention, 2 wo, 3 ffn gate,
-   4 ffn down, 5 logits.  With flush != 0 a 256 MiB buffer is written between
-   launches (outside the timed interval) so every launch starts from a cold L2.
-   Every op rewrites the same outputs from unchanged inputs, so the state after
-   the probe is the state before it.  avg_ms receives the mean launch time. */
+   launch with CUDA events.  op: 0 qkv, 1 attention, 2 wo, 3 ffn (gate/up,
+   SwiGLU and the w2 partial sums), 5 logits; 4 is refused (w2 runs inside
+   op 3).  With flush != 0 a 256 MiB buffer is written between launches
+   (outside the timed interval) so every launch starts from a cold L2.  The KV
+   cache and the sequences' state are unchanged afterwards (the FFN partial
+   sums the replays accumulate are cleared before returning).  avg_ms receives
+   the mean launch time. */
 VC4_API int vc4_profile_op(vc4_session* s, int op, int layer, int n, const int* slots, const int* tokens,
                            const int* pos, int reps, int flush, double* avg_ms);
 /* Algorithmic bytes one launch of `op` moves for n sequences at the given

@@ -165,6 +165,8 @@ std::string upload_model(HModel&& h, DModel& d) {
     d.ffn_width = h.ffn_width();
     d.ffn_chunked = d.ffn_width > 2048;                       // model.cpp:217-277
     d.ffn_chunk = d.ffn_chunked ? (d.ffn_width + 1) / 2 : d.ffn_width;
+    // the FFN kernel's 32-row tiles of the hidden vector must not straddle the w2 halves
+    if (d.ffn_chunked && d.ffn_chunk % 32) return "chunked FFN with a chunk width that is not a multiple of 32";
     std::vector<void*>& al = d.allocs;
     auto add = [&](const HMat& m, int c0, int c1) -> int {
         DMat x;
@@ -270,8 +272,7 @@ void enqueue_pass(vc4_session* s, const PassArgs& a, cudaStream_t st) {
         launch_embed_qkv(m, s->st, b, l, st);
         launch_attention(m, s->st, b, l, st);
         launch_wo(m, s->st, b, l, st);
-        launch_ffn_gate(m, s->st, b, l, st);
-        launch_ffn_down(m, s->st, b, l, st);
+        launch_ffn_gate(m, s->st, b, l, st);   // gate/up, SwiGLU and the w2 partial sums
     }
     launch_logits(m, s->st, b, a.next, a.tokens, a.pos, a.advance, a.forced, st);
 }
@@ -461,7 +462,8 @@ int vc4_session_create(vc4_model* m, int slots, int seq, int kv_bits, const floa
               alloc((void**)&st.rope_cos, (size_t)seq * (h.head_dim / 2) * 4) &&
               alloc((void**)&st.rope_sin, (size_t)seq * (h.head_dim / 2) * 4) &&
               alloc((void**)&s->d_slot, (size_t)(3 * slots + 1) * 4) && alloc((void**)&s->d_next, (size_t)slots * 4) &&
-              alloc((void**)&s->d_pos, (size_t)seq * 4 + 16) && alloc((void**)&st.done, 16) && alloc((void**)&st.err, 16);
+              alloc((void**)&s->d_pos, (size_t)seq * 4 + 16) && alloc((void**)&st.done, 16) && alloc((void**)&st.err, 16) &&
+              alloc((void**)&st.sdown, (size_t)L * slots * 2 * D * 8);
     if (!ok) { vc4_session_destroy(s); return fail(VC4_ECUDA, "session allocation failed (slots*seq too large?)"); }
     s->d_tok = s->d_slot + slots;
     if (cudaMallocHost((void**)&s->h_pin, (size_t)(4 * slots + 16) * 4) != cudaSuccess ||
@@ -803,7 +805,6 @@ void launch_op(vc4_session* s, int op, int layer, const Batch& b, cudaStream_t s
         case 1: launch_attention(m, s->st, b, layer, st); break;
         case 2: launch_wo(m, s->st, b, layer, st); break;
         case 3: launch_ffn_gate(m, s->st, b, layer, st); break;
-        case 4: launch_ffn_down(m, s->st, b, layer, st); break;
         default: launch_logits(m, s->st, b, s->d_next, nullptr, nullptr, 0, nullptr, st); break;
     }
 }
@@ -814,6 +815,7 @@ extern "C" int vc4_profile_op(vc4_session* s, int op, int layer, int n, const in
                               const int* pos, int reps, int flush, double* avg_ms) {
     if (op < 0 || op > 5 || layer < 0 || layer >= s->m->d.h.layers || n <= 0 || n > s->slots || reps <= 0)
         return fail(VC4_EINVAL, "profile_op: bad arguments");
+    if (op == 4) return fail(VC4_EINVAL, "profile_op: w2 runs inside op 3 (the FFN kernel)");
     for (int i = 0; i < n; ++i)
         if (int e = check_slot_pos(s, slots[i], pos[i])) return e;
     CK(cudaSetDevice(s->m->d.device));
@@ -844,6 +846,10 @@ extern "C" int vc4_profile_op(vc4_session* s, int op, int layer, int n, const in
     CK(cudaGetLastError());
     cudaEventDestroy(e0);
     cudaEventDestroy(e1);
+    // replays of the FFN op add their w2 partial sums again: restore the
+    // all-zero state every pass starts from
+    const HModel& hm = s->m->d.h;
+    CK(cudaMemsetAsync(s->st.sdown, 0, (size_t)hm.layers * s->slots * 2 * hm.dim * 8, s->stream));
     if (int e = check_kernel_word(s)) return e;
     *avg_ms = total / reps;
     return VC4_OK;
@@ -853,6 +859,7 @@ extern "C" int vc4_op_bytes(const vc4_session* s, int op, int layer, int n, cons
     const DModel& m = s->m->d;
     const HModel& h = m.h;
     if (op < 0 || op > 5 || layer < 0 || layer >= h.layers || n <= 0) return fail(VC4_EINVAL, "op_bytes: bad arguments");
+    if (op == 4) return fail(VC4_EINVAL, "op_bytes: w2 runs inside op 3 (the FFN kernel)");
     auto wbytes = [&](int idx) -> double {
         if (idx < 0) return 0.0;
         const DMat& w = m.mats[idx];
@@ -872,25 +879,17 @@ extern "C" int vc4_op_bytes(const vc4_session* s, int op, int layer, int n, cons
         }
         case 2: b = wbytes(m.wo[layer]) + n * (2 * D + 2 * D + 2 * D); break;
         case 3: {
-            if (h.experts) {   // every expert's gate/up the batch touches: at most min(n, E)
-                const int touched = std::min(n, h.experts);
-                const int e0 = m.e_w1[(size_t)layer * h.experts];
-                b = touched * (wbytes(e0) + wbytes(e0 + 1)) + wbytes(m.router[layer]);
-            } else {
-                b = wbytes(m.w1[layer]) + wbytes(m.w3[layer]);
-            }
-            b += n * (2 * D + 2 * F);
-            break;
-        }
-        case 4: {
+            // gate/up of every expert the batch touches (at most min(n, E)), the router, and their w2
             if (h.experts) {
                 const int touched = std::min(n, h.experts);
                 const int e0 = m.e_w1[(size_t)layer * h.experts];
-                b = touched * (wbytes(e0 + 2) + (m.ffn_chunked ? wbytes(e0 + 3) : 0.0));
+                b = touched * (wbytes(e0) + wbytes(e0 + 1) + wbytes(e0 + 2) + (m.ffn_chunked ? wbytes(e0 + 3) : 0.0)) +
+                    wbytes(m.router[layer]);
             } else {
-                b = wbytes(m.w2a[layer]) + wbytes(m.w2b[layer]);
+                b = wbytes(m.w1[layer]) + wbytes(m.w3[layer]) + wbytes(m.w2a[layer]) +
+                    (m.ffn_chunked ? wbytes(m.w2b[layer]) : 0.0);
             }
-            b += n * (2 * F + 4 * D);
+            b += n * (2 * D + 8.0 * 2 * D);   // x1 in, int64 partial sums out
             break;
         }
         default: b = wbytes(m.logits_mat) + n * (2 * D + 4.0 * h.vocab); break;

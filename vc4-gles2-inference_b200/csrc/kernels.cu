@@ -29,10 +29,6 @@ void launch_ffn_gate(const DModel& m, const State& s, const Batch& b, int layer,
     const DMat& W = m.h.experts ? m.mats[m.e_w1[(size_t)layer * m.h.experts]] : m.mats[m.w1[layer]];
     VC4_BY_TYPE(W.wtype, gate, m, s, b, layer, st);
 }
-void launch_ffn_down(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st) {
-    const DMat& W = m.h.experts ? m.mats[m.e_w1[(size_t)layer * m.h.experts] + 2] : m.mats[m.w2a[layer]];
-    VC4_BY_TYPE(W.wtype, down, m, s, b, layer, st);
-}
 void launch_logits(const DModel& m, const State& s, const Batch& b, int* next, int* tokens, int* pos, int advance,
                    const int* forced, cudaStream_t st) {
     const DMat& W = m.mats[m.logits_mat];
@@ -58,8 +54,8 @@ void launch_matvec_raw(const DModel& m, int mat, const int16_t* xq, int n, int32
 }
 
 int kernel_launches_per_step(const DModel& m, int n) {
-    const int g = (n + kNB - 1) / kNB;
-    return m.h.layers * (4 * g + 1) + g;
+    const int g = n == 1 ? 1 : (n + kNB - 1) / kNB;
+    return m.h.layers * (3 * g + 1) + g;
 }
 
 int max_input_cols() { return kPer * kThreads; }

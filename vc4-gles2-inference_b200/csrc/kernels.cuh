@@ -576,6 +576,7 @@ __device__ __forceinline__ int xscale(int a, int k, float sk) {
 }
 __device__ __forceinline__ long long warp_sumsq(const int16_t* x, int D) {
     long long ss = 0;
+#pragma unroll 8
     for (int c = (threadIdx.x & 31); c < D; c += 32) { const int a = x[c]; ss += a * a; }
     return warp_sum_i64(ss);
 }
@@ -590,6 +591,7 @@ __device__ __forceinline__ void warp_stage(const WStage& ws, int b, int nch, int
     const float sk = ldexpf(1.0f, k);
     uint8_t* lo = ws.lo + (size_t)b * ws.wst;
     int8_t* hi = ws.hi + (size_t)b * ws.wst;
+#pragma unroll 4
     for (int e = lane; e < ws.wst; e += 32) {
         const int slot = e / cpc, j = warp + slot * kWarps, c = j * cpc + e % cpc;
         const int q = (j < nch && c < D) ? xscale(value(c), k, sk) : 0;
@@ -602,6 +604,7 @@ __device__ __forceinline__ void warp_stage(const WStage& ws, int b, int nch, int
     }
     if (WT == W_T3) {
         int t = 0;
+#pragma unroll 8
         for (int c = lane; c < D; c += 32) t += xscale(value(c), k, sk);
         t = __reduce_add_sync(0xffffffffu, t);
         if (lane == 0) ws.gsum[b * ws.gst] = t;
@@ -630,12 +633,138 @@ __device__ __forceinline__ void reduce_once(const long long (&S)[V][NB], int nb,
 }
 
 // ---------------------------------------------------------------------------
+// FFN output by partial sums.  The w2 matvec takes the q16 hidden vector
+// without input scaling, so its exact integer dot product is the sum over any
+// split of the columns.  Each gate CTA multiplies its own 32 hidden values by
+// the matching 32 columns of w2 and adds the per-row partial sums into
+// State::sdown (int64, so the order of the additions does not matter); the
+// consumer of the layer's output (the next layer's qkv kernel, or logits)
+// applies the w2 row scales and the residual add.  A chunked w2 (hidden width
+// above the chunk) keeps one sum per column half, each rounded to q16 before
+// add_q16, as the chunked FFN does (gpu_ffn.cpp:67-132, session.cpp:2052-2067).
+// ---------------------------------------------------------------------------
+
+__host__ __device__ inline size_t sdown_at(int layer, int b, int half, int dim, int slots) {
+    return (((size_t)layer * slots + b) * 2 + half) * dim;
+}
+
+// Where the consumer finds the w2 row scales of the layer it rebuilds.
+struct DownSrc {
+    int layer;            // the layer whose FFN output is rebuilt; -1: none (layer 0 input is the embedding)
+    int two;              // chunked w2
+    const float* ra;      // dense model: row scales of the two w2 halves
+    const float* rb;
+    const DMat* dm;       // MoE: the device matrix table, expert e's halves at dm[ia + 4e], dm[ib + 4e]
+    int ia, ib;
+};
+
+// One chunk of one row: the same integer arithmetic as mv_compute for input
+// bytes lo/hi of the chunk's columns; q4: gsum = the chunk's input sum.
+template <int WT>
+__device__ __forceinline__ long long chunk_dot(const int4 w, int sp, const uint8_t* lo, const int8_t* hi, int gsum) {
+    if (WT == W_Q8) {
+        const uint4 L = *reinterpret_cast<const uint4*>(lo), H = *reinterpret_cast<const uint4*>(hi);
+        int a = 0, c = 0;
+        a = dp4a_su(w.x, L.x, a); a = dp4a_su(w.y, L.y, a); a = dp4a_su(w.z, L.z, a); a = dp4a_su(w.w, L.w, a);
+        c = dp4a_ss(w.x, (int)H.x, c); c = dp4a_ss(w.y, (int)H.y, c); c = dp4a_ss(w.z, (int)H.z, c); c = dp4a_ss(w.w, (int)H.w, c);
+        return (long long)a + 256LL * c;
+    } else if (WT == W_T3) {
+        const unsigned wd[4] = {(unsigned)w.x, (unsigned)w.y, (unsigned)w.z, (unsigned)w.w};
+        const uint4* L4 = reinterpret_cast<const uint4*>(lo);
+        const uint4* H4 = reinterpret_cast<const uint4*>(hi);
+        int a = 0, c = 0;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const uint4 L = L4[q], H = H4[q];
+            const unsigned e0 = wd[q] & 0x03030303u, e1 = (wd[q] >> 2) & 0x03030303u;
+            const unsigned e2 = (wd[q] >> 4) & 0x03030303u, e3 = (wd[q] >> 6) & 0x03030303u;
+            a = dp4a_uu(e0, L.x, a); a = dp4a_uu(e1, L.y, a); a = dp4a_uu(e2, L.z, a); a = dp4a_uu(e3, L.w, a);
+            c = dp4a_us(e0, (int)H.x, c); c = dp4a_us(e1, (int)H.y, c); c = dp4a_us(e2, (int)H.z, c); c = dp4a_us(e3, (int)H.w, c);
+        }
+        return (long long)a + 256LL * c;
+    } else {
+        const long long s16 = (short)(sp & 0xFFFF), m16 = (short)(sp >> 16);
+        const unsigned wd[4] = {(unsigned)w.x, (unsigned)w.y, (unsigned)w.z, (unsigned)w.w};
+        const uint4* L4 = reinterpret_cast<const uint4*>(lo);
+        const uint4* H4 = reinterpret_cast<const uint4*>(hi);
+        const uint4 L0 = L4[0], L1 = L4[1], H0 = H4[0], H1 = H4[1];
+        const unsigned l[8] = {L0.x, L0.y, L0.z, L0.w, L1.x, L1.y, L1.z, L1.w};
+        const unsigned h[8] = {H0.x, H0.y, H0.z, H0.w, H1.x, H1.y, H1.z, H1.w};
+        int nlo = 0, nhi = 0;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const unsigned n0 = wd[q] & 0x0F0F0F0Fu, n1 = (wd[q] >> 4) & 0x0F0F0F0Fu;
+            nlo = dp4a_uu(n0, l[2 * q], nlo); nlo = dp4a_uu(n1, l[2 * q + 1], nlo);
+            nhi = dp4a_us(n0, (int)h[2 * q], nhi); nhi = dp4a_us(n1, (int)h[2 * q + 1], nhi);
+        }
+        return s16 * ((long long)nlo + 256LL * nhi) + m16 * (long long)gsum;
+    }
+}
+
+// x = add_q16(x1, FFN output) of input bi (its batch position) from the
+// layer's partial sums, block-wide into xout; `write` also stores it to s.x.
+__device__ __forceinline__ void rebuild_x(const State& s, const Dims& d, const DownSrc& ds, int bi, int16_t* xout,
+                                          bool write) {
+    const float* ra = ds.ra;
+    const float* rb = ds.rb;
+    if (d.experts) {
+        const int e = __ldcg(s.route + (size_t)bi * d.layers + ds.layer);
+        ra = ds.dm[ds.ia + 4 * e].rscale;
+        if (ds.two) rb = ds.dm[ds.ib + 4 * e].rscale;
+    }
+    const long long* S = s.sdown + sdown_at(ds.layer, bi, 0, d.dim, s.slots);
+    const int16_t* x1 = s.x1 + (size_t)bi * d.dim;
+    // kU rows per thread per round: every load of a round is issued before the first use
+    constexpr int kU = 4;
+    for (int base = 0; base < d.dim; base += kU * kThreads) {
+        long long sa[kU], sb[kU];
+        float fa[kU], fb[kU];
+        int xv[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            const int r = base + u * kThreads + threadIdx.x;
+            sa[u] = sb[u] = 0;
+            fa[u] = fb[u] = 0.0f;
+            xv[u] = 0;
+            if (r < d.dim) {
+                sa[u] = __ldcg(S + r);
+                fa[u] = __ldg(ra + r);
+                if (ds.two) { sb[u] = __ldcg(S + d.dim + r); fb[u] = __ldg(rb + r); }
+                xv[u] = __ldcg(x1 + r);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            const int r = base + u * kThreads + threadIdx.x;
+            if (r >= d.dim) continue;
+            float o2 = __fmul_rn((float)mv_epi(sa[u], fa[u]), 1.0f / 256.0f);
+            if (ds.two) {
+                const int vb = mv_epi(sb[u], fb[u]);
+                o2 = __fmul_rn((float)q16h(__fadd_rn(o2, __fmul_rn((float)vb, 1.0f / 256.0f))), 1.0f / 256.0f);
+            }
+            const int16_t x = (int16_t)q16h(__fadd_rn(__fmul_rn((float)xv[u], 1.0f / 256.0f), o2));
+            xout[r] = x;
+            if (write) s.x[(size_t)bi * d.dim + r] = x;
+        }
+    }
+}
+
+// Zeroes the partial sums of `layer` for every batch position, split over the grid.
+__device__ __forceinline__ void zero_sdown(const State& s, const Dims& d, int layer) {
+    const size_t n = (size_t)s.slots * 2 * d.dim;                  // int64 values, a multiple of 2
+    uint4* p = reinterpret_cast<uint4*>(s.sdown + sdown_at(layer, 0, 0, d.dim, s.slots));
+    const size_t nv = n / 2, per = (nv + gridDim.x - 1) / gridDim.x;
+    const size_t v0 = (size_t)blockIdx.x * per, v1 = v0 + per < nv ? v0 + per : nv;
+    for (size_t v = v0 + threadIdx.x; v < v1; v += kThreads) p[v] = make_uint4(0u, 0u, 0u, 0u);
+}
+
+// ---------------------------------------------------------------------------
 // qkv: embedding (layer 0) or x, RMSNorm, matvec_s(qkv) -> fp32 qkv
 // ---------------------------------------------------------------------------
 
 template <int WT, int NB, int MAXC>
 __global__ void __launch_bounds__(kThreads) k_qkv(DMat W, DMat E, const float* emb_scale, const float* rms_w,
-                                                  State s, Batch bt, Dims d, int layer, int b0) {
+                                                  State s, Batch bt, Dims d, int layer, int b0, DownSrc ds) {
     const MvLayout L = mv_layout(wstage_bytes(W, NB), NB, NB * d.dim, d.dim, 0);
     if (!smem_ok(L.total, s.err)) return;
     char* sm = SmemLayout::base();
@@ -657,6 +786,7 @@ __global__ void __launch_bounds__(kThreads) k_qkv(DMat W, DMat E, const float* e
             const float es = emb_scale[tok];
             const int8_t* eb = reinterpret_cast<const int8_t*>(E.body) + ((size_t)(tok / 32) * E.nchunks * 32 + (tok % 32)) * 16;
             int16_t* x = s.x + (size_t)bi * d.dim;
+#pragma unroll 4
             for (int c = threadIdx.x; c < d.dim; c += kThreads) {
                 const int16_t q = (int16_t)q16h(__fmul_rn((float)eb[(size_t)(c / 16) * 512 + (c % 16)], es));
                 xin[c] = q;
@@ -664,9 +794,11 @@ __global__ void __launch_bounds__(kThreads) k_qkv(DMat W, DMat E, const float* e
             }
             if (blockIdx.x == 0 && threadIdx.x == 0) s.best[bi] = 0ull;
         } else {
-            load_vec(s.x + (size_t)bi * d.dim, d.dim, xin);
+            rebuild_x(s, d, ds, bi, xin, blockIdx.x == 0);
         }
     }
+    // the logits of the previous pass have consumed the last layer's sums
+    if (layer == 0 && b0 == 0) zero_sdown(s, d, d.layers - 1);
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const WStage ws = wstage_at(W, NB, sm + L.ws);
@@ -677,6 +809,7 @@ __global__ void __launch_bounds__(kThreads) k_qkv(DMat W, DMat E, const float* e
         const int16_t* x = xv + (size_t)b * d.dim;
         const float rr = rms_rr(warp_sumsq(x, d.dim), d.dim, d.eps);
         int mx = 0;
+#pragma unroll 8
         for (int c = lane; c < d.dim; c += 32) mx = max(mx, abs(xnorm(x[c], nws[c], rr)));
         const int k = exp_from_max(__reduce_max_sync(0xffffffffu, mx));
         if (b == warp) kw = k;
@@ -702,7 +835,7 @@ __global__ void __launch_bounds__(kThreads) k_qkv(DMat W, DMat E, const float* e
 // ---------------------------------------------------------------------------
 
 template <int WT, int NB, int MAXC>
-__global__ void __launch_bounds__(kThreads) k_wo(DMat W, State s, Batch bt, Dims d, int b0) {
+__global__ void __launch_bounds__(kThreads) k_wo(DMat W, State s, Batch bt, Dims d, int layer, int b0) {
     const MvLayout L = mv_layout(wstage_bytes(W, NB), NB, NB * d.dim, 0, 0);
     if (!smem_ok(L.total, s.err)) return;
     char* sm = SmemLayout::base();
@@ -715,6 +848,7 @@ __global__ void __launch_bounds__(kThreads) k_wo(DMat W, State s, Batch bt, Dims
     const int row = blockIdx.x * 32 + lane;
     // the residual this thread's epilogue adds, fetched with the inputs
     const int xres = (warp < nb && row < W.rows) ? (int)__ldcg(s.x + (size_t)(b0 + warp) * d.dim + row) : 0;
+    if (layer > 0 && b0 == 0) zero_sdown(s, d, layer - 1);   // this layer's qkv has consumed them
     int16_t* av = reinterpret_cast<int16_t*>(sm + L.x);
     for (int b = 0; b < nb; ++b) load_vec(s.att + (size_t)(b0 + b) * d.dim, d.dim, av + (size_t)b * d.dim);
     __syncthreads();
@@ -725,6 +859,7 @@ __global__ void __launch_bounds__(kThreads) k_wo(DMat W, State s, Batch bt, Dims
         if (b >= nb) break;
         const int16_t* a = av + (size_t)b * d.dim;
         int mx = 0;
+#pragma unroll 8
         for (int c = lane; c < d.dim; c += 32) mx = max(mx, abs((int)a[c]));
         const int k = exp_from_max(__reduce_max_sync(0xffffffffu, mx));
         if (b == warp) kw = k;
@@ -744,30 +879,66 @@ __global__ void __launch_bounds__(kThreads) k_wo(DMat W, State s, Batch bt, Dims
 }
 
 // ---------------------------------------------------------------------------
-// gate: RMSNorm(x1), optional MoE routing (top-1, shaders.cpp:1216-1230 and
+// ffn: RMSNorm(x1), optional MoE routing (top-1, shaders.cpp:1216-1230 and
 // session.cpp:110-115), w1/w3 matvecs and SwiGLU (q16 pair rounding,
-// shaders.cpp:116-136) -> h (the GPU FFN path the CPU session draws)
+// shaders.cpp:116-136) for this CTA's 32 hidden rows, then their share of w2:
+// the rows' q16 values times the matching 32 columns of w2, added into the
+// layer's partial sums (the GPU FFN path the CPU session draws).
 // ---------------------------------------------------------------------------
 
+constexpr int kFfnRB = 4;   // w2 row blocks per warp fetched before the dependency wait
+
+template <int WT>
+__host__ __device__ inline size_t ffn_down_bytes(int nb) {
+    constexpr int span = WT == W_T3 ? 64 : 32;
+    return align16((size_t)2 * nb * span) + align16(sizeof(int) * (size_t)nb * 33);
+}
+
 template <int WT, int NB, int MAXC>
-__global__ void __launch_bounds__(kThreads) k_gate(MatSet M, const float* rms_w, State s, Batch bt, Dims d,
+__global__ void __launch_bounds__(kThreads) k_gate(MatSet M, MatSet M2, const float* rms_w, State s, Batch bt, Dims d,
                                                    int layer, int b0, int hs, int early) {
+    constexpr int cpc = WT == W_Q8 ? 16 : WT == W_Q4 ? 32 : 64;
+    constexpr int span = WT == W_T3 ? 64 : 32;       // staged w2 input columns: the chunk(s) holding the 32 rows
     const int expert = blockIdx.y;
     const DMat& W1 = M.a[expert];
     const DMat& W3 = M.b[expert];
+    // this CTA's hidden rows [32*bx, 32*bx + 32) are columns [c0, c0 + 32) of w2 half `half`
+    const bool two = d.chunk < d.ffn;
+    const int half = (two && 32 * (int)blockIdx.x >= d.chunk) ? 1 : 0;
+    const DMat& W2 = half ? M2.b[expert] : M2.a[expert];
+    const int c0 = 32 * (int)blockIdx.x - (half ? d.chunk : 0);
+    const int j0 = c0 / cpc, off = c0 % cpc, nch2 = W2.nchunks;
     const size_t rbytes = d.experts ? sizeof(int16_t) * (size_t)d.experts * d.dim : 0;
-    const MvLayout L = mv_layout(wstage_bytes(W1, NB), NB, NB * d.dim, d.dim, rbytes + 64);
+    const MvLayout L = mv_layout(wstage_bytes(W1, NB), NB, NB * d.dim, d.dim, align16(rbytes + 64) + ffn_down_bytes<WT>(NB));
     if (!smem_ok(L.total, s.err)) return;
     char* sm = SmemLayout::base();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     WRegs<MAXC> R1, R3;
-    if (early) {
+    int4 w2a[kFfnRB], w2b[kFfnRB];
+    int w2p[kFfnRB];
+    auto fetch_w2 = [&](int i, int4& wa, int4& wb, int& sp) {
+        const int rb = warp + i * kWarps;
+        const int4* body = reinterpret_cast<const int4*>(W2.body) + lane;
+        wa = ld_weights(body + ((size_t)rb * nch2 + j0) * 32);
+        if (WT == W_Q8 && j0 + 1 < nch2) wb = ld_weights(body + ((size_t)rb * nch2 + j0 + 1) * 32);
+        if (WT == W_Q4) sp = __ldg(W2.q4p + ((size_t)rb * nch2 + j0) * 32 + lane);
+    };
+    auto prefetch = [&]() {
         mv_prefetch<WT, MAXC>(W1, blockIdx.x, R1);
         mv_prefetch<WT, MAXC>(W3, blockIdx.x, R3);
-    }
+#pragma unroll
+        for (int i = 0; i < kFfnRB; ++i)
+            if (warp + i * kWarps < W2.rblocks) fetch_w2(i, w2a[i], w2b[i], w2p[i]);
+    };
+    if (early) prefetch();
     float* nws = reinterpret_cast<float*>(sm + L.nw);
     for (int c = threadIdx.x; c < d.dim; c += kThreads) nws[c] = __ldg(rms_w + c);
     int16_t* rw = reinterpret_cast<int16_t*>(sm + L.extra);             // router rows
     int* members = reinterpret_cast<int*>(sm + L.extra + align16(rbytes));
+    uint8_t* dlo = reinterpret_cast<uint8_t*>(sm + L.extra + align16(rbytes + 64));
+    int8_t* dhi = reinterpret_cast<int8_t*>(dlo + (size_t)NB * span);
+    int* dsum = reinterpret_cast<int*>(sm + L.extra + align16(rbytes + 64) + align16((size_t)2 * NB * span));
+    int* hq = dsum + NB;                                                  // [NB][32] q16 hidden values
     for (int i = threadIdx.x; i < d.experts * d.dim; i += kThreads) rw[i] = M.router.w16[i];
     pdl_launch_dependents();
     pdl_wait();
@@ -775,7 +946,6 @@ __global__ void __launch_bounds__(kThreads) k_gate(MatSet M, const float* rms_w,
     const int n_all = min(NB, bt.n - b0);
     for (int b = 0; b < n_all; ++b) load_vec(s.x1 + (size_t)(b0 + b) * d.dim, d.dim, xv + (size_t)b * d.dim);
     __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const WStage ws = wstage_at(W1, NB, sm + L.ws);
     int nb = 0;
 #pragma unroll
@@ -786,13 +956,15 @@ __global__ void __launch_bounds__(kThreads) k_gate(MatSet M, const float* rms_w,
         if (d.experts) {
             // router: matvec_s over the normalised input, first maximum wins
             int mx = 0;
-            for (int c = lane; c < d.dim; c += 32) mx = max(mx, abs(xnorm(x[c], nws[c], rr)));
+    #pragma unroll 8
+        for (int c = lane; c < d.dim; c += 32) mx = max(mx, abs(xnorm(x[c], nws[c], rr)));
             const int k = exp_from_max(__reduce_max_sync(0xffffffffu, mx));
             const float sk = ldexpf(1.0f, k);
             int best = 0;
             float bestv = 0.0f;
             for (int e = 0; e < d.experts; ++e) {
                 long long acc = 0;
+#pragma unroll 8
                 for (int c = lane; c < d.dim; c += 32)
                     acc += (long long)rw[(size_t)e * d.dim + c] * xscale(xnorm(x[c], nws[c], rr), k, sk);
                 const int v = mv_epi(warp_sum_i64(acc), M.router.rscale[e]);
@@ -808,10 +980,7 @@ __global__ void __launch_bounds__(kThreads) k_gate(MatSet M, const float* rms_w,
         ++nb;
     }
     if (nb == 0) return;   // the same in every warp: no input routed to this expert
-    if (!early) {
-        mv_prefetch<WT, MAXC>(W1, blockIdx.x, R1);
-        mv_prefetch<WT, MAXC>(W3, blockIdx.x, R3);
-    }
+    if (!early) prefetch();
     __syncwarp();
     long long S[2][NB], tot[2];
     const XStage xs = xstage_of(ws);
@@ -820,95 +989,60 @@ __global__ void __launch_bounds__(kThreads) k_gate(MatSet M, const float* rms_w,
     reduce_once<NB, 2>(S, nb, reinterpret_cast<long long*>(sm + L.part), tot);
     if (warp < nb) {
         const int row = blockIdx.x * 32 + lane;
+        int q = 0;
         if (row < W1.rows) {
-            const int bi = b0 + members[warp];
             const int corr = WT == W_T3 ? ws.gsum[warp * ws.gst] : 0;
             const int g = mv_epi(tot[0] - corr, R1.rs);
             const int u = mv_epi(tot[1] - corr, R3.rs);
             float y = swiglu1(__fmul_rn((float)g, 1.0f / 256.0f), __fmul_rn((float)u, 1.0f / 256.0f));
             if (hs > 0) y = __fmul_rn(y, ldexpf(1.0f, -hs));     // metadata key 15 store scale
-            s.h[(size_t)bi * d.ffn + row] = (int16_t)q16s(y);
+            q = q16s(y);
         }
-    }
-}
-
-// ---------------------------------------------------------------------------
-// down: w2 (one or two column chunks) + residual -> x
-// ---------------------------------------------------------------------------
-
-template <int WT, int NB, int MAXC>
-__global__ void __launch_bounds__(kThreads) k_down(MatSet M, State s, Batch bt, Dims d, int layer, int b0, int early) {
-    const int expert = blockIdx.y;
-    const bool two = d.chunk < d.ffn;
-    const DMat& Wa = M.a[expert];
-    const DMat& Wb = M.b[expert];
-    const size_t wsa = wstage_bytes(Wa, NB), wsb = two ? wstage_bytes(Wb, NB) : 0;
-    const MvLayout L = mv_layout(wsa + wsb, NB, NB * d.ffn, 0, 64);
-    if (!smem_ok(L.total, s.err)) return;
-    char* sm = SmemLayout::base();
-    WRegs<MAXC> Ra, Rb;
-    if (early) {
-        mv_prefetch<WT, MAXC>(Wa, blockIdx.x, Ra);
-        if (two) mv_prefetch<WT, MAXC>(Wb, blockIdx.x, Rb);
-    }
-    pdl_launch_dependents();
-    pdl_wait();
-    int* members = reinterpret_cast<int*>(sm + L.extra);
-    int16_t* hv = reinterpret_cast<int16_t*>(sm + L.x);
-    const int n_all = min(NB, bt.n - b0);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int row = blockIdx.x * 32 + lane;
-    int nb = 0;
-    for (int b = 0; b < n_all; ++b) {
-        if (d.experts && __ldcg(s.route + (size_t)(b0 + b) * d.layers + layer) != expert) continue;
-        if (threadIdx.x == 0) members[nb] = b;
-        load_vec(s.h + (size_t)(b0 + b) * d.ffn, d.ffn, hv + (size_t)nb * d.ffn);
-        ++nb;
+        hq[warp * 32 + lane] = q;
+        const int sum = __reduce_add_sync(0xffffffffu, q);
+        if (lane == 0) dsum[warp] = sum;
     }
     __syncthreads();
-    if (nb == 0) return;
-    const int xres = (warp < nb && row < Wa.rows) ? (int)__ldcg(s.x1 + (size_t)(b0 + members[warp]) * d.dim + row) : 0;
-    char* wbase = sm + L.ws;
-    const WStage xa = wstage_at(Wa, NB, wbase);
-    WStage xb = xa;
-    if (two) {
-        // the second chunk's slices follow all first-chunk slices
-        xb = wstage_at(Wb, NB, wbase + kWarps * wsa);
+    // the w2 input bytes of this CTA's columns (zero for the rest of the chunk)
+    for (int t = threadIdx.x; t < nb * span; t += kThreads) {
+        const int m = t / span, col = t % span;
+        const int v = (col >= off && col < off + 32) ? hq[m * 32 + col - off] : 0;
+        dlo[m * span + col] = (uint8_t)(v & 0xFF);
+        dhi[m * span + col] = (int8_t)(v >> 8);
     }
+    __syncthreads();
+    // w2 rows: warp w takes row blocks w, w + kWarps, ...; lanes are rows
+    for (int i = 0; warp + i * kWarps < W2.rblocks; ++i) {
+        const int rb = warp + i * kWarps, row = rb * 32 + lane;
+        int4 wa = make_int4(0, 0, 0, 0), wb = make_int4(0, 0, 0, 0);
+        int sp = 0;
+        if (i < kFfnRB) {
 #pragma unroll
-    for (int b = 0; b < NB; ++b) {
-        if (b >= nb) break;
-        const int16_t* h = hv + (size_t)b * d.ffn;
-        warp_stage<WT>(xa, b, Wa.nchunks, d.chunk, 0, [&](int c) { return (int)h[c]; });
-        if (two) warp_stage<WT>(xb, b, Wb.nchunks, d.ffn - d.chunk, 0, [&](int c) { return (int)h[d.chunk + c]; });
-    }
-    if (!early) {
-        mv_prefetch<WT, MAXC>(Wa, blockIdx.x, Ra);
-        if (two) mv_prefetch<WT, MAXC>(Wb, blockIdx.x, Rb);
-    }
-    __syncwarp();
-    long long S[2][NB], tot[2];
-    mv_compute<WT, NB, MAXC, true>(Wa, Ra, xstage_of(xa), nb, S[0]);
-    if (two) {
-        mv_compute<WT, NB, MAXC, true>(Wb, Rb, xstage_of(xb), nb, S[1]);
-    } else {
-#pragma unroll
-        for (int b = 0; b < NB; ++b) S[1][b] = 0;
-    }
-    reduce_once<NB, 2>(S, nb, reinterpret_cast<long long*>(sm + L.part), tot);
-    if (warp < nb && row < Wa.rows) {
-        const int bi = b0 + members[warp];
-        const int va = mv_epi(WT == W_T3 ? tot[0] - xa.gsum[warp * xa.gst] : tot[0], Ra.rs);
-        float o2 = __fmul_rn((float)va, 1.0f / 256.0f);
-        if (two) {
-            const int vb = mv_epi(WT == W_T3 ? tot[1] - xb.gsum[warp * xb.gst] : tot[1], Rb.rs);
-            // add_q16 of the two chunk outputs (session.cpp:2052-2067)
-            o2 = __fmul_rn((float)q16h(__fadd_rn(o2, __fmul_rn((float)vb, 1.0f / 256.0f))), 1.0f / 256.0f);
+            for (int u = 0; u < kFfnRB; ++u)
+                if (u == i) { wa = w2a[u]; wb = w2b[u]; sp = w2p[u]; }
+        } else {
+            fetch_w2(i, wa, wb, sp);
         }
-        const float x1 = __fmul_rn((float)xres, 1.0f / 256.0f);
-        s.x[(size_t)bi * d.dim + row] = (int16_t)q16h(__fadd_rn(x1, o2));
+        for (int m = 0; m < nb; ++m) {
+            const uint8_t* lo = dlo + m * span;
+            const int8_t* hi = dhi + m * span;
+            long long S2;
+            if (WT == W_Q8) {
+                S2 = chunk_dot<W_Q8>(wa, 0, lo, hi, 0);
+                if (j0 + 1 < nch2) S2 += chunk_dot<W_Q8>(wb, 0, lo + 16, hi + 16, 0);
+            } else if (WT == W_Q4) {
+                S2 = chunk_dot<W_Q4>(wa, sp, lo, hi, dsum[m]);
+            } else {
+                S2 = chunk_dot<W_T3>(wa, 0, lo, hi, 0) - dsum[m];   // codes are w + 1
+            }
+            if (row < W2.rows)
+                atomicAdd(reinterpret_cast<unsigned long long*>(
+                              s.sdown + sdown_at(layer, b0 + members[m], half, d.dim, s.slots) + row),
+                          (unsigned long long)S2);
+        }
     }
 }
+
 
 // ---------------------------------------------------------------------------
 // logits: RMSNorm(x) + logits matvec + first-max argmax; the last CTA of the
@@ -962,10 +1096,11 @@ __device__ __forceinline__ void logits_finish(State& s, int b0, int nb, const Fi
 
 template <int NB>
 __device__ __forceinline__ void logits_stage_inputs(const DMat& W, const float (&nw)[kPer], State& s, const Dims& d,
-                                                    int b0, int nb, XStage& xs, Red*& red, int16_t*& tmp) {
+                                                    const DownSrc& ds, int b0, int nb, XStage& xs, Red*& red,
+                                                    int16_t*& tmp) {
     long long* part;
     carve<NB>(x_stride(W), g_stride(W), xs, red, part, tmp);
-    for (int b = 0; b < nb; ++b) load_vec(s.x + (size_t)(b0 + b) * d.dim, d.dim, tmp + (size_t)b * d.dim);
+    for (int b = 0; b < nb; ++b) rebuild_x(s, d, ds, b0 + b, tmp + (size_t)b * d.dim, false);
     __syncthreads();
     for (int b = 0; b < nb; ++b) {
         int16_t* xin = tmp + (size_t)b * d.dim;
@@ -977,7 +1112,7 @@ __device__ __forceinline__ void logits_stage_inputs(const DMat& W, const float (
 
 template <int NB, int MAXC>
 __global__ void __launch_bounds__(kThreads) k_logits(DMat W, const float* rms_w, State s, Batch bt, Dims d, int b0,
-                                                     Finalize fz) {
+                                                     Finalize fz, DownSrc ds) {
     const MvLayout L = mv_layout(wstage_bytes(W, NB), NB, NB * d.dim, d.dim, 0);
     if (!smem_ok(L.total, s.err)) return;
     char* sm = SmemLayout::base();
@@ -989,7 +1124,7 @@ __global__ void __launch_bounds__(kThreads) k_logits(DMat W, const float* rms_w,
     pdl_wait();
     int16_t* xv = reinterpret_cast<int16_t*>(sm + L.x);
     const int nb = min(NB, bt.n - b0);
-    for (int b = 0; b < nb; ++b) load_vec(s.x + (size_t)(b0 + b) * d.dim, d.dim, xv + (size_t)b * d.dim);
+    for (int b = 0; b < nb; ++b) rebuild_x(s, d, ds, b0 + b, xv + (size_t)b * d.dim, false);
     __syncthreads();
     const WStage ws = wstage_at(W, NB, sm + L.ws);
 #pragma unroll
@@ -1048,7 +1183,7 @@ __host__ __device__ inline size_t wide_smem(const DMat& W, int nb, int dim, int 
 
 template <int NB>
 __global__ void __launch_bounds__(kThreads) k_logits_wide(DMat W, const float* rms_w, State s, Batch bt, Dims d,
-                                                         int b0, Finalize fz, int stages) {
+                                                         int b0, Finalize fz, int stages, DownSrc ds) {
     if (!smem_ok(wide_smem(W, NB, d.dim, stages), s.err)) return;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nch = W.nchunks;
     char* ring = SmemLayout::base() + wide_base(W, NB, d.dim) + (size_t)warp * stages * kWidePiece * 512;
@@ -1077,7 +1212,7 @@ __global__ void __launch_bounds__(kThreads) k_logits_wide(DMat W, const float* r
     pdl_wait();
     XStage xs; Red* red; int16_t* tmp;
     const int nb = min(NB, bt.n - b0);
-    logits_stage_inputs<NB>(W, nw, s, d, b0, nb, xs, red, tmp);   // block-wide; publishes the mbarriers
+    logits_stage_inputs<NB>(W, nw, s, d, ds, b0, nb, xs, red, tmp);   // block-wide; publishes the mbarriers
     unsigned long long best[NB];
 #pragma unroll
     for (int b = 0; b < NB; ++b) best[b] = 0ull;
@@ -1560,6 +1695,24 @@ inline int maxc_for(int nch) {
         else F<20>(__VA_ARGS__);                                     \
     } while (0)
 
+// The w2 row scales the consumer of `layer`'s FFN output needs.
+inline DownSrc down_src(const DModel& m, int layer) {
+    DownSrc ds{};
+    ds.layer = layer;
+    ds.two = m.ffn_chunked ? 1 : 0;
+    if (layer < 0) return ds;
+    if (m.h.experts) {
+        const int eb = m.e_w1[(size_t)layer * m.h.experts];
+        ds.dm = m.d_mats;
+        ds.ia = eb + 2;
+        ds.ib = eb + 3;
+    } else {
+        ds.ra = m.mats[m.w2a[layer]].rscale;
+        ds.rb = ds.two ? m.mats[m.w2b[layer]].rscale : nullptr;
+    }
+    return ds;
+}
+
 template <int WT>
 struct Ops {
     template <int NB, int MAXC>
@@ -1568,62 +1721,49 @@ struct Ops {
         const DMat& E = m.mats[m.emb_mat];
         Dims d = dims_of(m, s);
         const size_t sm = mv_layout(wstage_bytes(W, NB), NB, NB * d.dim, d.dim, 0).total;
+        const DownSrc ds = down_src(m, layer - 1);
         for (int b0 = 0; b0 < bt.n; b0 += NB)
             launch_pdl(k_qkv<WT, NB, MAXC>, dim3(W.rblocks), sm, st, W, E, m.d_emb_scale,
-                       (const float*)(m.d_rms_att + (size_t)layer * d.dim), s, bt, d, layer, b0);
+                       (const float*)(m.d_rms_att + (size_t)layer * d.dim), s, bt, d, layer, b0, ds);
     }
     template <int NB, int MAXC>
     static void wo_nb(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
         const DMat& W = m.mats[m.wo[layer]];
         Dims d = dims_of(m, s);
         const size_t sm = mv_layout(wstage_bytes(W, NB), NB, NB * d.dim, 0, 0).total;
-        for (int b0 = 0; b0 < bt.n; b0 += NB) launch_pdl(k_wo<WT, NB, MAXC>, dim3(W.rblocks), sm, st, W, s, bt, d, b0);
+        for (int b0 = 0; b0 < bt.n; b0 += NB)
+            launch_pdl(k_wo<WT, NB, MAXC>, dim3(W.rblocks), sm, st, W, s, bt, d, layer, b0);
     }
     template <int NB, int MAXC>
     static void gate_nb(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
         Dims d = dims_of(m, s);
-        MatSet M;
-        if (d.experts) {
-            const int eb = m.e_w1[(size_t)layer * d.experts];
-            for (int e = 0; e < d.experts; ++e) { M.a[e] = m.mats[eb + 4 * e]; M.b[e] = m.mats[eb + 4 * e + 1]; }
-            M.router = m.mats[m.router[layer]];
-        } else {
-            M.a[0] = m.mats[m.w1[layer]];
-            M.b[0] = m.mats[m.w3[layer]];
-        }
-        const DMat& W1 = M.a[0];
-        const size_t rbytes = d.experts ? sizeof(int16_t) * (size_t)d.experts * d.dim : 0;
-        const size_t sm = mv_layout(wstage_bytes(W1, NB), NB, NB * d.dim, d.dim, rbytes + 64).total;
-        const dim3 grid(W1.rblocks, d.experts ? d.experts : 1);
-        const int hs = layer < (int)m.h.hid_scale.size() ? (int)m.h.hid_scale[layer] : 0;
-        const int early = d.experts == 0 || bt.n >= 2 * d.experts;
-        for (int b0 = 0; b0 < bt.n; b0 += NB)
-            launch_pdl(k_gate<WT, NB, MAXC>, grid, sm, st, M, (const float*)(m.d_rms_ffn + (size_t)layer * d.dim),
-                       s, bt, d, layer, b0, hs, early);
-    }
-    template <int NB, int MAXC>
-    static void down_nb(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
-        Dims d = dims_of(m, s);
-        MatSet M;
+        MatSet M, M2;
         const bool two = m.ffn_chunked;
         if (d.experts) {
             const int eb = m.e_w1[(size_t)layer * d.experts];
             for (int e = 0; e < d.experts; ++e) {
-                M.a[e] = m.mats[eb + 4 * e + 2];
-                M.b[e] = two ? m.mats[eb + 4 * e + 3] : m.mats[eb + 4 * e + 2];
+                M.a[e] = m.mats[eb + 4 * e];
+                M.b[e] = m.mats[eb + 4 * e + 1];
+                M2.a[e] = m.mats[eb + 4 * e + 2];
+                M2.b[e] = two ? m.mats[eb + 4 * e + 3] : m.mats[eb + 4 * e + 2];
             }
+            M.router = m.mats[m.router[layer]];
         } else {
-            M.a[0] = m.mats[m.w2a[layer]];
-            M.b[0] = two ? m.mats[m.w2b[layer]] : m.mats[m.w2a[layer]];
+            M.a[0] = m.mats[m.w1[layer]];
+            M.b[0] = m.mats[m.w3[layer]];
+            M2.a[0] = m.mats[m.w2a[layer]];
+            M2.b[0] = two ? m.mats[m.w2b[layer]] : m.mats[m.w2a[layer]];
         }
-        const DMat& Wa = M.a[0];
-        const DMat& Wb = M.b[0];
+        const DMat& W1 = M.a[0];
+        const size_t rbytes = d.experts ? sizeof(int16_t) * (size_t)d.experts * d.dim : 0;
         const size_t sm =
-            mv_layout(wstage_bytes(Wa, NB) + (two ? wstage_bytes(Wb, NB) : 0), NB, NB * d.ffn, 0, 64).total;
-        const dim3 grid(Wa.rblocks, d.experts ? d.experts : 1);
+            mv_layout(wstage_bytes(W1, NB), NB, NB * d.dim, d.dim, align16(rbytes + 64) + ffn_down_bytes<WT>(NB)).total;
+        const dim3 grid(W1.rblocks, d.experts ? d.experts : 1);
+        const int hs = layer < (int)m.h.hid_scale.size() ? (int)m.h.hid_scale[layer] : 0;
         const int early = d.experts == 0 || bt.n >= 2 * d.experts;
         for (int b0 = 0; b0 < bt.n; b0 += NB)
-            launch_pdl(k_down<WT, NB, MAXC>, grid, sm, st, M, s, bt, d, layer, b0, early);
+            launch_pdl(k_gate<WT, NB, MAXC>, grid, sm, st, M, M2, (const float*)(m.d_rms_ffn + (size_t)layer * d.dim),
+                       s, bt, d, layer, b0, hs, early);
     }
     template <int NB, int MAXC>
     static void logits_nb(const DModel& m, const State& s, const Batch& bt, const Finalize& fz, cudaStream_t st) {
@@ -1636,12 +1776,12 @@ struct Ops {
             const size_t wsm = wide_smem(W, NB, d.dim, stages);
             for (int b0 = 0; b0 < bt.n; b0 += NB)
                 launch_pdl(k_logits_wide<NB>, dim3(grid), wsm, st, W, (const float*)m.d_rms_final, s, bt, d, b0, fz,
-                           stages);
+                           stages, down_src(m, m.h.layers - 1));
         } else {
             const size_t csm = mv_layout(wstage_bytes(W, NB), NB, NB * d.dim, d.dim, 0).total;
             for (int b0 = 0; b0 < bt.n; b0 += NB)
                 launch_pdl(k_logits<NB, MAXC>, dim3(W.rblocks), csm, st, W, (const float*)m.d_rms_final, s, bt, d, b0,
-                           fz);
+                           fz, down_src(m, m.h.layers - 1));
         }
     }
     template <int MAXC>
@@ -1658,11 +1798,6 @@ struct Ops {
     static void gate(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
         if (bt.n == 1) gate_nb<1, MAXC>(m, s, bt, layer, st);
         else gate_nb<kNB, MAXC>(m, s, bt, layer, st);
-    }
-    template <int MAXC>
-    static void down(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
-        if (bt.n == 1) down_nb<1, MAXC>(m, s, bt, layer, st);
-        else down_nb<kNB, MAXC>(m, s, bt, layer, st);
     }
     template <int MAXC>
     static void logits(const DModel& m, const State& s, const Batch& bt, const Finalize& fz, cudaStream_t st) {
@@ -1684,7 +1819,6 @@ struct Ops {
     void qkv_##SUF(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st);  \
     void wo_##SUF(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st);   \
     void gate_##SUF(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st); \
-    void down_##SUF(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st); \
     void raw_##SUF(const DMat& W, const int16_t* xq, int n, int32_t* out, cudaStream_t st);
 VC4_OPS_DECL(q8)
 VC4_OPS_DECL(q4)

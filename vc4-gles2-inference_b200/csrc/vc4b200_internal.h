@@ -138,6 +138,7 @@ struct State {                      // per-slot activations, [slot][...]
     float* rope_sin = nullptr;
     int* done = nullptr;             // CTA arrival counter of the logits kernel (reset by its last CTA)
     int* err = nullptr;              // kernel self-check word: nonzero = a launch reserved too little shared memory
+    long long* sdown = nullptr;      // w2 partial sums [layers][slots][2][dim] (int64, zero between uses)
 };
 
 // Kernel launchers (kernels.cu).  All enqueue on `st`; none synchronises.
@@ -145,7 +146,6 @@ void launch_embed_qkv(const DModel& m, const State& s, const Batch& b, int layer
 void launch_attention(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st);
 void launch_wo(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st);
 void launch_ffn_gate(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st);
-void launch_ffn_down(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st);
 // Logits + first-max argmax; the launch's last CTA writes the greedy tokens to
 // `next` and, with `advance`, moves each sequence on (token, position + 1);
 // `forced` (indexed by position) replaces the greedy token during a prefill.
