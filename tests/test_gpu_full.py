@@ -66,13 +66,15 @@ def test_single_stream_full_shape(gpu, key, prompt_len, steps):
 
 
 @pytest.mark.gpu
-def test_moe_batch_full_shape(gpu):
-    """c2: MoE q4, KV q8, several sequences per pass routed to different experts."""
+@pytest.mark.parametrize("n", [6, 10])
+def test_moe_batch_full_shape(gpu, n):
+    """c2: MoE q4, KV q8, several sequences per pass routed to different
+    experts (10: the many-sequence kernels)."""
     cfg = synth.CONFIGS["c2"]
     path = _path("c2")
     om = oracle.Model(path)
     model = vc4b200.Model(gpu, path)
-    n, P = 6, 10
+    P = 10
     prompts = [synth.prompt_tokens(cfg, i)[:P] for i in range(n)]
     sess = vc4b200.Session(model, slots=n, seq=cfg.seq, kv="q8")
     got = []
@@ -93,9 +95,11 @@ def test_moe_batch_full_shape(gpu):
 
 
 @pytest.mark.gpu
-def test_prefix_restore_batch_full_shape(gpu, tmp_path):
+@pytest.mark.parametrize("n", [4, 9])
+def test_prefix_restore_batch_full_shape(gpu, tmp_path, n):
     """c4: one prefix prefilled once, saved as MMKV1, restored into every slot
-    of a batch, then greedy decode of all slots in one pass (KV q8)."""
+    of a batch, then greedy decode of all slots in one pass (KV q8; 9 runs the
+    many-sequence kernels)."""
     cfg = synth.CONFIGS["c4"]
     path = _path("c4")
     om = oracle.Model(path)
@@ -105,7 +109,7 @@ def test_prefix_restore_batch_full_shape(gpu, tmp_path):
     first.prefill(prefix, 0, want_logits=False)
     mmkv = str(tmp_path / "prefix.mmkv")
     first.save_prefix_cache(mmkv, prefix)
-    n, steps = 4, 6
+    steps = 6
     batch = vc4b200.Session(model, slots=n, seq=cfg.seq, kv="q8")
     for s in range(n):
         assert batch.load_prefix_cache(mmkv, slot=s) == prefix

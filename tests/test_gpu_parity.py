@@ -89,11 +89,13 @@ def test_matvec_s_matches_oracle(gpu, tiny_paths, key):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("key", ["tiny_q8", "tiny_moe_q4", "tiny_t3"])
-def test_batched_equals_serial(gpu, tiny_paths, key):
-    """Several sequences in one pass give each sequence's serial result."""
+@pytest.mark.parametrize("n", [6, 10])
+def test_batched_equals_serial(gpu, tiny_paths, key, n):
+    """Several sequences in one pass give each sequence's serial result: 6
+    runs the one-sequence kernels four inputs at a time, 10 the many-sequence
+    (prep + matmat) kernels."""
     cfg = synth.TINY_CONFIGS[key]
     model = vc4b200.Model(gpu, tiny_paths[key])
-    n = 6
     prompts = [synth.prompt_tokens(cfg, i)[:10] for i in range(n)]
     bs = vc4b200.Session(model, slots=n, seq=cfg.seq, kv=KV[cfg.kv_bits])
     logs_b = []

@@ -313,7 +313,7 @@ static int run_pass(vc4_session* s, const PassArgs& a) {
         if (e != cudaSuccess) return fail(VC4_ECUDA, std::string("cudaGraphInstantiate: ") + cudaGetErrorString(e));
         tab[a] = ex;
     }
-    s->launches += kernel_launches_per_step(s->m->d, a.n);
+    s->launches += kernel_launches_per_step(s->m->d, s->st, a.n);
     return VC4_OK;
 }
 
@@ -463,7 +463,9 @@ int vc4_session_create(vc4_model* m, int slots, int seq, int kv_bits, const floa
               alloc((void**)&st.rope_sin, (size_t)seq * (h.head_dim / 2) * 4) &&
               alloc((void**)&s->d_slot, (size_t)(3 * slots + 1) * 4) && alloc((void**)&s->d_next, (size_t)slots * 4) &&
               alloc((void**)&s->d_pos, (size_t)seq * 4 + 16) && alloc((void**)&st.done, 16) && alloc((void**)&st.err, 16) &&
-              alloc((void**)&st.sdown, (size_t)L * slots * 2 * D * 8);
+              alloc((void**)&st.sdown, (size_t)L * slots * 2 * D * 8) &&
+              alloc((void**)&st.xrec, (size_t)slots * batch_record_bytes(m->d));
+    st.batch_ok = batch_path_fits(m->d, slots) ? 1 : 0;
     if (!ok) { vc4_session_destroy(s); return fail(VC4_ECUDA, "session allocation failed (slots*seq too large?)"); }
     s->d_tok = s->d_slot + slots;
     if (cudaMallocHost((void**)&s->h_pin, (size_t)(4 * slots + 16) * 4) != cudaSuccess ||
@@ -497,7 +499,8 @@ void vc4_session_destroy(vc4_session* s) {
     State& st = s->st;
     for (void* p : {(void*)st.x, (void*)st.x1, (void*)st.qkv, (void*)st.att, (void*)st.h, (void*)st.logits,
                     (void*)st.best, (void*)st.next, (void*)st.route, (void*)st.kv, (void*)st.rope_cos,
-                    (void*)st.rope_sin, (void*)s->d_slot, (void*)s->d_next, (void*)s->d_pos, (void*)st.done, (void*)st.err})
+                    (void*)st.rope_sin, (void*)s->d_slot, (void*)s->d_next, (void*)s->d_pos, (void*)st.done, (void*)st.err,
+                    (void*)st.sdown, (void*)st.xrec})
         if (p) cudaFree(p);
     if (s->h_pin) cudaFreeHost(s->h_pin);
     if (s->h_logits) cudaFreeHost(s->h_logits);
@@ -626,7 +629,7 @@ int vc4_counters(const vc4_session* s, long long* launches, long long* syncs) {
     return VC4_OK;
 }
 
-int vc4_launches_per_step(const vc4_session* s, int n) { return kernel_launches_per_step(s->m->d, n); }
+int vc4_launches_per_step(const vc4_session* s, int n) { return kernel_launches_per_step(s->m->d, s->st, n); }
 
 int vc4_matvec_s(vc4_model* m, int which, int layer, int expert, const float* x, float* out) {
     const DModel& d = m->d;

@@ -17,23 +17,58 @@ using LogitsOps = Ops<W_Q8>;
         else FN##_t3(__VA_ARGS__);                \
     } while (0)
 
+// The many-sequence kernels serve a pass of at least kBatchMin sequences
+// when every weight block fits shared memory next to one staged input.
+static bool batched(const State& s, const Batch& b) { return s.batch_ok && b.n >= kBatchMin; }
+
 void launch_embed_qkv(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st) {
     const DMat& W = m.mats[m.qkv[layer]];
-    VC4_BY_TYPE(W.wtype, qkv, m, s, b, layer, st);
+    if (batched(s, b)) VC4_BY_TYPE(W.wtype, bqkv, m, s, b, layer, st);
+    else VC4_BY_TYPE(W.wtype, qkv, m, s, b, layer, st);
 }
 void launch_wo(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st) {
     const DMat& W = m.mats[m.wo[layer]];
-    VC4_BY_TYPE(W.wtype, wo, m, s, b, layer, st);
+    if (batched(s, b)) VC4_BY_TYPE(W.wtype, bwo, m, s, b, layer, st);
+    else VC4_BY_TYPE(W.wtype, wo, m, s, b, layer, st);
 }
 void launch_ffn_gate(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st) {
     const DMat& W = m.h.experts ? m.mats[m.e_w1[(size_t)layer * m.h.experts]] : m.mats[m.w1[layer]];
-    VC4_BY_TYPE(W.wtype, gate, m, s, b, layer, st);
+    if (batched(s, b)) VC4_BY_TYPE(W.wtype, bffn, m, s, b, layer, st);
+    else VC4_BY_TYPE(W.wtype, gate, m, s, b, layer, st);
 }
 void launch_logits(const DModel& m, const State& s, const Batch& b, int* next, int* tokens, int* pos, int advance,
                    const int* forced, cudaStream_t st) {
     const DMat& W = m.mats[m.logits_mat];
     Finalize fz{next, tokens, pos, forced, advance};
+    if (batched(s, b)) {
+        MatSet M;
+        M.a[0] = M.b[0] = W;
+        BOps<W_Q8>::prep(m, s, b, m.h.layers - 1, kOpLogits, W, st);
+        BOps<W_Q8>::mm<kOpLogits>(m, s, b, m.h.layers - 1, M, 0, 0, fz, st);
+        return;
+    }
     VC4_MAXC(maxc_for(W.nchunks), LogitsOps::logits, m, s, b, fz, st);
+}
+
+// Bytes of one staged input record of the many-sequence path (the largest over
+// the matrices a prep kernel stages for) and whether every weight block of
+// the model fits the matmat kernels' shared memory.
+size_t batch_record_bytes(const DModel& m) {
+    const DMat& w1 = m.h.experts ? m.mats[m.e_w1[0]] : m.mats[m.w1[0]];
+    return std::max(std::max(xrec_bytes(m.mats[m.qkv[0]]), xrec_bytes(m.mats[m.wo[0]])),
+                    std::max(xrec_bytes(w1), xrec_bytes(m.mats[m.logits_mat])));
+}
+bool batch_path_fits(const DModel& m, int slots) {
+    for (int l = 0; l < m.h.layers; ++l) {
+        const int eb = m.h.experts ? m.e_w1[(size_t)l * m.h.experts] : -1;
+        const DMat& w1 = eb >= 0 ? m.mats[eb] : m.mats[m.w1[l]];
+        const DMat& wa = eb >= 0 ? m.mats[eb + 2] : m.mats[m.w2a[l]];
+        const DMat& wb = m.ffn_chunked ? (eb >= 0 ? m.mats[eb + 3] : m.mats[m.w2b[l]]) : wa;
+        if (mm_smem(m.mats[m.qkv[l]], 1, 1, slots) > kMaxDynSmem || mm_smem(m.mats[m.wo[l]], 1, 1, slots) > kMaxDynSmem ||
+            mm_smem(w1, 2, 1, slots) > kMaxDynSmem || mmdown_smem(wa, wb, m.ffn_chunked, 1, slots) > kMaxDynSmem)
+            return false;
+    }
+    return mm_smem(m.mats[m.logits_mat], 1, 1, slots) <= kMaxDynSmem;
 }
 
 // q heads per cluster: two when the group divides by two, else one
@@ -53,7 +88,10 @@ void launch_matvec_raw(const DModel& m, int mat, const int16_t* xq, int n, int32
     VC4_BY_TYPE(W.wtype, raw, W, xq, n, out, st);
 }
 
-int kernel_launches_per_step(const DModel& m, int n) {
+int kernel_launches_per_step(const DModel& m, const State& s, int n) {
+    Batch b;
+    b.n = n;
+    if (batched(s, b)) return m.h.layers * 8 + 2;   // prep + matmat per op, w2, attention; prep + logits
     const int g = n == 1 ? 1 : (n + kNB - 1) / kNB;
     return m.h.layers * (3 * g + 1) + g;
 }

@@ -1080,8 +1080,8 @@ __device__ __forceinline__ void logits_finish(State& s, int b0, int nb, const Fi
     __syncthreads();
     if (!last) return;
     __threadfence();
-    if (threadIdx.x < nb) {
-        const int bi = b0 + threadIdx.x;
+    for (int i = threadIdx.x; i < nb; i += blockDim.x) {
+        const int bi = b0 + i;
         const unsigned long long key = __ldcg(&s.best[bi]);
         const int tok = (int)(0xFFFFFFFFu - (unsigned)(key & 0xFFFFFFFFull));
         fz.next[bi] = tok;
@@ -1678,6 +1678,8 @@ void launch_pdl(void (*kernel)(KArgs...), dim3 grid, size_t smem, cudaStream_t s
     cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
+#include "batch.cuh"
+
 constexpr int kNB = 4;   // inputs per CTA for the batched matvecs
 
 // Registers per warp for a matrix: the smallest of 4/8/12/20 chunks that
@@ -1812,6 +1814,74 @@ struct Ops {
     }
 };
 
+// Launchers of the many-sequence path (batch.cuh).
+template <int WT>
+struct BOps {
+    static void prep(const DModel& m, const State& s, const Batch& bt, int layer, int op, const DMat& W,
+                     cudaStream_t st) {
+        Dims d = dims_of(m, s);
+        const float* rw = op == kOpWo ? m.d_rms_att
+                        : op == kOpQkv ? m.d_rms_att + (size_t)layer * d.dim
+                        : op == kOpGate ? m.d_rms_ffn + (size_t)layer * d.dim
+                        : m.d_rms_final;
+        DMat router{};
+        if (op == kOpGate && d.experts) router = m.mats[m.router[layer]];
+        launch_pdl(k_prep<WT>, dim3(bt.n), sizeof(int16_t) * (size_t)d.dim, st, W, m.mats[m.emb_mat], m.d_emb_scale,
+                   rw, router, s, bt, d, layer, op);
+    }
+    template <int OP>
+    static void mm(const DModel& m, const State& s, const Batch& bt, int layer, const MatSet& M, int experts, int hs,
+                   const Finalize& fz, cudaStream_t st) {
+        Dims d = dims_of(m, s);
+        const DMat& W = M.a[0];
+        const int nm = OP == kOpGate ? 2 : 1;
+        const size_t fixed = mm_smem(W, nm, 0, bt.n);
+        const int group = std::max(1, std::min(bt.n, (int)((kMaxDynSmem - fixed) / xrec_bytes(W))));
+        launch_pdl(k_mm<WT, OP>, dim3(W.rblocks, experts ? experts : 1), mm_smem(W, nm, group, bt.n), st, M, s, bt, d,
+                   layer, group, hs, fz);
+    }
+    static void qkv(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
+        MatSet M;
+        M.a[0] = M.b[0] = m.mats[m.qkv[layer]];
+        prep(m, s, bt, layer, kOpQkv, M.a[0], st);
+        mm<kOpQkv>(m, s, bt, layer, M, 0, 0, Finalize{}, st);
+    }
+    static void wo(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
+        MatSet M;
+        M.a[0] = M.b[0] = m.mats[m.wo[layer]];
+        prep(m, s, bt, layer, kOpWo, M.a[0], st);
+        mm<kOpWo>(m, s, bt, layer, M, 0, 0, Finalize{}, st);
+    }
+    static void ffn(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
+        Dims d = dims_of(m, s);
+        MatSet M, M2;
+        const bool two = m.ffn_chunked;
+        if (d.experts) {
+            const int eb = m.e_w1[(size_t)layer * d.experts];
+            for (int e = 0; e < d.experts; ++e) {
+                M.a[e] = m.mats[eb + 4 * e];
+                M.b[e] = m.mats[eb + 4 * e + 1];
+                M2.a[e] = m.mats[eb + 4 * e + 2];
+                M2.b[e] = two ? m.mats[eb + 4 * e + 3] : m.mats[eb + 4 * e + 2];
+            }
+        } else {
+            M.a[0] = m.mats[m.w1[layer]];
+            M.b[0] = m.mats[m.w3[layer]];
+            M2.a[0] = m.mats[m.w2a[layer]];
+            M2.b[0] = two ? m.mats[m.w2b[layer]] : m.mats[m.w2a[layer]];
+        }
+        const int hs = layer < (int)m.h.hid_scale.size() ? (int)m.h.hid_scale[layer] : 0;
+        prep(m, s, bt, layer, kOpGate, M.a[0], st);
+        mm<kOpGate>(m, s, bt, layer, M, d.experts, hs, Finalize{}, st);
+        const DMat& Wa = M2.a[0];
+        const DMat& Wb = M2.b[0];
+        const size_t fixed = mmdown_smem(Wa, Wb, two, 0, bt.n);
+        const int group = std::max(1, std::min(bt.n, (int)((kMaxDynSmem - fixed) / down_rec(Wa, Wb, two).bytes)));
+        launch_pdl(k_mmdown<WT>, dim3(Wa.rblocks, d.experts ? d.experts : 1), mmdown_smem(Wa, Wb, two, group, bt.n),
+                   st, M2, s, bt, d, layer, group);
+    }
+};
+
 }  // namespace
 
 // Per-weight-type launch entry points (ops_q8.cu, ops_q4.cu, ops_t3.cu).
@@ -1819,7 +1889,10 @@ struct Ops {
     void qkv_##SUF(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st);  \
     void wo_##SUF(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st);   \
     void gate_##SUF(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st); \
-    void raw_##SUF(const DMat& W, const int16_t* xq, int n, int32_t* out, cudaStream_t st);
+    void raw_##SUF(const DMat& W, const int16_t* xq, int n, int32_t* out, cudaStream_t st);          \
+    void bqkv_##SUF(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st);    \
+    void bwo_##SUF(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st);     \
+    void bffn_##SUF(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st);
 VC4_OPS_DECL(q8)
 VC4_OPS_DECL(q4)
 VC4_OPS_DECL(t3)

@@ -139,6 +139,8 @@ struct State {                      // per-slot activations, [slot][...]
     int* done = nullptr;             // CTA arrival counter of the logits kernel (reset by its last CTA)
     int* err = nullptr;              // kernel self-check word: nonzero = a launch reserved too little shared memory
     long long* sdown = nullptr;      // w2 partial sums [layers][slots][2][dim] (int64, zero between uses)
+    char* xrec = nullptr;            // many-sequence path: staged matvec inputs [slots][record]
+    int batch_ok = 0;                // the many-sequence kernels fit this model
 };
 
 // Kernel launchers (kernels.cu).  All enqueue on `st`; none synchronises.
@@ -154,7 +156,9 @@ void launch_logits(const DModel& m, const State& s, const Batch& b, int* next, i
 // A bare matvec of one model matrix over q16 inputs (the CPU-path entry,
 // GPU::matvec_s): xq are already scaled ints, out receives clamped q16 ints.
 void launch_matvec_raw(const DModel& m, int mat, const int16_t* xq, int n, int32_t* out, cudaStream_t st);
-int kernel_launches_per_step(const DModel& m, int n);
+int kernel_launches_per_step(const DModel& m, const State& s, int n);
+size_t batch_record_bytes(const DModel& m);
+bool batch_path_fits(const DModel& m, int slots);
 // Shape limits of the kernels (checked at upload / session creation).
 bool attention_fits(int seq, int head_dim, int kv_bits, int kv_dim, int group);
 int matvec_max_chunks();
