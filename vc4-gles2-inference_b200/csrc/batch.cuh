@@ -34,6 +34,21 @@ __host__ __device__ inline size_t mm_wbytes(const DMat& W) {
     return (size_t)W.nchunks * 512 + (W.wtype == W_Q4 ? (size_t)W.nchunks * 128 : 0) + 128;
 }
 
+// The w2 input of one sequence, written by the gate matmat as it produces the
+// hidden values (x' = h: no input scale): lo | hi | chunk sums (q4) or total
+// (t3) of column half a, then the same for half b of a chunked w2.
+struct DownRec {   // byte offsets inside one staged hidden vector
+    size_t lo_a, hi_a, g_a, lo_b, hi_b, g_b, bytes;
+};
+__host__ __device__ inline DownRec down_rec(const DMat& Wa, const DMat& Wb, bool two) {
+    DownRec r;
+    const size_t sa = x_stride(Wa), sb = two ? x_stride(Wb) : 0;
+    r.lo_a = 0; r.hi_a = sa; r.g_a = 2 * sa;
+    r.lo_b = r.g_a + align16(sizeof(int) * (g_stride(Wa) + 1));
+    r.hi_b = r.lo_b + sb; r.g_b = r.hi_b + sb;
+    r.bytes = r.g_b + (two ? align16(sizeof(int) * (g_stride(Wb) + 1)) : 0);
+    return r;
+}
 // Top-1 MoE route of a normalised input (block-wide; the first maximum wins,
 // shaders.cpp:1216-1230 and session.cpp:110-115).
 __device__ int route_block(const int16_t* xn, const DMat& R, int D, int experts, Red& r) {
@@ -55,7 +70,8 @@ __device__ int route_block(const int16_t* xn, const DMat& R, int D, int experts,
 // prep: one CTA per sequence (blockIdx.x = its batch position).
 template <int WT>
 __global__ void __launch_bounds__(kThreads) k_prep(DMat W, DMat E, const float* emb_scale, const float* rms_w,
-                                                   DMat router, State s, Batch bt, Dims d, int layer, int op) {
+                                                   DMat router, State s, Batch bt, Dims d, int layer, int op,
+                                                   DownRec dr) {
     __shared__ Red red;
     extern __shared__ __align__(16) char smem[];
     if (!smem_ok(sizeof(int16_t) * (size_t)d.dim, s.err)) return;
@@ -96,20 +112,37 @@ __global__ void __launch_bounds__(kThreads) k_prep(DMat W, DMat E, const float* 
     xs.gsum = reinterpret_cast<int*>(rec + 2 * (size_t)xs.stride);
     stage_one<WT>(xs, 0, x, d.dim, k, red);
     if (threadIdx.x == 0) xs.gsum[xs.gstride] = k;
+    if (op == kOpGate && WT == W_T3 && threadIdx.x == 0) {
+        // the gate matmat adds the hidden totals into the sequence's w2 record
+        char* hr = s.hrec + (size_t)b * dr.bytes;
+        *reinterpret_cast<int*>(hr + dr.g_a) = 0;
+        if (d.chunk < d.ffn) *reinterpret_cast<int*>(hr + dr.g_b) = 0;
+    }
 }
 
-// Sequences a matmat CTA serves: all of them, or (MoE) those routed to `expert`.
+// Sequences a matmat CTA serves: all of them, or (MoE) those routed to
+// `expert`, in batch order; the route loads are issued by all threads at once
+// and the list is compacted with warp ballots.
 __device__ __forceinline__ int mm_members(const State& s, const Dims& d, int n, int layer, int expert, bool moe,
                                           int* members) {
-    __shared__ int cnt;
-    if (threadIdx.x == 0) {
-        int c = 0;
-        for (int b = 0; b < n; ++b)
-            if (!moe || __ldcg(s.route + (size_t)b * d.layers + layer) == expert) members[c++] = b;
-        cnt = c;
+    __shared__ int wc[kWarps];
+    __shared__ int base;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) base = 0;
+    for (int r = 0; r < n; r += kThreads) {
+        const int b = r + threadIdx.x;
+        const bool f = b < n && (!moe || __ldcg(s.route + (size_t)b * d.layers + layer) == expert);
+        const unsigned m = __ballot_sync(0xffffffffu, f);
+        if (lane == 0) wc[warp] = __popc(m);
+        __syncthreads();
+        int off = base;
+        for (int w = 0; w < warp; ++w) off += wc[w];
+        if (f) members[off + __popc(m & ((1u << lane) - 1u))] = b;
+        __syncthreads();
+        if (threadIdx.x == 0) for (int w = 0; w < kWarps; ++w) base += wc[w];
+        __syncthreads();
     }
-    __syncthreads();
-    return cnt;
+    return base;
 }
 
 // Dot products of `ni` staged inputs (records in shared memory) with the
@@ -146,7 +179,7 @@ __host__ __device__ inline size_t mm_smem(const DMat& W, int nmat, int group, in
 // matmat: one CTA per 32-row block (blockIdx.x) and expert (blockIdx.y).
 template <int WT, int OP>
 __global__ void __launch_bounds__(kThreads) k_mm(MatSet M, State s, Batch bt, Dims d, int layer, int group, int hs,
-                                                 Finalize fz) {
+                                                 Finalize fz, DownRec dr) {
     constexpr int NM = OP == kOpGate ? 2 : 1;
     const int blk = blockIdx.x, expert = blockIdx.y;
     const DMat& W = M.a[expert];
@@ -175,7 +208,11 @@ __global__ void __launch_bounds__(kThreads) k_mm(MatSet M, State s, Batch bt, Di
     }
     pdl_launch_dependents();
     pdl_wait();
-    const int nm = mm_members(s, d, n, layer, expert, OP == kOpGate && d.experts > 0, members);
+    // this CTA's share of the members (grid z splits them)
+    const int nall = mm_members(s, d, n, layer, expert, OP == kOpGate && d.experts > 0, members);
+    const int per = (nall + (int)gridDim.z - 1) / (int)gridDim.z;
+    const int m0 = min(nall, (int)blockIdx.z * per), nm = min(nall, m0 + per) - m0;
+    members += m0;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row = blk * 32 + lane;
     const float* rs = reinterpret_cast<const float*>(sm + wbody + qbytes);
@@ -207,21 +244,42 @@ __global__ void __launch_bounds__(kThreads) k_mm(MatSet M, State s, Batch bt, Di
                 const int* gs = reinterpret_cast<const int*>(recs[i] + 2 * (size_t)stride);
                 const int k = gs[gst];
                 const long long corr = WT == W_T3 ? gs[0] : 0;
-                if (row >= W.rows) continue;
-                const int v = mv_epi(S[i] - corr, rs[lane]);
+                const bool live = row < W.rows;
+                const int v = live ? mv_epi(S[i] - corr, rs[lane]) : 0;
                 if (OP == kOpQkv) {
-                    s.qkv[(size_t)b * (d.dim + 2 * d.kv_dim) + row] =
-                        __fmul_rn(__fmul_rn((float)v, 1.0f / 256.0f), ldexpf(1.0f, -k));
+                    if (live)
+                        s.qkv[(size_t)b * (d.dim + 2 * d.kv_dim) + row] =
+                            __fmul_rn(__fmul_rn((float)v, 1.0f / 256.0f), ldexpf(1.0f, -k));
                 } else if (OP == kOpWo) {
-                    const float wo = __fmul_rn(__fmul_rn((float)v, 1.0f / 256.0f), ldexpf(1.0f, -k));
-                    const float xr = __fmul_rn((float)__ldcg(s.x + (size_t)b * d.dim + row), 1.0f / 256.0f);
-                    s.x1[(size_t)b * d.dim + row] = (int16_t)q16h(__fadd_rn(xr, wo));
+                    if (live) {
+                        const float wo = __fmul_rn(__fmul_rn((float)v, 1.0f / 256.0f), ldexpf(1.0f, -k));
+                        const float xr = __fmul_rn((float)__ldcg(s.x + (size_t)b * d.dim + row), 1.0f / 256.0f);
+                        s.x1[(size_t)b * d.dim + row] = (int16_t)q16h(__fadd_rn(xr, wo));
+                    }
                 } else if (OP == kOpGate) {
-                    const int u = mv_epi(S3[i] - corr, rs3[lane]);
-                    float y = swiglu1(__fmul_rn((float)v, 1.0f / 256.0f), __fmul_rn((float)u, 1.0f / 256.0f));
-                    if (hs > 0) y = __fmul_rn(y, ldexpf(1.0f, -hs));     // metadata key 15 store scale
-                    s.h[(size_t)b * d.ffn + row] = (int16_t)q16s(y);
-                } else {
+                    int q = 0;
+                    if (live) {
+                        const int u = mv_epi(S3[i] - corr, rs3[lane]);
+                        float y = swiglu1(__fmul_rn((float)v, 1.0f / 256.0f), __fmul_rn((float)u, 1.0f / 256.0f));
+                        if (hs > 0) y = __fmul_rn(y, ldexpf(1.0f, -hs));     // metadata key 15 store scale
+                        q = q16s(y);
+                    }
+                    // the w2 input record of sequence b: this block's 32 hidden rows are
+                    // columns [c0, c0 + 32) of one w2 column half (the chunk is a multiple of 32)
+                    const int half = (d.chunk < d.ffn && blk * 32 >= d.chunk) ? 1 : 0;
+                    const int c0 = blk * 32 - (half ? d.chunk : 0);
+                    char* hr = s.hrec + (size_t)b * dr.bytes;
+                    const size_t lo = half ? dr.lo_b : dr.lo_a, hi = half ? dr.hi_b : dr.hi_a, g = half ? dr.g_b : dr.g_a;
+                    if (live) {
+                        hr[lo + c0 + lane] = (char)(q & 0xFF);
+                        hr[hi + c0 + lane] = (char)(q >> 8);
+                    }
+                    const int sum = __reduce_add_sync(0xffffffffu, q);
+                    if (lane == 0) {
+                        if (WT == W_Q4) reinterpret_cast<int*>(hr + g)[c0 / 32] = sum;
+                        if (WT == W_T3) atomicAdd(reinterpret_cast<int*>(hr + g), sum);
+                    }
+                } else if (live) {
                     s.logits[(size_t)b * d.vocab + row] = v;
                     best[i] = logit_key(v, row);
                 }
@@ -251,48 +309,9 @@ __global__ void __launch_bounds__(kThreads) k_mm(MatSet M, State s, Batch bt, Di
     if (OP == kOpLogits) logits_finish(s, 0, n, fz);
 }
 
-// w2 for many sequences: the hidden vectors (no input scale) staged by the
-// CTA itself, both column halves of a chunked w2, x = x1 + add_q16(halves).
-struct DownRec {   // byte offsets inside one staged hidden vector
-    size_t lo_a, hi_a, g_a, lo_b, hi_b, g_b, bytes;
-};
-__host__ __device__ inline DownRec down_rec(const DMat& Wa, const DMat& Wb, bool two) {
-    DownRec r;
-    const size_t sa = x_stride(Wa), sb = two ? x_stride(Wb) : 0;
-    r.lo_a = 0; r.hi_a = sa; r.g_a = 2 * sa;
-    r.lo_b = r.g_a + align16(sizeof(int) * (g_stride(Wa) + 1));
-    r.hi_b = r.lo_b + sb; r.g_b = r.hi_b + sb;
-    r.bytes = r.g_b + (two ? align16(sizeof(int) * (g_stride(Wb) + 1)) : 0);
-    return r;
-}
 __host__ __device__ inline size_t mmdown_smem(const DMat& Wa, const DMat& Wb, bool two, int group, int n) {
     return align128(mm_wbytes(Wa) + (two ? mm_wbytes(Wb) : 0)) + (size_t)group * down_rec(Wa, Wb, two).bytes +
            align16(sizeof(int) * (size_t)n) + 64;
-}
-
-// Stage hidden columns [c0, c0 + width) of one sequence as the input of W
-// (x' = h, lo/hi bytes zero-padded to the stride; q4 chunk sums; t3 total).
-template <int WT>
-__device__ __forceinline__ void stage_hidden(const int16_t* h, int c0, int width, int stride, uint8_t* lo, int8_t* hi,
-                                             int* gs) {
-    constexpr int cpc = WT == W_Q8 ? 16 : WT == W_Q4 ? 32 : 64;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    int tot = 0;
-    for (int c = threadIdx.x; c < stride; c += kThreads) {   // stride is a multiple of 32: warps stay converged
-        const int q = c < width ? (int)h[c0 + c] : 0;
-        lo[c] = (uint8_t)(q & 0xFF);
-        hi[c] = (int8_t)(q >> 8);
-        if (WT == W_Q4) {
-            const int g = __reduce_add_sync(0xffffffffu, q);
-            if (lane == 0) gs[c / cpc] = g;
-        }
-        tot += q;
-    }
-    if (WT == W_T3) {
-        tot = __reduce_add_sync(0xffffffffu, tot);
-        if (lane == 0) atomicAdd(&gs[0], tot);
-    }
-    (void)warp;
 }
 
 template <int WT>
@@ -312,6 +331,7 @@ __global__ void __launch_bounds__(kThreads) k_mmdown(MatSet M2, State s, Batch b
         sm + align128(wba + wbb) + (size_t)group * R.bytes + align16(sizeof(int) * (size_t)n));
     if (threadIdx.x == 0) {
         mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
         mbar_fence_init();
         unsigned total = 0;
         for (int m = 0; m < (two ? 2 : 1); ++m) total += (unsigned)mm_wbytes(m ? Wb : Wa);
@@ -327,7 +347,10 @@ __global__ void __launch_bounds__(kThreads) k_mmdown(MatSet M2, State s, Batch b
     }
     pdl_launch_dependents();
     pdl_wait();
-    const int nm = mm_members(s, d, n, layer, expert, d.experts > 0, members);
+    const int nall = mm_members(s, d, n, layer, expert, d.experts > 0, members);
+    const int per = (nall + (int)gridDim.z - 1) / (int)gridDim.z;
+    const int m0 = min(nall, (int)blockIdx.z * per), nm = min(nall, m0 + per) - m0;
+    members += m0;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row = blk * 32 + lane;
     const int sa = x_stride(Wa), sb = two ? x_stride(Wb) : 0;
@@ -337,22 +360,15 @@ __global__ void __launch_bounds__(kThreads) k_mmdown(MatSet M2, State s, Batch b
                            : rsa;
     bool ok = !__syncthreads_or(!mbar_wait(&bar[0], 0));   // the same verdict in every thread
     for (int g0 = 0; g0 < nm && ok; g0 += group) {
-        const int gn = min(group, nm - g0);
-        for (int i = threadIdx.x; i < gn * 2; i += kThreads) {   // zero the t3 totals before staging adds into them
-            int* g = reinterpret_cast<int*>(rsm + (size_t)(i / 2) * R.bytes + ((i & 1) ? R.g_b : R.g_a));
-            if (!(i & 1) || two) g[0] = 0;
+        const int gn = min(group, nm - g0), gi = g0 / group;
+        if (threadIdx.x == 0) {
+            fence_proxy_async();
+            mbar_expect_tx(&bar[1], (unsigned)(gn * R.bytes));
+            for (int i = 0; i < gn; ++i)
+                bulk_g2s(rsm + i * R.bytes, s.hrec + (size_t)members[g0 + i] * R.bytes, (unsigned)R.bytes, &bar[1]);
         }
-        __syncthreads();
-        for (int i = 0; i < gn; ++i) {
-            const int16_t* h = s.h + (size_t)members[g0 + i] * d.ffn;
-            char* r = rsm + (size_t)i * R.bytes;
-            stage_hidden<WT>(h, 0, d.chunk, sa, reinterpret_cast<uint8_t*>(r + R.lo_a),
-                             reinterpret_cast<int8_t*>(r + R.hi_a), reinterpret_cast<int*>(r + R.g_a));
-            if (two)
-                stage_hidden<WT>(h, d.chunk, d.ffn - d.chunk, sb, reinterpret_cast<uint8_t*>(r + R.lo_b),
-                                 reinterpret_cast<int8_t*>(r + R.hi_b), reinterpret_cast<int*>(r + R.g_b));
-        }
-        __syncthreads();
+        ok = mbar_wait(&bar[1], (unsigned)gi & 1u);
+        if (__syncthreads_or(!ok)) { ok = false; break; }
         for (int i0 = warp * kMmNI; i0 < gn; i0 += kWarps * kMmNI) {
             const int ni = min(kMmNI, gn - i0);
             const char* ra[kMmNI];
@@ -386,5 +402,7 @@ __global__ void __launch_bounds__(kThreads) k_mmdown(MatSet M2, State s, Batch b
     if (!ok && threadIdx.x == 0) {
         atomicExch(s.err, kErrCopyTimeout);
         mbar_wait(&bar[0], 0, 10000000ull);
+        mbar_wait(&bar[1], 0, 10000000ull);
+        mbar_wait(&bar[1], 1, 10000000ull);
     }
 }

@@ -464,7 +464,8 @@ int vc4_session_create(vc4_model* m, int slots, int seq, int kv_bits, const floa
               alloc((void**)&s->d_slot, (size_t)(3 * slots + 1) * 4) && alloc((void**)&s->d_next, (size_t)slots * 4) &&
               alloc((void**)&s->d_pos, (size_t)seq * 4 + 16) && alloc((void**)&st.done, 16) && alloc((void**)&st.err, 16) &&
               alloc((void**)&st.sdown, (size_t)L * slots * 2 * D * 8) &&
-              alloc((void**)&st.xrec, (size_t)slots * batch_record_bytes(m->d));
+              alloc((void**)&st.xrec, (size_t)slots * batch_record_bytes(m->d)) &&
+              alloc((void**)&st.hrec, (size_t)slots * batch_hidden_bytes(m->d));
     st.batch_ok = batch_path_fits(m->d, slots) ? 1 : 0;
     if (!ok) { vc4_session_destroy(s); return fail(VC4_ECUDA, "session allocation failed (slots*seq too large?)"); }
     s->d_tok = s->d_slot + slots;
@@ -500,7 +501,7 @@ void vc4_session_destroy(vc4_session* s) {
     for (void* p : {(void*)st.x, (void*)st.x1, (void*)st.qkv, (void*)st.att, (void*)st.h, (void*)st.logits,
                     (void*)st.best, (void*)st.next, (void*)st.route, (void*)st.kv, (void*)st.rope_cos,
                     (void*)st.rope_sin, (void*)s->d_slot, (void*)s->d_next, (void*)s->d_pos, (void*)st.done, (void*)st.err,
-                    (void*)st.sdown, (void*)st.xrec})
+                    (void*)st.sdown, (void*)st.xrec, (void*)st.hrec})
         if (p) cudaFree(p);
     if (s->h_pin) cudaFreeHost(s->h_pin);
     if (s->h_logits) cudaFreeHost(s->h_logits);

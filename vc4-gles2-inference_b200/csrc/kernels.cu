@@ -58,6 +58,11 @@ size_t batch_record_bytes(const DModel& m) {
     return std::max(std::max(xrec_bytes(m.mats[m.qkv[0]]), xrec_bytes(m.mats[m.wo[0]])),
                     std::max(xrec_bytes(w1), xrec_bytes(m.mats[m.logits_mat])));
 }
+size_t batch_hidden_bytes(const DModel& m) {
+    const DMat& wa = m.h.experts ? m.mats[m.e_w1[0] + 2] : m.mats[m.w2a[0]];
+    const DMat& wb = m.ffn_chunked ? (m.h.experts ? m.mats[m.e_w1[0] + 3] : m.mats[m.w2b[0]]) : wa;
+    return down_rec(wa, wb, m.ffn_chunked).bytes;
+}
 bool batch_path_fits(const DModel& m, int slots) {
     for (int l = 0; l < m.h.layers; ++l) {
         const int eb = m.h.experts ? m.e_w1[(size_t)l * m.h.experts] : -1;

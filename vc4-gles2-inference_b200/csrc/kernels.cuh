@@ -1075,7 +1075,7 @@ __device__ __forceinline__ void logits_finish(State& s, int b0, int nb, const Fi
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence();
-        last = atomicAdd(s.done, 1) == (int)(gridDim.x * gridDim.y) - 1;
+        last = atomicAdd(s.done, 1) == (int)(gridDim.x * gridDim.y * gridDim.z) - 1;
     }
     __syncthreads();
     if (!last) return;
@@ -1815,10 +1815,21 @@ struct Ops {
 };
 
 // Launchers of the many-sequence path (batch.cuh).
+constexpr int kMmGroupMax = 32;   // staged records per CTA at a time (two CTAs fit an SM)
+
+// Grid z of a matmat launch: split the sequences so that about two CTAs per
+// SM exist, each keeping at least 4 sequences (expected per expert for MoE).
+inline int mm_splits(const DModel& m, int ctas, int seqs) {
+    const int target = 2 * std::max(1, m.num_sms);
+    int z = (target + ctas - 1) / ctas;
+    z = std::min(z, std::max(1, seqs / 4));
+    return std::max(1, z);
+}
+
 template <int WT>
 struct BOps {
     static void prep(const DModel& m, const State& s, const Batch& bt, int layer, int op, const DMat& W,
-                     cudaStream_t st) {
+                     cudaStream_t st, DownRec dr = DownRec{}) {
         Dims d = dims_of(m, s);
         const float* rw = op == kOpWo ? m.d_rms_att
                         : op == kOpQkv ? m.d_rms_att + (size_t)layer * d.dim
@@ -1827,18 +1838,21 @@ struct BOps {
         DMat router{};
         if (op == kOpGate && d.experts) router = m.mats[m.router[layer]];
         launch_pdl(k_prep<WT>, dim3(bt.n), sizeof(int16_t) * (size_t)d.dim, st, W, m.mats[m.emb_mat], m.d_emb_scale,
-                   rw, router, s, bt, d, layer, op);
+                   rw, router, s, bt, d, layer, op, dr);
     }
     template <int OP>
     static void mm(const DModel& m, const State& s, const Batch& bt, int layer, const MatSet& M, int experts, int hs,
-                   const Finalize& fz, cudaStream_t st) {
+                   const Finalize& fz, cudaStream_t st, DownRec dr = DownRec{}) {
         Dims d = dims_of(m, s);
         const DMat& W = M.a[0];
         const int nm = OP == kOpGate ? 2 : 1;
+        const int ctas = W.rblocks * (experts ? experts : 1);
+        const int splits = mm_splits(m, ctas, bt.n / (experts ? experts : 1));
         const size_t fixed = mm_smem(W, nm, 0, bt.n);
-        const int group = std::max(1, std::min(bt.n, (int)((kMaxDynSmem - fixed) / xrec_bytes(W))));
-        launch_pdl(k_mm<WT, OP>, dim3(W.rblocks, experts ? experts : 1), mm_smem(W, nm, group, bt.n), st, M, s, bt, d,
-                   layer, group, hs, fz);
+        const int want = (bt.n + splits - 1) / splits;
+        const int group = std::max(1, std::min(std::min(want, kMmGroupMax), (int)((kMaxDynSmem - fixed) / xrec_bytes(W))));
+        launch_pdl(k_mm<WT, OP>, dim3(W.rblocks, experts ? experts : 1, splits), mm_smem(W, nm, group, bt.n), st, M, s,
+                   bt, d, layer, group, hs, fz, dr);
     }
     static void qkv(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
         MatSet M;
@@ -1871,14 +1885,19 @@ struct BOps {
             M2.b[0] = two ? m.mats[m.w2b[layer]] : m.mats[m.w2a[layer]];
         }
         const int hs = layer < (int)m.h.hid_scale.size() ? (int)m.h.hid_scale[layer] : 0;
-        prep(m, s, bt, layer, kOpGate, M.a[0], st);
-        mm<kOpGate>(m, s, bt, layer, M, d.experts, hs, Finalize{}, st);
         const DMat& Wa = M2.a[0];
         const DMat& Wb = M2.b[0];
+        const DownRec dr = down_rec(Wa, Wb, two);
+        prep(m, s, bt, layer, kOpGate, M.a[0], st, dr);
+        mm<kOpGate>(m, s, bt, layer, M, d.experts, hs, Finalize{}, st, dr);
+        const int e = d.experts ? d.experts : 1;
+        const int splits = mm_splits(m, Wa.rblocks * e, bt.n / e);
         const size_t fixed = mmdown_smem(Wa, Wb, two, 0, bt.n);
-        const int group = std::max(1, std::min(bt.n, (int)((kMaxDynSmem - fixed) / down_rec(Wa, Wb, two).bytes)));
-        launch_pdl(k_mmdown<WT>, dim3(Wa.rblocks, d.experts ? d.experts : 1), mmdown_smem(Wa, Wb, two, group, bt.n),
-                   st, M2, s, bt, d, layer, group);
+        const int want = (bt.n + splits - 1) / splits;
+        const int group =
+            std::max(1, std::min(std::min(want, kMmGroupMax), (int)((kMaxDynSmem - fixed) / down_rec(Wa, Wb, two).bytes)));
+        launch_pdl(k_mmdown<WT>, dim3(Wa.rblocks, e, splits), mmdown_smem(Wa, Wb, two, group, bt.n), st, M2, s, bt, d,
+                   layer, group);
     }
 };
 

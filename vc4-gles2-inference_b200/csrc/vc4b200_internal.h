@@ -140,6 +140,7 @@ struct State {                      // per-slot activations, [slot][...]
     int* err = nullptr;              // kernel self-check word: nonzero = a launch reserved too little shared memory
     long long* sdown = nullptr;      // w2 partial sums [layers][slots][2][dim] (int64, zero between uses)
     char* xrec = nullptr;            // many-sequence path: staged matvec inputs [slots][record]
+    char* hrec = nullptr;            // many-sequence path: staged w2 inputs [slots][record]
     int batch_ok = 0;                // the many-sequence kernels fit this model
 };
 
@@ -158,6 +159,7 @@ void launch_logits(const DModel& m, const State& s, const Batch& b, int* next, i
 void launch_matvec_raw(const DModel& m, int mat, const int16_t* xq, int n, int32_t* out, cudaStream_t st);
 int kernel_launches_per_step(const DModel& m, const State& s, int n);
 size_t batch_record_bytes(const DModel& m);
+size_t batch_hidden_bytes(const DModel& m);
 bool batch_path_fits(const DModel& m, int slots);
 // Shape limits of the kernels (checked at upload / session creation).
 bool attention_fits(int seq, int head_dim, int kv_bits, int kv_dim, int group);
