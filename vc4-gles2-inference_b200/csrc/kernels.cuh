@@ -1818,11 +1818,12 @@ struct Ops {
 constexpr int kMmGroupMax = 32;   // staged records per CTA at a time (two CTAs fit an SM)
 
 // Grid z of a matmat launch: split the sequences so that about two CTAs per
-// SM exist, each keeping at least 4 sequences (expected per expert for MoE).
-inline int mm_splits(const DModel& m, int ctas, int seqs) {
+// SM exist, each keeping at least `min_seqs` sequences (the expected count per
+// expert for MoE); a CTA's warps serve kMmNI sequences each per sweep.
+inline int mm_splits(const DModel& m, int ctas, int seqs, int min_seqs) {
     const int target = 2 * std::max(1, m.num_sms);
     int z = (target + ctas - 1) / ctas;
-    z = std::min(z, std::max(1, seqs / 4));
+    z = std::min(z, std::max(1, seqs / min_seqs));
     return std::max(1, z);
 }
 
@@ -1847,7 +1848,7 @@ struct BOps {
         const DMat& W = M.a[0];
         const int nm = OP == kOpGate ? 2 : 1;
         const int ctas = W.rblocks * (experts ? experts : 1);
-        const int splits = mm_splits(m, ctas, bt.n / (experts ? experts : 1));
+        const int splits = mm_splits(m, ctas, bt.n / (experts ? experts : 1), 4);
         const size_t fixed = mm_smem(W, nm, 0, bt.n);
         const int want = (bt.n + splits - 1) / splits;
         const int group = std::max(1, std::min(std::min(want, kMmGroupMax), (int)((kMaxDynSmem - fixed) / xrec_bytes(W))));
@@ -1891,7 +1892,7 @@ struct BOps {
         prep(m, s, bt, layer, kOpGate, M.a[0], st, dr);
         mm<kOpGate>(m, s, bt, layer, M, d.experts, hs, Finalize{}, st, dr);
         const int e = d.experts ? d.experts : 1;
-        const int splits = mm_splits(m, Wa.rblocks * e, bt.n / e);
+        const int splits = mm_splits(m, Wa.rblocks * e, bt.n / e, kWarps * kMmNI);
         const size_t fixed = mmdown_smem(Wa, Wb, two, 0, bt.n);
         const int want = (bt.n + splits - 1) / splits;
         const int group =
