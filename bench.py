@@ -408,12 +408,18 @@ def run_ours(args, cfg, dist):
         pass
     hbm = float(peaks.get("hbm_gbs") or 6650.0)
     achieved = op_bytes[dom] / (op_ms[dom] / 1000.0) / 1e9
+    # DRAM bytes of one launch of the dominant op from an ncu capture
+    # (profiles/traffic_<config>.txt: "op bytes [kv_positions]"; an attention
+    # capture is scaled by the KV positions, which its traffic is proportional to)
     traffic = None
     try:
         with open(os.path.join(ROOT, "profiles", "traffic_%s.txt" % cfg.key)) as f:
             for line in f:
-                if line.startswith(dom + " "):
-                    traffic = float(line.split()[1])
+                parts = line.split()
+                if parts and parts[0] == dom:
+                    traffic = float(parts[1])
+                    if len(parts) > 2 and dom == "attention":
+                        traffic *= (prof_pos[0] + 1) / float(parts[2])
     except OSError:
         pass
     step_bytes = sum(op_bytes[k] * (1 if k == "logits" else L) for k in op_bytes)
