@@ -61,11 +61,12 @@ def model_path(cfg) -> str:
     from vc4b200 import mmcf_writer
     d = os.path.join(tempfile.gettempdir(), "vc4b200_models")
     os.makedirs(d, exist_ok=True)
-    path = os.path.join(d, "%s_%d.mmcf" % (cfg.key, cfg.seed))
+    key = cfg.extra.get("model", cfg.key)   # the c4 sweep shares one container
+    path = os.path.join(d, "%s_%d.mmcf" % (key, cfg.seed))
     want = None
     try:
         with open(os.path.join(ROOT, "tests", "golden", "golden.json")) as f:
-            want = json.load(f)["containers"].get(cfg.key, {}).get("sha256")
+            want = json.load(f)["containers"].get(key, {}).get("sha256")
     except OSError:
         pass
     if os.path.exists(path):
@@ -305,10 +306,23 @@ def run_ours(args, cfg, dist):
     B = cfg.batch
     sess = vc4b200.Session(model, slots=B, seq=cfg.seq, kv=KV_NAME[cfg.kv_bits])
     info = model.info
-    prompts = [synth.prompt_tokens(cfg, i) for i in sequence_ids(dist.rank, B)]
     t0 = time.perf_counter()
-    for b in range(B):
-        sess.prefill(prompts[b][:-1], 0, slot=b, want_logits=False)
+    if cfg.extra.get("prefix_restore"):
+        # one prefix prefilled once, saved as MMKV1 and restored into every slot;
+        # the sequences part at the prefix's last position with distinct tokens
+        prefix = synth.prompt_tokens(cfg, 0)
+        sess.prefill(prefix[:-1], 0, slot=0, want_logits=False)
+        mmkv = os.path.join(tempfile.gettempdir(), "vc4b200_prefix_%d_%d.mmkv" % (os.getpid(), dist.rank))
+        sess.save_prefix_cache(mmkv, prefix[:-1])
+        for b in range(1, B):
+            sess.load_prefix_cache(mmkv, slot=b)
+        os.unlink(mmkv)
+        os.unlink(mmkv + ".json") if os.path.exists(mmkv + ".json") else None
+        prompts = [prefix[:-1] + [(prefix[-1] + 97 * i) % info.vocab] for i in sequence_ids(dist.rank, B)]
+    else:
+        prompts = [synth.prompt_tokens(cfg, i) for i in sequence_ids(dist.rank, B)]
+        for b in range(B):
+            sess.prefill(prompts[b][:-1], 0, slot=b, want_logits=False)
     prefill_s = time.perf_counter() - t0
     P = cfg.prompt
     stream = torch.cuda.ExternalStream(sess.stream())

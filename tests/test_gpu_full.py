@@ -95,11 +95,11 @@ def test_moe_batch_full_shape(gpu, n):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("n", [4, 9])
+@pytest.mark.parametrize("n", [4, 9, 33])
 def test_prefix_restore_batch_full_shape(gpu, tmp_path, n):
     """c4: one prefix prefilled once, saved as MMKV1, restored into every slot
     of a batch, then greedy decode of all slots in one pass (KV q8; 9 runs the
-    many-sequence kernels)."""
+    many-sequence kernels, 33 their tcgen05 tensor-core form)."""
     cfg = synth.CONFIGS["c4"]
     path = _path("c4")
     om = oracle.Model(path)

@@ -125,11 +125,11 @@ __global__ void __launch_bounds__(kThreads) k_prep(DMat W, DMat E, const float* 
 // and the list is compacted with warp ballots.
 __device__ __forceinline__ int mm_members(const State& s, const Dims& d, int n, int layer, int expert, bool moe,
                                           int* members) {
-    __shared__ int wc[kWarps];
+    __shared__ int wc[32];
     __shared__ int base;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = (int)blockDim.x >> 5;   // any block size
     if (threadIdx.x == 0) base = 0;
-    for (int r = 0; r < n; r += kThreads) {
+    for (int r = 0; r < n; r += (int)blockDim.x) {
         const int b = r + threadIdx.x;
         const bool f = b < n && (!moe || __ldcg(s.route + (size_t)b * d.layers + layer) == expert);
         const unsigned m = __ballot_sync(0xffffffffu, f);
@@ -139,7 +139,7 @@ __device__ __forceinline__ int mm_members(const State& s, const Dims& d, int n, 
         for (int w = 0; w < warp; ++w) off += wc[w];
         if (f) members[off + __popc(m & ((1u << lane) - 1u))] = b;
         __syncthreads();
-        if (threadIdx.x == 0) for (int w = 0; w < kWarps; ++w) base += wc[w];
+        if (threadIdx.x == 0) for (int w = 0; w < nw; ++w) base += wc[w];
         __syncthreads();
     }
     return base;
@@ -405,4 +405,274 @@ __global__ void __launch_bounds__(kThreads) k_mmdown(MatSet M2, State s, Batch b
         mbar_wait(&bar[1], 0, 10000000ull);
         mbar_wait(&bar[1], 1, 10000000ull);
     }
+}
+
+// ---------------------------------------------------------------------------
+// Tensor-core matmat for q8 weights (tcgen05.mma kind::i8, TMEM accumulators).
+//
+// One CTA (one warpgroup) computes a 128-row tile of one matrix (or of two:
+// w1 and w3 of the ffn, or the two column halves of a chunked w2) for a group
+// of sequences.  The weights are 32-row blocks in HBM; 512-byte bulk copies
+// place chunk j of row block q at shared offset j*2048 + q*512, which is the
+// K-major core-matrix layout with the 8-row groups 128 bytes apart (SBO) and
+// the 16-byte K chunks 2048 bytes apart (LBO).  The sequences' input bytes
+// form the B operand [chunk][sequence][16 bytes] per plane: x' = lo + 256*hi
+// with lo unsigned and hi signed, so every K step is two MMAs (s8 x u8 into
+// one accumulator, s8 x s8 into another) and S = D_lo + 256*D_hi is the exact
+// integer dot (|D| < 2^31 for every shape here).  tcgen05.ld brings row r of
+// the accumulators to thread r of the warpgroup for the usual epilogues.
+// ---------------------------------------------------------------------------
+
+constexpr int kOpDown = 4;
+constexpr int kTcThreads = 128;
+
+__device__ __forceinline__ uint64_t umma_sdesc(unsigned addr, unsigned lbo, unsigned sbo) {
+    uint64_t d = 0;
+    d |= (uint64_t)((addr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;   // descriptor version (sm_100); base offset 0, no swizzle
+    return d;
+}
+__host__ __device__ constexpr uint32_t umma_idesc_i8(bool b_signed, int m, int n) {
+    // D s32, A s8 (K-major), B u8 or s8 (K-major), shape m x n
+    return (2u << 4) | (1u << 7) | ((b_signed ? 1u : 0u) << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+__device__ __forceinline__ void umma_i8(uint32_t tmem, uint64_t da, uint64_t db, uint32_t idesc, uint32_t accumulate) {
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n"
+                 ::"r"(tmem), "l"(da), "l"(db), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0) : "memory");
+}
+__device__ __forceinline__ void umma_commit(unsigned long long* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// 16 consecutive 32-bit accumulator columns of this thread's TMEM lane
+__device__ __forceinline__ void tmem_ld16(uint32_t addr, uint32_t (&v)[16]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+                   "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+                 : "r"(addr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+struct TcPass {        // one matrix of a tensor-core matmat and where its B bytes live in a record
+    DMat W;
+    int lo_off, hi_off;
+};
+struct TcArgs {
+    TcPass p[2];
+    int npass;
+    int rec_bytes;       // bytes per sequence record (State::xrec or State::hrec)
+    int from_hrec;       // the records are w2 inputs (State::hrec)
+    int group;           // sequences per MMA group (multiple of 16)
+    int tmem_cols;       // power of two >= 2 * npass * group
+    int hs;
+    DownRec dr;
+};
+
+__host__ __device__ inline int tc_kchunks(const DMat& W) { return (W.nchunks + 1) & ~1; }   // even: K steps of 32
+__host__ __device__ inline size_t tc_smem(const TcArgs& a, int n) {
+    int kc = 0;
+    for (int m = 0; m < a.npass; ++m) kc = kc > tc_kchunks(a.p[m].W) ? kc : tc_kchunks(a.p[m].W);
+    return (size_t)kc * 2048 + (size_t)kc * a.group * 32 + align16(sizeof(int) * (size_t)n) + 64;
+}
+
+template <int OP>
+__global__ void __launch_bounds__(kTcThreads) k_tmm(TcArgs a, State s, Batch bt, Dims d, int layer, Finalize fz) {
+    const int tile = blockIdx.x, expert = blockIdx.y;
+    const int n = bt.n, G = a.group;
+    if (!smem_ok(tc_smem(a, n), s.err)) return;
+    int kc = 0;
+    for (int m = 0; m < a.npass; ++m) kc = max(kc, tc_kchunks(a.p[m].W));
+    char* sm = SmemLayout::base();
+    uint8_t* sa = reinterpret_cast<uint8_t*>(sm);                        // [kc][128 rows][16]
+    uint8_t* sbl = sa + (size_t)kc * 2048;                              // [kc][G][16] lo plane
+    uint8_t* sbh = sbl + (size_t)kc * G * 16;                            // [kc][G][16] hi plane
+    int* members = reinterpret_cast<int*>(sbh + (size_t)kc * G * 16);
+    unsigned long long* bar = reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(members) +
+                                                                   align16(sizeof(int) * (size_t)n));
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 2);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const TcPass P0 = a.p[0], P1 = a.p[a.npass > 1 ? 1 : 0];   // the passes have equal shapes
+    auto issue_a = [&](const DMat& W) {   // warp 0: the tile's weights, one 512-byte copy per (chunk, row block)
+        const int nch = W.nchunks;
+        const int nq = min(4, W.rblocks - tile * 4);
+        if (lane == 0) mbar_expect_tx(&bar[0], (unsigned)(nq * nch * 512));
+        __syncwarp();
+        for (int i = lane; i < nq * nch; i += 32) {
+            const int q = i / nch, j = i % nch;
+            bulk_g2s(sa + (size_t)j * 2048 + q * 512, W.body + ((size_t)(tile * 4 + q) * nch + j) * 512, 512u, &bar[0]);
+        }
+    };
+    if (warp == 0) {
+        if (lane == 0) {
+            mbar_init(&bar[0], 1);
+            mbar_init(&bar[1], 1);
+            mbar_fence_init();
+        }
+        __syncwarp();
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tslot)),
+                     "r"(a.tmem_cols) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        issue_a(P0.W);
+    }
+    // zero the padding the copies do not cover: row blocks past the matrix, the odd K chunk
+    {
+        const DMat& W = P0.W;
+        const int nq = min(4, W.rblocks - tile * 4);
+        for (int i = tid; i < kc * 128; i += kTcThreads) {
+            const int j = i / 128, r = i % 128;
+            if (j >= W.nchunks || r / 32 >= nq) *reinterpret_cast<uint4*>(sa + (size_t)j * 2048 + r * 16) = make_uint4(0, 0, 0, 0);
+        }
+    }
+    pdl_launch_dependents();
+    pdl_wait();
+    const int nall = mm_members(s, d, n, layer, expert, false, members);
+    const int per = (nall + (int)gridDim.z - 1) / (int)gridDim.z;
+    const int m0 = min(nall, (int)blockIdx.z * per), nm = min(nall, m0 + per) - m0;
+    members += m0;
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
+    const char* recs = a.from_hrec ? s.hrec : s.xrec;
+    int a_issued = 1, a_waited = 0;   // weight-tile loads issued / waited for (phases of bar[0])
+    unsigned mph = 0;                 // phase of bar[1] (MMA completion)
+    bool ok = true;
+    const int row = tile * 128 + tid;
+    for (int g0 = 0; g0 < nm && ok; g0 += G) {
+        const int gn = min(G, nm - g0);
+        const int gp = (gn + 15) & ~15;                 // MMA N: a multiple of 16
+        for (int m = 0; m < a.npass && ok; ++m) {
+            const TcPass& P = m ? P1 : P0;
+            const int nch = P.W.nchunks;
+            if (a.npass > 1 && (m > 0 || g0 > 0)) {
+                // reload the weight tile of this pass (the previous pass's MMAs are complete)
+                if (warp == 0) { fence_proxy_async(); issue_a(P.W); }
+                ++a_issued;
+            }
+            // B planes of this group: [chunk][sequence][16 bytes]
+            if (m == 0 || P.lo_off != P0.lo_off) {
+                for (int i = tid; i < kc * gp; i += kTcThreads) {
+                    const int j = i / gp, q = i % gp;
+                    uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
+                    if (q < gn && j < nch) {
+                        const char* r = recs + (size_t)members[g0 + q] * a.rec_bytes;
+                        lo = __ldcg(reinterpret_cast<const uint4*>(r + P.lo_off) + j);
+                        hi = __ldcg(reinterpret_cast<const uint4*>(r + P.hi_off) + j);
+                    }
+                    *reinterpret_cast<uint4*>(sbl + ((size_t)j * gp + q) * 16) = lo;
+                    *reinterpret_cast<uint4*>(sbh + ((size_t)j * gp + q) * 16) = hi;
+                }
+            }
+            fence_proxy_async();
+            tc_fence_before();
+            __syncthreads();
+            tc_fence_after();
+            if (tid == 0) {
+                if (a_waited < a_issued) ok = mbar_wait(&bar[0], (unsigned)a_waited & 1u);
+                if (ok) {
+                    const uint32_t dlo = tmem + (uint32_t)(m * 2 * gp), dhi = dlo + (uint32_t)gp;
+                    const uint32_t il = umma_idesc_i8(false, 128, gp), ih = umma_idesc_i8(true, 128, gp);
+                    for (int k = 0; k < kc / 2; ++k) {
+                        const uint64_t da = umma_sdesc(smem_addr(sa) + k * 4096, 2048, 128);
+                        const uint64_t dbl = umma_sdesc(smem_addr(sbl) + k * 2 * gp * 16, gp * 16, 128);
+                        const uint64_t dbh = umma_sdesc(smem_addr(sbh) + k * 2 * gp * 16, gp * 16, 128);
+                        umma_i8(dlo, da, dbl, il, k > 0);
+                        umma_i8(dhi, da, dbh, ih, k > 0);
+                    }
+                    umma_commit(&bar[1]);
+                }
+            }
+            a_waited = a_issued;
+            ok = !__syncthreads_or(!(tid != 0 || ok));
+            if (!ok) break;
+            ok = !__syncthreads_or(!mbar_wait(&bar[1], mph & 1u));
+            ++mph;
+            tc_fence_after();
+        }
+        if (!ok) break;
+        // epilogue: row `row` (this thread's TMEM lane), sequences of the group in pieces of 16
+        const uint32_t lane_base = tmem + ((uint32_t)(32 * warp) << 16);
+        for (int c = 0; c < gp; c += 16) {
+            uint32_t lo0[16], hi0[16], lo1[16], hi1[16];
+            tmem_ld16(lane_base + c, lo0);
+            tmem_ld16(lane_base + gp + c, hi0);
+            if (a.npass > 1) {
+                tmem_ld16(lane_base + 2 * gp + c, lo1);
+                tmem_ld16(lane_base + 3 * gp + c, hi1);
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const int q = c + i;
+                if (q >= gn) break;
+                const int b = members[g0 + q];
+                const long long S0 = (long long)(int)lo0[i] + 256LL * (long long)(int)hi0[i];
+                const long long S1 = a.npass > 1 ? (long long)(int)lo1[i] + 256LL * (long long)(int)hi1[i] : 0;
+                const bool live = row < P0.W.rows;
+                const int* gs = reinterpret_cast<const int*>(recs + (size_t)b * a.rec_bytes + 2 * (size_t)x_stride(P0.W));
+                if (OP == kOpQkv || OP == kOpWo) {
+                    if (!live) continue;
+                    const int k = gs[g_stride(P0.W)];
+                    const float o = __fmul_rn(__fmul_rn((float)mv_epi(S0, __ldg(P0.W.rscale + row)), 1.0f / 256.0f),
+                                              ldexpf(1.0f, -k));
+                    if (OP == kOpQkv) {
+                        s.qkv[(size_t)b * (d.dim + 2 * d.kv_dim) + row] = o;
+                    } else {
+                        const float xr = __fmul_rn((float)__ldcg(s.x + (size_t)b * d.dim + row), 1.0f / 256.0f);
+                        s.x1[(size_t)b * d.dim + row] = (int16_t)q16h(__fadd_rn(xr, o));
+                    }
+                } else if (OP == kOpGate) {
+                    if (!live) continue;
+                    const int g = mv_epi(S0, __ldg(P0.W.rscale + row));
+                    const int u = mv_epi(S1, __ldg(P1.W.rscale + row));
+                    float y = swiglu1(__fmul_rn((float)g, 1.0f / 256.0f), __fmul_rn((float)u, 1.0f / 256.0f));
+                    if (a.hs > 0) y = __fmul_rn(y, ldexpf(1.0f, -a.hs));   // metadata key 15 store scale
+                    const int qv = q16s(y);
+                    const int half = (d.chunk < d.ffn && row >= d.chunk) ? 1 : 0;
+                    const int col = row - (half ? d.chunk : 0);
+                    char* hr = s.hrec + (size_t)b * a.dr.bytes;
+                    hr[(half ? a.dr.lo_b : a.dr.lo_a) + col] = (char)(qv & 0xFF);
+                    hr[(half ? a.dr.hi_b : a.dr.hi_a) + col] = (char)(qv >> 8);
+                } else if (OP == kOpDown) {
+                    if (!live) continue;
+                    float o2 = __fmul_rn((float)mv_epi(S0, __ldg(P0.W.rscale + row)), 1.0f / 256.0f);
+                    if (a.npass > 1) {
+                        const int vb = mv_epi(S1, __ldg(P1.W.rscale + row));
+                        // add_q16 of the two chunk outputs (session.cpp:2052-2067)
+                        o2 = __fmul_rn((float)q16h(__fadd_rn(o2, __fmul_rn((float)vb, 1.0f / 256.0f))), 1.0f / 256.0f);
+                    }
+                    const float x1 = __fmul_rn((float)__ldcg(s.x1 + (size_t)b * d.dim + row), 1.0f / 256.0f);
+                    s.x[(size_t)b * d.dim + row] = (int16_t)q16h(__fadd_rn(x1, o2));
+                } else {
+                    unsigned long long key = 0ull;
+                    if (live) {
+                        const int v = mv_epi(S0, __ldg(P0.W.rscale + row));
+                        s.logits[(size_t)b * d.vocab + row] = v;
+                        key = logit_key(v, row);
+                    }
+                    for (int o = 16; o; o >>= 1) {
+                        const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, key, o);
+                        key = k2 > key ? k2 : key;
+                    }
+                    if (lane == 0 && key) atomicMax(&s.best[b], key);
+                }
+            }
+        }
+        tc_fence_before();
+        __syncthreads();   // accumulators and B planes are free for the next group
+        tc_fence_after();
+    }
+    if (!ok && tid == 0) {
+        // a copy or the MMAs did not complete in time: report, and wait (bounded) before freeing TMEM
+        atomicExch(s.err, kErrCopyTimeout);
+        mbar_wait(&bar[0], (unsigned)a_waited & 1u, 10000000ull);
+        mbar_wait(&bar[1], mph & 1u, 10000000ull);
+    }
+    __syncthreads();
+    if (warp == 0)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(a.tmem_cols) : "memory");
+    if (OP == kOpLogits) logits_finish(s, 0, n, fz);
 }

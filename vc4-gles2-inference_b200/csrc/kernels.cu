@@ -44,7 +44,9 @@ void launch_logits(const DModel& m, const State& s, const Batch& b, int* next, i
         MatSet M;
         M.a[0] = M.b[0] = W;
         BOps<W_Q8>::prep(m, s, b, m.h.layers - 1, kOpLogits, W, st);
-        BOps<W_Q8>::mm<kOpLogits>(m, s, b, m.h.layers - 1, M, 0, 0, fz, st);
+        if (!tc_launch<kOpLogits>(m, s, b, m.h.layers - 1, W, nullptr, (int)xrec_bytes(W), 0, 0, x_stride(W), 0, 0, 0,
+                                  DownRec{}, fz, st))
+            BOps<W_Q8>::mm<kOpLogits>(m, s, b, m.h.layers - 1, M, 0, 0, fz, st);
         return;
     }
     VC4_MAXC(maxc_for(W.nchunks), LogitsOps::logits, m, s, b, fz, st);

@@ -1678,6 +1678,23 @@ void launch_pdl(void (*kernel)(KArgs...), dim3 grid, size_t smem, cudaStream_t s
     cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
+// launch_pdl with a block size other than kThreads.
+template <typename... KArgs, typename... Args>
+void launch_pdl_block(void (*kernel)(KArgs...), dim3 grid, int block, size_t smem, cudaStream_t st, Args... args) {
+    set_smem(kernel, smem);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 #include "batch.cuh"
 
 constexpr int kNB = 4;   // inputs per CTA for the batched matvecs
@@ -1827,6 +1844,44 @@ inline int mm_splits(const DModel& m, int ctas, int seqs, int min_seqs) {
     return std::max(1, z);
 }
 
+// Tensor-core matmat launch (q8 weights, sequences not split by expert);
+// false when the shapes do not fit, the caller then runs k_mm.
+// Below kTcMinSeqs sequences a 128-row tile leaves most SMs idle and the CUDA-
+// core kernel is faster; the logits head (many tiles) uses the tensor cores
+// from kBatchMin.
+constexpr int kTcMinSeqs = 32;
+
+template <int OP>
+inline bool tc_launch(const DModel& m, const State& s, const Batch& bt, int layer, const DMat& W0, const DMat* W1,
+                      int rec_bytes, int from_hrec, int lo0, int hi0, int lo1, int hi1, int hs, const DownRec& dr,
+                      const Finalize& fz, cudaStream_t st) {
+    if (OP != kOpLogits && bt.n < kTcMinSeqs) return false;
+    if (W0.wtype != W_Q8 || (W1 && (W1->wtype != W_Q8 || W1->rblocks != W0.rblocks || W1->nchunks != W0.nchunks)))
+        return false;
+    TcArgs a{};
+    a.p[0] = TcPass{W0, lo0, hi0};
+    a.npass = W1 ? 2 : 1;
+    a.p[1] = W1 ? TcPass{*W1, lo1, hi1} : a.p[0];
+    a.rec_bytes = rec_bytes;
+    a.from_hrec = from_hrec;
+    a.hs = hs;
+    a.dr = dr;
+    int g = std::min(a.npass == 2 ? 64 : 128, (bt.n + 15) & ~15);
+    for (;; g -= 16) {
+        a.group = g;
+        if (tc_smem(a, bt.n) <= kMaxDynSmem || g <= 16) break;
+    }
+    if (tc_smem(a, bt.n) > kMaxDynSmem) return false;
+    int cols = 32;
+    while (cols < 2 * a.npass * a.group) cols *= 2;
+    a.tmem_cols = cols;
+    Dims d = dims_of(m, s);
+    const int tiles = (W0.rows + 127) / 128;
+    const int splits = mm_splits(m, tiles, bt.n, 16);
+    launch_pdl_block(k_tmm<OP>, dim3(tiles, 1, splits), kTcThreads, tc_smem(a, bt.n), st, a, s, bt, d, layer, fz);
+    return true;
+}
+
 template <int WT>
 struct BOps {
     static void prep(const DModel& m, const State& s, const Batch& bt, int layer, int op, const DMat& W,
@@ -1859,13 +1914,19 @@ struct BOps {
         MatSet M;
         M.a[0] = M.b[0] = m.mats[m.qkv[layer]];
         prep(m, s, bt, layer, kOpQkv, M.a[0], st);
-        mm<kOpQkv>(m, s, bt, layer, M, 0, 0, Finalize{}, st);
+        const DMat& W = M.a[0];
+        if (!tc_launch<kOpQkv>(m, s, bt, layer, W, nullptr, (int)xrec_bytes(W), 0, 0, x_stride(W), 0, 0, 0, DownRec{},
+                               Finalize{}, st))
+            mm<kOpQkv>(m, s, bt, layer, M, 0, 0, Finalize{}, st);
     }
     static void wo(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
         MatSet M;
         M.a[0] = M.b[0] = m.mats[m.wo[layer]];
         prep(m, s, bt, layer, kOpWo, M.a[0], st);
-        mm<kOpWo>(m, s, bt, layer, M, 0, 0, Finalize{}, st);
+        const DMat& W = M.a[0];
+        if (!tc_launch<kOpWo>(m, s, bt, layer, W, nullptr, (int)xrec_bytes(W), 0, 0, x_stride(W), 0, 0, 0, DownRec{},
+                              Finalize{}, st))
+            mm<kOpWo>(m, s, bt, layer, M, 0, 0, Finalize{}, st);
     }
     static void ffn(const DModel& m, const State& s, const Batch& bt, int layer, cudaStream_t st) {
         Dims d = dims_of(m, s);
@@ -1890,7 +1951,14 @@ struct BOps {
         const DMat& Wb = M2.b[0];
         const DownRec dr = down_rec(Wa, Wb, two);
         prep(m, s, bt, layer, kOpGate, M.a[0], st, dr);
-        mm<kOpGate>(m, s, bt, layer, M, d.experts, hs, Finalize{}, st, dr);
+        const DMat& W1 = M.a[0];
+        const bool tc = d.experts == 0 &&
+                        tc_launch<kOpGate>(m, s, bt, layer, W1, &M.b[0], (int)xrec_bytes(W1), 0, 0, x_stride(W1), 0,
+                                           x_stride(W1), hs, dr, Finalize{}, st);
+        if (!tc) mm<kOpGate>(m, s, bt, layer, M, d.experts, hs, Finalize{}, st, dr);
+        if (tc && tc_launch<kOpDown>(m, s, bt, layer, Wa, two ? &Wb : nullptr, (int)dr.bytes, 1, (int)dr.lo_a,
+                                     (int)dr.hi_a, (int)dr.lo_b, (int)dr.hi_b, 0, dr, Finalize{}, st))
+            return;
         const int e = d.experts ? d.experts : 1;
         const int splits = mm_splits(m, Wa.rblocks * e, bt.n / e, kWarps * kMmNI);
         const size_t fixed = mmdown_smem(Wa, Wb, two, 0, bt.n);

@@ -72,7 +72,13 @@ CONFIGS = {
     "c2": Config("c2", MM3_MOE, "q4", 8, 512, 256, 128, batch=64),
     "c3": Config("c3", BITCPM, "t3", 16, 1024, 512, 128, head_dedup=True),
     "c3b32": Config("c3b32", BITCPM, "t3", 16, 1024, 512, 128, batch=32, head_dedup=True),
-    "c4": Config("c4", MM3, "q8", 8, 768, 512, 256, batch=16),
+    # config 4: one 512-token prefix prefilled once and restored into every
+    # sequence slot (MMKV1), swept over the sequences per GPU
+    "c4": Config("c4", MM3, "q8", 8, 768, 512, 256, batch=16, extra={"prefix_restore": True}),
+    "c4b1": Config("c4b1", MM3, "q8", 8, 768, 512, 256, batch=1, extra={"model": "c4", "prefix_restore": True}),
+    "c4b128": Config("c4b128", MM3, "q8", 8, 768, 512, 256, batch=128, extra={"model": "c4", "prefix_restore": True}),
+    "c4b1024": Config("c4b1024", MM3, "q8", 8, 768, 512, 256, batch=1024,
+                      extra={"model": "c4", "prefix_restore": True}),
 }
 
 TINY_CONFIGS = {
