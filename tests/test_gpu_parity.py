@@ -89,11 +89,12 @@ def test_matvec_s_matches_oracle(gpu, tiny_paths, key):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("key", ["tiny_q8", "tiny_moe_q4", "tiny_t3"])
-@pytest.mark.parametrize("n", [6, 10, 33])
+@pytest.mark.parametrize("n", [6, 10, 33, 64])
 def test_batched_equals_serial(gpu, tiny_paths, key, n):
     """Several sequences in one pass give each sequence's serial result: 6
     runs the one-sequence kernels four inputs at a time, 10 the many-sequence
-    (prep + matmat) kernels, 33 their tensor-core (tcgen05) form for q8."""
+    (prep + matmat) kernels, 33 their tensor-core (tcgen05) form for q8, 64
+    also the one-CTA-per-head attention for many sequences."""
     cfg = synth.TINY_CONFIGS[key]
     model = vc4b200.Model(gpu, tiny_paths[key])
     prompts = [synth.prompt_tokens(cfg, i)[:10] for i in range(n)]

@@ -81,9 +81,20 @@ bool batch_path_fits(const DModel& m, int slots) {
 // q heads per cluster: two when the group divides by two, else one
 int attn_heads_per_cluster(int group) { return group % 2 == 0 ? 2 : 1; }
 
+// From this many (sequence, KV head, q-head pair) units the one-CTA-per-unit
+// kernel beats the clusters (whose per-CTA softmax is redundant work).
+constexpr int kAttnBatchUnits = 128;
+
 void launch_attention(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st) {
     Dims d = dims_of(m, s);
     const int group = d.heads / d.kv_heads, hq = attn_heads_per_cluster(group);
+    const int units = b.n * d.kv_heads * (group / hq);
+    const size_t smb = attnb_smem_bytes(hq, d.head_dim, d.seq, d.kv_bits);
+    if (units >= kAttnBatchUnits && smb <= kMaxDynSmem && attnb_pairs(hq, d.head_dim) <= 8 * kThreads) {
+        launch_pdl(k_attn_b, dim3(d.kv_heads * (group / hq), b.n), smb, st, (const float*)m.d_q_norm,
+                   (const float*)m.d_k_norm, s, b, d, layer, hq);
+        return;
+    }
     const size_t sm = attn_smem_bytes(hq, d.head_dim, d.seq, d.kv_bits);
     launch_pdl(k_attn, dim3(d.kv_heads * (group / hq) * kAttnCtas, b.n), sm, st, (const float*)m.d_q_norm,
                (const float*)m.d_k_norm, s, b, d, layer, hq);

@@ -1401,6 +1401,54 @@ __device__ __forceinline__ unsigned kv_encode(float x, int kvb, float* dec) {
     return (unsigned)(int)q & 0xFFu;
 }
 
+// Softmax over positions 0..len-1 of hq heads' scores (sc[hh*seq + t]), in
+// place: kWarps / hq warps per head (one when there are more heads than warps),
+// max, exp(s - max) with the double denominator summed lane-strided, by xor
+// shuffles and then across the head's warps in order, p = e / sum.  The order
+// is fixed by hq alone, so every kernel that calls this gets the same bits.
+__device__ void attn_softmax(float* scores, int seq, int len, int hq, float* redf, double* redd) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    {
+        const int wph = hq >= kWarps ? 1 : kWarps / hq;
+        const int hpr = kWarps / wph;             // heads per round
+        const int hw = warp / wph, sub = warp % wph, step = wph * 32;
+        for (int r0 = 0; r0 < hq; r0 += hpr) {
+            const int hh = r0 + hw;
+            const bool act = hw < hpr && hh < hq;
+            float* p = scores + (act ? hh : 0) * seq;
+            float m = -1e30f;
+            if (act)
+                for (int t = sub * 32 + lane; t < len; t += step) m = fmaxf(m, p[t]);
+            for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            if (lane == 0) redf[warp] = m;
+            __syncthreads();
+            double a = 0.0;
+            if (act) {
+                m = redf[hw * wph];
+                for (int k = 1; k < wph; ++k) m = fmaxf(m, redf[hw * wph + k]);
+#pragma unroll 4
+                for (int t = sub * 32 + lane; t < len; t += step) {
+                    const float ev = vexp(__fsub_rn(p[t], m));
+                    p[t] = ev;
+                    a = __dadd_rn(a, (double)ev);
+                }
+            }
+            for (int o = 16; o; o >>= 1) a = __dadd_rn(a, __shfl_xor_sync(0xffffffffu, a, o));
+            if (lane == 0) redd[warp] = a;
+            __syncthreads();
+            if (act) {
+                double tot = redd[hw * wph];
+                for (int k = 1; k < wph; ++k) tot = __dadd_rn(tot, redd[hw * wph + k]);
+                const float fs = __double2float_rn(tot);
+#pragma unroll 4
+                for (int t = sub * 32 + lane; t < len; t += step) p[t] = __fdiv_rn(p[t], fs);
+            }
+        }
+    }
+    __syncthreads();
+
+}
+
 __global__ void __cluster_dims__(kAttnCtas, 1, 1) __launch_bounds__(kThreads)
 k_attn(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int layer, int hq) {
     namespace cg = cooperative_groups;
@@ -1539,47 +1587,8 @@ k_attn(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int 
     }
     cluster.sync();   // the last access to another CTA's shared memory
 
-    // 5. softmax over all positions: kWarps / hq warps per head (one when
-    //    a cluster serves more heads than warps), reductions through shared
-    //    memory in warp order
-    {
-        const int wph = hq >= kWarps ? 1 : kWarps / hq;
-        const int hpr = kWarps / wph;             // heads per round
-        const int hw = warp / wph, sub = warp % wph, step = wph * 32;
-        for (int r0 = 0; r0 < hq; r0 += hpr) {
-            const int hh = r0 + hw;
-            const bool act = hw < hpr && hh < hq;
-            float* p = sm.sc + (act ? hh : 0) * d.seq;
-            float m = -1e30f;
-            if (act)
-                for (int t = sub * 32 + lane; t < len; t += step) m = fmaxf(m, p[t]);
-            for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-            if (lane == 0) sm.redf[warp] = m;
-            __syncthreads();
-            double a = 0.0;
-            if (act) {
-                m = sm.redf[hw * wph];
-                for (int k = 1; k < wph; ++k) m = fmaxf(m, sm.redf[hw * wph + k]);
-#pragma unroll 4
-                for (int t = sub * 32 + lane; t < len; t += step) {
-                    const float ev = vexp(__fsub_rn(p[t], m));
-                    p[t] = ev;
-                    a = __dadd_rn(a, (double)ev);
-                }
-            }
-            for (int o = 16; o; o >>= 1) a = __dadd_rn(a, __shfl_xor_sync(0xffffffffu, a, o));
-            if (lane == 0) sm.redd[warp] = a;
-            __syncthreads();
-            if (act) {
-                double tot = sm.redd[hw * wph];
-                for (int k = 1; k < wph; ++k) tot = __dadd_rn(tot, sm.redd[hw * wph + k]);
-                const float fs = __double2float_rn(tot);
-#pragma unroll 4
-                for (int t = sub * 32 + lane; t < len; t += step) p[t] = __fdiv_rn(p[t], fs);
-            }
-        }
-    }
-    __syncthreads();
+    // 5. softmax over all positions (the same order in every CTA)
+    attn_softmax(sm.sc, d.seq, len, hq, sm.redf, sm.redd);
 
     // 6. P.V for this CTA's V columns: each output's positions split into ks
     //    contiguous ranges, partial sums in double combined in range order
@@ -1603,6 +1612,267 @@ k_attn(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int 
         for (int j = 0; j < ks; ++j) a = __dadd_rn(a, sm.pv[o * ks + j]);
         const int hh = o / nc, i = o % nc;
         s.att[(size_t)b * d.dim + (size_t)(g * group + h0 + hh) * hd + c0 + i] = (int16_t)q16h(__double2float_rn(a));
+    }
+}
+
+
+// Attention for many sequences at once: one CTA (no cluster) per (sequence,
+// KV head, pair of q heads), the sequence's K and then V rows streamed
+// through shared memory in tiles of kAbTile positions (cp.async, double
+// buffered, decoded to fp32).  Scores, softmax and the P.V reductions follow
+// exactly the cluster kernel's orders (sequential fp32 q.k, attn_softmax, and
+// for every output column the same position chunks as the cluster CTA that
+// owns that column, combined in the same order), so a sequence's attention
+// output is the same whichever kernel runs it.
+constexpr int kAbTile = 128;
+
+struct AbSmem {
+    uint8_t* raw;    // 2 x kAbTile x hbytes: cache rows of two tiles
+    float* ft;       // kAbTile x (hd + 4): decoded rows of the current tile
+    double* pv;      // P.V partials, one per (output, chunk)
+    float* q;        // (hq + 1) x hd: q heads, then the new k
+    float* vn;       // hd: the new v
+    float* rc;
+    float* rsn;
+    float* wq;
+    float* wk;
+    float* redf;
+    double* redd;
+    float* sc;       // hq x seq
+};
+
+__host__ __device__ inline int attnb_pairs(int hq, int hd) {   // (output, chunk) pairs of the cluster layout
+    const int vs = attn_vs(hd);
+    int total = 0;
+    for (int c0 = 0; c0 < hd; c0 += vs) {
+        const int nc = (hd - c0) < vs ? (hd - c0) : vs, nout = hq * nc;
+        const int ks = nout >= kThreads ? 1 : (kThreads / nout < 32 ? kThreads / nout : 32);
+        total += nout * ks;
+    }
+    return total;
+}
+__host__ __device__ inline size_t attnb_carve(int hq, int hd, int seq, int kv_bits, char* base, AbSmem* sm) {
+    const int kvb = kv_bits / 8;
+    size_t o = 0;
+    const size_t raw = o; o = align16(o + 2 * (size_t)kAbTile * hd * kvb);
+    const size_t ft = o;  o = align16(o + sizeof(float) * (size_t)kAbTile * (hd + 4));
+    const size_t pv = o;  o = align16(o + sizeof(double) * (size_t)attnb_pairs(hq, hd));
+    const size_t redd = o; o = align16(o + sizeof(double) * kWarps);
+    const size_t q = o;   o = align16(o + sizeof(float) * (size_t)(hq + 1) * hd);
+    const size_t vn = o;  o += sizeof(float) * hd;
+    const size_t rc = o;  o += sizeof(float) * (hd / 2);
+    const size_t rsn = o; o += sizeof(float) * (hd / 2);
+    const size_t wq = o;  o += sizeof(float) * hd;
+    const size_t wk = o;  o += sizeof(float) * hd;
+    const size_t redf = o; o += sizeof(float) * kWarps;
+    const size_t sc = o;  o += sizeof(float) * (size_t)hq * seq;
+    if (sm) {
+        sm->raw = reinterpret_cast<uint8_t*>(base + raw);
+        sm->ft = reinterpret_cast<float*>(base + ft);
+        sm->pv = reinterpret_cast<double*>(base + pv);
+        sm->redd = reinterpret_cast<double*>(base + redd);
+        sm->q = reinterpret_cast<float*>(base + q);
+        sm->vn = reinterpret_cast<float*>(base + vn);
+        sm->rc = reinterpret_cast<float*>(base + rc);
+        sm->rsn = reinterpret_cast<float*>(base + rsn);
+        sm->wq = reinterpret_cast<float*>(base + wq);
+        sm->wk = reinterpret_cast<float*>(base + wk);
+        sm->redf = reinterpret_cast<float*>(base + redf);
+        sm->sc = reinterpret_cast<float*>(base + sc);
+    }
+    return align16(o);
+}
+__host__ __device__ inline size_t attnb_smem_bytes(int hq, int hd, int seq, int kv_bits) {
+    return attnb_carve(hq, hd, seq, kv_bits, nullptr, nullptr);
+}
+
+__global__ void __launch_bounds__(kThreads)
+k_attn_b(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int layer, int hq) {
+    extern __shared__ __align__(16) char smem[];
+    const int hd = d.head_dim, group = d.heads / d.kv_heads, half = hd / 2, hp = hd + 4;
+    if (!smem_ok(attnb_smem_bytes(hq, hd, d.seq, d.kv_bits), s.err)) return;
+    AbSmem sm;
+    attnb_carve(hq, hd, d.seq, d.kv_bits, smem, &sm);
+    const int qsplit = group / hq, g = blockIdx.x / qsplit, split = blockIdx.x % qsplit;
+    const int h0 = split * hq, b = blockIdx.y;
+    const int slot = bt.slot[b], pos = bt.pos[b], len = pos + 1;
+    const int kvb = d.kv_bits / 8, hbytes = hd * kvb, vofs = d.kv_dim * kvb;
+    const int kvec = hbytes / 16, kw = hbytes / 4, vpw = 4 / kvb;
+    const int ntile = (len + kAbTile - 1) / kAbTile;
+    uint8_t* kvbase = s.kv + ((size_t)slot * d.layers + layer) * d.seq * d.row_bytes;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // tile u < ntile: K rows of positions [u*T, ...); tile u >= ntile: V rows
+    auto issue = [&](int u) {
+        const int kind = u >= ntile, t0 = (u % ntile) * kAbTile, nt = min(kAbTile, len - t0);
+        uint8_t* dst = sm.raw + (size_t)(u & 1) * kAbTile * hbytes;
+        for (int v = threadIdx.x; v < nt * kvec; v += kThreads) {
+            const int r = v / kvec, c = v % kvec, t = t0 + r;
+            if (t != pos)
+                cp_async16(dst + r * hbytes + c * 16, kvbase + (size_t)t * d.row_bytes + (kind ? vofs : 0) + g * hbytes + c * 16);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    issue(0);
+    for (int i = threadIdx.x; i < half; i += kThreads) {
+        sm.rc[i] = s.rope_cos[(size_t)pos * half + i];
+        sm.rsn[i] = s.rope_sin[(size_t)pos * half + i];
+    }
+    if (d.qk_norm)
+        for (int i = threadIdx.x; i < hd; i += kThreads) {
+            sm.wq[i] = q_norm[(size_t)layer * hd + i];
+            sm.wk[i] = k_norm[(size_t)layer * hd + i];
+        }
+    pdl_launch_dependents();
+    pdl_wait();
+
+    // q heads, new k and v, qk-norm and RoPE (as the cluster kernel)
+    const float* qkv = s.qkv + (size_t)b * (d.dim + 2 * d.kv_dim);
+    for (int i = threadIdx.x; i < hq * hd; i += kThreads) sm.q[i] = qkv[(g * group + h0) * hd + i];
+    for (int i = threadIdx.x; i < hd; i += kThreads) {
+        sm.q[hq * hd + i] = qkv[d.dim + g * hd + i];
+        sm.vn[i] = qkv[d.dim + d.kv_dim + g * hd + i];
+    }
+    __syncthreads();
+    for (int hh = warp; hh <= hq; hh += kWarps) {
+        float* v = sm.q + hh * hd;
+        if (d.qk_norm) {
+            double acc = 0.0;
+            for (int i = lane; i < hd; i += 32) acc = __dadd_rn(acc, __dmul_rn((double)v[i], (double)v[i]));
+            for (int o = 16; o; o >>= 1) acc = __dadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+            const float ss = __double2float_rn(acc);
+            const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)hd), 1e-6f)));
+            const float* w = hh < hq ? sm.wq : sm.wk;
+            for (int i = lane; i < hd; i += 32) v[i] = __fmul_rn(w[i], __fmul_rn(r, v[i]));
+            __syncwarp();
+        }
+        for (int i = lane; i < half; i += 32) {
+            const int ia = d.rope_half ? i : 2 * i, ib = d.rope_half ? i + half : 2 * i + 1;
+            const float a = v[ia], bb = v[ib], c = sm.rc[i], sv = sm.rsn[i];
+            v[ia] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(bb, sv));
+            v[ib] = __fadd_rn(__fmul_rn(a, sv), __fmul_rn(bb, c));
+        }
+    }
+    __syncthreads();
+    // encode the new row; the first q-head pair's CTA writes it to the cache,
+    // every CTA keeps the decoded values (new k in q[hq], new v in vn)
+    uint8_t* row = kvbase + (size_t)pos * d.row_bytes;
+    for (int e = threadIdx.x; e < 2 * kw; e += kThreads) {
+        const int w = e / kw, c = e % kw, i0 = c * vpw;
+        float* src = w ? sm.vn : sm.q + hq * hd;
+        unsigned word = 0;
+        float dec[4];
+        for (int j = 0; j < vpw; ++j) word |= kv_encode(src[i0 + j], kvb, &dec[j]) << (8 * kvb * j);
+        if (split == 0) *reinterpret_cast<unsigned*>(row + (w ? vofs : 0) + g * hbytes + c * 4) = word;
+        for (int j = 0; j < vpw; ++j) src[i0 + j] = dec[j];
+    }
+    __syncthreads();
+
+    // pass 1: scores, one K tile at a time
+    const float sq = __fsqrt_rn((float)hd);
+    for (int u = 0; u < ntile; ++u) {
+        issue(u + 1);                                   // the next K tile, or the first V tile
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+        __syncthreads();
+        const int t0 = u * kAbTile, nt = min(kAbTile, len - t0);
+        const uint8_t* src = sm.raw + (size_t)(u & 1) * kAbTile * hbytes;
+        for (int v = threadIdx.x; v < nt * kw; v += kThreads) {
+            const int r = v / kw, c = v % kw;
+            float f[4];
+            const int nv = kv_word(reinterpret_cast<const unsigned*>(src + r * hbytes)[c], kvb, f);
+            for (int j = 0; j < nv; ++j)
+                sm.ft[r * hp + c * nv + j] = (t0 + r == pos) ? sm.q[hq * hd + c * nv + j] : f[j];
+        }
+        __syncthreads();
+        for (int e = threadIdx.x; e < nt * hq; e += kThreads) {
+            const int r = e / hq, hh = e % hq;
+            const float4* kr = reinterpret_cast<const float4*>(sm.ft + r * hp);
+            const float4* qh = reinterpret_cast<const float4*>(sm.q + hh * hd);
+            float acc = 0.0f;
+#pragma unroll 4
+            for (int i = 0; i < hd / 4; ++i) {
+                const float4 k4 = kr[i], q4 = qh[i];
+                acc = __fadd_rn(acc, __fmul_rn(q4.x, k4.x));
+                acc = __fadd_rn(acc, __fmul_rn(q4.y, k4.y));
+                acc = __fadd_rn(acc, __fmul_rn(q4.z, k4.z));
+                acc = __fadd_rn(acc, __fmul_rn(q4.w, k4.w));
+            }
+            sm.sc[hh * d.seq + t0 + r] = __fdiv_rn(acc, sq);
+        }
+        __syncthreads();
+    }
+    attn_softmax(sm.sc, d.seq, len, hq, sm.redf, sm.redd);
+
+    // pass 2: P.V in the cluster kernel's (output, chunk) layout; thread e
+    // keeps the double partials of pairs e, e + kThreads, ...
+    const int vs = attn_vs(hd);
+    const int npairs = attnb_pairs(hq, hd);
+    constexpr int kMaxPairs = 8;                        // per thread: npairs <= 8 * kThreads
+    double acc[kMaxPairs];
+    int pa[kMaxPairs], pb[kMaxPairs], pcol[kMaxPairs], phh[kMaxPairs];
+#pragma unroll
+    for (int q = 0; q < kMaxPairs; ++q) {
+        acc[q] = 0.0;
+        pa[q] = pb[q] = 0;
+        pcol[q] = phh[q] = 0;
+        int e = threadIdx.x + q * kThreads;
+        if (e >= npairs) continue;
+        for (int c0 = 0; c0 < hd; c0 += vs) {           // locate the pair's column slice
+            const int nc = min(vs, hd - c0), nout = hq * nc;
+            const int ks = nout >= kThreads ? 1 : min(32, kThreads / nout);
+            if (e < nout * ks) {
+                const int o = e / ks, j = e % ks;
+                const int chunk = (len + ks - 1) / ks;
+                pa[q] = min(len, j * chunk);
+                pb[q] = min(len, pa[q] + chunk);
+                phh[q] = o / nc;
+                pcol[q] = c0 + o % nc;
+                break;
+            }
+            e -= nout * ks;
+        }
+    }
+    for (int u = ntile; u < 2 * ntile; ++u) {
+        if (u + 1 < 2 * ntile) issue(u + 1);
+        else asm volatile("cp.async.commit_group;" ::: "memory");   // keep the group count uniform
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+        __syncthreads();
+        const int t0 = (u - ntile) * kAbTile, nt = min(kAbTile, len - t0);
+        const uint8_t* src = sm.raw + (size_t)(u & 1) * kAbTile * hbytes;
+        for (int v = threadIdx.x; v < nt * kw; v += kThreads) {
+            const int r = v / kw, c = v % kw;
+            float f[4];
+            const int nv = kv_word(reinterpret_cast<const unsigned*>(src + r * hbytes)[c], kvb, f);
+            for (int j = 0; j < nv; ++j) sm.ft[r * hp + c * nv + j] = (t0 + r == pos) ? sm.vn[c * nv + j] : f[j];
+        }
+        __syncthreads();
+#pragma unroll
+        for (int q = 0; q < kMaxPairs; ++q) {
+            const int ta = max(pa[q], t0), tb = min(pb[q], t0 + nt);
+            const float* p = sm.sc + phh[q] * d.seq;
+            double a = acc[q];
+            for (int t = ta; t < tb; ++t) a = __fma_rn((double)p[t], (double)sm.ft[(t - t0) * hp + pcol[q]], a);
+            acc[q] = a;
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int q = 0; q < kMaxPairs; ++q) {
+        const int e = threadIdx.x + q * kThreads;
+        if (e < npairs) sm.pv[e] = acc[q];
+    }
+    __syncthreads();
+    // combine each output's chunks in order and store
+    int base = 0;
+    for (int c0 = 0; c0 < hd; c0 += vs) {
+        const int nc = min(vs, hd - c0), nout = hq * nc;
+        const int ks = nout >= kThreads ? 1 : min(32, kThreads / nout);
+        for (int o = threadIdx.x; o < nout; o += kThreads) {
+            double a = 0.0;
+            for (int j = 0; j < ks; ++j) a = __dadd_rn(a, sm.pv[base + o * ks + j]);
+            const int hh = o / nc, i = o % nc;
+            s.att[(size_t)b * d.dim + (size_t)(g * group + h0 + hh) * hd + c0 + i] = (int16_t)q16h(__double2float_rn(a));
+        }
+        base += nout * ks;
     }
 }
 
