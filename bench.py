@@ -248,6 +248,7 @@ def cpu_decode_rate(cfg, path, steps: int, seconds: float, threads: int) -> dict
     os.environ["OMP_NUM_THREADS"] = str(threads)
     import oracle
     from vc4b200 import synth
+    oracle.set_threads(threads)   # torchrun exports OMP_NUM_THREADS=1 to every rank
     om = oracle.Model(path)
     seqs = max(1, min(cfg.batch, 2))
     tokens_done, t_total = 0, 0.0

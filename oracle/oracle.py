@@ -52,6 +52,8 @@ def lib():
         L.orc_last_route.argtypes = [vp, ip]
         L.orc_expf.restype = C.c_float
         L.orc_expf.argtypes = [C.c_float]
+        L.orc_set_threads.restype = None
+        L.orc_set_threads.argtypes = [C.c_int]
         L.orc_q16.restype = C.c_int16
         L.orc_q16.argtypes = [C.c_float]
         L.orc_kv_q16.restype = C.c_int16
@@ -235,3 +237,9 @@ def ref_summary(path: str):
     if rc != 0:
         raise RuntimeError("reference loader failed (%d)" % rc)
     return json.loads(buf.value.decode())
+
+
+def set_threads(n: int) -> None:
+    """Host threads the oracle's row-parallel matvecs use (the launcher's
+    OMP_NUM_THREADS otherwise, which torchrun sets to 1)."""
+    lib().orc_set_threads(int(n))

@@ -79,6 +79,14 @@ static float pow2i(int k) { /* 2^k for -126 <= k <= 127 */
     uint32_t u = (uint32_t)(k + 127) << 23;
     float f; memcpy(&f, &u, 4); return f;
 }
+void orc_set_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
+
 float orc_expf(float x) {
     if (x != x) return x;
     if (x > 88.72283935546875f) return INFINITY;

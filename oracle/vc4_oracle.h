@@ -72,6 +72,8 @@ int orc_last_route(const orc_session* s, int layer);
 
 /* ---- primitives, for kernel unit tests ---- */
 float orc_expf(float x);
+/* Host threads of the row-parallel matvecs (OpenMP); <= 0 leaves the default. */
+void orc_set_threads(int n);
 /* matvec_s input scaling (gpu_conv.cpp:271-287): returns k, fills xq. */
 int orc_scale_input(const float* x, int n, int16_t* xq);
 /* q16 host quantisation (common.h:188-193). */
