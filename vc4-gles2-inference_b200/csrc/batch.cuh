@@ -553,19 +553,23 @@ __global__ void __launch_bounds__(kTcThreads) k_tmm(TcArgs a, State s, Batch bt,
                 if (warp == 0) { fence_proxy_async(); issue_a(P.W); }
                 ++a_issued;
             }
-            // B planes of this group: [chunk][sequence][16 bytes]
+            // B planes of this group: [chunk][sequence][16 bytes], each 16-byte
+            // piece an independent cp.async (the transpose costs nothing)
             if (m == 0 || P.lo_off != P0.lo_off) {
                 for (int i = tid; i < kc * gp; i += kTcThreads) {
                     const int j = i / gp, q = i % gp;
-                    uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
+                    uint8_t* dl = sbl + ((size_t)j * gp + q) * 16;
+                    uint8_t* dh = sbh + ((size_t)j * gp + q) * 16;
                     if (q < gn && j < nch) {
                         const char* r = recs + (size_t)members[g0 + q] * a.rec_bytes;
-                        lo = __ldcg(reinterpret_cast<const uint4*>(r + P.lo_off) + j);
-                        hi = __ldcg(reinterpret_cast<const uint4*>(r + P.hi_off) + j);
+                        cp_async16(dl, r + P.lo_off + (size_t)j * 16);
+                        cp_async16(dh, r + P.hi_off + (size_t)j * 16);
+                    } else {
+                        *reinterpret_cast<uint4*>(dl) = make_uint4(0, 0, 0, 0);
+                        *reinterpret_cast<uint4*>(dh) = make_uint4(0, 0, 0, 0);
                     }
-                    *reinterpret_cast<uint4*>(sbl + ((size_t)j * gp + q) * 16) = lo;
-                    *reinterpret_cast<uint4*>(sbh + ((size_t)j * gp + q) * 16) = hi;
                 }
+                cp_async_wait_all();
             }
             fence_proxy_async();
             tc_fence_before();

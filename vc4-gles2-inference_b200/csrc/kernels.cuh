@@ -309,6 +309,17 @@ __device__ __forceinline__ bool mbar_wait(unsigned long long* bar, unsigned pari
     return true;
 }
 
+// cp.async: 16- or 4-byte global -> shared copies, completed by cp_async_wait_all.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(d), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // Error word values besides shared-memory shortfalls (which record the bytes needed).
 constexpr int kErrCopyTimeout = -2;
 constexpr int kStreamStages = 4;   // ring depth of the streaming kernels
@@ -1363,15 +1374,7 @@ __host__ __device__ inline size_t attn_smem_bytes(int group, int hd, int seq, in
     return attn_carve(group, hd, seq, kv_bits, nullptr, nullptr);
 }
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-    const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
-    const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(d), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 
 // The values of one 32-bit word of a packed cache row: two q16 big-endian
 // values on the 1/2048 grid, or four q8 two's-complement values on the 1/16
