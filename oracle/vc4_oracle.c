@@ -779,6 +779,15 @@ static void kv_decode_row(orc_session* s, int layer, int pos) {
     }
 }
 
+/* Exponent k of the canonical attention weights' grid for len positions:
+   53 - (bits of the largest |cache level|: 7 for q8, 15 for q16) -
+   ceil(log2 len). */
+int orc_attn_weight_exp(int len, int kv_bits) {
+    int lg = 0;
+    while ((1L << lg) < (long)len) ++lg;
+    return 53 - (kv_bits == 16 ? 15 : 7) - lg;
+}
+
 /* attention (session.cpp:1989-2050) over the decoded cache. */
 static void attention(orc_session* s, int layer, int pos) {
     const orc_info* in = &s->m->in;
@@ -807,17 +816,35 @@ static void attention(orc_session* s, int layer, int pos) {
                 s->att[(size_t)h * hd + i] = a;
             }
         } else {
-            double sum = 0.0;
-            for (int t = 0; t <= pos; ++t) { s->scores[t] = orc_expf(s->scores[t] - mx); sum += (double)s->scores[t]; }
-            const float fsum = (float)sum;
-            for (int t = 0; t <= pos; ++t) s->scores[t] = s->scores[t] / fsum;
+            /* Canonical: integer weights E_t = rint(exp(s_t - max) * 2^k)
+               with k = orc_attn_weight_exp(len, kv_bits), then the exact sums
+               den = sum E_t and num_i = sum E_t * code_t,i (code = the cache's
+               integer level; |E_t * code| <= 2^(53 - ceil(log2 len)), so every
+               partial sum is an integer below 2^53 and any summation order
+               gives these bits), and att_i = rint(float(num_i / den * c)) (ties to
+               even, as the host's lrintf) on the q16 grid, c = 256 * the
+               cache grid.  The ratio is the
+               reference's sum_t (e_t / sum e) * v_t with e_t on a 2^-k grid. */
+            const float vscale = s->kv_bits == 16 ? 2048.0f : 16.0f;
+            const double c = s->kv_bits == 16 ? 0.125 : 16.0;
+            const int kexp = orc_attn_weight_exp(pos + 1, s->kv_bits);
+            double den = 0.0;
+            for (int t = 0; t <= pos; ++t) {
+                s->scores[t] = rintf(ldexpf(orc_expf(s->scores[t] - mx), kexp));
+                den += (double)s->scores[t];
+            }
             for (int i = 0; i < hd; ++i) s->pv[i] = 0.0;
             for (int t = 0; t <= pos; ++t) {
-                const double p = (double)s->scores[t];
+                const double e = (double)s->scores[t];
                 const float* vr = vb + (size_t)t * KD;
-                for (int i = 0; i < hd; ++i) s->pv[i] += p * (double)vr[i];
+                for (int i = 0; i < hd; ++i) s->pv[i] += e * (double)(vr[i] * vscale);
             }
-            for (int i = 0; i < hd; ++i) s->att[(size_t)h * hd + i] = (float)s->pv[i];
+            for (int i = 0; i < hd; ++i) {
+                /* the float output, then the host's lrintf rounding (ties to even) */
+                float q = rintf((float)(s->pv[i] / den * c));
+                q = q < -32768.0f ? -32768.0f : q > 32767.0f ? 32767.0f : q;
+                s->att[(size_t)h * hd + i] = q / 256.0f;
+            }
         }
     }
 }

@@ -16,8 +16,12 @@
  *   - the scale epilogue of a matvec is floor(double(S) * double(scale) + 0.5)
  *     clamped to the q16 rail (the shaders' floor(s*ws+0.5));
  *   - float loops are written out op by op with no fused multiply-add unless
- *     fmaf() is spelled out; sums over many positions (softmax denominator,
- *     probability x V) are accumulated in double and rounded once;
+ *     fmaf() is spelled out;
+ *   - attention weights are integers E_t = rint(exp(s_t - max) * 2^k) on a grid
+ *     fine enough for k to keep every sum of E_t and E_t x (cache level) an
+ *     exact integer in double (orc_attn_weight_exp), so the softmax
+ *     denominator and P x V are exact and independent of summation order; the
+ *     output is rint(float(num / den * c)) on the q16 grid (ties to even);
  *   - exp() is orc_expf(), a Cody-Waite range reduction with a degree-7
  *     Taylor polynomial (see vc4_oracle.c), identical op for op in the kernels.
  * ORC_LITERAL selects the reference's literal float orders instead (sequential
@@ -81,6 +85,9 @@ int16_t orc_q16(float v);
 /* KV codec: q16 grid 1/2048 big-endian, q8 grid 1/16. */
 int16_t orc_kv_q16(float v);
 int8_t orc_kv_q8(float v);
+/* Exponent k of the attention weights' grid for len positions and the cache
+   width: 53 - (7 for q8, 15 for q16) - ceil(log2 len). */
+int orc_attn_weight_exp(int len, int kv_bits);
 /* One matvec of a model matrix over q16 ints.  k is the power-of-two input
    scale already applied to xq (folded into the epilogue as 2^k); out receives
    the clamped q16 integers.  which: 0 qkv, 1 wo, 2 w1, 3 w3, 4 w2, 5 router,

@@ -85,14 +85,27 @@ int attn_heads_per_cluster(int group) { return group % 2 == 0 ? 2 : 1; }
 // kernel beats the clusters (whose per-CTA softmax is redundant work).
 constexpr int kAttnBatchUnits = 128;
 
+template <int KVB, int HQ>
+static void launch_attn_b(const DModel& m, const State& s, const Batch& b, const Dims& d, int layer, size_t smb,
+                          cudaStream_t st) {
+    const int group = d.heads / d.kv_heads;
+    launch_pdl(k_attn_b<KVB, HQ>, dim3(d.kv_heads * (group / HQ), b.n), smb, st, (const float*)m.d_q_norm,
+               (const float*)m.d_k_norm, s, b, d, layer);
+}
+
 void launch_attention(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st) {
     Dims d = dims_of(m, s);
     const int group = d.heads / d.kv_heads, hq = attn_heads_per_cluster(group);
     const int units = b.n * d.kv_heads * (group / hq);
     const size_t smb = attnb_smem_bytes(hq, d.head_dim, d.seq, d.kv_bits);
-    if (units >= kAttnBatchUnits && smb <= kMaxDynSmem && attnb_pairs(hq, d.head_dim) <= 8 * kThreads) {
-        launch_pdl(k_attn_b, dim3(d.kv_heads * (group / hq), b.n), smb, st, (const float*)m.d_q_norm,
-                   (const float*)m.d_k_norm, s, b, d, layer, hq);
+    if (units >= kAttnBatchUnits && smb <= kMaxDynSmem && d.head_dim <= 4 * kThreads) {
+        if (d.kv_bits == 8) {
+            if (hq == 2) launch_attn_b<1, 2>(m, s, b, d, layer, smb, st);
+            else launch_attn_b<1, 1>(m, s, b, d, layer, smb, st);
+        } else {
+            if (hq == 2) launch_attn_b<2, 2>(m, s, b, d, layer, smb, st);
+            else launch_attn_b<2, 1>(m, s, b, d, layer, smb, st);
+        }
         return;
     }
     const size_t sm = attn_smem_bytes(hq, d.head_dim, d.seq, d.kv_bits);
@@ -119,6 +132,8 @@ int max_input_cols() { return kPer * kThreads; }
 bool attention_fits(int seq, int head_dim, int kv_bits, int kv_dim, int group) {
     const int hbytes = head_dim * (kv_bits / 8);
     if (hbytes % 16 || kv_dim % 16 || head_dim % 4) return false;
+    // the attention weights' exact sums: 2^23 * 2^15 * seq < 2^53
+    if (seq > 32768) return false;
     return attn_smem_bytes(attn_heads_per_cluster(group), head_dim, seq, kv_bits) <= kMaxDynSmem;
 }
 

@@ -1310,8 +1310,8 @@ __global__ void __launch_bounds__(kThreads) k_logits_wide(DMat W, const float* r
 //    positions itself (the same order in every CTA) and computes P.V for its
 //    own V columns, so no partial results cross CTAs.
 // The arithmetic is the reference's (session.cpp:1989-2050): sequential fp32
-// q.k per position, global max, exp(s - max), p = e / sum (the sum in double,
-// rounded once), out = sum p*v in double.
+// q.k per position, global max, exp(s - max), out = sum_t (e_t / sum e) v_t,
+// with e_t on a 2^-k grid (attn_weights) so that every sum is exact.
 constexpr int kAttnCtas = 8;
 
 __host__ __device__ inline int attn_vs(int hd) { return (((hd + kAttnCtas - 1) / kAttnCtas) + 3) & ~3; }
@@ -1322,6 +1322,7 @@ struct AttnSmem {
     uint8_t* vraw;   // seq x vs*kvb: this CTA's V columns of every position (cache bytes)
     double* pv;      // max(kThreads, group*vs): P.V partials
     double* redd;    // kWarps: softmax sums per warp
+    double* den;     // group: sums of the attention weights
     float* kt;       // attn_rows(seq) x (hd + 4): decoded K rows
     float* vt;       // seq x vs: decoded V columns
     float* q;        // (group + 1) x hd: q heads, then the new k
@@ -1342,6 +1343,7 @@ __host__ __device__ inline size_t attn_carve(int group, int hd, int seq, int kv_
     const size_t vraw = o; o = align16(o + (size_t)seq * vs * kvb);
     const size_t pv = o;   o = align16(o + sizeof(double) * npv);
     const size_t redd = o; o = align16(o + sizeof(double) * kWarps);
+    const size_t den = o;  o = align16(o + sizeof(double) * group);
     const size_t kt = o;   o = align16(o + sizeof(float) * (size_t)rows * (hd + 4));
     const size_t vt = o;   o = align16(o + sizeof(float) * (size_t)seq * vs);
     const size_t q = o;    o = align16(o + sizeof(float) * (size_t)(group + 1) * hd);
@@ -1357,6 +1359,7 @@ __host__ __device__ inline size_t attn_carve(int group, int hd, int seq, int kv_
         sm->vraw = reinterpret_cast<uint8_t*>(base + vraw);
         sm->pv = reinterpret_cast<double*>(base + pv);
         sm->redd = reinterpret_cast<double*>(base + redd);
+        sm->den = reinterpret_cast<double*>(base + den);
         sm->kt = reinterpret_cast<float*>(base + kt);
         sm->vt = reinterpret_cast<float*>(base + vt);
         sm->q = reinterpret_cast<float*>(base + q);
@@ -1389,6 +1392,18 @@ __device__ __forceinline__ int kv_word(unsigned w, int kvb, float* out) {
     for (int j = 0; j < 4; ++j) out[j] = __fmul_rn((float)(signed char)((w >> (8 * j)) & 0xFFu), 1.0f / 16.0f);
     return 4;
 }
+// The integer levels of one 32-bit word of a packed cache row (kv_word
+// without the grid), as floats.
+__device__ __forceinline__ int kv_codes(unsigned w, int kvb, float* out) {
+    if (kvb == 2) {
+        out[0] = (float)(short)(((w & 0xFFu) << 8) | ((w >> 8) & 0xFFu));
+        out[1] = (float)(short)((((w >> 16) & 0xFFu) << 8) | (w >> 24));
+        return 2;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) out[j] = (float)(signed char)((w >> (8 * j)) & 0xFFu);
+    return 4;
+}
 // The packed bytes of one value (the inverse of kv_word), as the low bits of a word.
 __device__ __forceinline__ unsigned kv_encode(float x, int kvb, float* dec) {
     if (kvb == 2) {
@@ -1404,52 +1419,67 @@ __device__ __forceinline__ unsigned kv_encode(float x, int kvb, float* dec) {
     return (unsigned)(int)q & 0xFFu;
 }
 
-// Softmax over positions 0..len-1 of hq heads' scores (sc[hh*seq + t]), in
-// place: kWarps / hq warps per head (one when there are more heads than warps),
-// max, exp(s - max) with the double denominator summed lane-strided, by xor
-// shuffles and then across the head's warps in order, p = e / sum.  The order
-// is fixed by hq alone, so every kernel that calls this gets the same bits.
-__device__ void attn_softmax(float* scores, int seq, int len, int hq, float* redf, double* redd) {
+// Attention weights of hq heads over positions 0..len-1 (sc[hh*seq + t]), in
+// place: kWarps / hq warps per head (one when there are more heads than
+// warps) take the maximum, then E_t = rint(exp(s_t - max) * 2^k), an integer
+// stored as a float, and den[hh] = sum_t E_t.  k = 53 - (7 for q8 levels, 15
+// for q16) - ceil(log2 len) keeps every |E_t * level| at most 2^53 / len, so
+// the double sums here and in P.V are exact integers and their order is free:
+// any kernel layout gives the same bits.
+__host__ __device__ inline int attn_weight_exp(int len, int kvb) {
+    int lg = 0;
+    while ((1 << lg) < len) ++lg;
+    return 53 - (kvb == 2 ? 15 : 7) - lg;
+}
+
+__device__ void attn_weights(float* scores, int seq, int len, int hq, int kvb, float* redf, double* redd,
+                             double* den) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    {
-        const int wph = hq >= kWarps ? 1 : kWarps / hq;
-        const int hpr = kWarps / wph;             // heads per round
-        const int hw = warp / wph, sub = warp % wph, step = wph * 32;
-        for (int r0 = 0; r0 < hq; r0 += hpr) {
-            const int hh = r0 + hw;
-            const bool act = hw < hpr && hh < hq;
-            float* p = scores + (act ? hh : 0) * seq;
-            float m = -1e30f;
-            if (act)
-                for (int t = sub * 32 + lane; t < len; t += step) m = fmaxf(m, p[t]);
-            for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-            if (lane == 0) redf[warp] = m;
-            __syncthreads();
-            double a = 0.0;
-            if (act) {
-                m = redf[hw * wph];
-                for (int k = 1; k < wph; ++k) m = fmaxf(m, redf[hw * wph + k]);
+    const float wscale = __int_as_float((127 + attn_weight_exp(len, kvb)) << 23);   // 2^k, exact
+    const int wph = hq >= kWarps ? 1 : kWarps / hq;
+    const int hpr = kWarps / wph;                 // heads per round
+    const int hw = warp / wph, sub = warp % wph, step = wph * 32;
+    for (int r0 = 0; r0 < hq; r0 += hpr) {
+        const int hh = r0 + hw;
+        const bool act = hw < hpr && hh < hq;
+        float* p = scores + (act ? hh : 0) * seq;
+        float m = -1e30f;
+        if (act)
+            for (int t = sub * 32 + lane; t < len; t += step) m = fmaxf(m, p[t]);
+        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (lane == 0) redf[warp] = m;
+        __syncthreads();
+        double a = 0.0;
+        if (act) {
+            m = redf[hw * wph];
+            for (int k = 1; k < wph; ++k) m = fmaxf(m, redf[hw * wph + k]);
 #pragma unroll 4
-                for (int t = sub * 32 + lane; t < len; t += step) {
-                    const float ev = vexp(__fsub_rn(p[t], m));
-                    p[t] = ev;
-                    a = __dadd_rn(a, (double)ev);
-                }
-            }
-            for (int o = 16; o; o >>= 1) a = __dadd_rn(a, __shfl_xor_sync(0xffffffffu, a, o));
-            if (lane == 0) redd[warp] = a;
-            __syncthreads();
-            if (act) {
-                double tot = redd[hw * wph];
-                for (int k = 1; k < wph; ++k) tot = __dadd_rn(tot, redd[hw * wph + k]);
-                const float fs = __double2float_rn(tot);
-#pragma unroll 4
-                for (int t = sub * 32 + lane; t < len; t += step) p[t] = __fdiv_rn(p[t], fs);
+            for (int t = sub * 32 + lane; t < len; t += step) {
+                const float e = rintf(__fmul_rn(vexp(__fsub_rn(p[t], m)), wscale));
+                p[t] = e;
+                a = __dadd_rn(a, (double)e);
             }
         }
+        for (int o = 16; o; o >>= 1) a = __dadd_rn(a, __shfl_xor_sync(0xffffffffu, a, o));
+        if (lane == 0) redd[warp] = a;
+        __syncthreads();
+        if (act && sub == 0 && lane == 0) {
+            double tot = 0.0;
+            for (int k = 0; k < wph; ++k) tot = __dadd_rn(tot, redd[hw * wph + k]);
+            den[hh] = tot;
+        }
+        __syncthreads();
     }
-    __syncthreads();
+}
 
+// One attention output on the q16 grid: the float num / den * c rounded to
+// the nearest integer, ties to even (the host's lrintf, common.h:188-193),
+// clamped; num = sum E_t * code_t, c = 256 * the cache grid (16 for q8, 1/8
+// for q16).
+__device__ __forceinline__ int16_t att_q16(double num, double den, int kvb) {
+    const float y = __double2float_rn(__dmul_rn(__ddiv_rn(num, den), kvb == 2 ? 0.125 : 16.0));
+    const int q = __float2int_rn(y);
+    return (int16_t)(q < -32768 ? -32768 : q > 32767 ? 32767 : q);
 }
 
 __global__ void __cluster_dims__(kAttnCtas, 1, 1) __launch_bounds__(kThreads)
@@ -1509,7 +1539,7 @@ k_attn(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int 
     for (int v = threadIdx.x; v < pos * vw; v += kThreads) {
         const int t = v / vw, c = v % vw;
         float f[4];
-        const int n = kv_word(reinterpret_cast<const unsigned*>(sm.vraw + (size_t)t * vrow)[c], kvb, f);
+        const int n = kv_codes(reinterpret_cast<const unsigned*>(sm.vraw + (size_t)t * vrow)[c], kvb, f);
         for (int j = 0; j < n; ++j) sm.vt[(size_t)t * vs + c * n + j] = f[j];
     }
     pdl_launch_dependents();
@@ -1562,7 +1592,7 @@ k_attn(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int 
         for (int j = 0; j < vpw; ++j) {
             const int i = i0 + j;
             if (!w && owner) sm.kt[(pos - t0) * hp + i] = dec[j];
-            if (w && i >= c0 && i < c1) sm.vt[(size_t)pos * vs + i - c0] = dec[j];
+            if (w && i >= c0 && i < c1) sm.vt[(size_t)pos * vs + i - c0] = __fmul_rn(dec[j], kvb == 2 ? 2048.0f : 16.0f);
         }
     }
     __syncthreads();
@@ -1590,11 +1620,11 @@ k_attn(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int 
     }
     cluster.sync();   // the last access to another CTA's shared memory
 
-    // 5. softmax over all positions (the same order in every CTA)
-    attn_softmax(sm.sc, d.seq, len, hq, sm.redf, sm.redd);
+    // 5. integer weights over all positions (every CTA computes them all)
+    attn_weights(sm.sc, d.seq, len, hq, kvb, sm.redf, sm.redd, sm.den);
 
     // 6. P.V for this CTA's V columns: each output's positions split into ks
-    //    contiguous ranges, partial sums in double combined in range order
+    //    contiguous ranges; the sums of E_t * code are exact
     const int nout = hq * nc;
     if (nout == 0) return;
     const int ks = nout >= kThreads ? 1 : min(32, kThreads / nout);
@@ -1614,25 +1644,34 @@ k_attn(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int 
         double a = 0.0;
         for (int j = 0; j < ks; ++j) a = __dadd_rn(a, sm.pv[o * ks + j]);
         const int hh = o / nc, i = o % nc;
-        s.att[(size_t)b * d.dim + (size_t)(g * group + h0 + hh) * hd + c0 + i] = (int16_t)q16h(__double2float_rn(a));
+        s.att[(size_t)b * d.dim + (size_t)(g * group + h0 + hh) * hd + c0 + i] = att_q16(a, sm.den[hh], kvb);
     }
 }
 
 
 // Attention for many sequences at once: one CTA (no cluster) per (sequence,
-// KV head, pair of q heads), the sequence's K and then V rows streamed
-// through shared memory in tiles of kAbTile positions (cp.async, double
-// buffered, decoded to fp32).  Scores, softmax and the P.V reductions follow
-// exactly the cluster kernel's orders (sequential fp32 q.k, attn_softmax, and
-// for every output column the same position chunks as the cluster CTA that
-// owns that column, combined in the same order), so a sequence's attention
-// output is the same whichever kernel runs it.
-constexpr int kAbTile = 128;
+// KV head, pair of q heads).  The sequence's K rows and then its V rows stream
+// through a ring of kAbStages shared-memory tiles of kAbRows positions
+// (cp.async), rows padded to an odd number of 16-byte units so that 16-byte
+// reads of consecutive rows hit distinct banks.
+//  - scores: thread (position, head) decodes its K row from the cache bytes
+//    in registers and forms the sequential fp32 dot, as the cluster kernel;
+//  - weights: attn_weights (integer E_t, exact sums);
+//  - P.V: thread (4-column quad, position slice) accumulates E_t * code in
+//    double for every head, exactly; the slices are added at the end.
+// A sequence's output is therefore the cluster kernel's, bit for bit.
+constexpr int kAbRows = 128;
+constexpr int kAbStages = 3;
+
+__host__ __device__ inline int attnb_pitch(int hbytes) { return (hbytes / 16) % 2 ? hbytes : hbytes + 16; }
+__host__ __device__ inline int attnb_slices(int hd) { return kThreads / (hd / 4); }
 
 struct AbSmem {
-    uint8_t* raw;    // 2 x kAbTile x hbytes: cache rows of two tiles
-    float* ft;       // kAbTile x (hd + 4): decoded rows of the current tile
-    double* pv;      // P.V partials, one per (output, chunk)
+    uint8_t* ring;   // kAbStages x kAbRows x pitch cache bytes; P.V partials at the end
+    uint8_t* newrow; // 2 x hbytes: this step's K and V row
+    double* ed;      // hq x seq: the weights E_t as doubles
+    double* redd;
+    double* den;     // hq
     float* q;        // (hq + 1) x hd: q heads, then the new k
     float* vn;       // hd: the new v
     float* rc;
@@ -1640,40 +1679,33 @@ struct AbSmem {
     float* wq;
     float* wk;
     float* redf;
-    double* redd;
-    float* sc;       // hq x seq
+    float* sc;       // hq x seq: scores, then E_t
 };
 
-__host__ __device__ inline int attnb_pairs(int hq, int hd) {   // (output, chunk) pairs of the cluster layout
-    const int vs = attn_vs(hd);
-    int total = 0;
-    for (int c0 = 0; c0 < hd; c0 += vs) {
-        const int nc = (hd - c0) < vs ? (hd - c0) : vs, nout = hq * nc;
-        const int ks = nout >= kThreads ? 1 : (kThreads / nout < 32 ? kThreads / nout : 32);
-        total += nout * ks;
-    }
-    return total;
-}
 __host__ __device__ inline size_t attnb_carve(int hq, int hd, int seq, int kv_bits, char* base, AbSmem* sm) {
-    const int kvb = kv_bits / 8;
+    const int hbytes = hd * (kv_bits / 8);
+    const size_t ring_b = (size_t)kAbStages * kAbRows * attnb_pitch(hbytes);
+    const size_t part_b = sizeof(double) * (size_t)attnb_slices(hd) * hq * hd;
     size_t o = 0;
-    const size_t raw = o; o = align16(o + 2 * (size_t)kAbTile * hd * kvb);
-    const size_t ft = o;  o = align16(o + sizeof(float) * (size_t)kAbTile * (hd + 4));
-    const size_t pv = o;  o = align16(o + sizeof(double) * (size_t)attnb_pairs(hq, hd));
+    const size_t ring = o; o = align16(o + (ring_b > part_b ? ring_b : part_b));
+    const size_t nr = o;   o = align16(o + 2 * (size_t)hbytes);
+    const size_t ed = o;   o = align16(o + sizeof(double) * (size_t)hq * seq);
     const size_t redd = o; o = align16(o + sizeof(double) * kWarps);
-    const size_t q = o;   o = align16(o + sizeof(float) * (size_t)(hq + 1) * hd);
-    const size_t vn = o;  o += sizeof(float) * hd;
-    const size_t rc = o;  o += sizeof(float) * (hd / 2);
-    const size_t rsn = o; o += sizeof(float) * (hd / 2);
-    const size_t wq = o;  o += sizeof(float) * hd;
-    const size_t wk = o;  o += sizeof(float) * hd;
+    const size_t den = o;  o = align16(o + sizeof(double) * hq);
+    const size_t q = o;    o = align16(o + sizeof(float) * (size_t)(hq + 1) * hd);
+    const size_t vn = o;   o += sizeof(float) * hd;
+    const size_t rc = o;   o += sizeof(float) * (hd / 2);
+    const size_t rsn = o;  o += sizeof(float) * (hd / 2);
+    const size_t wq = o;   o += sizeof(float) * hd;
+    const size_t wk = o;   o += sizeof(float) * hd;
     const size_t redf = o; o += sizeof(float) * kWarps;
-    const size_t sc = o;  o += sizeof(float) * (size_t)hq * seq;
+    const size_t sc = o;   o += sizeof(float) * (size_t)hq * seq;
     if (sm) {
-        sm->raw = reinterpret_cast<uint8_t*>(base + raw);
-        sm->ft = reinterpret_cast<float*>(base + ft);
-        sm->pv = reinterpret_cast<double*>(base + pv);
+        sm->ring = reinterpret_cast<uint8_t*>(base + ring);
+        sm->newrow = reinterpret_cast<uint8_t*>(base + nr);
+        sm->ed = reinterpret_cast<double*>(base + ed);
         sm->redd = reinterpret_cast<double*>(base + redd);
+        sm->den = reinterpret_cast<double*>(base + den);
         sm->q = reinterpret_cast<float*>(base + q);
         sm->vn = reinterpret_cast<float*>(base + vn);
         sm->rc = reinterpret_cast<float*>(base + rc);
@@ -1689,33 +1721,96 @@ __host__ __device__ inline size_t attnb_smem_bytes(int hq, int hd, int seq, int 
     return attnb_carve(hq, hd, seq, kv_bits, nullptr, nullptr);
 }
 
+// Cache values of one 32-bit word (kv_word's values) by exponent-field
+// construction: a byte b (or a 16-bit level v) offset to unsigned and placed
+// in the mantissa of 2^19 (2^12) gives 2^19 + (b + 128)/16 (2^12 + (v +
+// 32768)/2048), and one subtraction leaves b/16 (v/2048), exactly.
+template <int KVB>
+__device__ __forceinline__ void kv_vals(unsigned w, float* f) {
+    if (KVB == 1) {
+        w ^= 0x80808080u;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) f[j] = __fsub_rn(__int_as_float(__byte_perm(w, 0x49000000u, 0x7440 | j)), 524296.0f);
+    } else {
+        w ^= 0x00800080u;
+        f[0] = __fsub_rn(__int_as_float(__byte_perm(w, 0x45800000u, 0x7601)), 4112.0f);
+        f[1] = __fsub_rn(__int_as_float(__byte_perm(w, 0x45800000u, 0x7623)), 4112.0f);
+    }
+}
+// Integer levels of one word as doubles (kv_codes): the offset level placed
+// in the mantissa of 2^52, minus 2^52 + offset.
+template <int KVB>
+__device__ __forceinline__ void kv_levels(unsigned w, double* f) {
+    if (KVB == 1) {
+        w ^= 0x80808080u;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            f[j] = __dsub_rn(__hiloint2double(0x43300000, (int)__byte_perm(w, 0u, 0x4440 | j)), 4503599627370624.0);
+    } else {
+        w ^= 0x00800080u;
+        f[0] = __dsub_rn(__hiloint2double(0x43300000, (int)__byte_perm(w, 0u, 0x4401)), 4503599627403264.0);
+        f[1] = __dsub_rn(__hiloint2double(0x43300000, (int)__byte_perm(w, 0u, 0x4423)), 4503599627403264.0);
+    }
+}
+
+// Sequential fp32 dot of q (hd floats) with one packed K row.
+template <int KVB>
+__device__ __forceinline__ float kdot(const uint8_t* krow, const float* qh, int hd) {
+    float acc = 0.0f;
+    constexpr int kPer = 4 / KVB;                       // values per word
+    for (int c = 0; c < hd * KVB / 16; ++c) {
+        const uint4 w = *reinterpret_cast<const uint4*>(krow + c * 16);
+        const unsigned ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            float f[4], qv[4];
+            kv_vals<KVB>(ws[k], f);
+            if (KVB == 1) {
+                const float4 q4 = *reinterpret_cast<const float4*>(qh + (c * 4 + k) * 4);
+                qv[0] = q4.x; qv[1] = q4.y; qv[2] = q4.z; qv[3] = q4.w;
+            } else {
+                const float2 q2 = *reinterpret_cast<const float2*>(qh + (c * 4 + k) * 2);
+                qv[0] = q2.x; qv[1] = q2.y;
+            }
+#pragma unroll
+            for (int j = 0; j < kPer; ++j) acc = __fadd_rn(acc, __fmul_rn(qv[j], f[j]));
+        }
+    }
+    return acc;
+}
+
+template <int KVB, int HQ>
 __global__ void __launch_bounds__(kThreads)
-k_attn_b(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int layer, int hq) {
+k_attn_b(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int layer) {
     extern __shared__ __align__(16) char smem[];
-    const int hd = d.head_dim, group = d.heads / d.kv_heads, half = hd / 2, hp = hd + 4;
-    if (!smem_ok(attnb_smem_bytes(hq, hd, d.seq, d.kv_bits), s.err)) return;
+    constexpr int hq = HQ;
+    const int hd = d.head_dim, group = d.heads / d.kv_heads, half = hd / 2;
+    if (!smem_ok(attnb_smem_bytes(hq, hd, d.seq, KVB * 8), s.err)) return;
     AbSmem sm;
-    attnb_carve(hq, hd, d.seq, d.kv_bits, smem, &sm);
+    attnb_carve(hq, hd, d.seq, KVB * 8, smem, &sm);
     const int qsplit = group / hq, g = blockIdx.x / qsplit, split = blockIdx.x % qsplit;
     const int h0 = split * hq, b = blockIdx.y;
     const int slot = bt.slot[b], pos = bt.pos[b], len = pos + 1;
-    const int kvb = d.kv_bits / 8, hbytes = hd * kvb, vofs = d.kv_dim * kvb;
-    const int kvec = hbytes / 16, kw = hbytes / 4, vpw = 4 / kvb;
-    const int ntile = (len + kAbTile - 1) / kAbTile;
-    uint8_t* kvbase = s.kv + ((size_t)slot * d.layers + layer) * d.seq * d.row_bytes;
+    const int hbytes = hd * KVB, vofs = d.kv_dim * KVB, pitch = attnb_pitch(hbytes);
+    const int kvec = hbytes / 16, kw = hbytes / 4;
+    const int ntile = (len + kAbRows - 1) / kAbRows;
+    const uint8_t* kvrd = s.kv + ((size_t)slot * d.layers + layer) * d.seq * d.row_bytes + g * hbytes;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // tile u < ntile: K rows of positions [u*T, ...); tile u >= ntile: V rows
+    // tile u < ntile: K rows of positions [u*R, ...); ntile <= u < 2*ntile: V rows
     auto issue = [&](int u) {
-        const int kind = u >= ntile, t0 = (u % ntile) * kAbTile, nt = min(kAbTile, len - t0);
-        uint8_t* dst = sm.raw + (size_t)(u & 1) * kAbTile * hbytes;
-        for (int v = threadIdx.x; v < nt * kvec; v += kThreads) {
-            const int r = v / kvec, c = v % kvec, t = t0 + r;
-            if (t != pos)
-                cp_async16(dst + r * hbytes + c * 16, kvbase + (size_t)t * d.row_bytes + (kind ? vofs : 0) + g * hbytes + c * 16);
+        if (u < 2 * ntile) {
+            const int kind = u >= ntile, t0 = (u % ntile) * kAbRows, nt = min(kAbRows, len - t0);
+            uint8_t* dst = sm.ring + (size_t)(u % kAbStages) * kAbRows * pitch;
+            const uint8_t* src = kvrd + (kind ? vofs : 0);
+            for (int v = threadIdx.x; v < nt * kvec; v += kThreads) {
+                const int r = v / kvec, c = v % kvec, t = t0 + r;
+                if (t != pos) cp_async16(dst + r * pitch + c * 16, src + (size_t)t * d.row_bytes + c * 16);
+            }
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
-    issue(0);
+#pragma unroll
+    for (int u = 0; u < kAbStages - 1; ++u) issue(u);
     for (int i = threadIdx.x; i < half; i += kThreads) {
         sm.rc[i] = s.rope_cos[(size_t)pos * half + i];
         sm.rsn[i] = s.rope_sin[(size_t)pos * half + i];
@@ -1757,125 +1852,90 @@ k_attn_b(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, in
     }
     __syncthreads();
     // encode the new row; the first q-head pair's CTA writes it to the cache,
-    // every CTA keeps the decoded values (new k in q[hq], new v in vn)
-    uint8_t* row = kvbase + (size_t)pos * d.row_bytes;
+    // every CTA keeps its bytes for position `pos`
+    uint8_t* row = s.kv + ((size_t)slot * d.layers + layer) * d.seq * d.row_bytes + (size_t)pos * d.row_bytes + g * hbytes;
     for (int e = threadIdx.x; e < 2 * kw; e += kThreads) {
-        const int w = e / kw, c = e % kw, i0 = c * vpw;
-        float* src = w ? sm.vn : sm.q + hq * hd;
+        const int w = e / kw, c = e % kw, i0 = c * (4 / KVB);
+        const float* src = w ? sm.vn : sm.q + hq * hd;
         unsigned word = 0;
-        float dec[4];
-        for (int j = 0; j < vpw; ++j) word |= kv_encode(src[i0 + j], kvb, &dec[j]) << (8 * kvb * j);
-        if (split == 0) *reinterpret_cast<unsigned*>(row + (w ? vofs : 0) + g * hbytes + c * 4) = word;
-        for (int j = 0; j < vpw; ++j) src[i0 + j] = dec[j];
+        float dec;
+        for (int j = 0; j < 4 / KVB; ++j) word |= kv_encode(src[i0 + j], KVB, &dec) << (8 * KVB * j);
+        if (split == 0) *reinterpret_cast<unsigned*>(row + (w ? vofs : 0) + c * 4) = word;
+        *reinterpret_cast<unsigned*>(sm.newrow + w * hbytes + c * 4) = word;
     }
     __syncthreads();
 
-    // pass 1: scores, one K tile at a time
     const float sq = __fsqrt_rn((float)hd);
-    for (int u = 0; u < ntile; ++u) {
-        issue(u + 1);                                   // the next K tile, or the first V tile
-        asm volatile("cp.async.wait_group 1;" ::: "memory");
-        __syncthreads();
-        const int t0 = u * kAbTile, nt = min(kAbTile, len - t0);
-        const uint8_t* src = sm.raw + (size_t)(u & 1) * kAbTile * hbytes;
-        for (int v = threadIdx.x; v < nt * kw; v += kThreads) {
-            const int r = v / kw, c = v % kw;
-            float f[4];
-            const int nv = kv_word(reinterpret_cast<const unsigned*>(src + r * hbytes)[c], kvb, f);
-            for (int j = 0; j < nv; ++j)
-                sm.ft[r * hp + c * nv + j] = (t0 + r == pos) ? sm.q[hq * hd + c * nv + j] : f[j];
-        }
-        __syncthreads();
-        for (int e = threadIdx.x; e < nt * hq; e += kThreads) {
-            const int r = e / hq, hh = e % hq;
-            const float4* kr = reinterpret_cast<const float4*>(sm.ft + r * hp);
-            const float4* qh = reinterpret_cast<const float4*>(sm.q + hh * hd);
-            float acc = 0.0f;
-#pragma unroll 4
-            for (int i = 0; i < hd / 4; ++i) {
-                const float4 k4 = kr[i], q4 = qh[i];
-                acc = __fadd_rn(acc, __fmul_rn(q4.x, k4.x));
-                acc = __fadd_rn(acc, __fmul_rn(q4.y, k4.y));
-                acc = __fadd_rn(acc, __fmul_rn(q4.z, k4.z));
-                acc = __fadd_rn(acc, __fmul_rn(q4.w, k4.w));
-            }
-            sm.sc[hh * d.seq + t0 + r] = __fdiv_rn(acc, sq);
-        }
-        __syncthreads();
-    }
-    attn_softmax(sm.sc, d.seq, len, hq, sm.redf, sm.redd);
+    const int nq = hd / 4, ns = attnb_slices(hd);
+    const int cq = threadIdx.x % nq, sl = threadIdx.x / nq;
+    double acc[HQ][4];
+#pragma unroll
+    for (int hh = 0; hh < HQ; ++hh)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[hh][j] = 0.0;
 
-    // pass 2: P.V in the cluster kernel's (output, chunk) layout; thread e
-    // keeps the double partials of pairs e, e + kThreads, ...
-    const int vs = attn_vs(hd);
-    const int npairs = attnb_pairs(hq, hd);
-    constexpr int kMaxPairs = 8;                        // per thread: npairs <= 8 * kThreads
-    double acc[kMaxPairs];
-    int pa[kMaxPairs], pb[kMaxPairs], pcol[kMaxPairs], phh[kMaxPairs];
-#pragma unroll
-    for (int q = 0; q < kMaxPairs; ++q) {
-        acc[q] = 0.0;
-        pa[q] = pb[q] = 0;
-        pcol[q] = phh[q] = 0;
-        int e = threadIdx.x + q * kThreads;
-        if (e >= npairs) continue;
-        for (int c0 = 0; c0 < hd; c0 += vs) {           // locate the pair's column slice
-            const int nc = min(vs, hd - c0), nout = hq * nc;
-            const int ks = nout >= kThreads ? 1 : min(32, kThreads / nout);
-            if (e < nout * ks) {
-                const int o = e / ks, j = e % ks;
-                const int chunk = (len + ks - 1) / ks;
-                pa[q] = min(len, j * chunk);
-                pb[q] = min(len, pa[q] + chunk);
-                phh[q] = o / nc;
-                pcol[q] = c0 + o % nc;
-                break;
+    for (int u = 0; u < 2 * ntile; ++u) {
+        issue(u + kAbStages - 1);
+        asm volatile("cp.async.wait_group %0;" ::"n"(kAbStages - 1) : "memory");
+        __syncthreads();
+        const uint8_t* tile = sm.ring + (size_t)(u % kAbStages) * kAbRows * pitch;
+        if (u < ntile) {
+            // scores of this K tile
+            const int t0 = u * kAbRows, nt = min(kAbRows, len - t0);
+            const int r = threadIdx.x % kAbRows;
+            if (r < nt) {
+                const int t = t0 + r;
+                const uint8_t* kp = t == pos ? sm.newrow : tile + r * pitch;
+                for (int hh = threadIdx.x / kAbRows; hh < hq; hh += kThreads / kAbRows)
+                    sm.sc[hh * d.seq + t] = __fdiv_rn(kdot<KVB>(kp, sm.q + hh * hd, hd), sq);
             }
-            e -= nout * ks;
-        }
-    }
-    for (int u = ntile; u < 2 * ntile; ++u) {
-        if (u + 1 < 2 * ntile) issue(u + 1);
-        else asm volatile("cp.async.commit_group;" ::: "memory");   // keep the group count uniform
-        asm volatile("cp.async.wait_group 1;" ::: "memory");
-        __syncthreads();
-        const int t0 = (u - ntile) * kAbTile, nt = min(kAbTile, len - t0);
-        const uint8_t* src = sm.raw + (size_t)(u & 1) * kAbTile * hbytes;
-        for (int v = threadIdx.x; v < nt * kw; v += kThreads) {
-            const int r = v / kw, c = v % kw;
-            float f[4];
-            const int nv = kv_word(reinterpret_cast<const unsigned*>(src + r * hbytes)[c], kvb, f);
-            for (int j = 0; j < nv; ++j) sm.ft[r * hp + c * nv + j] = (t0 + r == pos) ? sm.vn[c * nv + j] : f[j];
-        }
-        __syncthreads();
+        } else {
+            if (u == ntile) {
+                attn_weights(sm.sc, d.seq, len, hq, KVB, sm.redf, sm.redd, sm.den);
+                for (int i = threadIdx.x; i < hq * len; i += kThreads) {
+                    const int hh = i / len, t = i % len;
+                    sm.ed[hh * d.seq + t] = (double)sm.sc[hh * d.seq + t];
+                }
+                __syncthreads();
+            }
+            // P.V of this V tile
+            const int t0 = (u - ntile) * kAbRows, nt = min(kAbRows, len - t0);
+            if (sl < ns)
+                for (int r = sl; r < nt; r += ns) {
+                    const int t = t0 + r;
+                    const uint8_t* vp = (t == pos ? sm.newrow + hbytes : tile + r * pitch) + cq * 4 * KVB;
+                    double v[4];
+                    if (KVB == 1) {
+                        kv_levels<1>(*reinterpret_cast<const unsigned*>(vp), v);
+                    } else {
+                        const uint2 w2 = *reinterpret_cast<const uint2*>(vp);
+                        kv_levels<2>(w2.x, v);
+                        kv_levels<2>(w2.y, v + 2);
+                    }
 #pragma unroll
-        for (int q = 0; q < kMaxPairs; ++q) {
-            const int ta = max(pa[q], t0), tb = min(pb[q], t0 + nt);
-            const float* p = sm.sc + phh[q] * d.seq;
-            double a = acc[q];
-            for (int t = ta; t < tb; ++t) a = __fma_rn((double)p[t], (double)sm.ft[(t - t0) * hp + pcol[q]], a);
-            acc[q] = a;
+                    for (int hh = 0; hh < HQ; ++hh) {
+                        const double e = sm.ed[hh * d.seq + t];
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) acc[hh][j] = __fma_rn(e, v[j], acc[hh][j]);
+                    }
+                }
         }
         __syncthreads();
     }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    // add the slices' exact partials and store
+    double* part = reinterpret_cast<double*>(sm.ring);
+    if (sl < ns)
 #pragma unroll
-    for (int q = 0; q < kMaxPairs; ++q) {
-        const int e = threadIdx.x + q * kThreads;
-        if (e < npairs) sm.pv[e] = acc[q];
-    }
+        for (int hh = 0; hh < HQ; ++hh)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) part[((size_t)sl * hq + hh) * hd + cq * 4 + j] = acc[hh][j];
     __syncthreads();
-    // combine each output's chunks in order and store
-    int base = 0;
-    for (int c0 = 0; c0 < hd; c0 += vs) {
-        const int nc = min(vs, hd - c0), nout = hq * nc;
-        const int ks = nout >= kThreads ? 1 : min(32, kThreads / nout);
-        for (int o = threadIdx.x; o < nout; o += kThreads) {
-            double a = 0.0;
-            for (int j = 0; j < ks; ++j) a = __dadd_rn(a, sm.pv[base + o * ks + j]);
-            const int hh = o / nc, i = o % nc;
-            s.att[(size_t)b * d.dim + (size_t)(g * group + h0 + hh) * hd + c0 + i] = (int16_t)q16h(__double2float_rn(a));
-        }
-        base += nout * ks;
+    for (int o = threadIdx.x; o < hq * hd; o += kThreads) {
+        const int hh = o / hd, i = o % hd;
+        double a = 0.0;
+        for (int k = 0; k < ns; ++k) a = __dadd_rn(a, part[((size_t)k * hq + hh) * hd + i]);
+        s.att[(size_t)b * d.dim + (size_t)(g * group + h0 + hh) * hd + i] = att_q16(a, sm.den[hh], KVB);
     }
 }
 
