@@ -143,3 +143,38 @@ def test_prefix_restore_batch_full_shape(gpu, tmp_path, n):
             t, p = int(np.argmax(ref)), p + 1
             assert t == int(np.argmax(outs[k][s]))
     assert rows == batch.kv_rows(0, len(prefix), slot=2)[: len(rows)]
+
+
+@pytest.mark.gpu
+def test_batch_1024_equals_serial(gpu, tmp_path):
+    """c4 at the bench's 1024 sequences per pass: the tensor-core matmats run
+    their largest sequence groups (64-128 per CTA, all 512 TMEM columns for
+    w1/w3), two CTAs per SM with two-stage copy rings for the logits and
+    19-stage rings for w2; each sampled sequence gets its one-sequence result
+    bit for bit."""
+    cfg = synth.CONFIGS["c4"]
+    model = vc4b200.Model(gpu, _path("c4"))
+    prefix = synth.prompt_tokens(cfg)[:32]
+    first = vc4b200.Session(model, slots=1, seq=cfg.seq, kv="q8")
+    first.prefill(prefix, 0, want_logits=False)
+    mmkv = str(tmp_path / "prefix.mmkv")
+    first.save_prefix_cache(mmkv, prefix)
+    n, steps = 1024, 3
+    batch = vc4b200.Session(model, slots=n, seq=cfg.seq, kv="q8")
+    for s in range(n):
+        batch.load_prefix_cache(mmkv, slot=s)
+    toks = [(prefix[-1] + 97 * s) % cfg.shape.vocab for s in range(n)]
+    fed, outs = [], []
+    pos = len(prefix)
+    for _ in range(steps):
+        fed.append(list(toks))
+        nx, lg = batch.step_batch(list(range(n)), toks, [pos] * n, want_logits=True)
+        outs.append(lg)
+        toks = [int(t) for t in nx]
+        pos += 1
+    for s in (0, 1, 63, 64, 127, 128, 511, 777, 1000, 1023):
+        one = vc4b200.Session(model, slots=1, seq=cfg.seq, kv="q8")
+        one.load_prefix_cache(mmkv)
+        for k in range(steps):
+            lg = one.step(fed[k][s], len(prefix) + k)
+            assert np.array_equal(lg, outs[k][s]), "sequence %d step %d" % (s, k)

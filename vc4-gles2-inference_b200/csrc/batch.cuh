@@ -412,26 +412,48 @@ __global__ void __launch_bounds__(kThreads) k_mmdown(MatSet M2, State s, Batch b
 //
 // One CTA (one warpgroup) computes a 128-row tile of one matrix (or of two:
 // w1 and w3 of the ffn, or the two column halves of a chunked w2) for a group
-// of sequences.  The weights are 32-row blocks in HBM; 512-byte bulk copies
-// place chunk j of row block q at shared offset j*2048 + q*512, which is the
-// K-major core-matrix layout with the 8-row groups 128 bytes apart (SBO) and
-// the 16-byte K chunks 2048 bytes apart (LBO).  The sequences' input bytes
-// form the B operand [chunk][sequence][16 bytes] per plane: x' = lo + 256*hi
-// with lo unsigned and hi signed, so every K step is two MMAs (s8 x u8 into
-// one accumulator, s8 x s8 into another) and S = D_lo + 256*D_hi is the exact
-// integer dot (|D| < 2^31 for every shape here).  tcgen05.ld brings row r of
-// the accumulators to thread r of the warpgroup for the usual epilogues.
+// of N consecutive sequences of the batch.  K streams through a ring of
+// shared-memory stages of 128 bytes of every row, filled by 2-D TMA copies
+// (cp.async.bulk.tensor, 128-byte swizzle) and completed on `full` mbarriers;
+// one MMA thread consumes a stage as soon as it lands and hands it back
+// through `empty` (tcgen05.commit), so copies and MMAs overlap and K has no
+// shared-memory limit.
+//  - A (weights): the matrix's row-major copy; one box is 128 rows x 128
+//    bytes.  Rows past the matrix and K past its end read as zero
+//    (out-of-bounds fill).
+//  - B (inputs): the sequences' staged records, n rows of rec_bytes; one box
+//    is N rows x 128 bytes of the lo or hi plane.  x' = lo + 256*hi with lo
+//    unsigned and hi signed, so every K step is two MMAs (s8 x u8 into one
+//    accumulator, s8 x s8 into another) and S = D_lo + 256*D_hi is the exact
+//    integer dot (|D| < 2^31 for every shape here).
+// Measured on B200: one thread's TMA copies complete one after another (about
+// 0.2 us for a box with 16-byte rows, 0.55 us for a 16 KB box of 128-byte
+// rows), while copies issued by different warps proceed side by side.  So
+// every box is 128 bytes wide and three producer threads on three SM
+// sub-partitions take the stages in turn.
+// tcgen05.ld brings row r of the accumulators to thread r of the warpgroup
+// for the epilogues of the CUDA-core kernels, so the results are theirs bit
+// for bit.
 // ---------------------------------------------------------------------------
 
 constexpr int kOpDown = 4;
 constexpr int kTcThreads = 128;
+constexpr int kTcKs = 8;                  // 16-byte K chunks per ring stage: one 128-byte swizzle row
+constexpr int kTcMaxStages = 8;
+constexpr int kTcProducers = 3;           // threads issuing the stages' copies
+constexpr size_t kTcTileA = 128 * 128;    // bytes of one stage of a 128-row weight tile
 
-__device__ __forceinline__ uint64_t umma_sdesc(unsigned addr, unsigned lbo, unsigned sbo) {
+// K-major operand in the 128-byte swizzle layout that a SWIZZLE_128B TMA box
+// writes: rows of 128 bytes, 8-row groups 1024 bytes apart (SBO); the leading
+// offset is unused.  `addr` lies in a 1024-byte aligned atom, plus the K
+// step's byte offset within the row.
+__device__ __forceinline__ uint64_t umma_sdesc_sw128(unsigned addr) {
     uint64_t d = 0;
     d |= (uint64_t)((addr >> 4) & 0x3FFFu);
-    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
-    d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
-    d |= (uint64_t)1 << 46;   // descriptor version (sm_100); base offset 0, no swizzle
+    d |= (uint64_t)1 << 16;                 // leading byte offset (unused): 16 bytes
+    d |= (uint64_t)(1024u >> 4) << 32;      // stride byte offset
+    d |= (uint64_t)1 << 46;                 // descriptor version (sm_100)
+    d |= (uint64_t)2 << 61;                 // 128-byte swizzle
     return d;
 }
 __host__ __device__ constexpr uint32_t umma_idesc_i8(bool b_signed, int m, int n) {
@@ -448,233 +470,298 @@ __device__ __forceinline__ void umma_commit(unsigned long long* bar) {
 }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-// 16 consecutive 32-bit accumulator columns of this thread's TMEM lane
+// 16 consecutive 32-bit accumulator columns of this thread's TMEM lane (the
+// registers are valid after tmem_wait_ld)
 __device__ __forceinline__ void tmem_ld16(uint32_t addr, uint32_t (&v)[16]) {
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
                  : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
                    "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
                  : "r"(addr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// Adds `bytes` to the transaction count of the barrier's current phase
+// without arriving (the copies of a stage issued before its arrival).
+__device__ __forceinline__ void mbar_add_tx(unsigned long long* bar, unsigned bytes) {
+    asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+// 2-D tiled TMA load (no multicast) of box (x, y) of `map` into shared memory.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, unsigned long long* bar) {
+    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+                 ::"r"(smem_addr(dst)), "l"(map), "r"(x), "r"(y), "r"(smem_addr(bar)) : "memory");
 }
 
 struct TcPass {        // one matrix of a tensor-core matmat and where its B bytes live in a record
     DMat W;
     int lo_off, hi_off;
 };
+struct TcMaps {        // TMA descriptors, passed by value (__grid_constant__)
+    CUtensorMap a[2];  // weights of pass 0 / 1
+    CUtensorMap b;     // the records
+};
 struct TcArgs {
     TcPass p[2];
     int npass;
+    int nin;             // distinct B inputs: 2 when the passes read different record bytes
     int rec_bytes;       // bytes per sequence record (State::xrec or State::hrec)
     int from_hrec;       // the records are w2 inputs (State::hrec)
-    int group;           // sequences per MMA group (multiple of 16)
+    int group;           // N: sequences per CTA (multiple of 16, at most 256)
     int tmem_cols;       // power of two >= 2 * npass * group
+    int stages;          // ring depth, a multiple of producers
+    int producers;       // threads issuing copies; slot k is always refilled by producer k % producers
+    int kc;              // K chunks of the longer pass (even)
     int hs;
     DownRec dr;
 };
 
 __host__ __device__ inline int tc_kchunks(const DMat& W) { return (W.nchunks + 1) & ~1; }   // even: K steps of 32
-__host__ __device__ inline size_t tc_smem(const TcArgs& a, int n) {
-    int kc = 0;
-    for (int m = 0; m < a.npass; ++m) kc = kc > tc_kchunks(a.p[m].W) ? kc : tc_kchunks(a.p[m].W);
-    return (size_t)kc * 2048 + (size_t)kc * a.group * 32 + align16(sizeof(int) * (size_t)n) + 64;
+__host__ __device__ inline size_t tc_stage_bytes(const TcArgs& a) {
+    return (size_t)a.npass * kTcTileA + (size_t)a.nin * 2 * a.group * 128;
+}
+// ring (1024-byte aligned) | full[stages] | empty[stages] | done | TMEM address |
+// failure flag | the group's input exponents
+__host__ __device__ inline size_t tc_smem(const TcArgs& a) {
+    return 1024 + (size_t)a.stages * tc_stage_bytes(a) + 8 * (2 * (size_t)a.stages + 1) + 16 + 4 * (size_t)a.group;
 }
 
 template <int OP>
-__global__ void __launch_bounds__(kTcThreads) k_tmm(TcArgs a, State s, Batch bt, Dims d, int layer, Finalize fz) {
-    const int tile = blockIdx.x, expert = blockIdx.y;
-    const int n = bt.n, G = a.group;
-    if (!smem_ok(tc_smem(a, n), s.err)) return;
-    int kc = 0;
-    for (int m = 0; m < a.npass; ++m) kc = max(kc, tc_kchunks(a.p[m].W));
-    char* sm = SmemLayout::base();
-    uint8_t* sa = reinterpret_cast<uint8_t*>(sm);                        // [kc][128 rows][16]
-    uint8_t* sbl = sa + (size_t)kc * 2048;                              // [kc][G][16] lo plane
-    uint8_t* sbh = sbl + (size_t)kc * G * 16;                            // [kc][G][16] hi plane
-    int* members = reinterpret_cast<int*>(sbh + (size_t)kc * G * 16);
-    unsigned long long* bar = reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(members) +
-                                                                   align16(sizeof(int) * (size_t)n));
-    uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 2);
+__global__ void __launch_bounds__(kTcThreads) k_tmm(const __grid_constant__ TcMaps maps, TcArgs a, State s, Batch bt,
+                                                    Dims d, int layer, Finalize fz) {
+    const int tile = blockIdx.x, N = a.group, S = a.stages, P = a.producers;
+    const int n = bt.n, g0 = (int)blockIdx.z * N, gn = min(N, n - g0);
+    if (!smem_ok(tc_smem(a), s.err)) return;
+    if (P < 1 || P > kTcProducers || S % P) {   // see the producers below
+        if (threadIdx.x == 0) atomicExch(s.err, kErrRingShape);
+        return;
+    }
+    char* base = SmemLayout::base();
+    char* ring = base + ((1024u - (smem_addr(base) & 1023u)) & 1023u);
+    const size_t sb = tc_stage_bytes(a);
+    unsigned long long* full = reinterpret_cast<unsigned long long*>(ring + (size_t)S * sb);
+    unsigned long long* empty = full + S;
+    unsigned long long* done = empty + S;
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(done + 1);
+    int* fail = reinterpret_cast<int*>(tslot + 1);
+    int* kexp = fail + 1;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const TcPass P0 = a.p[0], P1 = a.p[a.npass > 1 ? 1 : 0];   // the passes have equal shapes
-    auto issue_a = [&](const DMat& W) {   // warp 0: the tile's weights, one 512-byte copy per (chunk, row block)
-        const int nch = W.nchunks;
-        const int nq = min(4, W.rblocks - tile * 4);
-        if (lane == 0) mbar_expect_tx(&bar[0], (unsigned)(nq * nch * 512));
-        __syncwarp();
-        for (int i = lane; i < nq * nch; i += 32) {
-            const int q = i / nch, j = i % nch;
-            bulk_g2s(sa + (size_t)j * 2048 + q * 512, W.body + ((size_t)(tile * 4 + q) * nch + j) * 512, 512u, &bar[0]);
-        }
-    };
+    const int npass = a.npass, nin = a.nin, kc = a.kc, nst = (kc + kTcKs - 1) / kTcKs;
+    const int kcp[2] = {tc_kchunks(a.p[0].W), tc_kchunks(a.p[npass > 1 ? 1 : 0].W)};
+    const size_t boff = (size_t)npass * kTcTileA;          // B planes inside a stage
+    const unsigned bplane = (unsigned)N * 128u;            // bytes of one plane of one stage
     if (warp == 0) {
         if (lane == 0) {
-            mbar_init(&bar[0], 1);
-            mbar_init(&bar[1], 1);
+            for (int i = 0; i < S; ++i) {
+                mbar_init(&full[i], 1);
+                mbar_init(&empty[i], 1);
+            }
+            mbar_init(done, 1);
+            *fail = 0;
             mbar_fence_init();
         }
         __syncwarp();
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tslot)),
                      "r"(a.tmem_cols) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-        issue_a(P0.W);
     }
-    // zero the padding the copies do not cover: row blocks past the matrix, the odd K chunk
-    {
-        const DMat& W = P0.W;
-        const int nq = min(4, W.rblocks - tile * 4);
-        for (int i = tid; i < kc * 128; i += kTcThreads) {
-            const int j = i / 128, r = i % 128;
-            if (j >= W.nchunks || r / 32 >= nq) *reinterpret_cast<uint4*>(sa + (size_t)j * 2048 + r * 16) = make_uint4(0, 0, 0, 0);
-        }
-    }
-    pdl_launch_dependents();
-    pdl_wait();
-    const int nall = mm_members(s, d, n, layer, expert, false, members);
-    const int per = (nall + (int)gridDim.z - 1) / (int)gridDim.z;
-    const int m0 = min(nall, (int)blockIdx.z * per), nm = min(nall, m0 + per) - m0;
-    members += m0;
+    // every CTA holds its TMEM before the dependent grid may start (a dependent
+    // tensor-core grid allocates before its own wait)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tslot;
-    const char* recs = a.from_hrec ? s.hrec : s.xrec;
-    int a_issued = 1, a_waited = 0;   // weight-tile loads issued / waited for (phases of bar[0])
-    unsigned mph = 0;                 // phase of bar[1] (MMA completion)
-    bool ok = true;
-    const int row = tile * 128 + tid;
-    for (int g0 = 0; g0 < nm && ok; g0 += G) {
-        const int gn = min(G, nm - g0);
-        const int gp = (gn + 15) & ~15;                 // MMA N: a multiple of 16
-        for (int m = 0; m < a.npass && ok; ++m) {
-            const TcPass& P = m ? P1 : P0;
-            const int nch = P.W.nchunks;
-            if (a.npass > 1 && (m > 0 || g0 > 0)) {
-                // reload the weight tile of this pass (the previous pass's MMAs are complete)
-                if (warp == 0) { fence_proxy_async(); issue_a(P.W); }
-                ++a_issued;
-            }
-            // B planes of this group: [chunk][sequence][16 bytes], each 16-byte
-            // piece an independent cp.async (the transpose costs nothing)
-            if (m == 0 || P.lo_off != P0.lo_off) {
-                for (int i = tid; i < kc * gp; i += kTcThreads) {
-                    const int j = i / gp, q = i % gp;
-                    uint8_t* dl = sbl + ((size_t)j * gp + q) * 16;
-                    uint8_t* dh = sbh + ((size_t)j * gp + q) * 16;
-                    if (q < gn && j < nch) {
-                        const char* r = recs + (size_t)members[g0 + q] * a.rec_bytes;
-                        cp_async16(dl, r + P.lo_off + (size_t)j * 16);
-                        cp_async16(dh, r + P.hi_off + (size_t)j * 16);
-                    } else {
-                        *reinterpret_cast<uint4*>(dl) = make_uint4(0, 0, 0, 0);
-                        *reinterpret_cast<uint4*>(dh) = make_uint4(0, 0, 0, 0);
-                    }
-                }
-                cp_async_wait_all();
-            }
-            fence_proxy_async();
-            tc_fence_before();
-            __syncthreads();
-            tc_fence_after();
-            if (tid == 0) {
-                if (a_waited < a_issued) ok = mbar_wait(&bar[0], (unsigned)a_waited & 1u);
-                if (ok) {
-                    const uint32_t dlo = tmem + (uint32_t)(m * 2 * gp), dhi = dlo + (uint32_t)gp;
-                    const uint32_t il = umma_idesc_i8(false, 128, gp), ih = umma_idesc_i8(true, 128, gp);
-                    for (int k = 0; k < kc / 2; ++k) {
-                        const uint64_t da = umma_sdesc(smem_addr(sa) + k * 4096, 2048, 128);
-                        const uint64_t dbl = umma_sdesc(smem_addr(sbl) + k * 2 * gp * 16, gp * 16, 128);
-                        const uint64_t dbh = umma_sdesc(smem_addr(sbh) + k * 2 * gp * 16, gp * 16, 128);
-                        umma_i8(dlo, da, dbl, il, k > 0);
-                        umma_i8(dhi, da, dbh, ih, k > 0);
-                    }
-                    umma_commit(&bar[1]);
-                }
-            }
-            a_waited = a_issued;
-            ok = !__syncthreads_or(!(tid != 0 || ok));
-            if (!ok) break;
-            ok = !__syncthreads_or(!mbar_wait(&bar[1], mph & 1u));
-            ++mph;
-            tc_fence_after();
+    pdl_launch_dependents();
+
+    // stage i covers K chunks 8i .. 8i+7 (128 bytes of every row): one box per
+    // pass of the weights, one per plane and input of the records
+    auto a_live = [&](int i, int p) { return i * kTcKs < kcp[p]; };
+    auto b_live = [&](int i, int in) { return i * kTcKs < (nin > 1 ? kcp[in] : kc); };
+    auto a_bytes = [&](int i) {
+        unsigned b = 0;
+        for (int p = 0; p < npass; ++p) b += a_live(i, p) ? (unsigned)kTcTileA : 0u;
+        return b;
+    };
+    auto b_bytes = [&](int i) {
+        unsigned b = 0;
+        for (int in = 0; in < nin; ++in) b += b_live(i, in) ? 2u * bplane : 0u;
+        return b;
+    };
+    auto issue_a = [&](int i) {
+        char* st = ring + (size_t)(i % S) * sb;
+        for (int p = 0; p < npass; ++p)
+            if (a_live(i, p)) tma_load_2d(st + (size_t)p * kTcTileA, &maps.a[p], i * 128, tile * 128, &full[i % S]);
+    };
+    auto issue_b = [&](int i) {
+        char* st = ring + (size_t)(i % S) * sb + boff;
+        for (int in = 0; in < nin; ++in) {
+            if (!b_live(i, in)) continue;
+            const TcPass& Pi = a.p[in];
+            tma_load_2d(st + (size_t)(in * 2 + 0) * bplane, &maps.b, Pi.lo_off + i * 128, g0, &full[i % S]);
+            tma_load_2d(st + (size_t)(in * 2 + 1) * bplane, &maps.b, Pi.hi_off + i * 128, g0, &full[i % S]);
         }
-        if (!ok) break;
-        // epilogue: row `row` (this thread's TMEM lane), sequences of the group in pieces of 16
-        const uint32_t lane_base = tmem + ((uint32_t)(32 * warp) << 16);
-        for (int c = 0; c < gp; c += 16) {
-            uint32_t lo0[16], hi0[16], lo1[16], hi1[16];
-            tmem_ld16(lane_base + c, lo0);
-            tmem_ld16(lane_base + gp + c, hi0);
-            if (a.npass > 1) {
-                tmem_ld16(lane_base + 2 * gp + c, lo1);
-                tmem_ld16(lane_base + 3 * gp + c, hi1);
+    };
+
+    // producers: lane 0 of warps 0, 2 and 3 take the stages in turn.  The ring
+    // depth is a multiple of the producer count and the count is at most the
+    // depth, so a slot is always refilled by the same producer and every wait
+    // on its `empty` barrier is for the phase right after the one that
+    // producer saw last (a parity wait cannot tell phases two apart).
+    if (warp != 1) {
+        const int pid = warp == 0 ? 0 : warp - 1;
+        if (lane == 0 && pid < P) {
+            if (pid == 0) {
+                asm volatile("prefetch.tensormap [%0];" ::"l"(&maps.a[0]) : "memory");
+                if (npass > 1) asm volatile("prefetch.tensormap [%0];" ::"l"(&maps.a[1]) : "memory");
+                asm volatile("prefetch.tensormap [%0];" ::"l"(&maps.b) : "memory");
             }
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                const int q = c + i;
-                if (q >= gn) break;
-                const int b = members[g0 + q];
-                const long long S0 = (long long)(int)lo0[i] + 256LL * (long long)(int)hi0[i];
-                const long long S1 = a.npass > 1 ? (long long)(int)lo1[i] + 256LL * (long long)(int)hi1[i] : 0;
-                const bool live = row < P0.W.rows;
-                const int* gs = reinterpret_cast<const int*>(recs + (size_t)b * a.rec_bytes + 2 * (size_t)x_stride(P0.W));
-                if (OP == kOpQkv || OP == kOpWo) {
-                    if (!live) continue;
-                    const int k = gs[g_stride(P0.W)];
-                    const float o = __fmul_rn(__fmul_rn((float)mv_epi(S0, __ldg(P0.W.rscale + row)), 1.0f / 256.0f),
-                                              ldexpf(1.0f, -k));
-                    if (OP == kOpQkv) {
-                        s.qkv[(size_t)b * (d.dim + 2 * d.kv_dim) + row] = o;
-                    } else {
-                        const float xr = __fmul_rn((float)__ldcg(s.x + (size_t)b * d.dim + row), 1.0f / 256.0f);
-                        s.x1[(size_t)b * d.dim + row] = (int16_t)q16h(__fadd_rn(xr, o));
-                    }
-                } else if (OP == kOpGate) {
-                    if (!live) continue;
-                    const int g = mv_epi(S0, __ldg(P0.W.rscale + row));
-                    const int u = mv_epi(S1, __ldg(P1.W.rscale + row));
-                    float y = swiglu1(__fmul_rn((float)g, 1.0f / 256.0f), __fmul_rn((float)u, 1.0f / 256.0f));
-                    if (a.hs > 0) y = __fmul_rn(y, ldexpf(1.0f, -a.hs));   // metadata key 15 store scale
-                    const int qv = q16s(y);
-                    const int half = (d.chunk < d.ffn && row >= d.chunk) ? 1 : 0;
-                    const int col = row - (half ? d.chunk : 0);
-                    char* hr = s.hrec + (size_t)b * a.dr.bytes;
-                    hr[(half ? a.dr.lo_b : a.dr.lo_a) + col] = (char)(qv & 0xFF);
-                    hr[(half ? a.dr.hi_b : a.dr.hi_a) + col] = (char)(qv >> 8);
-                } else if (OP == kOpDown) {
-                    if (!live) continue;
-                    float o2 = __fmul_rn((float)mv_epi(S0, __ldg(P0.W.rscale + row)), 1.0f / 256.0f);
-                    if (a.npass > 1) {
-                        const int vb = mv_epi(S1, __ldg(P1.W.rscale + row));
-                        // add_q16 of the two chunk outputs (session.cpp:2052-2067)
-                        o2 = __fmul_rn((float)q16h(__fadd_rn(o2, __fmul_rn((float)vb, 1.0f / 256.0f))), 1.0f / 256.0f);
-                    }
-                    const float x1 = __fmul_rn((float)__ldcg(s.x1 + (size_t)b * d.dim + row), 1.0f / 256.0f);
-                    s.x[(size_t)b * d.dim + row] = (int16_t)q16h(__fadd_rn(x1, o2));
+            // the first stages' weights before the grid-dependency wait
+            const int pre = min(S, nst);
+            for (int i = pid; i < pre; i += P) {
+                mbar_add_tx(&full[i], a_bytes(i));
+                issue_a(i);
+            }
+            pdl_wait();
+            for (int i = pid; i < nst; i += P) {
+                if (i >= S) {
+                    if (!mbar_wait(&empty[i % S], (unsigned)(i / S - 1) & 1u)) { atomicExch(fail, 1); break; }
+                    mbar_expect_tx(&full[i % S], a_bytes(i) + b_bytes(i));
+                    issue_a(i);
                 } else {
-                    unsigned long long key = 0ull;
-                    if (live) {
-                        const int v = mv_epi(S0, __ldg(P0.W.rscale + row));
-                        s.logits[(size_t)b * d.vocab + row] = v;
-                        key = logit_key(v, row);
-                    }
-                    for (int o = 16; o; o >>= 1) {
-                        const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, key, o);
-                        key = k2 > key ? k2 : key;
-                    }
-                    if (lane == 0 && key) atomicMax(&s.best[b], key);
+                    mbar_expect_tx(&full[i % S], b_bytes(i));
                 }
+                issue_b(i);
             }
         }
-        tc_fence_before();
-        __syncthreads();   // accumulators and B planes are free for the next group
-        tc_fence_after();
+        __syncwarp();
+    } else {
+        if (lane == 0) {
+            // MMA issuer: four K steps of 32 bytes per stage, inside the 128-byte
+            // swizzle row by advancing the descriptors' start address
+            const uint32_t il = umma_idesc_i8(false, 128, N), ih = umma_idesc_i8(true, 128, N);
+            for (int i = 0; i < nst; ++i) {
+                if (!mbar_wait(&full[i % S], (unsigned)(i / S) & 1u)) { atomicExch(fail, 1); break; }
+                tc_fence_after();
+                const char* st = ring + (size_t)(i % S) * sb;
+                for (int kk = 0; kk < kTcKs / 2; ++kk) {
+                    const int j = i * kTcKs + 2 * kk;
+                    for (int p = 0; p < npass; ++p) {
+                        if (j >= kcp[p]) continue;
+                        const int in = nin > 1 ? p : 0;
+                        const uint64_t da = umma_sdesc_sw128(smem_addr(st + (size_t)p * kTcTileA) + 32u * kk);
+                        const uint64_t dbl =
+                            umma_sdesc_sw128(smem_addr(st + boff + (size_t)(in * 2 + 0) * bplane) + 32u * kk);
+                        const uint64_t dbh =
+                            umma_sdesc_sw128(smem_addr(st + boff + (size_t)(in * 2 + 1) * bplane) + 32u * kk);
+                        const uint32_t dlo = tmem + (uint32_t)(p * 2 * N);
+                        umma_i8(dlo, da, dbl, il, j > 0);
+                        umma_i8(dlo + (uint32_t)N, da, dbh, ih, j > 0);
+                    }
+                }
+                umma_commit(&empty[i % S]);
+            }
+            umma_commit(done);   // every MMA issued above, also after a failure
+        } else {
+            // the other lanes fetch the group's input exponents for the epilogue
+            pdl_wait();
+            if (OP == kOpQkv || OP == kOpWo) {
+                const char* recs = a.from_hrec ? s.hrec : s.xrec;
+                for (int q = lane - 1; q < gn; q += 31)
+                    kexp[q] = reinterpret_cast<const int*>(recs + (size_t)(g0 + q) * a.rec_bytes +
+                                                           2 * (size_t)x_stride(a.p[0].W))[g_stride(a.p[0].W)];
+            }
+        }
+        __syncwarp();
+    }
+    // epilogue: all four warps once the accumulators are complete (the
+    // residuals it reads come from the previous grids).  The row scales sit in
+    // registers and each piece of 16 sequences loads its residuals before it
+    // stores anything, so no global load waits on another.
+    pdl_wait();
+    const TcPass P0 = a.p[0], P1 = a.p[npass > 1 ? 1 : 0];
+    if (!mbar_wait(done, 0u)) atomicExch(fail, 1);
+    tc_fence_after();
+    __syncthreads();
+    const bool ok = *fail == 0;
+    const int row = tile * 128 + tid;
+    const bool live = row < P0.W.rows;
+    const float rs0 = live ? __ldg(P0.W.rscale + row) : 0.0f;
+    const float rs1 = live && npass > 1 ? __ldg(P1.W.rscale + row) : 0.0f;
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * warp) << 16);
+    for (int c = 0; ok && c < gn; c += 16) {
+        uint32_t lo0[16], hi0[16], lo1[16], hi1[16];
+        tmem_ld16(lane_base + c, lo0);
+        tmem_ld16(lane_base + N + c, hi0);
+        if (npass > 1) {
+            tmem_ld16(lane_base + 2 * N + c, lo1);
+            tmem_ld16(lane_base + 3 * N + c, hi1);
+        }
+        int16_t res[16];
+        if (OP == kOpWo || OP == kOpDown) {
+            const int16_t* src = OP == kOpWo ? s.x : s.x1;
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+                res[i] = live && c + i < gn ? __ldcg(src + (size_t)(g0 + c + i) * d.dim + row) : (int16_t)0;
+        }
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const int q = c + i;
+            if (q >= gn) break;
+            const int b = g0 + q;
+            const long long S0 = (long long)(int)lo0[i] + 256LL * (long long)(int)hi0[i];
+            const long long S1 = npass > 1 ? (long long)(int)lo1[i] + 256LL * (long long)(int)hi1[i] : 0;
+            if (OP == kOpQkv || OP == kOpWo) {
+                if (!live) continue;
+                const float o = __fmul_rn(__fmul_rn((float)mv_epi(S0, rs0), 1.0f / 256.0f), ldexpf(1.0f, -kexp[q]));
+                if (OP == kOpQkv) {
+                    s.qkv[(size_t)b * (d.dim + 2 * d.kv_dim) + row] = o;
+                } else {
+                    const float xr = __fmul_rn((float)res[i], 1.0f / 256.0f);
+                    s.x1[(size_t)b * d.dim + row] = (int16_t)q16h(__fadd_rn(xr, o));
+                }
+            } else if (OP == kOpGate) {
+                if (!live) continue;
+                const int g = mv_epi(S0, rs0);
+                const int u = mv_epi(S1, rs1);
+                float y = swiglu1(__fmul_rn((float)g, 1.0f / 256.0f), __fmul_rn((float)u, 1.0f / 256.0f));
+                if (a.hs > 0) y = __fmul_rn(y, ldexpf(1.0f, -a.hs));   // metadata key 15 store scale
+                const int qv = q16s(y);
+                const int half = (d.chunk < d.ffn && row >= d.chunk) ? 1 : 0;
+                const int col = row - (half ? d.chunk : 0);
+                char* hr = s.hrec + (size_t)b * a.dr.bytes;
+                hr[(half ? a.dr.lo_b : a.dr.lo_a) + col] = (char)(qv & 0xFF);
+                hr[(half ? a.dr.hi_b : a.dr.hi_a) + col] = (char)(qv >> 8);
+            } else if (OP == kOpDown) {
+                if (!live) continue;
+                float o2 = __fmul_rn((float)mv_epi(S0, rs0), 1.0f / 256.0f);
+                if (npass > 1) {
+                    const int vb = mv_epi(S1, rs1);
+                    // add_q16 of the two chunk outputs (session.cpp:2052-2067)
+                    o2 = __fmul_rn((float)q16h(__fadd_rn(o2, __fmul_rn((float)vb, 1.0f / 256.0f))), 1.0f / 256.0f);
+                }
+                const float x1 = __fmul_rn((float)res[i], 1.0f / 256.0f);
+                s.x[(size_t)b * d.dim + row] = (int16_t)q16h(__fadd_rn(x1, o2));
+            } else {
+                unsigned long long key = 0ull;
+                if (live) {
+                    const int v = mv_epi(S0, rs0);
+                    s.logits[(size_t)b * d.vocab + row] = v;
+                    key = logit_key(v, row);
+                }
+                for (int o = 16; o; o >>= 1) {
+                    const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, key, o);
+                    key = k2 > key ? k2 : key;
+                }
+                if (lane == 0 && key) atomicMax(&s.best[b], key);
+            }
+        }
     }
     if (!ok && tid == 0) {
-        // a copy or the MMAs did not complete in time: report, and wait (bounded) before freeing TMEM
+        // a copy or the MMAs did not complete in time: report, and wait (bounded)
+        // for the stages still in flight before the shared memory and TMEM go
         atomicExch(s.err, kErrCopyTimeout);
-        mbar_wait(&bar[0], (unsigned)a_waited & 1u, 10000000ull);
-        mbar_wait(&bar[1], mph & 1u, 10000000ull);
+        for (int i = 0; i < S; ++i) mbar_wait(&full[i], 0u, 10000000ull), mbar_wait(&full[i], 1u, 10000000ull);
+        mbar_wait(done, 0u, 10000000ull);
     }
+    tc_fence_before();
     __syncthreads();
     if (warp == 0)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(a.tmem_cols) : "memory");

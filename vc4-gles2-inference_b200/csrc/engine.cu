@@ -154,6 +154,14 @@ std::string relay(const HMat& h, int c0, int c1, DMat& d, std::vector<void*>& al
     std::string e = dev(body.data(), body.size(), (void**)&d.body);
     if (e.empty()) e = dev(rs.data(), rs.size() * 4, (void**)&d.rscale);
     if (e.empty() && !q4p.empty()) e = dev(q4p.data(), q4p.size() * 4, (void**)&d.q4p);
+    if (e.empty() && h.wtype == W_Q8) {
+        // row-major copy for the tensor-core matmat: row r's signed levels at r*K
+        const size_t K = (size_t)d.nchunks * 16;
+        std::vector<int8_t> rm((size_t)R * K, 0);
+        for (int r = 0; r < h.rows; ++r)
+            for (int c = 0; c < ncols; ++c) rm[(size_t)r * K + c] = h.lev[(size_t)r * h.cols + c0 + c];
+        e = dev(rm.data(), rm.size(), (void**)&d.rm);
+    }
     return e;
 }
 
@@ -287,6 +295,7 @@ static int check_kernel_word(vc4_session* s) {
     CK(cudaMemcpy(&w, s->st.err, sizeof(int), cudaMemcpyDeviceToHost));
     if (w > 0) return fail(VC4_ECUDA, "a kernel found its shared-memory reservation too small (needs " + std::to_string(w) + " bytes)");
     if (w == -2) return fail(VC4_ECUDA, "a kernel's bulk copy did not complete within its time limit");
+    if (w == -3) return fail(VC4_ECUDA, "a tensor-core matmat was launched with a copy ring its producers cannot share");
     if (w) return fail(VC4_ECUDA, "kernel self-check failed (code " + std::to_string(w) + ")");
     return VC4_OK;
 }

@@ -20,6 +20,8 @@
 #include "vc4b200_internal.h"
 
 #include <cooperative_groups.h>
+#include <cuda.h>
+#include <cudaTypedefs.h>
 
 #include <cstdio>
 #include <map>
@@ -322,6 +324,7 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 
 // Error word values besides shared-memory shortfalls (which record the bytes needed).
 constexpr int kErrCopyTimeout = -2;
+constexpr int kErrRingShape = -3;   // a tensor-core ring whose stage count its producers cannot share
 constexpr int kStreamStages = 4;   // ring depth of the streaming kernels
 
 template <int MAXC>
@@ -2183,35 +2186,101 @@ inline int mm_splits(const DModel& m, int ctas, int seqs, int min_seqs) {
 // core kernel is faster; the logits head (many tiles) uses the tensor cores
 // from kBatchMin.
 constexpr int kTcMinSeqs = 32;
+constexpr size_t kSmemPerSm = 228 * 1024;   // shared memory of one SM (sm_100)
+
+// TMA descriptors of the tensor-core matmat, encoded on the host through the
+// runtime's driver entry point (the library does not link libcuda).
+inline PFN_cuTensorMapEncodeTiled_v12000 tmap_encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+// A q8 matrix's row-major copy, rows of nchunks*16 bytes; one box is 128 rows x
+// 128 bytes in the 128-byte swizzle layout (a weight tile's stage).
+inline bool tmap_weights(CUtensorMap* map, const DMat& W) {
+    const auto enc = tmap_encode_fn();
+    if (!enc || !W.rm) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)W.nchunks * 16, (cuuint64_t)W.rblocks * 32};
+    const cuuint64_t strides[1] = {(cuuint64_t)W.nchunks * 16};
+    const cuuint32_t box[2] = {128, 128}, es[2] = {1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, W.rm, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+// n staged records of rec_bytes (a multiple of 16); one box is N records x
+// 128 bytes in the 128-byte swizzle layout (a stage of one input plane).
+inline bool tmap_records(CUtensorMap* map, const char* recs, int rec_bytes, int n, int N) {
+    const auto enc = tmap_encode_fn();
+    if (!enc || rec_bytes % 16) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)rec_bytes, (cuuint64_t)n};
+    const cuuint64_t strides[1] = {(cuuint64_t)rec_bytes};
+    const cuuint32_t box[2] = {128, (cuuint32_t)N}, es[2] = {1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<char*>(recs), dims, strides, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 template <int OP>
 inline bool tc_launch(const DModel& m, const State& s, const Batch& bt, int layer, const DMat& W0, const DMat* W1,
                       int rec_bytes, int from_hrec, int lo0, int hi0, int lo1, int hi1, int hs, const DownRec& dr,
                       const Finalize& fz, cudaStream_t st) {
     if (OP != kOpLogits && bt.n < kTcMinSeqs) return false;
-    if (W0.wtype != W_Q8 || (W1 && (W1->wtype != W_Q8 || W1->rblocks != W0.rblocks || W1->nchunks != W0.nchunks)))
-        return false;
+    if (W0.wtype != W_Q8 || (W1 && (W1->wtype != W_Q8 || W1->rblocks != W0.rblocks))) return false;
     TcArgs a{};
     a.p[0] = TcPass{W0, lo0, hi0};
     a.npass = W1 ? 2 : 1;
     a.p[1] = W1 ? TcPass{*W1, lo1, hi1} : a.p[0];
+    a.nin = (W1 && (lo1 != lo0 || hi1 != hi0)) ? 2 : 1;
+    if (W1 && a.nin == 1 && W1->nchunks != W0.nchunks) return false;
     a.rec_bytes = rec_bytes;
     a.from_hrec = from_hrec;
     a.hs = hs;
     a.dr = dr;
-    int g = std::min(a.npass == 2 ? 64 : 128, (bt.n + 15) & ~15);
-    for (;; g -= 16) {
-        a.group = g;
-        if (tc_smem(a, bt.n) <= kMaxDynSmem || g <= 16) break;
-    }
-    if (tc_smem(a, bt.n) > kMaxDynSmem) return false;
-    int cols = 32;
-    while (cols < 2 * a.npass * a.group) cols *= 2;
-    a.tmem_cols = cols;
-    Dims d = dims_of(m, s);
+    a.kc = std::max(tc_kchunks(W0), W1 ? tc_kchunks(*W1) : 0);
     const int tiles = (W0.rows + 127) / 128;
-    const int splits = mm_splits(m, tiles, bt.n, 16);
-    launch_pdl_block(k_tmm<OP>, dim3(tiles, 1, splits), kTcThreads, tc_smem(a, bt.n), st, a, s, bt, d, layer, fz);
+    const int nsm = std::max(1, m.num_sms);
+    const int nmax = (bt.n + 15) & ~15;
+    // sequences per CTA: the fewest bytes streamed into the busiest SM (the
+    // tile's weights once per CTA, the group's inputs once per tile)
+    int N = 0, ctas = 0;
+    double best = 0.0;
+    for (int c = 16; c <= 256; c *= 2) {
+        if (2 * a.npass * c > 512 || (c > 16 && c / 2 >= nmax)) break;
+        if ((size_t)a.npass * kTcTileA * 2 + (size_t)a.nin * 2 * c * 128 * 2 > kMaxDynSmem) continue;   // two stages
+        const int k = tiles * ((bt.n + c - 1) / c);
+        const double per = (double)a.npass * a.kc * 2048 + (double)a.nin * a.kc * std::min(c, nmax) * 32;
+        const double load = (double)((k + nsm - 1) / nsm) * per;
+        if (N == 0 || load <= best) { N = c; ctas = k; best = load; }
+    }
+    if (N == 0) return false;
+    a.group = N;
+    int cols = 32;
+    while (cols < 2 * a.npass * N) cols *= 2;
+    a.tmem_cols = cols;
+    // ring depth: the shared memory of the CTAs that share an SM; the producer
+    // count divides it and does not exceed it (k_tmm relies on both)
+    const int resident = std::max(1, std::min(std::min((ctas + nsm - 1) / nsm, 512 / cols), 4));
+    const size_t budget = std::min(kMaxDynSmem, kSmemPerSm / resident - 1024);
+    a.stages = 0;
+    const size_t fixed = tc_smem(a), per_stage = tc_stage_bytes(a) + 16;   // ring stage + its two mbarriers
+    a.stages = budget > fixed ? (int)std::min<size_t>(kTcMaxStages, (budget - fixed) / per_stage) : 0;
+    if (a.stages < 2) return false;
+    a.producers = std::min(kTcProducers, a.stages);
+    a.stages -= a.stages % a.producers;
+    TcMaps maps;
+    if (!tmap_weights(&maps.a[0], W0) || !tmap_weights(&maps.a[1], W1 ? *W1 : W0) ||
+        !tmap_records(&maps.b, from_hrec ? s.hrec : s.xrec, rec_bytes, bt.n, N))
+        return false;
+    Dims d = dims_of(m, s);
+    launch_pdl_block(k_tmm<OP>, dim3(tiles, 1, (bt.n + N - 1) / N), kTcThreads, tc_smem(a), st, maps, a, s, bt, d,
+                     layer, fz);
     return true;
 }
 
