@@ -410,7 +410,7 @@ __global__ void __launch_bounds__(kThreads) k_mmdown(MatSet M2, State s, Batch b
 // ---------------------------------------------------------------------------
 // Tensor-core matmat for q8 weights (tcgen05.mma kind::i8, TMEM accumulators).
 //
-// One CTA (one warpgroup) computes a 128-row tile of one matrix (or of two:
+// One CTA computes a 128-row tile of one matrix (or of two:
 // w1 and w3 of the ffn, or the two column halves of a chunked w2) for a group
 // of N consecutive sequences of the batch.  K streams through a ring of
 // shared-memory stages of 128 bytes of every row, filled by 2-D TMA copies
@@ -431,13 +431,14 @@ __global__ void __launch_bounds__(kThreads) k_mmdown(MatSet M2, State s, Batch b
 // rows), while copies issued by different warps proceed side by side.  So
 // every box is 128 bytes wide and three producer threads on three SM
 // sub-partitions take the stages in turn.
-// tcgen05.ld brings row r of the accumulators to thread r of the warpgroup
-// for the epilogues of the CUDA-core kernels, so the results are theirs bit
-// for bit.
+// tcgen05.ld brings row r of the accumulators to lane r%32 of the warps of
+// quarter r/32; sixteen warps share the epilogues (those of the CUDA-core
+// kernels, so the results are theirs bit for bit), which are instruction-bound:
+// with one warpgroup they took most of the kernel's time.
 // ---------------------------------------------------------------------------
 
 constexpr int kOpDown = 4;
-constexpr int kTcThreads = 128;
+constexpr int kTcThreads = 512;          // warps 0-3 copy and issue; all 16 run the epilogue
 constexpr int kTcKs = 8;                  // 16-byte K chunks per ring stage: one 128-byte swizzle row
 constexpr int kTcMaxStages = 8;
 constexpr int kTcProducers = 3;           // threads issuing the stages' copies
@@ -680,12 +681,15 @@ __global__ void __launch_bounds__(kTcThreads) k_tmm(const __grid_constant__ TcMa
     tc_fence_after();
     __syncthreads();
     const bool ok = *fail == 0;
-    const int row = tile * 128 + tid;
+    // warp w reads TMEM lanes 32*(w%4) .. +31 (its rows) and every fourth
+    // piece of 16 sequences starting at piece w/4
+    const int quarter = warp & 3, slice = warp >> 2, nslice = kTcThreads / 128;
+    const int row = tile * 128 + 32 * quarter + lane;
     const bool live = row < P0.W.rows;
     const float rs0 = live ? __ldg(P0.W.rscale + row) : 0.0f;
     const float rs1 = live && npass > 1 ? __ldg(P1.W.rscale + row) : 0.0f;
-    const uint32_t lane_base = tmem + ((uint32_t)(32 * warp) << 16);
-    for (int c = 0; ok && c < gn; c += 16) {
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * quarter) << 16);
+    for (int c = 16 * slice; ok && c < gn; c += 16 * nslice) {
         uint32_t lo0[16], hi0[16], lo1[16], hi1[16];
         tmem_ld16(lane_base + c, lo0);
         tmem_ld16(lane_base + N + c, hi0);
