@@ -445,6 +445,25 @@ def run_ours(args, cfg, dist):
                 "step_bytes": step_bytes, "step_frac": step_bytes / (ms / args.steps / 1000.0) / 1e9 / hbm,
                 "per_op_ms": op_ms, "per_op_bytes": op_bytes}
 
+    # batch-1 matvec roofline: the matvec_s kernel on large synthetic matrices
+    # (q8 of the c3 logits head's shape, 64 MiB of q4 and t3 weights; the
+    # other matrices of the configurations are 0.3-5 MB, too small for one
+    # launch to reach HBM speed), cold L2 and warm
+    matvec = {}
+    for name, wt, rows, cols in (("q8", 0, 73448, 1024), ("q4", 1, 65536, 2048), ("t3", 2, 131072, 2048)):
+        ent = {"rows": rows, "cols": cols}
+        for mode, fl in (("cold", 1), ("warm", 0)):
+            ms, byt, dig = C.c_double(), C.c_double(), C.c_uint64()
+            rc = vc4b200.lib().vc4_matvec_probe(dev, wt, rows, cols, 0, 100, fl, C.byref(ms), C.byref(byt),
+                                                C.byref(dig))
+            if rc:
+                raise RuntimeError(vc4b200.lib().vc4_last_error().decode())
+            gbs = byt.value / (ms.value / 1000.0) / 1e9
+            ent["bytes"] = byt.value
+            ent[mode] = {"ms": ms.value, "gbs": gbs, "frac": gbs / hbm}
+        matvec[name] = ent
+    roofline["matvec_batch1"] = matvec
+
     cpu = None
     if dist.world == 1 and not args.no_cpu_baseline:
         cpu = cpu_decode_rate(cfg, path, args.steps, args.cpu_seconds, os.cpu_count() or 1)

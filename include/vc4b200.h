@@ -151,6 +151,19 @@ VC4_API int vc4_profile_op(vc4_session* s, int op, int layer, int n, const int* 
    activations in and out. */
 VC4_API int vc4_op_bytes(const vc4_session* s, int op, int layer, int n, const int* pos, double* bytes);
 
+/* No counterpart in the reference (a measurement helper for the batch-1
+   matvec roofline).  Times the matvec_s kernel, the one vc4_matvec_s
+   launches, on a synthetic rows x cols matrix of weight type wtype (0 q8,
+   1 q4, 2 t3) held in device memory: `reps` launches bracketed by CUDA
+   events, each after a 256 MiB write that evicts L2 when flush != 0.  path
+   selects the kernel: 0 as vc4_matvec_s picks it (by size), 1 one CTA per
+   32-row block, 2 the streaming kernel.  ms_avg receives the mean launch
+   time, bytes the algorithmic bytes of one launch (weights, q4 scale planes,
+   row scales, input and output), digest an FNV-1a hash of the output (equal
+   for equal results).  Allocates and frees its own device buffers. */
+VC4_API int vc4_matvec_probe(int device, int wtype, int rows, int cols, int path, int reps, int flush,
+                             double* ms_avg, double* bytes, unsigned long long* digest);
+
 /* No counterpart in the reference.  vc4_matvec_s for callers that cannot
    allocate device memory: a host whose device memory belongs to its own pool,
    or a thread that must not risk the device synchronisation an allocation can

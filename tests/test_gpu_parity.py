@@ -127,3 +127,20 @@ def test_prefix_cache_roundtrip(gpu, tiny_paths, tmp_path):
     la = a.step(7, len(prompt))
     lb = b.step(7, len(prompt), slot=1)
     assert np.array_equal(la, lb)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("wtype,rows,cols", [(0, 4100, 1024), (1, 4100, 2048), (2, 4100, 4096), (0, 16384, 2048)])
+def test_streaming_matvec_equals_block_kernel(gpu, wtype, rows, cols):
+    """matvec_s streams large matrices with persistent warps (lane = row,
+    whole 32-row blocks per warp); on the same synthetic matrix its output
+    equals the one-CTA-per-block kernel's (checked against the oracle above)
+    bit for bit, ragged last block included."""
+    import ctypes as C
+    digests = []
+    for path in (1, 2):
+        ms, byt, dig = C.c_double(), C.c_double(), C.c_uint64()
+        rc = vc4b200.lib().vc4_matvec_probe(0, wtype, rows, cols, path, 1, 0, C.byref(ms), C.byref(byt), C.byref(dig))
+        assert rc == 0, vc4b200.lib().vc4_last_error().decode()
+        digests.append(dig.value)
+    assert digests[0] == digests[1]

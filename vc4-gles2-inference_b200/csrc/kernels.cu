@@ -140,3 +140,96 @@ bool attention_fits(int seq, int head_dim, int kv_bits, int kv_dim, int group) {
 int matvec_max_chunks() { return 20 * kWarps; }
 
 }  // namespace vc4
+
+// ---------------------------------------------------------------------------
+// Matvec roofline probe: the matvec_s kernel on a synthetic matrix in HBM
+// ---------------------------------------------------------------------------
+
+#include "vc4b200.h"
+
+#include <vector>
+
+namespace vc4 {
+namespace {
+__global__ void k_fill_bytes(uint8_t* p, size_t n, uint32_t seed) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        uint32_t h = (uint32_t)i * 2654435761u ^ seed;
+        h ^= h >> 15;
+        h *= 2246822519u;
+        h ^= h >> 13;
+        p[i] = (uint8_t)h;
+    }
+}
+}  // namespace
+}  // namespace vc4
+
+extern "C" VC4_API int vc4_matvec_probe(int device, int wtype, int rows, int cols, int path, int reps, int flush,
+                                        double* ms_avg, double* bytes, unsigned long long* digest) {
+    using namespace vc4;
+    if (wtype < W_Q8 || wtype > W_T3 || rows <= 0 || cols <= 0 || path < 0 || path > 2 || reps <= 0 || !ms_avg ||
+        !bytes || !digest)
+        return set_error(VC4_EINVAL, "matvec_probe: bad arguments");
+    if (wtype == W_Q4 && cols % 32) return set_error(VC4_EINVAL, "matvec_probe: q4 columns must be whole groups of 32");
+    const int cpc = cols_per_chunk(wtype);
+    DMat W;
+    W.rows = rows; W.cols = cols; W.wtype = wtype;
+    W.rblocks = (rows + kRowBlock - 1) / kRowBlock;
+    W.nchunks = (cols + cpc - 1) / cpc;
+    if (W.nchunks > matvec_max_chunks() || W.nchunks * cpc > max_input_cols())
+        return set_error(VC4_EINVAL, "matvec_probe: matrix too wide for the matvec kernel");
+    if (cudaSetDevice(device) != cudaSuccess) return set_error(VC4_ECUDA, "matvec_probe: cudaSetDevice failed");
+    const size_t nbody = (size_t)W.rblocks * W.nchunks * 512, nq4 = wtype == W_Q4 ? (size_t)W.rblocks * W.nchunks * 128 : 0;
+    const size_t kFlush = flush ? (size_t)256 << 20 : 0;
+    void *body = nullptr, *q4p = nullptr, *rs = nullptr, *xq = nullptr, *out = nullptr, *fl = nullptr;
+    cudaStream_t st = nullptr;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    int rc = VC4_OK;
+    auto done = [&](int code, const char* msg) {
+        if (code != VC4_OK) rc = set_error(code, msg);
+        if (st) cudaStreamSynchronize(st);
+        for (void* p : {body, q4p, rs, xq, out, fl}) if (p) cudaFree(p);
+        if (e0) cudaEventDestroy(e0);
+        if (e1) cudaEventDestroy(e1);
+        if (st) cudaStreamDestroy(st);
+        return rc;
+    };
+    if (cudaMalloc(&body, nbody) != cudaSuccess || (nq4 && cudaMalloc(&q4p, nq4) != cudaSuccess) ||
+        cudaMalloc(&rs, (size_t)W.rblocks * kRowBlock * 4) != cudaSuccess || cudaMalloc(&xq, (size_t)cols * 2) != cudaSuccess ||
+        cudaMalloc(&out, (size_t)rows * 4) != cudaSuccess || (kFlush && cudaMalloc(&fl, kFlush) != cudaSuccess))
+        return done(VC4_ECUDA, "matvec_probe: cudaMalloc failed");
+    if (cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess || cudaEventCreate(&e0) != cudaSuccess ||
+        cudaEventCreate(&e1) != cudaSuccess)
+        return done(VC4_ECUDA, "matvec_probe: stream or event creation failed");
+    W.body = static_cast<uint8_t*>(body);
+    W.q4p = static_cast<int32_t*>(q4p);
+    W.rscale = static_cast<float*>(rs);
+    k_fill_bytes<<<1184, 256, 0, st>>>(W.body, nbody, 0x1234u);
+    if (nq4) k_fill_bytes<<<1184, 256, 0, st>>>(reinterpret_cast<uint8_t*>(q4p), nq4, 0x5678u);
+    k_fill_bytes<<<64, 256, 0, st>>>(static_cast<uint8_t*>(xq), (size_t)cols * 2, 0x9abcu);
+    cudaMemsetAsync(rs, 0x3A, (size_t)W.rblocks * kRowBlock * 4, st);   // row scales near 7e-4
+    VC4_BY_TYPE(wtype, raw, W, static_cast<const int16_t*>(xq), cols, static_cast<int32_t*>(out), st, path);   // warm-up
+    double total = 0.0;
+    for (int r = 0; r < reps; ++r) {
+        if (kFlush) cudaMemsetAsync(fl, r & 0xFF, kFlush, st);
+        cudaEventRecord(e0, st);
+        VC4_BY_TYPE(wtype, raw, W, static_cast<const int16_t*>(xq), cols, static_cast<int32_t*>(out), st, path);
+        cudaEventRecord(e1, st);
+        if (cudaEventSynchronize(e1) != cudaSuccess) return done(VC4_ECUDA, "matvec_probe: a launch failed");
+        float ms = 0.0f;
+        cudaEventElapsedTime(&ms, e0, e1);
+        total += ms;
+    }
+    if (cudaGetLastError() != cudaSuccess) return done(VC4_ECUDA, "matvec_probe: a launch failed");
+    const double per = wtype == W_Q8 ? 1.0 : wtype == W_Q4 ? 0.5 : 0.25;
+    *bytes = per * rows * cols + (wtype == W_Q4 ? 4.0 * rows * (cols / 32) : 0.0) + 4.0 * rows + 2.0 * cols + 4.0 * rows;
+    *ms_avg = total / reps;
+    std::vector<int32_t> h(rows);
+    if (cudaMemcpyAsync(h.data(), out, (size_t)rows * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+        return done(VC4_ECUDA, "matvec_probe: reading the output failed");
+    unsigned long long f = 1469598103934665603ull;   // FNV-1a over the output bytes
+    for (int32_t v : h)
+        for (int b = 0; b < 4; ++b) f = (f ^ (((uint32_t)v >> (8 * b)) & 0xFFu)) * 1099511628211ull;
+    *digest = f;
+    return done(VC4_OK, "");
+}

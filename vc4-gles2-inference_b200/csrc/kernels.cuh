@@ -1965,6 +1965,90 @@ __global__ void __launch_bounds__(kThreads) k_raw(DMat W, const int16_t* xq, int
     }
 }
 
+// matvec_s for large matrices: persistent CTAs (two per SM) stage the input
+// once, then each warp streams whole 32-row blocks, lane = row, with
+// kStreamUnroll 16-byte loads per lane (512 contiguous bytes per warp) in
+// flight while it multiplies the previous batch; no partial sum crosses warps
+// and no barrier sits in the stream.  k_raw pays a CTA launch, the input
+// staging and a cross-warp reduction for every block.  The integer
+// arithmetic is k_raw's (exact dp4a dots, the same epilogue), so the outputs
+// are equal.
+constexpr int kStreamUnroll = 8;
+constexpr int kStreamMinBlocks = 512;   // row blocks from which matvec_s streams
+
+template <int WT>
+__global__ void __launch_bounds__(kThreads, 2) k_raw_stream(DMat W, const int16_t* xq, int n, int32_t* out) {
+    constexpr int U = kStreamUnroll;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nch = W.nchunks;
+    const int nbat = (nch + U - 1) / U;
+    const int stride = gridDim.x * kWarps, first = blockIdx.x * kWarps + warp;
+    const int nblk = first < W.rblocks ? (W.rblocks - first + stride - 1) / stride : 0;
+    const int items = nblk * nbat;   // (block, batch of U chunks) pairs of this warp
+    int4 wn[U];
+    int spn[U];
+    auto load = [&](int t, int4 (&w)[U], int (&sp)[U]) {
+        const int blk = first + (t / nbat) * stride, j0 = (t % nbat) * U;
+        const int4* body = reinterpret_cast<const int4*>(W.body) + (size_t)blk * nch * 32 + lane;
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            if (j0 + u < nch) {
+                w[u] = ld_weights(body + (size_t)(j0 + u) * 32);
+                if (WT == W_Q4) sp[u] = __ldg(W.q4p + ((size_t)blk * nch + j0 + u) * 32 + lane);
+            }
+    };
+    if (items > 0) load(0, wn, spn);   // the first weights before the input staging
+    XStage xs; Red* red; long long* part; int16_t* tmp;
+    carve<1>(x_stride(W), g_stride(W), xs, red, part, tmp);
+    xs.k[0] = 0;
+    stage_one<WT>(xs, 0, xq, n, 0, *red);
+    int alo = 0, ahi = 0;
+    long long S = 0;
+    for (int t = 0; t < items; ++t) {
+        int4 w[U];
+        int sp[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) { w[u] = wn[u]; sp[u] = spn[u]; }
+        if (t + 1 < items) load(t + 1, wn, spn);
+        const int blk = first + (t / nbat) * stride, j0 = (t % nbat) * U;
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int j = j0 + u;
+            if (j >= nch) break;
+            if (WT == W_Q8) {
+                const uint4 L = *reinterpret_cast<const uint4*>(xs.lo + j * 16);
+                const uint4 H = *reinterpret_cast<const uint4*>(xs.hi + j * 16);
+                alo = dp4a_su(w[u].x, L.x, alo); alo = dp4a_su(w[u].y, L.y, alo);
+                alo = dp4a_su(w[u].z, L.z, alo); alo = dp4a_su(w[u].w, L.w, alo);
+                ahi = dp4a_ss(w[u].x, (int)H.x, ahi); ahi = dp4a_ss(w[u].y, (int)H.y, ahi);
+                ahi = dp4a_ss(w[u].z, (int)H.z, ahi); ahi = dp4a_ss(w[u].w, (int)H.w, ahi);
+            } else if (WT == W_T3) {
+                const unsigned wd[4] = {(unsigned)w[u].x, (unsigned)w[u].y, (unsigned)w[u].z, (unsigned)w[u].w};
+                const uint4* L4 = reinterpret_cast<const uint4*>(xs.lo + j * 64);
+                const uint4* H4 = reinterpret_cast<const uint4*>(xs.hi + j * 64);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const uint4 L = L4[q], H = H4[q];
+                    const unsigned e0 = wd[q] & 0x03030303u, e1 = (wd[q] >> 2) & 0x03030303u;
+                    const unsigned e2 = (wd[q] >> 4) & 0x03030303u, e3 = (wd[q] >> 6) & 0x03030303u;
+                    alo = dp4a_uu(e0, L.x, alo); alo = dp4a_uu(e1, L.y, alo);
+                    alo = dp4a_uu(e2, L.z, alo); alo = dp4a_uu(e3, L.w, alo);
+                    ahi = dp4a_us(e0, (int)H.x, ahi); ahi = dp4a_us(e1, (int)H.y, ahi);
+                    ahi = dp4a_us(e2, (int)H.z, ahi); ahi = dp4a_us(e3, (int)H.w, ahi);
+                }
+            } else {
+                S += chunk_dot<W_Q4>(w[u], sp[u], xs.lo + j * 32, xs.hi + j * 32, xs.gsum[j]);
+            }
+        }
+        if (j0 + U >= nch) {   // the block's last batch: epilogue of this lane's row
+            const long long tot = WT == W_Q4 ? S : (long long)alo + 256LL * (long long)ahi;
+            const int row = blk * 32 + lane;
+            if (row < W.rows) out[row] = mv_epi(WT == W_T3 ? tot - xs.gsum[0] : tot, __ldg(W.rscale + row));
+            alo = ahi = 0;
+            S = 0;
+        }
+    }
+}
+
 #ifdef VC4_COMMON_TU
 // i16 matrix (the MoE router, shaders.cpp:1216-1230): one block per row.
 __global__ void __launch_bounds__(kThreads) k_raw_i16(DMat W, const int16_t* xq, int n, int32_t* out) {
@@ -2164,6 +2248,15 @@ struct Ops {
         const size_t sm = smem_bytes(1, x_stride(W), g_stride(W), 0);
         set_smem(k_raw<WT, MAXC>, sm);
         k_raw<WT, MAXC><<<W.rblocks, kThreads, sm, st>>>(W, xq, n, out);
+    }
+    static void raw_stream(const DMat& W, const int16_t* xq, int n, int32_t* out, cudaStream_t st) {
+        const size_t sm = smem_bytes(1, x_stride(W), g_stride(W), 0);
+        set_smem(k_raw_stream<WT>, sm);
+        int dev = 0, nsm = 148;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+        const int grid = std::max(1, std::min(2 * nsm, (W.rblocks + kWarps - 1) / kWarps));
+        k_raw_stream<WT><<<grid, kThreads, sm, st>>>(W, xq, n, out);
     }
 };
 
@@ -2379,7 +2472,7 @@ struct BOps {
     void qkv_##SUF(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st);  \
     void wo_##SUF(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st);   \
     void gate_##SUF(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st); \
-    void raw_##SUF(const DMat& W, const int16_t* xq, int n, int32_t* out, cudaStream_t st);          \
+    void raw_##SUF(const DMat& W, const int16_t* xq, int n, int32_t* out, cudaStream_t st, int path = 0); \
     void bqkv_##SUF(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st);    \
     void bwo_##SUF(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st);     \
     void bffn_##SUF(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st);
