@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="bounded CPU baseline sample")
+    ap.add_argument("--seq", type=int, default=0,
+                    help="shorter KV cache (and prompt at most half of it) for small profiling captures")
     return ap.parse_args()
 
 
@@ -276,7 +278,7 @@ def cpu_decode_rate(cfg, path, steps: int, seconds: float, threads: int) -> dict
 def run_reference(args, cfg, dist):
     if dist.rank != 0:
         return
-    path = model_path(cfg)
+    path = model_path(args.model_cfg)
     threads = os.cpu_count() or 1
     r = cpu_decode_rate(cfg, path, max(1, args.steps + args.warmup), 10 * args.cpu_seconds, threads)
     line = {"metric": METRIC, "value": r["value"], "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
@@ -301,7 +303,7 @@ def run_ours(args, cfg, dist):
 
     dev = dist.local
     torch.cuda.set_device(dev)
-    path = model_path(cfg)
+    path = model_path(args.model_cfg)
     gpu = vc4b200.GPU(dev)
     model = vc4b200.Model(gpu, path)
     B = cfg.batch
@@ -488,6 +490,10 @@ def main():
     args = parse()
     from vc4b200 import synth
     cfg = dict(synth.CONFIGS, **synth.TINY_CONFIGS)[args.config]
+    args.model_cfg = cfg   # the container is always the configuration's own
+    if args.seq:
+        import dataclasses
+        cfg = dataclasses.replace(cfg, seq=args.seq, prompt=min(cfg.prompt, args.seq // 2))
     dist = Dist()
     try:
         if args.impl == "reference":
