@@ -139,8 +139,9 @@ VC4_API int vc4_matvec_s(vc4_model* m, int which, int layer, int expert, const f
    batch (slots, tokens, pos; host arrays) on the session stream, timing each
    launch with CUDA events.  op: 0 qkv, 1 attention, 2 wo, 3 ffn (gate/up,
    SwiGLU and the w2 partial sums), 5 logits; 4 is refused (w2 runs inside
-   op 3).  With flush != 0 a 256 MiB buffer is written between launches
-   (outside the timed interval) so every launch starts from a cold L2.  The KV
+   op 3).  With flush != 0 a 256 MiB buffer is written and read back between
+   launches (outside the timed interval) so every launch starts from a cold
+   L2 with no dirty line left to write back.  The KV
    cache and the sequences' state are unchanged afterwards (the FFN partial
    sums the replays accumulate are cleared before returning).  avg_ms receives
    the mean launch time. */
@@ -155,7 +156,8 @@ VC4_API int vc4_op_bytes(const vc4_session* s, int op, int layer, int n, const i
    matvec roofline).  Times the matvec_s kernel, the one vc4_matvec_s
    launches, on a synthetic rows x cols matrix of weight type wtype (0 q8,
    1 q4, 2 t3) held in device memory: `reps` launches bracketed by CUDA
-   events, each after a 256 MiB write that evicts L2 when flush != 0.  path
+   events, each after a 256 MiB write and read that leave L2 cold and clean
+   when flush != 0.  path
    selects the kernel: 0 as vc4_matvec_s picks it (by size), 1 one CTA per
    32-row block, 2 the streaming kernel.  ms_avg receives the mean launch
    time, bytes the algorithmic bytes of one launch (weights, q4 scale planes,

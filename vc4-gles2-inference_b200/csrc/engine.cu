@@ -847,7 +847,7 @@ extern "C" int vc4_profile_op(vc4_session* s, int op, int layer, int n, const in
     double total = 0.0;
     launch_op(s, op, layer, b, s->stream);   // warm: attributes, instruction cache
     for (int r = 0; r < reps; ++r) {
-        if (flush) CK(cudaMemsetAsync(scratch, r & 0xFF, kFlush, s->stream));
+        if (flush) l2_flush(scratch, kFlush, r, s->stream);
         CK(cudaEventRecord(e0, s->stream));
         launch_op(s, op, layer, b, s->stream);
         CK(cudaEventRecord(e1, s->stream));

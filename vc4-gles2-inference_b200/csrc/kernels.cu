@@ -139,6 +139,24 @@ bool attention_fits(int seq, int head_dim, int kv_bits, int kv_dim, int group) {
 
 int matvec_max_chunks() { return 20 * kWarps; }
 
+namespace {
+// Reads n 16-byte words; stores only if their xor is a value no fill produces,
+// so the loads stay and nothing is written.
+__global__ void k_read_all(const int4* __restrict__ p, size_t n, int* sink) {
+    int acc = 0;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const int4 v = __ldcs(p + i);
+        acc ^= v.x ^ v.y ^ v.z ^ v.w;
+    }
+    if (acc == 0x5A5A5A5B) *sink = acc;
+}
+}  // namespace
+
+void l2_flush(void* buf, size_t bytes, int val, cudaStream_t st) {
+    cudaMemsetAsync(buf, val & 0x7F, bytes, st);   // a uniform fill: every word's xor is 0, the sink is never written
+    k_read_all<<<1184, 512, 0, st>>>(static_cast<const int4*>(buf), bytes / 16, static_cast<int*>(buf));
+}
+
 }  // namespace vc4
 
 // ---------------------------------------------------------------------------
@@ -210,7 +228,7 @@ extern "C" VC4_API int vc4_matvec_probe(int device, int wtype, int rows, int col
     VC4_BY_TYPE(wtype, raw, W, static_cast<const int16_t*>(xq), cols, static_cast<int32_t*>(out), st, path);   // warm-up
     double total = 0.0;
     for (int r = 0; r < reps; ++r) {
-        if (kFlush) cudaMemsetAsync(fl, r & 0xFF, kFlush, st);
+        if (kFlush) l2_flush(fl, kFlush, r, st);
         cudaEventRecord(e0, st);
         VC4_BY_TYPE(wtype, raw, W, static_cast<const int16_t*>(xq), cols, static_cast<int32_t*>(out), st, path);
         cudaEventRecord(e1, st);

@@ -161,6 +161,10 @@ void launch_logits(const DModel& m, const State& s, const Batch& b, int* next, i
 // A bare matvec of one model matrix over q16 inputs (the CPU-path entry,
 // GPU::matvec_s): xq are already scaled ints, out receives clamped q16 ints.
 void launch_matvec_raw(const DModel& m, int mat, const int16_t* xq, int n, int32_t* out, cudaStream_t st);
+// Cold-L2 preparation between timed launches: writes `bytes` (more than L2)
+// of `buf`, then reads them back, so the lines the write left dirty are
+// written back before the timed launch instead of during it.
+void l2_flush(void* buf, size_t bytes, int val, cudaStream_t st);
 int kernel_launches_per_step(const DModel& m, const State& s, int n);
 size_t batch_record_bytes(const DModel& m);
 size_t batch_hidden_bytes(const DModel& m);
