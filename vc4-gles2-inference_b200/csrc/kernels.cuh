@@ -1799,15 +1799,18 @@ k_attn_b(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, in
     const int ntile = (len + kAbRows - 1) / kAbRows;
     const uint8_t* kvrd = s.kv + ((size_t)slot * d.layers + layer) * d.seq * d.row_bytes + g * hbytes;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // tile u < ntile: K rows of positions [u*R, ...); ntile <= u < 2*ntile: V rows
+    // tile u < ntile: K rows of positions [u*R, ...); ntile <= u < 2*ntile: V rows.
+    // Thread (row r0, 16-byte column cc) copies rows r0, r0 + rpp, ...: the
+    // division by the row's 16-byte count happens once, not per copy.
+    const int rpp = kThreads / kvec, cc = threadIdx.x % kvec, r0 = threadIdx.x / kvec;
     auto issue = [&](int u) {
-        if (u < 2 * ntile) {
+        if (u < 2 * ntile && r0 < rpp) {
             const int kind = u >= ntile, t0 = (u % ntile) * kAbRows, nt = min(kAbRows, len - t0);
-            uint8_t* dst = sm.ring + (size_t)(u % kAbStages) * kAbRows * pitch;
-            const uint8_t* src = kvrd + (kind ? vofs : 0);
-            for (int v = threadIdx.x; v < nt * kvec; v += kThreads) {
-                const int r = v / kvec, c = v % kvec, t = t0 + r;
-                if (t != pos) cp_async16(dst + r * pitch + c * 16, src + (size_t)t * d.row_bytes + c * 16);
+            uint8_t* dst = sm.ring + (size_t)(u % kAbStages) * kAbRows * pitch + cc * 16;
+            const uint8_t* src = kvrd + (kind ? vofs : 0) + cc * 16;
+            for (int r = r0; r < nt; r += rpp) {
+                const int t = t0 + r;
+                if (t != pos) cp_async16(dst + r * pitch, src + (size_t)t * d.row_bytes);
             }
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
@@ -1895,10 +1898,9 @@ k_attn_b(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, in
         } else {
             if (u == ntile) {
                 attn_weights(sm.sc, d.seq, len, hq, KVB, sm.redf, sm.redd, sm.den);
-                for (int i = threadIdx.x; i < hq * len; i += kThreads) {
-                    const int hh = i / len, t = i % len;
-                    sm.ed[hh * d.seq + t] = (double)sm.sc[hh * d.seq + t];
-                }
+#pragma unroll
+                for (int hh = 0; hh < HQ; ++hh)
+                    for (int t = threadIdx.x; t < len; t += kThreads) sm.ed[hh * d.seq + t] = (double)sm.sc[hh * d.seq + t];
                 __syncthreads();
             }
             // P.V of this V tile
