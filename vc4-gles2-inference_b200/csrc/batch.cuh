@@ -408,7 +408,7 @@ __global__ void __launch_bounds__(kThreads) k_mmdown(MatSet M2, State s, Batch b
 }
 
 // ---------------------------------------------------------------------------
-// Tensor-core matmat for q8 weights (tcgen05.mma kind::i8, TMEM accumulators).
+// Tensor-core matmat for q8 and t3 weights (tcgen05.mma kind::i8, TMEM accumulators).
 //
 // One CTA computes a 128-row tile of one matrix (or of two:
 // w1 and w3 of the ffn, or the two column halves of a chunked w2) for a group
@@ -418,7 +418,8 @@ __global__ void __launch_bounds__(kThreads) k_mmdown(MatSet M2, State s, Batch b
 // one MMA thread consumes a stage as soon as it lands and hands it back
 // through `empty` (tcgen05.commit), so copies and MMAs overlap and K has no
 // shared-memory limit.
-//  - A (weights): the matrix's row-major copy; one box is 128 rows x 128
+//  - A (weights): the matrix's row-major int8 copy (q8 levels, or t3's
+//    -1/0/+1, so S is the plain integer dot); one box is 128 rows x 128
 //    bytes.  Rows past the matrix and K past its end read as zero
 //    (out-of-bounds fill).
 //  - B (inputs): the sequences' staged records, n rows of rec_bytes; one box
@@ -509,12 +510,14 @@ struct TcArgs {
     int tmem_cols;       // power of two >= 2 * npass * group
     int stages;          // ring depth, a multiple of producers
     int producers;       // threads issuing copies; slot k is always refilled by producer k % producers
-    int kc;              // K chunks of the longer pass (even)
+    int kc;              // 16-byte K chunks of the longer pass (even)
+    int t3;              // ternary weights: the gate also adds the hidden totals the CUDA-core w2 uses
     int hs;
     DownRec dr;
 };
 
-__host__ __device__ inline int tc_kchunks(const DMat& W) { return (W.nchunks + 1) & ~1; }   // even: K steps of 32
+// 16-byte K chunks of a row-major row, even (K steps of 32)
+__host__ __device__ inline int tc_kchunks(const DMat& W) { return (x_stride(W) / 16 + 1) & ~1; }
 __host__ __device__ inline size_t tc_stage_bytes(const TcArgs& a) {
     return (size_t)a.npass * kTcTileA + (size_t)a.nin * 2 * a.group * 128;
 }
@@ -722,17 +725,26 @@ __global__ void __launch_bounds__(kTcThreads) k_tmm(const __grid_constant__ TcMa
                     s.x1[(size_t)b * d.dim + row] = (int16_t)q16h(__fadd_rn(xr, o));
                 }
             } else if (OP == kOpGate) {
-                if (!live) continue;
-                const int g = mv_epi(S0, rs0);
-                const int u = mv_epi(S1, rs1);
-                float y = swiglu1(__fmul_rn((float)g, 1.0f / 256.0f), __fmul_rn((float)u, 1.0f / 256.0f));
-                if (a.hs > 0) y = __fmul_rn(y, ldexpf(1.0f, -a.hs));   // metadata key 15 store scale
-                const int qv = q16s(y);
+                int qv = 0;
+                if (live) {
+                    const int g = mv_epi(S0, rs0);
+                    const int u = mv_epi(S1, rs1);
+                    float y = swiglu1(__fmul_rn((float)g, 1.0f / 256.0f), __fmul_rn((float)u, 1.0f / 256.0f));
+                    if (a.hs > 0) y = __fmul_rn(y, ldexpf(1.0f, -a.hs));   // metadata key 15 store scale
+                    qv = q16s(y);
+                }
+                // a warp's 32 rows lie in one w2 column half (the chunk is a multiple of 32)
                 const int half = (d.chunk < d.ffn && row >= d.chunk) ? 1 : 0;
                 const int col = row - (half ? d.chunk : 0);
                 char* hr = s.hrec + (size_t)b * a.dr.bytes;
-                hr[(half ? a.dr.lo_b : a.dr.lo_a) + col] = (char)(qv & 0xFF);
-                hr[(half ? a.dr.hi_b : a.dr.hi_a) + col] = (char)(qv >> 8);
+                if (live) {
+                    hr[(half ? a.dr.lo_b : a.dr.lo_a) + col] = (char)(qv & 0xFF);
+                    hr[(half ? a.dr.hi_b : a.dr.hi_a) + col] = (char)(qv >> 8);
+                }
+                if (a.t3) {   // the hidden total of the CUDA-core w2's offset codes
+                    const int sum = __reduce_add_sync(0xffffffffu, qv);
+                    if (lane == 0) atomicAdd(reinterpret_cast<int*>(hr + (half ? a.dr.g_b : a.dr.g_a)), sum);
+                }
             } else if (OP == kOpDown) {
                 if (!live) continue;
                 float o2 = __fmul_rn((float)mv_epi(S0, rs0), 1.0f / 256.0f);

@@ -154,9 +154,10 @@ std::string relay(const HMat& h, int c0, int c1, DMat& d, std::vector<void*>& al
     std::string e = dev(body.data(), body.size(), (void**)&d.body);
     if (e.empty()) e = dev(rs.data(), rs.size() * 4, (void**)&d.rscale);
     if (e.empty() && !q4p.empty()) e = dev(q4p.data(), q4p.size() * 4, (void**)&d.q4p);
-    if (e.empty() && h.wtype == W_Q8) {
-        // row-major copy for the tensor-core matmat: row r's signed levels at r*K
-        const size_t K = (size_t)d.nchunks * 16;
+    if (e.empty() && (h.wtype == W_Q8 || h.wtype == W_T3)) {
+        // row-major copy for the tensor-core matmat: row r's signed levels
+        // (q8, or the ternary -1/0/+1) at r*K, K the padded column count
+        const size_t K = (size_t)d.nchunks * cpc;
         std::vector<int8_t> rm((size_t)R * K, 0);
         for (int r = 0; r < h.rows; ++r)
             for (int c = 0; c < ncols; ++c) rm[(size_t)r * K + c] = h.lev[(size_t)r * h.cols + c0 + c];

@@ -2275,12 +2275,16 @@ inline int mm_splits(const DModel& m, int ctas, int seqs, int min_seqs) {
     return std::max(1, z);
 }
 
-// Tensor-core matmat launch (q8 weights, sequences not split by expert);
+// Tensor-core matmat launch (q8 or t3 weights, sequences not split by expert);
 // false when the shapes do not fit, the caller then runs k_mm.
 // Below kTcMinSeqs sequences a 128-row tile leaves most SMs idle and the CUDA-
 // core kernel is faster; the logits head (many tiles) uses the tensor cores
 // from kBatchMin.
 constexpr int kTcMinSeqs = 32;
+// t3 weights read as int8 levels move 4x the bytes of the packed 2-bit codes,
+// so the CUDA-core matmat stays faster up to more sequences (c3 at 32: 13.8k
+// vs 10.6k tokens/s)
+constexpr int kTcMinSeqsT3 = 64;
 constexpr size_t kSmemPerSm = 228 * 1024;   // shared memory of one SM (sm_100)
 
 // TMA descriptors of the tensor-core matmat, encoded on the host through the
@@ -2297,13 +2301,13 @@ inline PFN_cuTensorMapEncodeTiled_v12000 tmap_encode_fn() {
     });
     return fn;
 }
-// A q8 matrix's row-major copy, rows of nchunks*16 bytes; one box is 128 rows x
+// A q8 or t3 matrix's row-major int8 copy, rows of x_stride bytes; one box is 128 rows x
 // 128 bytes in the 128-byte swizzle layout (a weight tile's stage).
 inline bool tmap_weights(CUtensorMap* map, const DMat& W) {
     const auto enc = tmap_encode_fn();
     if (!enc || !W.rm) return false;
-    const cuuint64_t dims[2] = {(cuuint64_t)W.nchunks * 16, (cuuint64_t)W.rblocks * 32};
-    const cuuint64_t strides[1] = {(cuuint64_t)W.nchunks * 16};
+    const cuuint64_t dims[2] = {(cuuint64_t)x_stride(W), (cuuint64_t)W.rblocks * 32};
+    const cuuint64_t strides[1] = {(cuuint64_t)x_stride(W)};
     const cuuint32_t box[2] = {128, 128}, es[2] = {1, 1};
     return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, W.rm, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -2326,8 +2330,9 @@ template <int OP>
 inline bool tc_launch(const DModel& m, const State& s, const Batch& bt, int layer, const DMat& W0, const DMat* W1,
                       int rec_bytes, int from_hrec, int lo0, int hi0, int lo1, int hi1, int hs, const DownRec& dr,
                       const Finalize& fz, cudaStream_t st) {
-    if (OP != kOpLogits && bt.n < kTcMinSeqs) return false;
-    if (W0.wtype != W_Q8 || (W1 && (W1->wtype != W_Q8 || W1->rblocks != W0.rblocks))) return false;
+    if (OP != kOpLogits && bt.n < (W0.wtype == W_T3 ? kTcMinSeqsT3 : kTcMinSeqs)) return false;
+    if ((W0.wtype != W_Q8 && W0.wtype != W_T3) || (W1 && (W1->wtype != W0.wtype || W1->rblocks != W0.rblocks)))
+        return false;
     TcArgs a{};
     a.p[0] = TcPass{W0, lo0, hi0};
     a.npass = W1 ? 2 : 1;
@@ -2339,6 +2344,7 @@ inline bool tc_launch(const DModel& m, const State& s, const Batch& bt, int laye
     a.hs = hs;
     a.dr = dr;
     a.kc = std::max(tc_kchunks(W0), W1 ? tc_kchunks(*W1) : 0);
+    a.t3 = W0.wtype == W_T3;
     const int tiles = (W0.rows + 127) / 128;
     const int nsm = std::max(1, m.num_sms);
     const int nmax = (bt.n + 15) & ~15;

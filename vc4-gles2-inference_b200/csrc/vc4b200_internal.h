@@ -14,9 +14,9 @@
 //     32-bit word holds the codes of columns b, b+4, b+8, b+12 of a 16-column
 //     group at bits 0, 2, 4, 6, so (word >> 2i) & 0x03030303 is four
 //     consecutive columns as bytes.  The dot product subtracts sum(x) once.
-//   * q8 matrices also keep a plain row-major copy of their levels (rows of
-//     nchunks*16 bytes) that the tensor-core matmat loads as 128-byte-wide
-//     TMA boxes.
+//   * q8 and t3 matrices also keep a plain row-major int8 copy of their
+//     levels (rows of nchunks*cols_per_chunk bytes) that the tensor-core
+//     matmat loads as 128-byte-wide TMA boxes.
 //   * Every matrix carries one float epilogue scale per row (the reference's
 //     `ws`, or (p16*ws)/65536 for a row-scaled matrix) and is padded to whole
 //     blocks and chunks with zero weights.
@@ -86,7 +86,7 @@ struct DMat {
     float* rscale = nullptr;         // rblocks*32 epilogue scales
     int32_t* q4p = nullptr;          // q4: rblocks*nchunks*32 packed (s16 | m16<<16)
     int16_t* w16 = nullptr;          // i16 router, row-major
-    int8_t* rm = nullptr;            // q8: the levels row-major, [rblocks*32][nchunks*16] (tensor-core matmat)
+    int8_t* rm = nullptr;            // q8 / t3: the levels row-major, [rblocks*32][nchunks*cols_per_chunk] (tensor-core matmat)
     size_t bytes() const { return (size_t)rblocks * nchunks * 512 + (q4p ? (size_t)rblocks * nchunks * 128 : 0); }
 };
 
