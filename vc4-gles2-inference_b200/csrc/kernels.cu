@@ -89,8 +89,11 @@ template <int KVB, int HQ>
 static void launch_attn_b(const DModel& m, const State& s, const Batch& b, const Dims& d, int layer, size_t smb,
                           cudaStream_t st) {
     const int group = d.heads / d.kv_heads;
-    launch_pdl(k_attn_b<KVB, HQ>, dim3(d.kv_heads * (group / HQ), b.n), smb, st, (const float*)m.d_q_norm,
-               (const float*)m.d_k_norm, s, b, d, layer);
+    const dim3 grid(d.kv_heads * (group / HQ), b.n);
+    const float *qn = m.d_q_norm, *kn = m.d_k_norm;
+    if (d.head_dim == 96) launch_pdl(k_attn_b<KVB, HQ, 96>, grid, smb, st, qn, kn, s, b, d, layer);
+    else if (d.head_dim == 64) launch_pdl(k_attn_b<KVB, HQ, 64>, grid, smb, st, qn, kn, s, b, d, layer);
+    else launch_pdl(k_attn_b<KVB, HQ, 0>, grid, smb, st, qn, kn, s, b, d, layer);
 }
 
 void launch_attention(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st) {

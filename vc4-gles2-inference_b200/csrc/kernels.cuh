@@ -1756,12 +1756,15 @@ __device__ __forceinline__ void kv_levels(unsigned w, double* f) {
     }
 }
 
-// Sequential fp32 dot of q (hd floats) with one packed K row.
-template <int KVB>
+// Sequential fp32 dot of q (hd floats) with one packed K row; HD > 0 fixes
+// the head size at compile time (the loop unrolls).
+template <int KVB, int HD = 0>
 __device__ __forceinline__ float kdot(const uint8_t* krow, const float* qh, int hd) {
     float acc = 0.0f;
     constexpr int kPer = 4 / KVB;                       // values per word
-    for (int c = 0; c < hd * KVB / 16; ++c) {
+    const int n16 = (HD ? HD : hd) * KVB / 16;
+#pragma unroll
+    for (int c = 0; c < n16; ++c) {
         const uint4 w = *reinterpret_cast<const uint4*>(krow + c * 16);
         const unsigned ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
@@ -1782,12 +1785,14 @@ __device__ __forceinline__ float kdot(const uint8_t* krow, const float* qh, int 
     return acc;
 }
 
-template <int KVB, int HQ>
+// HD > 0: the head size fixed at compile time (64 and 96 in the benchmark
+// models), so the K loop unrolls and the P.V index arithmetic folds.
+template <int KVB, int HQ, int HD>
 __global__ void __launch_bounds__(kThreads)
 k_attn_b(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int layer) {
     extern __shared__ __align__(16) char smem[];
     constexpr int hq = HQ;
-    const int hd = d.head_dim, group = d.heads / d.kv_heads, half = hd / 2;
+    const int hd = HD ? HD : d.head_dim, group = d.heads / d.kv_heads, half = hd / 2;
     if (!smem_ok(attnb_smem_bytes(hq, hd, d.seq, KVB * 8), s.err)) return;
     AbSmem sm;
     attnb_carve(hq, hd, d.seq, KVB * 8, smem, &sm);
@@ -1893,7 +1898,7 @@ k_attn_b(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, in
                 const int t = t0 + r;
                 const uint8_t* kp = t == pos ? sm.newrow : tile + r * pitch;
                 for (int hh = threadIdx.x / kAbRows; hh < hq; hh += kThreads / kAbRows)
-                    sm.sc[hh * d.seq + t] = __fdiv_rn(kdot<KVB>(kp, sm.q + hh * hd, hd), sq);
+                    sm.sc[hh * d.seq + t] = __fdiv_rn(kdot<KVB, HD>(kp, sm.q + hh * hd, hd), sq);
             }
         } else {
             if (u == ntile) {
