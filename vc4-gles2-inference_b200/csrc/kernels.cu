@@ -112,7 +112,11 @@ void launch_attention(const DModel& m, const State& s, const Batch& b, int layer
         return;
     }
     const size_t sm = attn_smem_bytes(hq, d.head_dim, d.seq, d.kv_bits);
-    launch_pdl(k_attn, dim3(d.kv_heads * (group / hq) * kAttnCtas, b.n), sm, st, (const float*)m.d_q_norm,
+    if (d.head_dim == 96) launch_pdl(k_attn<96>, dim3(d.kv_heads * (group / hq) * kAttnCtas, b.n), sm, st, (const float*)m.d_q_norm,
+               (const float*)m.d_k_norm, s, b, d, layer, hq);
+    else if (d.head_dim == 64) launch_pdl(k_attn<64>, dim3(d.kv_heads * (group / hq) * kAttnCtas, b.n), sm, st, (const float*)m.d_q_norm,
+               (const float*)m.d_k_norm, s, b, d, layer, hq);
+    else launch_pdl(k_attn<0>, dim3(d.kv_heads * (group / hq) * kAttnCtas, b.n), sm, st, (const float*)m.d_q_norm,
                (const float*)m.d_k_norm, s, b, d, layer, hq);
 }
 

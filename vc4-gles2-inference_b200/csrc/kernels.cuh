@@ -1485,12 +1485,14 @@ __device__ __forceinline__ int16_t att_q16(double num, double den, int kvb) {
     return (int16_t)(q < -32768 ? -32768 : q > 32767 ? 32767 : q);
 }
 
+// HD > 0: the head size fixed at compile time (the loops unroll).
+template <int HD>
 __global__ void __cluster_dims__(kAttnCtas, 1, 1) __launch_bounds__(kThreads)
 k_attn(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int layer, int hq) {
     namespace cg = cooperative_groups;
     cg::cluster_group cluster = cg::this_cluster();
     extern __shared__ __align__(16) char smem[];
-    const int hd = d.head_dim, group = d.heads / d.kv_heads, half = hd / 2, hp = hd + 4;
+    const int hd = HD ? HD : d.head_dim, group = d.heads / d.kv_heads, half = hd / 2, hp = hd + 4;
     if (!smem_ok(attn_smem_bytes(hq, hd, d.seq, d.kv_bits), s.err)) return;
     AttnSmem sm;
     attn_carve(hq, hd, d.seq, d.kv_bits, smem, &sm);
