@@ -221,10 +221,13 @@ __global__ void __launch_bounds__(kThreads) k_mm(MatSet M, State s, Batch bt, Di
     bool ok = !__syncthreads_or(!mbar_wait(&bar[0], 0));   // the same verdict in every thread
     for (int g0 = 0; g0 < nm && ok; g0 += group) {
         const int gn = min(group, nm - g0), gi = g0 / group;
-        if (threadIdx.x == 0) {
+        // one copy per record, issued by lane 0 of every warp in turn: one
+        // thread's bulk copies complete one after another
+        if (lane == 0) {
             fence_proxy_async();
-            mbar_expect_tx(&bar[1], (unsigned)(gn * rb));
-            for (int i = 0; i < gn; ++i) bulk_g2s(rsm + i * rb, s.xrec + (size_t)members[g0 + i] * rb, (unsigned)rb, &bar[1]);
+            if (warp == 0) mbar_expect_tx(&bar[1], (unsigned)(gn * rb));
+            for (int i = warp; i < gn; i += kWarps)
+                bulk_g2s(rsm + i * rb, s.xrec + (size_t)members[g0 + i] * rb, (unsigned)rb, &bar[1]);
         }
         ok = mbar_wait(&bar[1], (unsigned)gi & 1u);
         if (__syncthreads_or(!ok)) { ok = false; break; }
@@ -361,10 +364,10 @@ __global__ void __launch_bounds__(kThreads) k_mmdown(MatSet M2, State s, Batch b
     bool ok = !__syncthreads_or(!mbar_wait(&bar[0], 0));   // the same verdict in every thread
     for (int g0 = 0; g0 < nm && ok; g0 += group) {
         const int gn = min(group, nm - g0), gi = g0 / group;
-        if (threadIdx.x == 0) {
+        if (lane == 0) {   // records issued by lane 0 of every warp in turn (as in k_mm)
             fence_proxy_async();
-            mbar_expect_tx(&bar[1], (unsigned)(gn * R.bytes));
-            for (int i = 0; i < gn; ++i)
+            if (warp == 0) mbar_expect_tx(&bar[1], (unsigned)(gn * R.bytes));
+            for (int i = warp; i < gn; i += kWarps)
                 bulk_g2s(rsm + i * R.bytes, s.hrec + (size_t)members[g0 + i] * R.bytes, (unsigned)R.bytes, &bar[1]);
         }
         ok = mbar_wait(&bar[1], (unsigned)gi & 1u);
