@@ -1,23 +1,28 @@
 #!/usr/bin/env python
 """Decode benchmark of the B200 quantized decode path.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c1] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c4b1024] [--secondary c1]
+                    [--impl ours|reference]
 
-One step = one greedy decode pass of every sequence of the configuration's
-batch (batch 1 for the default workload).  The default workload is BASELINE's
-MiniMind3-64M shaped, q4, batch 1, KV q16, SEQ 256, a 128-token
-seeded prompt (prefilled, untimed) then greedy decode.  Weights and prompts are
-seeded synthetic data of that shape, packed into an MMCF container byte-equal
-to the reference packer's output (sha256 checked against
-tests/golden/golden.json).
+One step = one greedy decode pass over every sequence of the configuration's
+batch.  The headline workload is the largest single-GPU configuration of the
+benchmark (BASELINE configs[4] at its top sweep point): MiniMind3-64M shaped,
+q8 weights, KV q8, SEQ 768, 1024 sequences per GPU, one seeded 512-token
+prefix prefilled once, saved as MMKV1 and restored into every sequence slot,
+then greedy decode from position 511.  The c1 configuration (q4, batch 1, KV
+q16, SEQ 256, 128-token prompt) is measured after it and reported inside the
+same JSON line (`secondary`).  Weights and prompts are seeded synthetic data
+of the configurations' shapes, packed into MMCF containers byte-equal to the
+reference packer's output (sha256 checked against tests/golden/golden.json).
 
 `value` times K device-resident decode steps (inputs already in HBM, one CUDA
-graph replay each, L2 flushed between steps), `e2e` times K steps through the
-public API with host buffers (token/position in, greedy token out).  For N > 1
-every rank runs its own replica ("replicas only": the batch-1 path does not
-shard) and the time is the max over ranks.  `--impl reference` times the
-reference arithmetic on the host cores instead: the CPU restatement in
-oracle/ (the reference has no CPU engine; its GL path cannot run here).
+graph replay each, L2 flushed between steps); `e2e` times K steps through the
+public API with host buffers (tokens and positions in, greedy tokens out).
+For N > 1 every rank decodes its own 1024 sequences (weak scaling, no
+data-path collective) and the time is the max over ranks.  `--impl reference`
+times the reference arithmetic on the host cores instead: the CPU
+restatement in oracle/ (the reference has no CPU engine; its GL path cannot
+run here), on a bounded sample of the same configuration's sequences.
 """
 from __future__ import annotations
 
@@ -41,6 +46,7 @@ for _p in (PKG, os.path.join(ROOT, "oracle")):
 METRIC = "decode tokens/s per GPU and per box (1/2/4/8)"
 KV_NAME = {16: "q16", 8: "q8"}
 OPS = ["qkv", "attention", "wo", "ffn", None, "logits"]   # op 4 (w2) runs inside op 3
+DTYPE = "int64 (exact integer dot products on dp4a / tcgen05 kind::i8), f32/f64 epilogues"
 
 
 def parse():
@@ -48,7 +54,10 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--config", default="c1")
+    ap.add_argument("--config", default="c4b1024")
+    ap.add_argument("--secondary", default="c1",
+                    help="comma-separated configurations measured after the headline one and reported inside "
+                         "its JSON line ('' for none)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="bounded CPU baseline sample")
@@ -91,8 +100,13 @@ def sequence_ids(rank: int, batch: int) -> list:
 
 def workload_desc(cfg) -> str:
     s = cfg.shape
-    return ("%s: %s %s, batch %d, KV %s, SEQ %d, %d-token seeded prompt then greedy decode"
-            % (cfg.key, s.name, cfg.quant, cfg.batch, KV_NAME[cfg.kv_bits], cfg.seq, cfg.prompt))
+    if cfg.extra.get("prefix_restore"):
+        how = ("one %d-token seeded prefix prefilled once, saved as MMKV1 and restored into every slot, "
+               "then greedy decode" % cfg.prompt)
+    else:
+        how = "%d-token seeded prompt then greedy decode" % cfg.prompt
+    return "%s: %s %s, batch %d, KV %s, SEQ %d, %s" % (cfg.key, s.name, cfg.quant, cfg.batch,
+                                                       KV_NAME[cfg.kv_bits], cfg.seq, how)
 
 
 # ---------------------------------------------------------------------------
@@ -241,38 +255,93 @@ class Dist:
 
 
 # ---------------------------------------------------------------------------
+# workload description (identical in both arms)
+# ---------------------------------------------------------------------------
+
+def config_of(cfg, world: int) -> dict:
+    return {"workload": workload_desc(cfg), "batch_per_gpu": cfg.batch, "seq": cfg.seq, "quant": cfg.quant,
+            "kv": KV_NAME[cfg.kv_bits], "prefix_restore": bool(cfg.extra.get("prefix_restore")),
+            "parallelism": ("dp%d (sequences sharded by rank)" % world) if cfg.batch > 1 else
+                           ("dp%d replicas" % world),
+            "l2": "flushed between timed steps (256 MiB write, then read back so no dirty line is left)"}
+
+
+def decode_prompts(cfg, rank: int) -> list:
+    """Each sequence's tokens up to and including the one its first decode
+    step consumes.  A prefix-restore configuration shares one seeded prefix
+    (prefilled once, restored into every slot) and parts at its last position
+    with a distinct token per sequence."""
+    from vc4b200 import synth
+    ids = sequence_ids(rank, cfg.batch)
+    if cfg.extra.get("prefix_restore"):
+        prefix = synth.prompt_tokens(cfg, 0)
+        return [prefix[:-1] + [(prefix[-1] + 97 * i) % cfg.shape.vocab] for i in ids]
+    return [synth.prompt_tokens(cfg, i) for i in ids]
+
+
+# ---------------------------------------------------------------------------
 # the reference arithmetic on the host cores (oracle/)
 # ---------------------------------------------------------------------------
 
-def cpu_decode_rate(cfg, path, steps: int, seconds: float, threads: int) -> dict:
-    """Greedy decode through the CPU restatement: prompt prefilled (untimed),
-    then up to `steps` decode passes or `seconds` of decode, whichever first."""
-    os.environ["OMP_NUM_THREADS"] = str(threads)
-    import oracle
-    from vc4b200 import synth
-    oracle.set_threads(threads)   # torchrun exports OMP_NUM_THREADS=1 to every rank
-    om = oracle.Model(path)
-    seqs = max(1, min(cfg.batch, 2))
-    tokens_done, t_total = 0, 0.0
-    for si in range(seqs):
-        prompt = synth.prompt_tokens(cfg, si)
-        s = oracle.Session(om, cfg.kv_bits)
-        for p, t in enumerate(prompt[:-1]):
-            s.step(t, p, want_logits=False)
-        tok, pos = prompt[-1], len(prompt) - 1
-        t0 = time.perf_counter()
-        for _ in range(steps):
-            lg = s.step(tok, pos)
-            tok = oracle.argmax(lg)
-            pos += 1
-            tokens_done += 1
-            if pos >= cfg.seq or time.perf_counter() - t0 > seconds / seqs:
-                break
-        t_total += time.perf_counter() - t0
-        s.close()
-    return {"value": tokens_done / t_total, "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": "%d greedy decode steps of %d sequence(s) after a %d-token prompt (prompt untimed), "
-                      "oracle/ C restatement, OpenMP over matrix rows" % (tokens_done, seqs, cfg.prompt)}
+class CpuDecode:
+    """Greedy decode through the CPU restatement of the reference layer loop.
+    The prompts are prefilled once (untimed, all host threads); a timed sample
+    then decodes `seqs` of the configuration's sequences from their prompts'
+    ends.  Sequences of one pass are independent, so the rate of a sample of
+    them is the configuration's CPU tokens/s."""
+
+    def __init__(self, cfg, path, seqs: int = 2):
+        import oracle
+        self.oracle = oracle
+        self.cfg = cfg
+        oracle.set_threads(os.cpu_count() or 1)
+        self.om = oracle.Model(path)
+        self.prompts = decode_prompts(cfg, 0)[:max(1, min(cfg.batch, seqs))]
+        self.rows = []   # per sampled sequence: the prompt's KV rows of every layer
+        shared = None
+        for p in self.prompts:
+            if cfg.extra.get("prefix_restore") and shared is not None:
+                self.rows.append(shared)
+                continue
+            s = oracle.Session(self.om, cfg.kv_bits)
+            for i, t in enumerate(p[:-1]):
+                s.step(t, i, want_logits=False)
+            r = [s.kv_rows(l, len(p) - 1) for l in range(self.om.info.layers)]
+            s.close()
+            self.rows.append(r)
+            if cfg.extra.get("prefix_restore"):
+                shared = r
+
+    def rate(self, steps: int, seconds: float, threads: int) -> dict:
+        self.oracle.set_threads(threads)
+        done, total = 0, 0.0
+        for p, rows in zip(self.prompts, self.rows):
+            s = self.oracle.Session(self.om, self.cfg.kv_bits)
+            for l, r in enumerate(rows):
+                s.kv_write(l, len(p) - 1, r)
+            tok, pos = p[-1], len(p) - 1
+            t0 = time.perf_counter()
+            for _ in range(steps):
+                tok = self.oracle.argmax(s.step(tok, pos))
+                pos += 1
+                done += 1
+                if pos >= self.cfg.seq or time.perf_counter() - t0 > seconds / len(self.prompts):
+                    break
+            total += time.perf_counter() - t0
+            s.close()
+        return {"value": done / total, "unit": "tokens/s", "cores": threads, "kind": "port",
+                "sample": "%d greedy decode steps of %d of the configuration's sequences from position %d "
+                          "(prompt prefilled untimed), oracle/ C restatement, OpenMP over matrix rows"
+                          % (done, len(self.prompts), len(self.prompts[0]) - 1)}
+
+
+def cpu_baseline(cfg, path, steps: int, seconds: float) -> dict:
+    """All-core rate, plus the single-thread rate on a shorter sample."""
+    cd = CpuDecode(cfg, path)
+    allc = cd.rate(steps, seconds, os.cpu_count() or 1)
+    one = cd.rate(steps, max(2.0, seconds / 3.0), 1)
+    allc["single_thread"] = {"value": one["value"], "cores": 1, "sample": one["sample"]}
+    return allc
 
 
 def run_reference(args, cfg, dist):
@@ -280,12 +349,14 @@ def run_reference(args, cfg, dist):
         return
     path = model_path(args.model_cfg)
     threads = os.cpu_count() or 1
-    r = cpu_decode_rate(cfg, path, max(1, args.steps + args.warmup), 10 * args.cpu_seconds, threads)
+    cd = CpuDecode(cfg, path)
+    # a step is one decode token of each sampled sequence
+    r = cd.rate(max(1, args.steps + args.warmup), 10 * args.cpu_seconds, threads)
     line = {"metric": METRIC, "value": r["value"], "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": 1000.0 / r["value"] * cfg.batch, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int64 (exact integer dot), f32/f64 epilogues",
+            "warmup": args.warmup, "ms_per_step": 1000.0 / r["value"] * len(cd.prompts), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": DTYPE,
             "data": "synthetic (seeded weights and prompts of the configuration's shape)",
-            "config": {"workload": workload_desc(cfg), "impl_note": "reference arithmetic on host cores"},
+            "config": config_of(cfg, args.gpus),
             "impl": "reference", "cpu_baseline": r,
             "e2e": {"value": r["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -295,42 +366,55 @@ def run_reference(args, cfg, dist):
 # the B200 path
 # ---------------------------------------------------------------------------
 
-def run_ours(args, cfg, dist):
+def peaks() -> tuple:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            pk = json.load(f)
+        return float(pk["hbm_gbs"]), "MEASURED_PEAKS.json hbm_gbs (measured)"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback 6650 GB/s"
+
+
+def measure(args, cfg, dist, full: bool = True) -> dict:
+    """Decode throughput of one configuration on this rank's GPU: device-
+    resident graph replays (`value`), then the public API with host buffers
+    (`e2e`), then the live per-op replay probe for the roofline."""
+    import ctypes as C
+
     import numpy as np
     import torch
     import vc4b200
-    from vc4b200 import synth
 
     dev = dist.local
     torch.cuda.set_device(dev)
-    path = model_path(args.model_cfg)
+    path = model_path(cfg)
     gpu = vc4b200.GPU(dev)
     model = vc4b200.Model(gpu, path)
     B = cfg.batch
     sess = vc4b200.Session(model, slots=B, seq=cfg.seq, kv=KV_NAME[cfg.kv_bits])
     info = model.info
+    prompts = decode_prompts(cfg, dist.rank)
     t0 = time.perf_counter()
     if cfg.extra.get("prefix_restore"):
-        # one prefix prefilled once, saved as MMKV1 and restored into every slot;
-        # the sequences part at the prefix's last position with distinct tokens
-        prefix = synth.prompt_tokens(cfg, 0)
-        sess.prefill(prefix[:-1], 0, slot=0, want_logits=False)
+        # one prefix prefilled once, saved as MMKV1 and restored into every slot
+        prefix = prompts[0][:-1]
+        sess.prefill(prefix, 0, slot=0, want_logits=False)
         mmkv = os.path.join(tempfile.gettempdir(), "vc4b200_prefix_%d_%d.mmkv" % (os.getpid(), dist.rank))
-        sess.save_prefix_cache(mmkv, prefix[:-1])
+        sess.save_prefix_cache(mmkv, prefix)
         for b in range(1, B):
             sess.load_prefix_cache(mmkv, slot=b)
         os.unlink(mmkv)
-        os.unlink(mmkv + ".json") if os.path.exists(mmkv + ".json") else None
-        prompts = [prefix[:-1] + [(prefix[-1] + 97 * i) % info.vocab] for i in sequence_ids(dist.rank, B)]
+        if os.path.exists(mmkv + ".json"):
+            os.unlink(mmkv + ".json")
     else:
-        prompts = [synth.prompt_tokens(cfg, i) for i in sequence_ids(dist.rank, B)]
         for b in range(B):
             sess.prefill(prompts[b][:-1], 0, slot=b, want_logits=False)
     prefill_s = time.perf_counter() - t0
-    P = cfg.prompt
+    P = len(prompts[0])
     stream = torch.cuda.ExternalStream(sess.stream())
     d_slots = torch.arange(B, dtype=torch.int32, device="cuda")
-    d_tok = torch.tensor([p[-1] for p in prompts], dtype=torch.int32, device="cuda")
+    first = torch.tensor([p[-1] for p in prompts], dtype=torch.int32)
+    d_tok = first.to("cuda")
     d_pos = torch.full((B,), P - 1, dtype=torch.int32, device="cuda")
     d_next = torch.zeros(B, dtype=torch.int32, device="cuda")
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
@@ -343,16 +427,12 @@ def run_ours(args, cfg, dist):
     torch.cuda.synchronize()
     pos_now = [P - 1]
 
-    def wrap_positions():
-        # positions cycle within [P-1, seq): restart from the prompt's end
-        if pos_now[0] >= cfg.seq:
+    def step():
+        if pos_now[0] >= cfg.seq:      # positions cycle within [P-1, seq)
             with torch.cuda.stream(stream):
-                d_tok.copy_(torch.tensor([p[-1] for p in prompts], dtype=torch.int32))
+                d_tok.copy_(first)
                 d_pos.fill_(P - 1)
             pos_now[0] = P - 1
-
-    def step():
-        wrap_positions()
         sess.step_batch_device(B, d_slots.data_ptr(), d_tok.data_ptr(), d_pos.data_ptr(), d_next.data_ptr(), True)
         pos_now[0] += 1
 
@@ -380,17 +460,16 @@ def run_ours(args, cfg, dist):
     tokens = dist.sum(B * args.steps)
     value = tokens / (ms_max / 1000.0)
 
-    # e2e: the public API with host buffers, greedy token read back each step
-    import ctypes as C
+    # e2e: the public API with host buffers, greedy tokens read back each step
     slots_h = np.arange(B, dtype=np.int32)
-    tok_h = np.array([p[-1] for p in prompts], np.int32)
+    tok_h = first.numpy().astype(np.int32)
     pos_h = np.full(B, P - 1, np.int32)
     torch.cuda.synchronize()
     e2e_s = 0.0
+    dist.barrier()
     for i in range(args.steps):
         if pos_h[0] >= cfg.seq:
-            tok_h[:] = [p[-1] for p in prompts]
-            pos_h[:] = P - 1
+            tok_h, pos_h = first.numpy().astype(np.int32), np.full(B, P - 1, np.int32)
         l2_flush(i)
         torch.cuda.synchronize()
         t = time.perf_counter()
@@ -405,59 +484,67 @@ def run_ours(args, cfg, dist):
 
     # live per-op timing (replay probe, cold L2) for the roofline
     L = info.layers
-    prof_pos = [min(int(pos_h[0]), cfg.seq - 1)] * B
+    prof_pos = np.array([min(int(pos_h[0]), cfg.seq - 1)] * B, np.int32)
     op_ms, op_bytes = {}, {}
+    P_ = vc4b200.engine._p
     for op in range(6):
         if OPS[op] is None:
             continue
-        avg = C.c_double()
-        byt = C.c_double()
-        pos_arr = np.array(prof_pos, np.int32)
-        rc = vc4b200.lib().vc4_profile_op(sess._h, op, L - 1, B, vc4b200.engine._p(slots_h),
-                                          vc4b200.engine._p(tok_h), vc4b200.engine._p(pos_arr), 20, 1,
+        avg, byt = C.c_double(), C.c_double()
+        rc = vc4b200.lib().vc4_profile_op(sess._h, op, L - 1, B, P_(slots_h), P_(tok_h), P_(prof_pos), 20, 1,
                                           C.byref(avg))
         if rc:
             raise RuntimeError(vc4b200.lib().vc4_last_error().decode())
-        vc4b200.lib().vc4_op_bytes(sess._h, op, L - 1, B, vc4b200.engine._p(pos_arr), C.byref(byt))
+        vc4b200.lib().vc4_op_bytes(sess._h, op, L - 1, B, P_(prof_pos), C.byref(byt))
         op_ms[OPS[op]] = avg.value
         op_bytes[OPS[op]] = byt.value
     per_step = {k: op_ms[k] * (1 if k == "logits" else L) for k in op_ms}
     dom = max(per_step, key=per_step.get)
-    peaks = {}
-    try:
-        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-            peaks = json.load(f)
-    except OSError:
-        pass
-    hbm = float(peaks.get("hbm_gbs") or 6650.0)
+    hbm, peak_src = peaks()
     achieved = op_bytes[dom] / (op_ms[dom] / 1000.0) / 1e9
-    # DRAM bytes of one launch of the dominant op from an ncu capture
-    # (profiles/traffic_<config>.txt: "op bytes [kv_positions]"; an attention
-    # capture is scaled by the KV positions, which its traffic is proportional to)
-    traffic = None
-    try:
-        with open(os.path.join(ROOT, "profiles", "traffic_%s.txt" % cfg.key)) as f:
-            for line in f:
-                parts = line.split()
-                if parts and parts[0] == dom:
-                    traffic = float(parts[1])
-                    if len(parts) > 2 and dom == "attention":
-                        traffic *= (prof_pos[0] + 1) / float(parts[2])
-    except OSError:
-        pass
     step_bytes = sum(op_bytes[k] * (1 if k == "logits" else L) for k in op_bytes)
-    roofline = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                "frac": achieved / hbm, "traffic": traffic,
-                "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)" if peaks else "fallback 6650 GB/s",
-                "bytes_per_launch": op_bytes[dom], "ms_per_launch": op_ms[dom],
-                "step_bytes": step_bytes, "step_frac": step_bytes / (ms / args.steps / 1000.0) / 1e9 / hbm,
-                "per_op_ms": op_ms, "per_op_bytes": op_bytes}
+    roofline = {"bound": "hbm", "kernel": KERNEL_OF[dom](B, info), "op": dom, "achieved": achieved, "peak": hbm,
+                "unit": "GB/s", "frac": achieved / hbm,
+                # DRAM bytes need an ncu capture, which this run does not make
+                "traffic": None, "peak_source": peak_src,
+                "bytes_per_launch": op_bytes[dom], "ms_per_launch": op_ms[dom], "kv_position": int(prof_pos[0]),
+                "step_bytes": step_bytes, "step_frac": step_bytes / (ms_max / args.steps / 1000.0) / 1e9 / hbm,
+                "per_op_ms": op_ms, "per_op_bytes": op_bytes, "share_per_step": {
+                    k: per_step[k] / (ms_max / args.steps) for k in per_step}}
+    if full:
+        roofline["matvec_batch1"] = matvec_roofline(dev, hbm)
+    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": dist.world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": DTYPE,
+            "data": "synthetic (seeded weights and prompts of the configuration's shape)",
+            "config": config_of(cfg, dist.world), "prefill_s": prefill_s,
+            "roofline": roofline, "e2e": e2e, "clocks": clk, "gpu_launches": l1 - l0}
+    sess.close()
+    model.close()
+    gpu.close()
+    return line
 
-    # batch-1 matvec roofline: the matvec_s kernel on large synthetic matrices
-    # (q8 of the c3 logits head's shape, 64 MiB of q4 and t3 weights; the
-    # other matrices of the configurations are 0.3-5 MB, too small for one
-    # launch to reach HBM speed), cold L2 and warm
-    matvec = {}
+
+# which kernel serves an op at a batch size (kernels.cu launch_* selection)
+KERNEL_OF = {
+    "qkv": lambda B, i: "k_tmm<qkv> (tcgen05)" if B >= 32 and i.wtype == 0 else "k_qkv" if B < 8 else "k_mm<qkv>",
+    "attention": lambda B, i: "k_attn_b" if B * i.kv_heads * (1 if (i.heads // i.kv_heads) % 2 else
+                                                                (i.heads // i.kv_heads) // 2) >= 128 else "k_attn",
+    "wo": lambda B, i: "k_tmm<wo> (tcgen05)" if B >= 32 and i.wtype == 0 else "k_wo" if B < 8 else "k_mm<wo>",
+    "ffn": lambda B, i: "k_tmm<w13>+k_tmm<w2> (tcgen05)" if B >= 32 and i.wtype == 0 else
+                        "k_gate" if B < 8 else "k_mm<ffn>+k_mmdown",
+    "logits": lambda B, i: "k_tmm<logits> (tcgen05)" if B >= 8 else "k_logits",
+}
+
+
+def matvec_roofline(dev: int, hbm: float) -> dict:
+    """Batch-1 matvec_s on large synthetic matrices (q8 of the c3 logits
+    head's shape, 64 MiB of q4 and t3 weights; the configurations' other
+    matrices are 0.3-5 MB, too small for one launch to reach HBM speed),
+    cold L2 and warm, 100 launches each."""
+    import ctypes as C
+    import vc4b200
+    out = {}
     for name, wt, rows, cols in (("q8", 0, 73448, 1024), ("q4", 1, 65536, 2048), ("t3", 2, 131072, 2048)):
         ent = {"rows": rows, "cols": cols}
         for mode, fl in (("cold", 1), ("warm", 0)):
@@ -469,27 +556,32 @@ def run_ours(args, cfg, dist):
             gbs = byt.value / (ms.value / 1000.0) / 1e9
             ent["bytes"] = byt.value
             ent[mode] = {"ms": ms.value, "gbs": gbs, "frac": gbs / hbm}
-        matvec[name] = ent
-    roofline["matvec_batch1"] = matvec
+        out[name] = ent
+    return out
 
-    cpu = None
+
+def run_ours(args, cfg, dist):
+    line = measure(args, cfg, dist, full=True)
     if dist.world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_decode_rate(cfg, path, args.steps, args.cpu_seconds, os.cpu_count() or 1)
-
-    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": dist.world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None,
-            "dtype": "int64 (exact dp4a integer dot), f32/f64 epilogues",
-            "data": "synthetic (seeded weights and prompts of the configuration's shape)",
-            "config": {"workload": workload_desc(cfg), "batch_per_gpu": B, "seq": cfg.seq, "quant": cfg.quant,
-                       "kv": KV_NAME[cfg.kv_bits], "parallelism": "dp%d replicas" % dist.world,
-                       "l2": "flushed between timed steps (256 MiB write, then read back so no dirty line is left)", "prefill_s": prefill_s},
-            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk, "gpu_launches": l1 - l0}
+        line["cpu_baseline"] = cpu_baseline(cfg, model_path(cfg), args.steps, args.cpu_seconds)
+    else:
+        line["cpu_baseline"] = None
+    if args.secondary:
+        from vc4b200 import synth
+        sec = []
+        for key in args.secondary.split(","):
+            c2 = synth.CONFIGS[key]
+            l2 = measure(args, c2, dist, full=False)
+            ent = {k: l2[k] for k in ("value", "ms_per_step", "e2e", "gpu_launches", "clocks")}
+            ent["config"] = l2["config"]
+            ent["roofline"] = {k: l2["roofline"][k] for k in ("kernel", "op", "achieved", "frac", "step_frac",
+                                                             "per_op_ms", "share_per_step")}
+            if dist.world == 1 and not args.no_cpu_baseline:
+                ent["cpu_baseline"] = cpu_baseline(c2, model_path(c2), args.steps, args.cpu_seconds / 2)
+            sec.append(ent)
+        line["secondary"] = sec
     if dist.rank == 0:
         print(json.dumps(line), flush=True)
-    sess.close()
-    model.close()
-    gpu.close()
 
 
 def main():
@@ -499,7 +591,8 @@ def main():
     args.model_cfg = cfg   # the container is always the configuration's own
     if args.seq:
         import dataclasses
-        cfg = dataclasses.replace(cfg, seq=args.seq, prompt=min(cfg.prompt, args.seq // 2))
+        cfg = dataclasses.replace(cfg, seq=args.seq, prompt=min(cfg.prompt, args.seq // 2),
+                                  extra=dict(cfg.extra, model=cfg.extra.get("model", cfg.key)))
     dist = Dist()
     try:
         if args.impl == "reference":

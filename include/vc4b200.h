@@ -166,6 +166,14 @@ VC4_API int vc4_op_bytes(const vc4_session* s, int op, int layer, int n, const i
 VC4_API int vc4_matvec_probe(int device, int wtype, int rows, int cols, int path, int reps, int flush,
                              double* ms_avg, double* bytes, unsigned long long* digest);
 
+/* No counterpart in the reference (a test helper for the packed KV codec,
+   shaders_attn.cpp:141-159).  Runs the attention kernels' own cache encoder
+   on n arbitrary floats on `device` and writes each value's cache bytes to
+   out: kv_bits 16 gives two bytes a value (q16 level on the 1/2048 grid,
+   big-endian), 8 gives one (q8 level on the 1/16 grid).  Allocates and frees
+   its own device buffers; synchronous. */
+VC4_API int vc4_kv_codec_probe(int device, int kv_bits, const float* x, int n, void* out);
+
 /* No counterpart in the reference.  vc4_matvec_s for callers that cannot
    allocate device memory: a host whose device memory belongs to its own pool,
    or a thread that must not risk the device synchronisation an allocation can

@@ -31,3 +31,21 @@ def golden():
     import json
     with open(os.path.join(ROOT, "tests", "golden", "golden.json")) as f:
         return json.load(f)
+
+
+def full_model_path(key: str) -> str:
+    """The container of a benchmark configuration at its full shape, written
+    once per host by the MMCF writer (c3b32 shares c3's container)."""
+    import tempfile
+    from vc4b200 import mmcf_writer, synth
+    cfg = synth.CONFIGS[key]
+    key = cfg.extra.get("model", "c3" if key == "c3b32" else key)
+    cfg = synth.CONFIGS[key]
+    d = os.path.join(tempfile.gettempdir(), "vc4b200_models")
+    os.makedirs(d, exist_ok=True)
+    p = os.path.join(d, "%s_%d.mmcf" % (key, cfg.seed))
+    if not os.path.exists(p):
+        tmp = p + ".%d.tmp" % os.getpid()
+        mmcf_writer.write_config(cfg, tmp)
+        os.replace(tmp, p)
+    return p

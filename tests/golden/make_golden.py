@@ -15,7 +15,9 @@ host).  For every synthetic configuration it
 It also lifts the x_pack byte vectors out of engine/tests/test_xformat.cpp.
 Output: tests/golden/golden.json.
 
-    python tests/golden/make_golden.py [--ref /root/reference] [--full]
+    python tests/golden/make_golden.py [--ref REFERENCE_CHECKOUT] [--full]
+
+--ref defaults to the environment variable VC4_REFERENCE.
 """
 from __future__ import annotations
 
@@ -66,9 +68,11 @@ def pack_with_reference(ref: str, cfg: synth.Config, workdir: str) -> tuple:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("VC4_REFERENCE"))
     ap.add_argument("--full", action="store_true", help="also pack the five full-size configurations")
     args = ap.parse_args()
+    if not args.ref or not os.path.isdir(os.path.join(args.ref, "engine", "src")):
+        raise SystemExit("name the reference checkout with --ref or VC4_REFERENCE")
     subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), "ref", "REF=" + args.ref], check=True)
     golden = {"xformat": xformat_vectors(args.ref), "containers": {}}
     cfgs = dict(synth.TINY_CONFIGS)

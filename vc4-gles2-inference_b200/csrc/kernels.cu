@@ -188,6 +188,46 @@ __global__ void k_fill_bytes(uint8_t* p, size_t n, uint32_t seed) {
 }  // namespace
 }  // namespace vc4
 
+namespace vc4 {
+namespace {
+// The cache codec of the attention kernels (kv_encode) on arbitrary inputs:
+// value i's packed bytes, as the cache row holds them (q16: two bytes,
+// big-endian; q8: one two's-complement byte).
+__global__ void k_kv_codec(const float* __restrict__ x, int n, int kvb, uint8_t* __restrict__ out) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        float dec;
+        const unsigned w = kv_encode(x[i], kvb, &dec);
+        out[(size_t)i * kvb] = (uint8_t)w;
+        if (kvb == 2) out[(size_t)i * 2 + 1] = (uint8_t)(w >> 8);
+    }
+}
+}  // namespace
+}  // namespace vc4
+
+extern "C" VC4_API int vc4_kv_codec_probe(int device, int kv_bits, const float* x, int n, void* out) {
+    using namespace vc4;
+    if ((kv_bits != 16 && kv_bits != 8) || n <= 0 || !x || !out) return set_error(VC4_EINVAL, "kv_codec_probe: bad arguments");
+    if (cudaSetDevice(device) != cudaSuccess) return set_error(VC4_ECUDA, "kv_codec_probe: cudaSetDevice failed");
+    const int kvb = kv_bits / 8;
+    float* dx = nullptr;
+    uint8_t* dy = nullptr;
+    if (cudaMalloc(&dx, (size_t)n * 4) != cudaSuccess) return set_error(VC4_ECUDA, "kv_codec_probe: cudaMalloc failed");
+    if (cudaMalloc(&dy, (size_t)n * kvb) != cudaSuccess) {
+        cudaFree(dx);
+        return set_error(VC4_ECUDA, "kv_codec_probe: cudaMalloc failed");
+    }
+    cudaError_t e = cudaMemcpy(dx, x, (size_t)n * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) {
+        k_kv_codec<<<(n + 255) / 256 < 1184 ? (n + 255) / 256 : 1184, 256>>>(dx, n, kvb, dy);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaMemcpy(out, dy, (size_t)n * kvb, cudaMemcpyDeviceToHost);
+    cudaFree(dx);
+    cudaFree(dy);
+    if (e != cudaSuccess) return set_error(VC4_ECUDA, "kv_codec_probe: a CUDA call failed");
+    return VC4_OK;
+}
+
 extern "C" VC4_API int vc4_matvec_probe(int device, int wtype, int rows, int cols, int path, int reps, int flush,
                                         double* ms_avg, double* bytes, unsigned long long* digest) {
     using namespace vc4;

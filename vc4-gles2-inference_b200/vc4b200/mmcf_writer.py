@@ -6,8 +6,10 @@ the same float tensors.  What has to be alike is alike by necessity -- the
 container format (docs/checkpoint-container.md), the quantisers' arithmetic
 (mmcf_hf.py qmat/q8mat/q4mat/t3mat, lines 51-165) and the record order
 (mmcf_hf.py tensors_from_hf, lines 1658-2013; mmcf_pack.py build, 284-432) --
-and tests/test_mmcf_writer.py checks the output against the reference
-packer's bytes (sha256 recorded by tests/golden/make_golden.py).
+and tests/test_oracle_pins.py::test_writer_matches_reference_packer checks
+the output against the reference packer's bytes (sha256 recorded by
+tests/golden/make_golden.py).  The q4 quantiser follows mmcf_hf.py q4mat
+expression for expression: the byte contract leaves no freedom there.
 
 The rail calibration pass the reference packer runs (metadata key 15, written
 only when a model's SwiGLU hidden exceeds the q16 rail) is not restated: the
