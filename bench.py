@@ -454,6 +454,7 @@ def measure(args, cfg, dist, full: bool = True) -> dict:
     torch.cuda.synchronize()
     dist.barrier()
     clk = clocks.stop()
+    sess.check()
     l1, _ = sess.counters()
     ms = sum(a.elapsed_time(b) for a, b in ev)
     ms_max = dist.max(ms)

@@ -36,6 +36,7 @@ extern "C" {
 #define VC4_ECUDA 3       /* a CUDA call failed                             */
 #define VC4_EIO 4         /* file I/O                                       */
 #define VC4_ESTATE 5      /* wrong call order / mismatched cache            */
+#define VC4_ERANGE 6      /* an activation left the range the kernels compute */
 
 typedef struct vc4_gpu vc4_gpu;         /* device + stream (class GPU)            */
 typedef struct vc4_model vc4_model;     /* uploaded weights (Model + GPU::upload) */
@@ -107,6 +108,12 @@ VC4_API int vc4_step_batch_device(vc4_session* s, int n, const int* d_slots, int
                           int* d_next_tokens, int advance);
 /* The session's CUDA stream (cudaStream_t), for event timing. */
 VC4_API void* vc4_session_stream(vc4_session* s);
+/* The kernels' self-check word after device-resident passes (GPU::sync,
+   gpu.cpp:53, plus the error the reference's shaders cannot report):
+   synchronises the session stream; VC4_OK, or the status of the first
+   failed check (VC4_ERANGE: an activation left the kernels' range; VC4_ECUDA:
+   a launch or copy check).  vc4_step* calls check it themselves. */
+VC4_API int vc4_session_check(vc4_session* s);
 
 /* Prefill of a prompt on one slot: positions pos0 .. pos0+n-1 run in order
    (the serial prompt loop, chat.cpp:245-297); the logits of the last position

@@ -620,6 +620,7 @@ struct orc_session {
     /* scratch */
     float *x, *xb, *x1, *xbf, *qkv, *q, *k, *v, *att, *o2, *gate, *h, *scores;
     double* pv;
+    int32_t* qi;         /* one query head on its integer grid */
     int16_t* xq;
     int32_t *iv, *iv2, *g, *u;
 };
@@ -630,7 +631,7 @@ void orc_session_free(orc_session* s) {
     free(s->kv); free(s->kdec); free(s->vdec); free(s->rope_cos); free(s->rope_sin);
     free(s->x); free(s->xb); free(s->x1); free(s->xbf); free(s->qkv); free(s->q); free(s->k);
     free(s->v); free(s->att); free(s->o2); free(s->gate); free(s->h); free(s->scores); free(s->pv);
-    free(s->xq); free(s->iv); free(s->iv2); free(s->g); free(s->u);
+    free(s->qi); free(s->xq); free(s->iv); free(s->iv2); free(s->g); free(s->u);
     free(s);
 }
 
@@ -665,6 +666,7 @@ orc_session* orc_session_new(const orc_model* m, int kv_bits, int literal) {
     s->h = (float*)malloc(sizeof(float) * in->ffn_width);
     s->scores = (float*)malloc(sizeof(float) * S);
     s->pv = (double*)malloc(sizeof(double) * in->head_dim);
+    s->qi = (int32_t*)malloc(sizeof(int32_t) * in->head_dim);
     s->xq = (int16_t*)malloc(sizeof(int16_t) * big);
     s->iv = (int32_t*)malloc(sizeof(int32_t) * big); s->iv2 = (int32_t*)malloc(sizeof(int32_t) * big);
     s->g = (int32_t*)malloc(sizeof(int32_t) * in->ffn_width); s->u = (int32_t*)malloc(sizeof(int32_t) * in->ffn_width);
@@ -749,6 +751,13 @@ static void kv_store(orc_session* s, int layer, int pos, const float* k, const f
     uint8_t* row = s->kv[layer] + (size_t)pos * s->row_bytes;
     float* kd = s->kdec[layer] + (size_t)pos * KD;
     float* vd = s->vdec[layer] + (size_t)pos * KD;
+    if (s->literal == ORC_LITERAL_FLOAT_KV) {
+        /* the reference CPU path's own cache: the float K and V as computed
+           (session.cpp:446-447); the packed row is not kept */
+        memcpy(kd, k, sizeof(float) * KD);
+        memcpy(vd, v, sizeof(float) * KD);
+        return;
+    }
     for (int i = 0; i < KD; ++i) {
         if (s->kv_bits == 16) {
             const int16_t qk = orc_kv_q16(k[i]), qv = orc_kv_q16(v[i]);
@@ -788,6 +797,17 @@ int orc_attn_weight_exp(int len, int kv_bits) {
     return 53 - (kv_bits == 16 ? 15 : 7) - lg;
 }
 
+/* Exponent F of a query head's integer grid: with max|q| = f * 2^e (f in
+   [0.5, 1)), F = 22 - e, so every |q * 2^F| < 2^22 and rint(q * 2^F) splits
+   into three balanced signed bytes; clamped to [-100, 100]. */
+int orc_q_grid_exp(float qmax) {
+    if (!(qmax > 0.0f)) return 0;
+    int e = 0;
+    frexpf(qmax, &e);
+    int F = 22 - e;
+    return F > 100 ? 100 : F < -100 ? -100 : F;
+}
+
 /* attention (session.cpp:1989-2050) over the decoded cache. */
 static void attention(orc_session* s, int layer, int pos) {
     const orc_info* in = &s->m->in;
@@ -799,12 +819,33 @@ static void attention(orc_session* s, int layer, int pos) {
         const float* vb = s->vdec[layer] + (size_t)kvh * hd;
         const float* qh = s->q + (size_t)h * hd;
         float mx = -1e30f;
-        for (int t = 0; t <= pos; ++t) {
-            float acc = 0.0f;
-            for (int i = 0; i < hd; ++i) acc = acc + qh[i] * kb[(size_t)t * KD + i];
-            acc = acc / sq;
-            s->scores[t] = acc;
-            if (acc > mx) mx = acc;
+        if (s->literal) {
+            for (int t = 0; t <= pos; ++t) {
+                float acc = 0.0f;
+                for (int i = 0; i < hd; ++i) acc = acc + qh[i] * kb[(size_t)t * KD + i];
+                acc = acc / sq;
+                s->scores[t] = acc;
+                if (acc > mx) mx = acc;
+            }
+        } else {
+            /* Canonical: q on a per-head power-of-two grid (orc_q_grid_exp),
+               an exact integer dot with the cache levels, one rounding to
+               float, then the power-of-two grid scale and / sqrt(hd). */
+            float qm = 0.0f;
+            for (int i = 0; i < hd; ++i) { const float a = fabsf(qh[i]); if (a > qm) qm = a; }
+            const int F = orc_q_grid_exp(qm);
+            const float sF = ldexpf(1.0f, F);
+            for (int i = 0; i < hd; ++i) s->qi[i] = (int32_t)rintf(qh[i] * sF);
+            const float gscale = ldexpf(1.0f, -F - (s->kv_bits == 16 ? 11 : 4));
+            const float vgrid = s->kv_bits == 16 ? 2048.0f : 16.0f;
+            for (int t = 0; t <= pos; ++t) {
+                const float* kr = kb + (size_t)t * KD;
+                int64_t S = 0;
+                for (int i = 0; i < hd; ++i) S += (int64_t)s->qi[i] * (int64_t)(kr[i] * vgrid);
+                const float acc = ((float)S * gscale) / sq;
+                s->scores[t] = acc;
+                if (acc > mx) mx = acc;
+            }
         }
         if (s->literal) {
             float sum = 0.0f;
@@ -850,8 +891,8 @@ static void attention(orc_session* s, int layer, int pos) {
 }
 
 /* SiLU(g)*u with the shaders' fp32 order (shaders.cpp:116-136, 1850-1922). */
-static float swiglu1(const orc_session* s, float g, float u) {
-    const float e = s->literal ? expf(-g) : orc_expf(-g);
+static float swiglu_lit(int literal, float g, float u) {
+    const float e = literal ? expf(-g) : orc_expf(-g);
     const float den = 1.0f + e;
     const float a = g / den;
     return a * u;
@@ -861,22 +902,30 @@ static float swiglu1(const orc_session* s, float g, float u) {
    (session.cpp:491-551, gpu_ffn.cpp:67-132): gate/up matvecs rounded to q16,
    SiLU(gate)*up stored as q16 pairs, w2 per chunk rounded to q16, the two
    chunk outputs added with add_q16. */
+/* The FFN gate kernel: gate/up matvecs of the q16 input, SiLU(g)*u (times
+   2^-hs for a key-15 layer) stored on the q16 grid (the shaders' floor(v+0.5)
+   store); g, u and hq hold F values. */
+static void ffn_gate(const orc_model* m, int layer, const omat* w1, const omat* w3, const int16_t* xq,
+                     int literal, int32_t* g, int32_t* u, int16_t* hq) {
+    const int D = m->in.dim, F = m->in.ffn_width;
+    const int hs = m->hid_scale[layer];
+    const float hsm = hs > 0 ? ldexpf(1.0f, -hs) : 1.0f;
+    mv_range(w1, 0, D, xq, g, literal);
+    mv_range(w3, 0, D, xq, u, literal);
+    for (int r = 0; r < F; ++r) {
+        const float gf = (float)g[r] / 256.0f, uf = (float)u[r] / 256.0f;
+        float y = swiglu_lit(literal, gf, uf);
+        if (hs > 0) y = y * hsm;
+        hq[r] = (int16_t)q16s(y);
+    }
+}
+
 static void ffn(orc_session* s, int layer, const omat* w1, const omat* w3, const omat* w2, float* o2) {
     const orc_info* in = &s->m->in;
     const int D = in->dim, F = in->ffn_width;
-    const int hs = s->m->hid_scale[layer];
-    const float hsm = hs > 0 ? ldexpf(1.0f, -hs) : 1.0f;
     for (int i = 0; i < D; ++i) s->xq[i] = orc_q16(s->xbf[i]);
-    mv_range(w1, 0, D, s->xq, s->g, s->literal);
-    mv_range(w3, 0, D, s->xq, s->u, s->literal);
-    for (int r = 0; r < F; ++r) {
-        const float g = (float)s->g[r] / 256.0f, u = (float)s->u[r] / 256.0f;
-        float y = swiglu1(s, g, u);
-        if (hs > 0) y = y * hsm;
-        s->h[r] = (float)q16s(y) / 256.0f;
-    }
     int16_t* hq = (int16_t*)malloc(sizeof(int16_t) * F);
-    for (int r = 0; r < F; ++r) hq[r] = (int16_t)lrintf(s->h[r] * 256.0f);
+    ffn_gate(s->m, layer, w1, w3, s->xq, s->literal, s->g, s->u, hq);
     if (!in->ffn_chunked) {
         mv_range(w2, 0, F, hq, s->iv, s->literal);
         for (int i = 0; i < D; ++i) o2[i] = (float)s->iv[i] / 256.0f;
@@ -888,6 +937,43 @@ static void ffn(orc_session* s, int layer, const omat* w1, const omat* w3, const
             const float a = (float)s->iv[i] / 256.0f, b = (float)s->iv2[i] / 256.0f;
             o2[i] = q16f(a + b);                               /* add_q16 */
         }
+    }
+    free(hq);
+}
+
+/* The dense FFN of a model whose hidden width is split into two chunks
+   (Model::split_ffn, model.cpp:217-270, as App::prepare_model runs it): the
+   split leaves w1 empty, so the CPU layer loop takes its host FFN
+   (session.cpp:499-524), not the GPU FFN kernels: matvec_s of the gate and
+   up halves (2^k input scaling, gpu_conv.cpp:271-287), the host SwiGLU
+   rounded with quantize_act (session.cpp:2069-2080), times 2^-hs for a
+   key-15 layer, matvec_s of each w2 column half with its own 2^k, and
+   add_q16 of the two halves.  The a/b halves of w1 and w3 are row slices,
+   so one matvec over all rows gives both. */
+static void ffn_host(orc_session* s, int layer, const omat* w1, const omat* w3, const omat* w2, float* o2) {
+    const orc_info* in = &s->m->in;
+    const int D = in->dim, F = in->ffn_width, c = in->ffn_chunk;
+    const int hs = s->m->hid_scale[layer];
+    const float hsm = hs > 0 ? ldexpf(1.0f, -hs) : 1.0f;
+    const int k = orc_scale_input(s->xbf, D, s->xq);
+    mv_range(w1, 0, D, s->xq, s->g, s->literal);
+    mv_range(w3, 0, D, s->xq, s->u, s->literal);
+    const float inv = ldexpf(1.0f, -k);
+    for (int r = 0; r < F; ++r) {
+        const float g = ((float)s->g[r] / 256.0f) * inv, u = ((float)s->u[r] / 256.0f) * inv;
+        float h = q16f(swiglu_lit(s->literal, g, u));
+        if (hs > 0) h = h * hsm;
+        s->h[r] = h;
+    }
+    int16_t* hq = (int16_t*)malloc(sizeof(int16_t) * F);
+    const int ka = orc_scale_input(s->h, c, hq);
+    mv_range(w2, 0, c, hq, s->iv, s->literal);
+    const int kb = orc_scale_input(s->h + c, F - c, hq + c);
+    mv_range(w2, c, F, hq + c, s->iv2, s->literal);
+    const float ia = ldexpf(1.0f, -ka), ib = ldexpf(1.0f, -kb);
+    for (int i = 0; i < D; ++i) {
+        const float a = ((float)s->iv[i] / 256.0f) * ia, b = ((float)s->iv2[i] / 256.0f) * ib;
+        o2[i] = q16f(a + b);                                   /* add_q16 */
     }
     free(hq);
 }
@@ -940,6 +1026,8 @@ int orc_step(orc_session* s, int token, int pos, float* logits) {
         if (expert >= 0) {
             const oexpert* ex = &m->moe[(size_t)l * in->experts + expert];
             ffn(s, l, &ex->w1, &ex->w3, &ex->w2, s->o2);
+        } else if (in->ffn_chunked) {
+            ffn_host(s, l, &m->w1[l], &m->w3[l], &m->w2[l], s->o2);
         } else {
             ffn(s, l, &m->w1[l], &m->w3[l], &m->w2[l], s->o2);
         }
@@ -1013,6 +1101,34 @@ int orc_model_matvec(const orc_model* m, int which, int layer, int expert,
     const omat* w = pick(m, which, layer, expert);
     if (!w) return ORC_EARG;
     mv_range(w, 0, w->cols, xq, out, 0);
+    return ORC_OK;
+}
+
+int orc_model_mv(const orc_model* m, int which, int layer, int expert, int c0, int c1,
+                 const int16_t* xq, int literal, int32_t* out) {
+    const omat* w = pick(m, which, layer, expert);
+    if (!w || w->wtype == -1 || c0 < 0 || c1 > w->cols || c0 >= c1) return ORC_EARG;
+    if (w->wtype == ORC_W_Q4 && (c0 % 32 || c1 % 32)) return ORC_EARG;
+    mv_range(w, c0, c1, xq, out, which == 5 ? 0 : literal);
+    return ORC_OK;
+}
+
+int orc_ffn_hidden(const orc_model* m, int layer, int expert, const int16_t* xq, int literal, int16_t* hq) {
+    const orc_info* in = &m->in;
+    if (layer < 0 || layer >= in->layers) return ORC_EARG;
+    const omat *w1, *w3;
+    if (in->experts > 0) {
+        if (expert < 0 || expert >= in->experts) return ORC_EARG;
+        const oexpert* e = &m->moe[(size_t)layer * in->experts + expert];
+        w1 = &e->w1; w3 = &e->w3;
+    } else {
+        w1 = &m->w1[layer]; w3 = &m->w3[layer];
+    }
+    const int F = in->ffn_width;
+    int32_t* g = (int32_t*)malloc(sizeof(int32_t) * F);
+    int32_t* u = (int32_t*)malloc(sizeof(int32_t) * F);
+    ffn_gate(m, layer, w1, w3, xq, literal, g, u, hq);
+    free(g); free(u);
     return ORC_OK;
 }
 

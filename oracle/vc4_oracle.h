@@ -17,6 +17,10 @@
  *     clamped to the q16 rail (the shaders' floor(s*ws+0.5));
  *   - float loops are written out op by op with no fused multiply-add unless
  *     fmaf() is spelled out;
+ *   - a query head is put on a power-of-two integer grid (orc_q_grid_exp)
+ *     and its score with a cached key is the exact integer dot with the
+ *     cache levels, rounded once to float and scaled by the grids and
+ *     1/sqrt(head_dim); the reference sums q*k sequentially in fp32;
  *   - attention weights are integers E_t = rint(exp(s_t - max) * 2^k) on a grid
  *     fine enough for k to keep every sum of E_t and E_t x (cache level) an
  *     exact integer in double (orc_attn_weight_exp), so the softmax
@@ -59,7 +63,12 @@ int orc_model_info(const orc_model* m, orc_info* info);
 void orc_rope_tables(float theta, int head_dim, int seq, const float* factors,
                      float* cos_out, float* sin_out);
 
-/* A decode session.  kv_bits is 16 or 8 (the KV axis). */
+/* A decode session.  kv_bits is 16 or 8 (the KV axis).  literal: 0 the
+   canonical arithmetic, ORC_LITERAL the reference's literal float orders with
+   the packed KV cache, ORC_LITERAL_FLOAT_KV the literal orders with the
+   reference CPU path's float K/V cache (session.cpp:446-447; the packed rows
+   are then not kept). */
+enum { ORC_CANONICAL = 0, ORC_LITERAL = 1, ORC_LITERAL_FLOAT_KV = 2 };
 orc_session* orc_session_new(const orc_model* m, int kv_bits, int literal);
 void orc_session_free(orc_session* s);
 /* One position through the layer loop.  logits (vocab floats, q16 grid) may be
@@ -85,6 +94,9 @@ int16_t orc_q16(float v);
 /* KV codec: q16 grid 1/2048 big-endian, q8 grid 1/16. */
 int16_t orc_kv_q16(float v);
 int8_t orc_kv_q8(float v);
+/* Exponent F of a query head's integer grid for max|q| = qmax: 22 - e with
+   qmax = f * 2^e, f in [0.5, 1), clamped to [-100, 100]. */
+int orc_q_grid_exp(float qmax);
 /* Exponent k of the attention weights' grid for len positions and the cache
    width: 53 - (7 for q8, 15 for q16) - ceil(log2 len). */
 int orc_attn_weight_exp(int len, int kv_bits);
@@ -94,6 +106,16 @@ int orc_attn_weight_exp(int len, int kv_bits);
    6 logits tile (layer = tile index), expert selects an MoE expert. */
 int orc_model_matvec(const orc_model* m, int which, int layer, int expert,
                      const int16_t* xq, int k, int32_t* out);
+/* The shader matvec of one model matrix over columns [c0, c1) (xq holds
+   c1 - c0 q16 ints; no input scaling), every row: out receives the clamped
+   q16 ints.  literal selects the shaders' fp32 accumulation for q8 / t3
+   (the i16 router is exact in both). */
+int orc_model_mv(const orc_model* m, int which, int layer, int expert, int c0, int c1,
+                 const int16_t* xq, int literal, int32_t* out);
+/* The GPU FFN gate kernel the CPU path draws (gpu_ffn.cpp:17-132): gate/up
+   matvecs of the q16 input xq (dim values), SiLU(g)*u (times 2^-hs for a
+   key-15 layer), stored as q16 ints in hq (ffn_width values). */
+int orc_ffn_hidden(const orc_model* m, int layer, int expert, const int16_t* xq, int literal, int16_t* hq);
 /* Decoded weight level of one entry (for dequant parity). */
 int orc_model_mat_shape(const orc_model* m, int which, int layer, int expert,
                         int* rows, int* cols, int* wtype, float* scale);

@@ -13,7 +13,10 @@ host).  For every synthetic configuration it
      summary (shapes, scales, FNV digests of every tensor's values).
 
 It also lifts the x_pack byte vectors out of engine/tests/test_xformat.cpp.
-Output: tests/golden/golden.json.
+Output: tests/golden/golden.json.  With --session it instead runs the
+reference's own CPU layer loop (engine/src/session.cpp, built into
+oracle/_ref/ref_session) on every configuration's seeded prompt and writes
+its logits to tests/golden/reference_logits.npz.
 
     python tests/golden/make_golden.py [--ref REFERENCE_CHECKOUT] [--full]
 
@@ -70,10 +73,16 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("VC4_REFERENCE"))
     ap.add_argument("--full", action="store_true", help="also pack the five full-size configurations")
+    ap.add_argument("--session", action="store_true",
+                    help="only record the reference layer loop's logits (oracle/_ref/ref_session) into "
+                         "reference_logits.npz")
     args = ap.parse_args()
     if not args.ref or not os.path.isdir(os.path.join(args.ref, "engine", "src")):
         raise SystemExit("name the reference checkout with --ref or VC4_REFERENCE")
     subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), "ref", "REF=" + args.ref], check=True)
+    if args.session:
+        reference_session_logits()
+        return
     golden = {"xformat": xformat_vectors(args.ref), "containers": {}}
     cfgs = dict(synth.TINY_CONFIGS)
     if args.full:
@@ -95,6 +104,32 @@ def main():
         golden["containers"].setdefault(k, v)
     with open(gp, "w") as f:
         json.dump(golden, f, indent=1, sort_keys=True)
+
+
+def reference_session_logits() -> None:
+    """The reference's own CPU layer loop (engine/src/session.cpp compiled by
+    `make -C oracle ref`, shader calls through the oracle's restatement) on
+    the seeded prompts of every configuration, teacher-forced; the logits are
+    on the q16 grid and are stored as int16 (value * 256)."""
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import numpy as np
+    import refsession
+    from vc4b200 import mmcf_writer
+    out = {}
+    cfgs = dict(synth.TINY_CONFIGS, **{k: synth.CONFIGS[k] for k in ("c0", "c1", "c2", "c3", "c4")})
+    with tempfile.TemporaryDirectory() as wd:
+        for key, n in refsession.POSITIONS.items():
+            cfg = cfgs[key]
+            path = os.path.join(wd, key + ".mmcf")
+            mmcf_writer.write_config(cfg, path)
+            toks = synth.prompt_tokens(cfg)[:n]
+            lg = refsession.run(path, cfg.kv_bits, toks)
+            q = np.rint(lg * 256.0)
+            assert np.array_equal(q / 256.0, lg) and np.abs(q).max() < 32768
+            out[key] = q.astype(np.int16)
+            out[key + "_tokens"] = np.array(toks, np.int32)
+            print(key, lg.shape, flush=True)
+    np.savez_compressed(os.path.join(HERE, "reference_logits.npz"), **out)
 
 
 if __name__ == "__main__":

@@ -102,7 +102,9 @@ __global__ void __launch_bounds__(kThreads) k_prep(DMat W, DMat E, const float* 
         const int e = route_block(x, router, d.dim, d.experts, red);
         if (threadIdx.x == 0) s.route[(size_t)b * d.layers + layer] = e;
     }
-    const int k = (op == kOpQkv || op == kOpWo) ? scale_exponent(x, d.dim, red) : 0;
+    // matvec_s scales qkv, wo and, in the host FFN, the gate/up input
+    const int k = (op == kOpQkv || op == kOpWo || (op == kOpGate && d.hostffn)) ? scale_exponent(x, d.dim, red) : 0;
+    if (op == kOpGate && d.hostffn && threadIdx.x < 2) s.hmax[hmax_at(layer, b, threadIdx.x, s.slots)] = 0;
     char* rec = s.xrec + (size_t)b * xrec_bytes(W);
     XStage xs;
     xs.stride = x_stride(W);
@@ -263,9 +265,13 @@ __global__ void __launch_bounds__(kThreads) k_mm(MatSet M, State s, Batch bt, Di
                     int q = 0;
                     if (live) {
                         const int u = mv_epi(S3[i] - corr, rs3[lane]);
-                        float y = swiglu1(__fmul_rn((float)v, 1.0f / 256.0f), __fmul_rn((float)u, 1.0f / 256.0f));
-                        if (hs > 0) y = __fmul_rn(y, ldexpf(1.0f, -hs));     // metadata key 15 store scale
-                        q = q16s(y);
+                        if (d.hostffn) {
+                            q = host_hidden(v, u, k);
+                        } else {
+                            float y = swiglu1(__fmul_rn((float)v, 1.0f / 256.0f), __fmul_rn((float)u, 1.0f / 256.0f));
+                            if (hs > 0) y = __fmul_rn(y, ldexpf(1.0f, -hs));     // metadata key 15 store scale
+                            q = q16s(y);
+                        }
                     }
                     // the w2 input record of sequence b: this block's 32 hidden rows are
                     // columns [c0, c0 + 32) of one w2 column half (the chunk is a multiple of 32)
@@ -281,6 +287,10 @@ __global__ void __launch_bounds__(kThreads) k_mm(MatSet M, State s, Batch bt, Di
                     if (lane == 0) {
                         if (WT == W_Q4) reinterpret_cast<int*>(hr + g)[c0 / 32] = sum;
                         if (WT == W_T3) atomicAdd(reinterpret_cast<int*>(hr + g), sum);
+                    }
+                    if (d.hostffn) {
+                        const int mq = __reduce_max_sync(0xffffffffu, abs(q));
+                        if (lane == 0 && mq) atomicMax(s.hmax + hmax_at(layer, b, half, s.slots), mq);
                     }
                 } else if (live) {
                     s.logits[(size_t)b * d.vocab + row] = v;
@@ -318,7 +328,8 @@ __host__ __device__ inline size_t mmdown_smem(const DMat& Wa, const DMat& Wb, bo
 }
 
 template <int WT>
-__global__ void __launch_bounds__(kThreads) k_mmdown(MatSet M2, State s, Batch bt, Dims d, int layer, int group) {
+__global__ void __launch_bounds__(kThreads) k_mmdown(MatSet M2, State s, Batch bt, Dims d, int layer, int group,
+                                                     int hs) {
     const int blk = blockIdx.x, expert = blockIdx.y;
     const bool two = d.chunk < d.ffn;
     const DMat& Wa = M2.a[expert];
@@ -389,12 +400,20 @@ __global__ void __launch_bounds__(kThreads) k_mmdown(MatSet M2, State s, Batch b
                 if (i >= ni || row >= Wa.rows) continue;
                 const int b = members[g0 + i0 + i];
                 const long long ca = WT == W_T3 ? reinterpret_cast<const int*>(ra[i] + R.g_a)[0] : 0;
-                float o2 = __fmul_rn((float)mv_epi(Sa[i] - ca, rsa[lane]), 1.0f / 256.0f);
-                if (two) {
+                float o2;
+                if (d.hostffn) {
                     const long long cb = WT == W_T3 ? reinterpret_cast<const int*>(ra[i] + R.g_b)[0] : 0;
-                    const int vb = mv_epi(Sb[i] - cb, rsb[lane]);
-                    // add_q16 of the two chunk outputs (session.cpp:2052-2067)
-                    o2 = __fmul_rn((float)q16h(__fadd_rn(o2, __fmul_rn((float)vb, 1.0f / 256.0f))), 1.0f / 256.0f);
+                    const float oa = host_w2_out(Sa[i] - ca, rsa[lane], hidden_exp(s, layer, b, 0), hs, s.err);
+                    const float ob = host_w2_out(Sb[i] - cb, rsb[lane], hidden_exp(s, layer, b, 1), hs, s.err);
+                    o2 = __fmul_rn((float)q16h(__fadd_rn(oa, ob)), 1.0f / 256.0f);
+                } else {
+                    o2 = __fmul_rn((float)mv_epi(Sa[i] - ca, rsa[lane]), 1.0f / 256.0f);
+                    if (two) {
+                        const long long cb = WT == W_T3 ? reinterpret_cast<const int*>(ra[i] + R.g_b)[0] : 0;
+                        const int vb = mv_epi(Sb[i] - cb, rsb[lane]);
+                        // add_q16 of the two chunk outputs (session.cpp:2052-2067)
+                        o2 = __fmul_rn((float)q16h(__fadd_rn(o2, __fmul_rn((float)vb, 1.0f / 256.0f))), 1.0f / 256.0f);
+                    }
                 }
                 const float x1 = __fmul_rn((float)__ldcg(s.x1 + (size_t)b * d.dim + row), 1.0f / 256.0f);
                 s.x[(size_t)b * d.dim + row] = (int16_t)q16h(__fadd_rn(x1, o2));
@@ -668,7 +687,7 @@ __global__ void __launch_bounds__(kTcThreads) k_tmm(const __grid_constant__ TcMa
         } else {
             // the other lanes fetch the group's input exponents for the epilogue
             pdl_wait();
-            if (OP == kOpQkv || OP == kOpWo) {
+            if (OP == kOpQkv || OP == kOpWo || (OP == kOpGate && d.hostffn)) {
                 const char* recs = a.from_hrec ? s.hrec : s.xrec;
                 for (int q = lane - 1; q < gn; q += 31)
                     kexp[q] = reinterpret_cast<const int*>(recs + (size_t)(g0 + q) * a.rec_bytes +
@@ -732,9 +751,13 @@ __global__ void __launch_bounds__(kTcThreads) k_tmm(const __grid_constant__ TcMa
                 if (live) {
                     const int g = mv_epi(S0, rs0);
                     const int u = mv_epi(S1, rs1);
-                    float y = swiglu1(__fmul_rn((float)g, 1.0f / 256.0f), __fmul_rn((float)u, 1.0f / 256.0f));
-                    if (a.hs > 0) y = __fmul_rn(y, ldexpf(1.0f, -a.hs));   // metadata key 15 store scale
-                    qv = q16s(y);
+                    if (d.hostffn) {
+                        qv = host_hidden(g, u, kexp[q]);
+                    } else {
+                        float y = swiglu1(__fmul_rn((float)g, 1.0f / 256.0f), __fmul_rn((float)u, 1.0f / 256.0f));
+                        if (a.hs > 0) y = __fmul_rn(y, ldexpf(1.0f, -a.hs));   // metadata key 15 store scale
+                        qv = q16s(y);
+                    }
                 }
                 // a warp's 32 rows lie in one w2 column half (the chunk is a multiple of 32)
                 const int half = (d.chunk < d.ffn && row >= d.chunk) ? 1 : 0;
@@ -748,13 +771,24 @@ __global__ void __launch_bounds__(kTcThreads) k_tmm(const __grid_constant__ TcMa
                     const int sum = __reduce_add_sync(0xffffffffu, qv);
                     if (lane == 0) atomicAdd(reinterpret_cast<int*>(hr + (half ? a.dr.g_b : a.dr.g_a)), sum);
                 }
+                if (d.hostffn) {
+                    const int mq = __reduce_max_sync(0xffffffffu, abs(qv));
+                    if (lane == 0 && mq) atomicMax(s.hmax + hmax_at(layer, b, half, s.slots), mq);
+                }
             } else if (OP == kOpDown) {
                 if (!live) continue;
-                float o2 = __fmul_rn((float)mv_epi(S0, rs0), 1.0f / 256.0f);
-                if (npass > 1) {
-                    const int vb = mv_epi(S1, rs1);
-                    // add_q16 of the two chunk outputs (session.cpp:2052-2067)
-                    o2 = __fmul_rn((float)q16h(__fadd_rn(o2, __fmul_rn((float)vb, 1.0f / 256.0f))), 1.0f / 256.0f);
+                float o2;
+                if (d.hostffn) {
+                    const float oa = host_w2_out(S0, rs0, hidden_exp(s, layer, b, 0), a.hs, s.err);
+                    const float ob = host_w2_out(S1, rs1, hidden_exp(s, layer, b, 1), a.hs, s.err);
+                    o2 = __fmul_rn((float)q16h(__fadd_rn(oa, ob)), 1.0f / 256.0f);
+                } else {
+                    o2 = __fmul_rn((float)mv_epi(S0, rs0), 1.0f / 256.0f);
+                    if (npass > 1) {
+                        const int vb = mv_epi(S1, rs1);
+                        // add_q16 of the two chunk outputs (session.cpp:2052-2067)
+                        o2 = __fmul_rn((float)q16h(__fadd_rn(o2, __fmul_rn((float)vb, 1.0f / 256.0f))), 1.0f / 256.0f);
+                    }
                 }
                 const float x1 = __fmul_rn((float)res[i], 1.0f / 256.0f);
                 s.x[(size_t)b * d.dim + row] = (int16_t)q16h(__fadd_rn(x1, o2));

@@ -70,7 +70,7 @@ struct vc4_session {
     State st;
     int slots = 0;
     int *d_slot = nullptr, *d_tok = nullptr, *d_pos = nullptr, *d_next = nullptr;
-    int* h_pin = nullptr;                     // pinned staging: slot, tok, pos, next (4*slots)
+    int* h_pin = nullptr;                     // pinned staging: slot, tok, pos, next, error word (5*slots + 16)
     int32_t* h_logits = nullptr;              // pinned logits staging (slots*vocab)
     std::map<PassArgs, cudaGraphExec_t> graphs;
     long long launches = 0, syncs = 0;
@@ -297,6 +297,9 @@ static int check_kernel_word(vc4_session* s) {
     if (w > 0) return fail(VC4_ECUDA, "a kernel found its shared-memory reservation too small (needs " + std::to_string(w) + " bytes)");
     if (w == -2) return fail(VC4_ECUDA, "a kernel's bulk copy did not complete within its time limit");
     if (w == -3) return fail(VC4_ECUDA, "a tensor-core matmat was launched with a copy ring its producers cannot share");
+    if (w == -4)
+        return fail(VC4_ERANGE, "an FFN hidden value reached 64 or more: the w2 input scale of the host FFN would "
+                                "round its input, which this engine does not compute (the session's results are void)");
     if (w) return fail(VC4_ECUDA, "kernel self-check failed (code " + std::to_string(w) + ")");
     return VC4_OK;
 }
@@ -474,12 +477,13 @@ int vc4_session_create(vc4_model* m, int slots, int seq, int kv_bits, const floa
               alloc((void**)&s->d_slot, (size_t)(3 * slots + 1) * 4) && alloc((void**)&s->d_next, (size_t)slots * 4) &&
               alloc((void**)&s->d_pos, (size_t)seq * 4 + 16) && alloc((void**)&st.done, 16) && alloc((void**)&st.err, 16) &&
               alloc((void**)&st.sdown, (size_t)L * slots * 2 * D * 8) &&
+              alloc((void**)&st.hmax, (size_t)L * slots * 2 * 4) &&
               alloc((void**)&st.xrec, (size_t)slots * batch_record_bytes(m->d)) &&
               alloc((void**)&st.hrec, (size_t)slots * batch_hidden_bytes(m->d));
     st.batch_ok = batch_path_fits(m->d, slots) ? 1 : 0;
     if (!ok) { vc4_session_destroy(s); return fail(VC4_ECUDA, "session allocation failed (slots*seq too large?)"); }
     s->d_tok = s->d_slot + slots;
-    if (cudaMallocHost((void**)&s->h_pin, (size_t)(4 * slots + 16) * 4) != cudaSuccess ||
+    if (cudaMallocHost((void**)&s->h_pin, (size_t)(5 * slots + 16) * 4) != cudaSuccess ||
         cudaMallocHost((void**)&s->h_logits, (size_t)slots * V * 4) != cudaSuccess) {
         vc4_session_destroy(s);
         return fail(VC4_ECUDA, "pinned staging allocation failed");
@@ -511,7 +515,7 @@ void vc4_session_destroy(vc4_session* s) {
     for (void* p : {(void*)st.x, (void*)st.x1, (void*)st.qkv, (void*)st.att, (void*)st.h, (void*)st.logits,
                     (void*)st.best, (void*)st.next, (void*)st.route, (void*)st.kv, (void*)st.rope_cos,
                     (void*)st.rope_sin, (void*)s->d_slot, (void*)s->d_next, (void*)s->d_pos, (void*)st.done, (void*)st.err,
-                    (void*)st.sdown, (void*)st.xrec, (void*)st.hrec})
+                    (void*)st.sdown, (void*)st.hmax, (void*)st.xrec, (void*)st.hrec})
         if (p) cudaFree(p);
     if (s->h_pin) cudaFreeHost(s->h_pin);
     if (s->h_logits) cudaFreeHost(s->h_logits);
@@ -519,6 +523,11 @@ void vc4_session_destroy(vc4_session* s) {
 }
 
 void* vc4_session_stream(vc4_session* s) { return (void*)s->stream; }
+
+int vc4_session_check(vc4_session* s) {
+    CK(cudaSetDevice(s->m->d.device));
+    return check_kernel_word(s);
+}
 
 static int check_slot_pos(const vc4_session* s, int slot, int pos) {
     if (slot < 0 || slot >= s->slots) return fail(VC4_EINVAL, "slot out of range");
@@ -546,12 +555,14 @@ static int host_step(vc4_session* s, int n, const int* slots, const int* tokens,
     PassArgs a{n, dcall, dcall + n, dcall + 2 * n, s->d_next, 0, nullptr};
     if (int e = run_pass(s, a)) return e;
     CK(cudaMemcpyAsync(hp + 3 * n, s->d_next, sizeof(int) * n, cudaMemcpyDeviceToHost, s->stream));
+    CK(cudaMemcpyAsync(hp + 4 * n, s->st.err, sizeof(int), cudaMemcpyDeviceToHost, s->stream));
     if (logits)
         for (int i = 0; i < n; ++i)
             CK(cudaMemcpyAsync(s->h_logits + (size_t)i * V, s->st.logits + (size_t)i * V, sizeof(int32_t) * V,
                                cudaMemcpyDeviceToHost, s->stream));
     CK(cudaStreamSynchronize(s->stream));
     s->syncs++;
+    if (hp[4 * n]) return check_kernel_word(s);
     if (next) for (int i = 0; i < n; ++i) next[i] = hp[3 * n + i];
     if (logits)
         for (size_t i = 0; i < (size_t)n * V; ++i) logits[i] = (float)s->h_logits[i] / 256.0f;

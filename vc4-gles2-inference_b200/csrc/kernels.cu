@@ -93,7 +93,7 @@ static void launch_attn_b(const DModel& m, const State& s, const Batch& b, const
     const float *qn = m.d_q_norm, *kn = m.d_k_norm;
     if (d.head_dim == 96) launch_pdl(k_attn_b<KVB, HQ, 96>, grid, smb, st, qn, kn, s, b, d, layer);
     else if (d.head_dim == 64) launch_pdl(k_attn_b<KVB, HQ, 64>, grid, smb, st, qn, kn, s, b, d, layer);
-    else launch_pdl(k_attn_b<KVB, HQ, 0>, grid, smb, st, qn, kn, s, b, d, layer);
+    else launch_pdl(k_attn_b<KVB, HQ, 128>, grid, smb, st, qn, kn, s, b, d, layer);
 }
 
 void launch_attention(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st) {
@@ -101,7 +101,9 @@ void launch_attention(const DModel& m, const State& s, const Batch& b, int layer
     const int group = d.heads / d.kv_heads, hq = attn_heads_per_cluster(group);
     const int units = b.n * d.kv_heads * (group / hq);
     const size_t smb = attnb_smem_bytes(hq, d.head_dim, d.seq, d.kv_bits);
-    if (units >= kAttnBatchUnits && smb <= kMaxDynSmem && d.head_dim <= 4 * kThreads) {
+    // the many-sequence kernel is instantiated for head sizes 64, 96 and 128
+    const bool hd_ok = d.head_dim == 64 || d.head_dim == 96 || d.head_dim == 128;
+    if (units >= kAttnBatchUnits && smb <= kMaxDynSmem && hd_ok) {
         if (d.kv_bits == 8) {
             if (hq == 2) launch_attn_b<1, 2>(m, s, b, d, layer, smb, st);
             else launch_attn_b<1, 1>(m, s, b, d, layer, smb, st);

@@ -481,6 +481,7 @@ __host__ __device__ inline int g_stride(const DMat& W) { return W.wtype == W_Q4 
 struct Dims {
     int dim, kv_dim, heads, kv_heads, head_dim, layers, vocab, ffn, chunk, experts, seq, row_bytes, kv_bits;
     int rope_half, qk_norm;
+    int hostffn;     // dense FFN in two chunks: the CPU layer loop's host FFN (see ffn_host below)
     float eps;
 };
 
@@ -490,7 +491,58 @@ Dims dims_of(const DModel& m, const State& s) {
     d.head_dim = m.h.head_dim; d.layers = m.h.layers; d.vocab = m.h.vocab; d.ffn = m.ffn_width;
     d.chunk = m.ffn_chunk; d.experts = m.h.experts; d.seq = s.seq; d.row_bytes = s.row_bytes;
     d.kv_bits = s.kv_bits; d.rope_half = m.h.rope_half; d.qk_norm = m.h.qk_norm; d.eps = m.h.rms_eps;
+    d.hostffn = (!m.h.experts && m.ffn_chunked) ? 1 : 0;
     return d;
+}
+
+// ---------------------------------------------------------------------------
+// The two FFN forms of the reference CPU layer loop (session.cpp:475-551).
+//  - GPU FFN (MoE, or a dense FFN of at most 2048 rows): the gate kernel
+//    reads the q16 input as uploaded, stores SiLU(g)*u*2^-hs with the
+//    shaders' floor(v*256 + 0.5), and w2 reads that q16 hidden vector as is
+//    (gpu_ffn.cpp:17-132, gpu_matvec.cpp:32-55).
+//  - Host FFN (a dense FFN split into two chunks): Model::split_ffn
+//    (model.cpp:217-270, run by App::prepare_model) leaves w1 empty, so the
+//    loop runs matvec_s on the gate/up halves (2^k input scale), the host
+//    SwiGLU rounded with quantize_act (lrintf), times 2^-hs, then matvec_s of
+//    each w2 half with its own 2^k (session.cpp:499-524, 2069-2080).  With
+//    q = the q16 hidden ints of a half and max|q|/256 = f*2^e, that half's w2
+//    input is rint(q * 2^(6-e)) and its output (v/256) * 2^-(6-e+hs).  For
+//    6-e >= 0 the input is q shifted, so the exact dot is the unscaled one
+//    times 2^(6-e): the w2 partial sums and records stay unscaled and the
+//    epilogue applies the exponent from the half's maximum (State::hmax).
+//    6-e < 0 (a hidden value of 64 or more) would round the input; the
+//    kernels report it (kErrHiddenRange) rather than return other numbers.
+// ---------------------------------------------------------------------------
+constexpr int kErrHiddenRange = -4;
+
+__host__ __device__ inline size_t hmax_at(int layer, int b, int half, int slots) {
+    return (((size_t)layer * slots + b) * 2 + half);
+}
+// The w2 input exponent of one hidden half from its max |q16| (matvec_s: 6 - e).
+__device__ __forceinline__ int hidden_exp(const State& s, int layer, int b, int half) {
+    int e = 0;
+    const int mx = __ldcg(s.hmax + hmax_at(layer, b, half, s.slots));
+    if (mx == 0) return 0;
+    frexpf(__fmul_rn((float)mx, 1.0f / 256.0f), &e);
+    return 6 - e;
+}
+// One w2 half of the host FFN: (floor(S * 2^k * ws + 0.5) clamped)/256 * 2^-(k + hs).
+__device__ __forceinline__ float host_w2_out(long long S, float ws, int k, int hs, int* err) {
+    if (k < 0) {
+        atomicExch(err, kErrHiddenRange);
+        k = 0;
+    }
+    const float v = __fmul_rn((float)mv_epi(S * (1LL << k), ws), 1.0f / 256.0f);
+    return __fmul_rn(v, ldexpf(1.0f, -(k + hs)));
+}
+// The host FFN's gate value: the hidden q16 int of SiLU(g)*u with g, u the
+// matvec_s outputs of a 2^k scaled input (quantize_act: lrintf).
+__device__ __forceinline__ int host_hidden(int g, int u, int k) {
+    const float sk = ldexpf(1.0f, -k);
+    const float gf = __fmul_rn(__fmul_rn((float)g, 1.0f / 256.0f), sk);
+    const float uf = __fmul_rn(__fmul_rn((float)u, 1.0f / 256.0f), sk);
+    return q16h(swiglu1(gf, uf));
 }
 
 // ---------------------------------------------------------------------------
@@ -666,6 +718,7 @@ __host__ __device__ inline size_t sdown_at(int layer, int b, int half, int dim, 
 struct DownSrc {
     int layer;            // the layer whose FFN output is rebuilt; -1: none (layer 0 input is the embedding)
     int two;              // chunked w2
+    int hs;               // that layer's key-15 hidden shift (host FFN output scale)
     const float* ra;      // dense model: row scales of the two w2 halves
     const float* rb;
     const DMat* dm;       // MoE: the device matrix table, expert e's halves at dm[ia + 4e], dm[ib + 4e]
@@ -728,6 +781,8 @@ __device__ __forceinline__ void rebuild_x(const State& s, const Dims& d, const D
     }
     const long long* S = s.sdown + sdown_at(ds.layer, bi, 0, d.dim, s.slots);
     const int16_t* x1 = s.x1 + (size_t)bi * d.dim;
+    const int ka = d.hostffn ? hidden_exp(s, ds.layer, bi, 0) : 0;
+    const int kb = d.hostffn ? hidden_exp(s, ds.layer, bi, 1) : 0;
     // kU rows per thread per round: every load of a round is issued before the first use
     constexpr int kU = 4;
     for (int base = 0; base < d.dim; base += kU * kThreads) {
@@ -751,10 +806,17 @@ __device__ __forceinline__ void rebuild_x(const State& s, const Dims& d, const D
         for (int u = 0; u < kU; ++u) {
             const int r = base + u * kThreads + threadIdx.x;
             if (r >= d.dim) continue;
-            float o2 = __fmul_rn((float)mv_epi(sa[u], fa[u]), 1.0f / 256.0f);
-            if (ds.two) {
-                const int vb = mv_epi(sb[u], fb[u]);
-                o2 = __fmul_rn((float)q16h(__fadd_rn(o2, __fmul_rn((float)vb, 1.0f / 256.0f))), 1.0f / 256.0f);
+            float o2;
+            if (d.hostffn) {
+                const float oa = host_w2_out(sa[u], fa[u], ka, ds.hs, s.err);
+                const float ob = host_w2_out(sb[u], fb[u], kb, ds.hs, s.err);
+                o2 = __fmul_rn((float)q16h(__fadd_rn(oa, ob)), 1.0f / 256.0f);
+            } else {
+                o2 = __fmul_rn((float)mv_epi(sa[u], fa[u]), 1.0f / 256.0f);
+                if (ds.two) {
+                    const int vb = mv_epi(sb[u], fb[u]);
+                    o2 = __fmul_rn((float)q16h(__fadd_rn(o2, __fmul_rn((float)vb, 1.0f / 256.0f))), 1.0f / 256.0f);
+                }
             }
             const int16_t x = (int16_t)q16h(__fadd_rn(__fmul_rn((float)xv[u], 1.0f / 256.0f), o2));
             xout[r] = x;
@@ -790,6 +852,9 @@ __global__ void __launch_bounds__(kThreads) k_qkv(DMat W, DMat E, const float* e
     pdl_wait();
     int16_t* xv = reinterpret_cast<int16_t*>(sm + L.x);
     const int nb = min(NB, bt.n - b0);
+    // the host FFN maxima this layer's gate kernel accumulates start from zero
+    if (d.hostffn && blockIdx.x == 0 && threadIdx.x < 2 * nb)
+        s.hmax[hmax_at(layer, b0 + threadIdx.x / 2, threadIdx.x % 2, s.slots)] = 0;
     for (int b = 0; b < nb; ++b) {
         const int bi = b0 + b;
         int16_t* xin = xv + (size_t)b * d.dim;
@@ -962,6 +1027,7 @@ __global__ void __launch_bounds__(kThreads) k_gate(MatSet M, MatSet M2, const fl
     __syncthreads();
     const WStage ws = wstage_at(W1, NB, sm + L.ws);
     int nb = 0;
+    int kx_own = 0;   // the input exponent of member `warp` (the warp's epilogue input)
 #pragma unroll
     for (int b = 0; b < NB; ++b) {
         if (b >= n_all) break;
@@ -990,7 +1056,15 @@ __global__ void __launch_bounds__(kThreads) k_gate(MatSet M, MatSet M2, const fl
             if (best != expert) continue;
         }
         if (threadIdx.x == 0) members[nb] = b;
-        warp_stage<WT>(ws, nb, W1.nchunks, d.dim, 0, [&](int c) { return xnorm(x[c], nws[c], rr); });
+        int kx = 0;
+        if (d.hostffn) {   // matvec_s of the normalised input (gpu_conv.cpp:271-287)
+            int mx = 0;
+#pragma unroll 8
+            for (int c = lane; c < d.dim; c += 32) mx = max(mx, abs(xnorm(x[c], nws[c], rr)));
+            kx = exp_from_max(__reduce_max_sync(0xffffffffu, mx));
+        }
+        if (warp == nb) kx_own = kx;
+        warp_stage<WT>(ws, nb, W1.nchunks, d.dim, kx, [&](int c) { return xnorm(x[c], nws[c], rr); });
         ++nb;
     }
     if (nb == 0) return;   // the same in every warp: no input routed to this expert
@@ -1008,13 +1082,21 @@ __global__ void __launch_bounds__(kThreads) k_gate(MatSet M, MatSet M2, const fl
             const int corr = WT == W_T3 ? ws.gsum[warp * ws.gst] : 0;
             const int g = mv_epi(tot[0] - corr, R1.rs);
             const int u = mv_epi(tot[1] - corr, R3.rs);
-            float y = swiglu1(__fmul_rn((float)g, 1.0f / 256.0f), __fmul_rn((float)u, 1.0f / 256.0f));
-            if (hs > 0) y = __fmul_rn(y, ldexpf(1.0f, -hs));     // metadata key 15 store scale
-            q = q16s(y);
+            if (d.hostffn) {
+                q = host_hidden(g, u, kx_own);
+            } else {
+                float y = swiglu1(__fmul_rn((float)g, 1.0f / 256.0f), __fmul_rn((float)u, 1.0f / 256.0f));
+                if (hs > 0) y = __fmul_rn(y, ldexpf(1.0f, -hs));     // metadata key 15 store scale
+                q = q16s(y);
+            }
         }
         hq[warp * 32 + lane] = q;
         const int sum = __reduce_add_sync(0xffffffffu, q);
         if (lane == 0) dsum[warp] = sum;
+        if (d.hostffn) {
+            const int mq = __reduce_max_sync(0xffffffffu, abs(q));
+            if (lane == 0 && mq) atomicMax(s.hmax + hmax_at(layer, b0 + members[warp], half, s.slots), mq);
+        }
     }
     __syncthreads();
     // the w2 input bytes of this CTA's columns (zero for the rest of the chunk)
@@ -1336,6 +1418,8 @@ struct AttnSmem {
     float* wk;       // hd: k_norm weights of the layer
     float* redf;     // kWarps: softmax maxima per warp
     float* sc;       // group x seq: scores, then probabilities (cluster-written)
+    int* qi;         // group x hd: the q heads on their integer grids
+    float* gsc;      // group: 2^-F / cache grid of each q head
 };
 
 __host__ __device__ inline size_t attn_carve(int group, int hd, int seq, int kv_bits, char* base, AttnSmem* sm) {
@@ -1357,7 +1441,12 @@ __host__ __device__ inline size_t attn_carve(int group, int hd, int seq, int kv_
     const size_t wk = o;   o += sizeof(float) * hd;
     const size_t redf = o; o += sizeof(float) * kWarps;
     const size_t sc = o;   o += sizeof(float) * (size_t)group * seq;
+    o = align16(o);
+    const size_t qi = o;   o += sizeof(int) * (size_t)group * hd;
+    const size_t gsc = o;  o += sizeof(float) * (size_t)group;
     if (sm) {
+        sm->qi = reinterpret_cast<int*>(base + qi);
+        sm->gsc = reinterpret_cast<float*>(base + gsc);
         sm->kraw = reinterpret_cast<uint8_t*>(base + kraw);
         sm->vraw = reinterpret_cast<uint8_t*>(base + vraw);
         sm->pv = reinterpret_cast<double*>(base + pv);
@@ -1433,6 +1522,33 @@ __host__ __device__ inline int attn_weight_exp(int len, int kvb) {
     int lg = 0;
     while ((1 << lg) < len) ++lg;
     return 53 - (kvb == 2 ? 15 : 7) - lg;
+}
+
+// Exponent F of a query head's integer grid: with max|q| = f * 2^e (f in
+// [0.5, 1)), F = 22 - e, so every |rint(q * 2^F)| <= 2^22 splits into three
+// balanced signed bytes; clamped to [-100, 100].  A score is the exact
+// integer dot of rint(q * 2^F) with the cache levels, rounded once to float,
+// times 2^-F / grid (exact), divided by sqrt(hd).
+__device__ __forceinline__ int q_grid_exp(float qmax) {
+    if (!(qmax > 0.0f)) return 0;
+    int e = 0;
+    frexpf(qmax, &e);
+    const int F = 22 - e;
+    return F > 100 ? 100 : F < -100 ? -100 : F;
+}
+__device__ __forceinline__ float pow2f(int k) { return __int_as_float((127 + k) << 23); }   // 2^k, -126 <= k <= 127
+
+// One warp puts q head v (hd floats) on its integer grid: qi[i] = rint(v[i]
+// * 2^F); returns 2^-F / grid (kvb 2: grid 2048, 1: grid 16).
+__device__ __forceinline__ float warp_q_grid(const float* v, int hd, int kvb, int* qi) {
+    const int lane = threadIdx.x & 31;
+    float m = 0.0f;
+    for (int i = lane; i < hd; i += 32) m = fmaxf(m, fabsf(v[i]));
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const int F = q_grid_exp(m);
+    const float sF = pow2f(F);
+    for (int i = lane; i < hd; i += 32) qi[i] = __float2int_rn(__fmul_rn(v[i], sF));
+    return pow2f(-F - (kvb == 2 ? 11 : 4));
 }
 
 __device__ void attn_weights(float* scores, int seq, int len, int hq, int kvb, float* redf, double* redd,
@@ -1538,7 +1654,7 @@ k_attn(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int 
         const int r = v / kw, c = v % kw;
         if (t0 + r == pos) continue;
         float f[4];
-        const int n = kv_word(reinterpret_cast<const unsigned*>(sm.kraw + r * hbytes)[c], kvb, f);
+        const int n = kv_codes(reinterpret_cast<const unsigned*>(sm.kraw + r * hbytes)[c], kvb, f);
         for (int j = 0; j < n; ++j) sm.kt[r * hp + c * n + j] = f[j];
     }
     for (int v = threadIdx.x; v < pos * vw; v += kThreads) {
@@ -1580,6 +1696,10 @@ k_attn(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int 
         }
     }
     __syncthreads();
+    for (int hh = warp; hh < hq; hh += kWarps) {
+        const float g = warp_q_grid(sm.q + hh * hd, hd, kvb, sm.qi + hh * hd);
+        if (lane == 0) sm.gsc[hh] = g;
+    }
 
     // 3. encode the new row one 32-bit word at a time (shaders_attn.cpp:141-159);
     //    every CTA encodes it identically, the one whose share holds `pos`
@@ -1596,29 +1716,29 @@ k_attn(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int 
         if (writer) *reinterpret_cast<unsigned*>(row + (w ? vofs : 0) + g * hbytes + c * 4) = word;
         for (int j = 0; j < vpw; ++j) {
             const int i = i0 + j;
-            if (!w && owner) sm.kt[(pos - t0) * hp + i] = dec[j];
+            if (!w && owner) sm.kt[(pos - t0) * hp + i] = __fmul_rn(dec[j], kvb == 2 ? 2048.0f : 16.0f);
             if (w && i >= c0 && i < c1) sm.vt[(size_t)pos * vs + i - c0] = __fmul_rn(dec[j], kvb == 2 ? 2048.0f : 16.0f);
         }
     }
     __syncthreads();
 
-    // 4. scores of this CTA's positions: sequential fp32 dot, / sqrt(hd);
-    //    stored into every CTA of the cluster
+    // 4. scores of this CTA's positions: the exact integer dot of the q head
+    //    on its grid with the cache levels, one rounding to float, the grid
+    //    scale, / sqrt(hd); stored into every CTA of the cluster
     const float sq = __fsqrt_rn((float)hd);
     for (int e = threadIdx.x; e < nt * hq; e += kThreads) {
         const int r = e / hq, hh = e % hq;
         const float4* kr = reinterpret_cast<const float4*>(sm.kt + r * hp);
-        const float4* qh = reinterpret_cast<const float4*>(sm.q + hh * hd);
-        float acc = 0.0f;
+        const int4* qh = reinterpret_cast<const int4*>(sm.qi + hh * hd);
+        long long S = 0;
 #pragma unroll 4
         for (int i = 0; i < hd / 4; ++i) {
-            const float4 k4 = kr[i], q4 = qh[i];
-            acc = __fadd_rn(acc, __fmul_rn(q4.x, k4.x));
-            acc = __fadd_rn(acc, __fmul_rn(q4.y, k4.y));
-            acc = __fadd_rn(acc, __fmul_rn(q4.z, k4.z));
-            acc = __fadd_rn(acc, __fmul_rn(q4.w, k4.w));
+            const float4 k4 = kr[i];
+            const int4 q4 = qh[i];
+            S += (long long)q4.x * (int)k4.x + (long long)q4.y * (int)k4.y + (long long)q4.z * (int)k4.z +
+                 (long long)q4.w * (int)k4.w;
         }
-        acc = __fdiv_rn(acc, sq);
+        const float acc = __fdiv_rn(__fmul_rn(__ll2float_rn(S), sm.gsc[hh]), sq);
         float* dst = sm.sc + hh * d.seq + t0 + r;
 #pragma unroll
         for (int c = 0; c < kAttnCtas; ++c) *cluster.map_shared_rank(dst, c) = acc;
@@ -1655,26 +1775,51 @@ k_attn(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int 
 
 
 // Attention for many sequences at once: one CTA (no cluster) per (sequence,
-// KV head, pair of q heads).  The sequence's K rows and then its V rows stream
-// through a ring of kAbStages shared-memory tiles of kAbRows positions
-// (cp.async), rows padded to an odd number of 16-byte units so that 16-byte
-// reads of consecutive rows hit distinct banks.
-//  - scores: thread (position, head) decodes its K row from the cache bytes
-//    in registers and forms the sequential fp32 dot, as the cluster kernel;
-//  - weights: attn_weights (integer E_t, exact sums);
-//  - P.V: thread (4-column quad, position slice) accumulates E_t * code in
-//    double for every head, exactly; the slices are added at the end.
+// KV head, q heads of the CTA), both contractions on the tensor cores as exact
+// integer MMAs (mma.sync m16n8k32 with 8-bit operands and int32
+// accumulators):
+//  - K rows and then V rows stream through a ring of kAbStages shared-memory
+//    tiles of kAbRows positions (cp.async), rows padded to an odd number of
+//    16-byte units so ldmatrix reads hit distinct banks;
+//  - scores: each q head on its integer grid (warp_q_grid) is split into
+//    three balanced signed bytes, the B operand (column 2*limb + head); the
+//    A operand is a K tile: q8 levels as they are, q16 levels as a signed
+//    high-byte and an unsigned low-byte plane; S = sum_limb 256^limb (256 D_hi
+//    + D_lo) is the exact integer dot;
+//  - weights: attn_weights (integer E_t < 2^47, exact double sums);
+//  - P.V: E_t split into unsigned byte limbs is the A operand (row h*NL +
+//    limb), a V tile read with ldmatrix.trans the B operand (q8: even and odd
+//    columns; q16: high and low byte planes); every limb product and their
+//    combination into num = sum_t E_t * level_t are exact integers, added into
+//    shared int64 sums in any order.
 // A sequence's output is therefore the cluster kernel's, bit for bit.
+// Positions inside a 32-wide MMA k block are taken in the order ldmatrix of
+// 16-bit pairs delivers them (attnb_k_of); the weight limbs are stored in it.
 constexpr int kAbRows = 128;
 constexpr int kAbStages = 3;
+constexpr int kAbMaxLimbs = 6;      // E_t < 2^47: six bytes
 
 __host__ __device__ inline int attnb_pitch(int hbytes) { return (hbytes / 16) % 2 ? hbytes : hbytes + 16; }
-__host__ __device__ inline int attnb_slices(int hd) { return kThreads / (hd / 4); }
+// bytes of one row of the weight-limb matrix: whole tiles of positions,
+// padded to an odd number of 16-byte units
+__host__ __device__ inline int attnb_epitch(int seq) {
+    const int p = (seq + kAbRows - 1) / kAbRows * kAbRows;
+    return (p / 16) % 2 ? p : p + 16;
+}
+// The k index (0..31 inside a 32-wide MMA block) that holds element p of the
+// block when the operand rows were read as 16-bit pairs and split by
+// byte_perm: k = 4q + r holds element 16*(k/16) + {2q, 2q+1, 8+2q, 9+2q}[r].
+__host__ __device__ inline int attnb_k_of(int p) {
+    const int b = p >> 4, r = p & 15;
+    return 16 * b + (r < 8 ? 4 * (r >> 1) + (r & 1) : 4 * ((r - 8) >> 1) + 2 + (r & 1));
+}
 
 struct AbSmem {
-    uint8_t* ring;   // kAbStages x kAbRows x pitch cache bytes; P.V partials at the end
+    uint8_t* ring;   // kAbStages x kAbRows x pitch cache bytes
     uint8_t* newrow; // 2 x hbytes: this step's K and V row
-    double* ed;      // hq x seq: the weights E_t as doubles
+    uint8_t* ea;     // 16 x epitch: weight limbs, row h*NL + limb, positions in MMA k order
+    uint8_t* qb;     // 8 x hd: q limbs, column 2*limb + head, dims in MMA k order
+    long long* num;  // hq x hd: exact P.V sums
     double* redd;
     double* den;     // hq
     float* q;        // (hq + 1) x hd: q heads, then the new k
@@ -1684,17 +1829,19 @@ struct AbSmem {
     float* wq;
     float* wk;
     float* redf;
+    float* gsc;      // hq: 2^-F / cache grid per q head
     float* sc;       // hq x seq: scores, then E_t
+    int* qi;         // hq x hd: the q heads on their integer grids
 };
 
 __host__ __device__ inline size_t attnb_carve(int hq, int hd, int seq, int kv_bits, char* base, AbSmem* sm) {
     const int hbytes = hd * (kv_bits / 8);
-    const size_t ring_b = (size_t)kAbStages * kAbRows * attnb_pitch(hbytes);
-    const size_t part_b = sizeof(double) * (size_t)attnb_slices(hd) * hq * hd;
     size_t o = 0;
-    const size_t ring = o; o = align16(o + (ring_b > part_b ? ring_b : part_b));
+    const size_t ring = o; o = align16(o + (size_t)kAbStages * kAbRows * attnb_pitch(hbytes));
     const size_t nr = o;   o = align16(o + 2 * (size_t)hbytes);
-    const size_t ed = o;   o = align16(o + sizeof(double) * (size_t)hq * seq);
+    const size_t ea = o;   o = align16(o + 16 * (size_t)attnb_epitch(seq));
+    const size_t qb = o;   o = align16(o + 8 * (size_t)hd);
+    const size_t num = o;  o = align16(o + sizeof(long long) * (size_t)hq * hd);
     const size_t redd = o; o = align16(o + sizeof(double) * kWarps);
     const size_t den = o;  o = align16(o + sizeof(double) * hq);
     const size_t q = o;    o = align16(o + sizeof(float) * (size_t)(hq + 1) * hd);
@@ -1704,11 +1851,15 @@ __host__ __device__ inline size_t attnb_carve(int hq, int hd, int seq, int kv_bi
     const size_t wq = o;   o += sizeof(float) * hd;
     const size_t wk = o;   o += sizeof(float) * hd;
     const size_t redf = o; o += sizeof(float) * kWarps;
+    const size_t gsc = o;  o += sizeof(float) * hq;
     const size_t sc = o;   o += sizeof(float) * (size_t)hq * seq;
+    const size_t qi = o;   o += sizeof(int) * (size_t)hq * hd;
     if (sm) {
         sm->ring = reinterpret_cast<uint8_t*>(base + ring);
         sm->newrow = reinterpret_cast<uint8_t*>(base + nr);
-        sm->ed = reinterpret_cast<double*>(base + ed);
+        sm->ea = reinterpret_cast<uint8_t*>(base + ea);
+        sm->qb = reinterpret_cast<uint8_t*>(base + qb);
+        sm->num = reinterpret_cast<long long*>(base + num);
         sm->redd = reinterpret_cast<double*>(base + redd);
         sm->den = reinterpret_cast<double*>(base + den);
         sm->q = reinterpret_cast<float*>(base + q);
@@ -1718,7 +1869,9 @@ __host__ __device__ inline size_t attnb_carve(int hq, int hd, int seq, int kv_bi
         sm->wq = reinterpret_cast<float*>(base + wq);
         sm->wk = reinterpret_cast<float*>(base + wk);
         sm->redf = reinterpret_cast<float*>(base + redf);
+        sm->gsc = reinterpret_cast<float*>(base + gsc);
         sm->sc = reinterpret_cast<float*>(base + sc);
+        sm->qi = reinterpret_cast<int*>(base + qi);
     }
     return align16(o);
 }
@@ -1726,89 +1879,59 @@ __host__ __device__ inline size_t attnb_smem_bytes(int hq, int hd, int seq, int 
     return attnb_carve(hq, hd, seq, kv_bits, nullptr, nullptr);
 }
 
-// Cache values of one 32-bit word (kv_word's values) by exponent-field
-// construction: a byte b (or a 16-bit level v) offset to unsigned and placed
-// in the mantissa of 2^19 (2^12) gives 2^19 + (b + 128)/16 (2^12 + (v +
-// 32768)/2048), and one subtraction leaves b/16 (v/2048), exactly.
-template <int KVB>
-__device__ __forceinline__ void kv_vals(unsigned w, float* f) {
-    if (KVB == 1) {
-        w ^= 0x80808080u;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) f[j] = __fsub_rn(__int_as_float(__byte_perm(w, 0x49000000u, 0x7440 | j)), 524296.0f);
-    } else {
-        w ^= 0x00800080u;
-        f[0] = __fsub_rn(__int_as_float(__byte_perm(w, 0x45800000u, 0x7601)), 4112.0f);
-        f[1] = __fsub_rn(__int_as_float(__byte_perm(w, 0x45800000u, 0x7623)), 4112.0f);
-    }
+// ldmatrix of four 8x8 16-bit matrices (row addresses from lanes 0-7, 8-15,
+// 16-23, 24-31), plain and transposed.
+__device__ __forceinline__ void ldsm_x4(unsigned addr, unsigned (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
 }
-// Integer levels of one word as doubles (kv_codes): the offset level placed
-// in the mantissa of 2^52, minus 2^52 + offset.
-template <int KVB>
-__device__ __forceinline__ void kv_levels(unsigned w, double* f) {
-    if (KVB == 1) {
-        w ^= 0x80808080u;
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-            f[j] = __dsub_rn(__hiloint2double(0x43300000, (int)__byte_perm(w, 0u, 0x4440 | j)), 4503599627370624.0);
-    } else {
-        w ^= 0x00800080u;
-        f[0] = __dsub_rn(__hiloint2double(0x43300000, (int)__byte_perm(w, 0u, 0x4401)), 4503599627403264.0);
-        f[1] = __dsub_rn(__hiloint2double(0x43300000, (int)__byte_perm(w, 0u, 0x4423)), 4503599627403264.0);
-    }
+__device__ __forceinline__ void ldsm_x4_t(unsigned addr, unsigned (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
 }
-
-// Sequential fp32 dot of q (hd floats) with one packed K row; HD > 0 fixes
-// the head size at compile time (the loop unrolls).
-template <int KVB, int HD = 0>
-__device__ __forceinline__ float kdot(const uint8_t* krow, const float* qh, int hd) {
-    float acc = 0.0f;
-    constexpr int kPer = 4 / KVB;                       // values per word
-    const int n16 = (HD ? HD : hd) * KVB / 16;
-#pragma unroll
-    for (int c = 0; c < n16; ++c) {
-        const uint4 w = *reinterpret_cast<const uint4*>(krow + c * 16);
-        const unsigned ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            float f[4], qv[4];
-            kv_vals<KVB>(ws[k], f);
-            if (KVB == 1) {
-                const float4 q4 = *reinterpret_cast<const float4*>(qh + (c * 4 + k) * 4);
-                qv[0] = q4.x; qv[1] = q4.y; qv[2] = q4.z; qv[3] = q4.w;
-            } else {
-                const float2 q2 = *reinterpret_cast<const float2*>(qh + (c * 4 + k) * 2);
-                qv[0] = q2.x; qv[1] = q2.y;
-            }
-#pragma unroll
-            for (int j = 0; j < kPer; ++j) acc = __fadd_rn(acc, __fmul_rn(qv[j], f[j]));
-        }
-    }
-    return acc;
+// D += A (16x32, 8-bit, row) * B (32x8, 8-bit, col), int32 accumulators;
+// AU / BU select unsigned operands.
+template <bool AU, bool BU>
+__device__ __forceinline__ void mma_i8(int (&d)[4], const unsigned (&a)[4], unsigned b0, unsigned b1) {
+    if (!AU && !BU)
+        asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                     : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+                     : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    else if (AU && !BU)
+        asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                     : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+                     : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    else if (AU && BU)
+        asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                     : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+                     : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    else
+        asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                     : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+                     : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// HD > 0: the head size fixed at compile time (64 and 96 in the benchmark
-// models), so the K loop unrolls and the P.V index arithmetic folds.
+// HD: the head size (a multiple of 32, at most 128); HQ: q heads per CTA (1 or 2).
 template <int KVB, int HQ, int HD>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, KVB == 1 && HD <= 96 ? 3 : 2)
 k_attn_b(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int layer) {
+    static_assert(HD % 32 == 0 && HD <= 128 && (HQ == 1 || HQ == 2), "k_attn_b shape");
     extern __shared__ __align__(16) char smem[];
-    constexpr int hq = HQ;
-    const int hd = HD ? HD : d.head_dim, group = d.heads / d.kv_heads, half = hd / 2;
+    constexpr int hq = HQ, hd = HD, half = HD / 2, hbytes = HD * KVB, kw = hbytes / 4, kvec = hbytes / 16;
+    constexpr int KS = HD / 32;                        // MMA k blocks per head
+    const int group = d.heads / d.kv_heads;
     if (!smem_ok(attnb_smem_bytes(hq, hd, d.seq, KVB * 8), s.err)) return;
     AbSmem sm;
     attnb_carve(hq, hd, d.seq, KVB * 8, smem, &sm);
     const int qsplit = group / hq, g = blockIdx.x / qsplit, split = blockIdx.x % qsplit;
     const int h0 = split * hq, b = blockIdx.y;
     const int slot = bt.slot[b], pos = bt.pos[b], len = pos + 1;
-    const int hbytes = hd * KVB, vofs = d.kv_dim * KVB, pitch = attnb_pitch(hbytes);
-    const int kvec = hbytes / 16, kw = hbytes / 4;
+    const int vofs = d.kv_dim * KVB, pitch = attnb_pitch(hbytes), epitch = attnb_epitch(d.seq);
     const int ntile = (len + kAbRows - 1) / kAbRows;
     const uint8_t* kvrd = s.kv + ((size_t)slot * d.layers + layer) * d.seq * d.row_bytes + g * hbytes;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gq = lane >> 2, tq = lane & 3;
     // tile u < ntile: K rows of positions [u*R, ...); ntile <= u < 2*ntile: V rows.
-    // Thread (row r0, 16-byte column cc) copies rows r0, r0 + rpp, ...: the
-    // division by the row's 16-byte count happens once, not per copy.
+    // Thread (row r0, 16-byte column cc) copies rows r0, r0 + rpp, ...
     const int rpp = kThreads / kvec, cc = threadIdx.x % kvec, r0 = threadIdx.x / kvec;
     auto issue = [&](int u) {
         if (u < 2 * ntile && r0 < rpp) {
@@ -1833,6 +1956,11 @@ k_attn_b(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, in
             sm.wq[i] = q_norm[(size_t)layer * hd + i];
             sm.wk[i] = k_norm[(size_t)layer * hd + i];
         }
+    // zero the limb matrices and the P.V sums (absent heads, limbs and
+    // positions past the sequence multiply as zero)
+    for (int i = threadIdx.x; i < 16 * epitch / 16; i += kThreads) reinterpret_cast<int4*>(sm.ea)[i] = make_int4(0, 0, 0, 0);
+    for (int i = threadIdx.x; i < 8 * hd / 16; i += kThreads) reinterpret_cast<int4*>(sm.qb)[i] = make_int4(0, 0, 0, 0);
+    for (int i = threadIdx.x; i < hq * hd; i += kThreads) sm.num[i] = 0;
     pdl_launch_dependents();
     pdl_wait();
 
@@ -1864,7 +1992,7 @@ k_attn_b(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, in
         }
     }
     __syncthreads();
-    // encode the new row; the first q-head pair's CTA writes it to the cache,
+    // encode the new row; the first q-head split's CTA writes it to the cache,
     // every CTA keeps its bytes for position `pos`
     uint8_t* row = s.kv + ((size_t)slot * d.layers + layer) * d.seq * d.row_bytes + (size_t)pos * d.row_bytes + g * hbytes;
     for (int e = threadIdx.x; e < 2 * kw; e += kThreads) {
@@ -1876,78 +2004,173 @@ k_attn_b(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, in
         if (split == 0) *reinterpret_cast<unsigned*>(row + (w ? vofs : 0) + c * 4) = word;
         *reinterpret_cast<unsigned*>(sm.newrow + w * hbytes + c * 4) = word;
     }
+    // each q head on its integer grid, split into balanced signed bytes: the
+    // score MMAs' B operand, column 2*limb + head, dims in MMA k order
+    if (warp < hq) {
+        const float gs = warp_q_grid(sm.q + warp * hd, hd, KVB, sm.qi + warp * hd);
+        if (lane == 0) sm.gsc[warp] = gs;
+    }
     __syncthreads();
+    for (int e = threadIdx.x; e < hq * hd; e += kThreads) {
+        const int hh = e / hd, i = e % hd;
+        int v = sm.qi[e];
+        const int l0 = ((v + 128) & 255) - 128;
+        v = (v - l0) >> 8;
+        const int l1 = ((v + 128) & 255) - 128;
+        const int l2 = (v - l1) >> 8;
+        const int k = KVB == 2 ? (i & ~31) + attnb_k_of(i & 31) : i;
+        sm.qb[(0 + hh) * hd + k] = (uint8_t)l0;
+        sm.qb[(2 + hh) * hd + k] = (uint8_t)l1;
+        sm.qb[(4 + hh) * hd + k] = (uint8_t)l2;
+    }
+    __syncthreads();
+    // B fragments of the q limbs for every k block (column n = lane/4)
+    unsigned bq[KS][2];
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+        bq[ks][0] = *reinterpret_cast<const unsigned*>(sm.qb + gq * hd + ks * 32 + 4 * tq);
+        bq[ks][1] = *reinterpret_cast<const unsigned*>(sm.qb + gq * hd + ks * 32 + 16 + 4 * tq);
+    }
 
     const float sq = __fsqrt_rn((float)hd);
-    const int nq = hd / 4, ns = attnb_slices(hd);
-    const int cq = threadIdx.x % nq, sl = threadIdx.x / nq;
-    double acc[HQ][4];
+    // P.V work of a warp: position block pb (32 of a tile's 128 rows) and half
+    // of the V columns; q8 blocks of 16 columns (even and odd MMAs), q16
+    // blocks of 8 (high and low byte MMAs)
+    constexpr int kDB = KVB == 1 ? HD / 16 : HD / 8;   // column blocks
+    constexpr int kDBW = kDB / 2;                       // per warp
+    const int pb = warp & 3, dh = warp >> 2;
+    int acc[kDBW][2][4];
 #pragma unroll
-    for (int hh = 0; hh < HQ; ++hh)
+    for (int i = 0; i < kDBW; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[hh][j] = 0.0;
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) acc[i][j][k] = 0;
+    int nl = 0;                                         // weight limbs
+    const unsigned ea_base = smem_addr(sm.ea);
 
     for (int u = 0; u < 2 * ntile; ++u) {
         issue(u + kAbStages - 1);
         asm volatile("cp.async.wait_group %0;" ::"n"(kAbStages - 1) : "memory");
         __syncthreads();
-        const uint8_t* tile = sm.ring + (size_t)(u % kAbStages) * kAbRows * pitch;
-        if (u < ntile) {
-            // scores of this K tile
-            const int t0 = u * kAbRows, nt = min(kAbRows, len - t0);
-            const int r = threadIdx.x % kAbRows;
-            if (r < nt) {
-                const int t = t0 + r;
-                const uint8_t* kp = t == pos ? sm.newrow : tile + r * pitch;
-                for (int hh = threadIdx.x / kAbRows; hh < hq; hh += kThreads / kAbRows)
-                    sm.sc[hh * d.seq + t] = __fdiv_rn(kdot<KVB, HD>(kp, sm.q + hh * hd, hd), sq);
+        uint8_t* tile = sm.ring + (size_t)(u % kAbStages) * kAbRows * pitch;
+        const int kind = u >= ntile, t0 = (u % ntile) * kAbRows, nt = min(kAbRows, len - t0);
+        if (pos >= t0 && pos < t0 + nt) {
+            // this step's row, which the copies skipped
+            for (int i = threadIdx.x; i < hbytes / 4; i += kThreads)
+                reinterpret_cast<unsigned*>(tile + (pos - t0) * pitch)[i] =
+                    reinterpret_cast<const unsigned*>(sm.newrow + kind * hbytes)[i];
+            __syncthreads();
+        }
+        const unsigned tb = smem_addr(tile);
+        if (!kind) {
+            // scores of this K tile: warp w takes rows 16w .. 16w+15
+            const int rb = warp * 16;
+            if (rb < nt) {
+                const int lr = rb + (lane & 7) + 8 * ((lane >> 3) & 1);   // ldmatrix row of this lane
+                int dlo[4] = {0, 0, 0, 0}, dhi[4] = {0, 0, 0, 0};
+#pragma unroll
+                for (int ks = 0; ks < KS; ++ks) {
+                    if (KVB == 1) {
+                        unsigned a[4];
+                        ldsm_x4(tb + lr * pitch + ks * 32 + 16 * (lane >> 4), a);
+                        mma_i8<false, false>(dhi, a, bq[ks][0], bq[ks][1]);
+                    } else {
+                        unsigned m[4], n[4], ah[4], al[4];
+                        ldsm_x4(tb + lr * pitch + ks * 64 + 16 * (lane >> 4), m);
+                        ldsm_x4(tb + lr * pitch + ks * 64 + 32 + 16 * (lane >> 4), n);
+                        ah[0] = __byte_perm(m[0], m[2], 0x6420); al[0] = __byte_perm(m[0], m[2], 0x7531);
+                        ah[1] = __byte_perm(m[1], m[3], 0x6420); al[1] = __byte_perm(m[1], m[3], 0x7531);
+                        ah[2] = __byte_perm(n[0], n[2], 0x6420); al[2] = __byte_perm(n[0], n[2], 0x7531);
+                        ah[3] = __byte_perm(n[1], n[3], 0x6420); al[3] = __byte_perm(n[1], n[3], 0x7531);
+                        mma_i8<false, false>(dhi, ah, bq[ks][0], bq[ks][1]);
+                        mma_i8<true, false>(dlo, al, bq[ks][0], bq[ks][1]);
+                    }
+                }
+                // column 2*limb + head: lane tq holds limb tq of heads 0 and 1
+                long long v[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) v[j] = KVB == 1 ? (long long)dhi[j] : (long long)dhi[j] * 256 + dlo[j];
+                long long S[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const long long v1 = __shfl_down_sync(0xffffffffu, v[j], 1);
+                    const long long v2 = __shfl_down_sync(0xffffffffu, v[j], 2);
+                    S[j] = v[j] + v1 * 256 + v2 * 65536;
+                }
+                if (tq == 0)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int r = rb + gq + 8 * (j >> 1), hh = j & 1;
+                        if (hh < hq && r < nt)
+                            sm.sc[hh * d.seq + t0 + r] = __fdiv_rn(__fmul_rn(__ll2float_rn(S[j]), sm.gsc[hh]), sq);
+                    }
             }
         } else {
             if (u == ntile) {
                 attn_weights(sm.sc, d.seq, len, hq, KVB, sm.redf, sm.redd, sm.den);
-#pragma unroll
-                for (int hh = 0; hh < HQ; ++hh)
-                    for (int t = threadIdx.x; t < len; t += kThreads) sm.ed[hh * d.seq + t] = (double)sm.sc[hh * d.seq + t];
+                // limbs of E_t (< 2^kexp + 1): row h*NL + limb, position t at
+                // column 32*(t/32) + attnb_k_of(t%32)
+                nl = (attn_weight_exp(len, KVB) + 8) / 8;
+                for (int e = threadIdx.x; e < hq * len; e += kThreads) {
+                    const int hh = e / len, t = e % len;
+                    unsigned long long E = (unsigned long long)sm.sc[hh * d.seq + t];
+                    uint8_t* dst = sm.ea + (size_t)(hh * nl) * epitch + (t & ~31) + attnb_k_of(t & 31);
+                    for (int l = 0; l < nl; ++l, E >>= 8) dst[(size_t)l * epitch] = (uint8_t)E;
+                }
                 __syncthreads();
             }
             // P.V of this V tile
-            const int t0 = (u - ntile) * kAbRows, nt = min(kAbRows, len - t0);
-            if (sl < ns)
-                for (int r = sl; r < nt; r += ns) {
-                    const int t = t0 + r;
-                    const uint8_t* vp = (t == pos ? sm.newrow + hbytes : tile + r * pitch) + cq * 4 * KVB;
-                    double v[4];
+            const int pr = pb * 32;
+            if (pr < nt) {
+                unsigned a[4];
+                ldsm_x4(ea_base + ((lane & 7) + 8 * ((lane >> 3) & 1)) * epitch + t0 + pr + 16 * (lane >> 4), a);
+                const unsigned vrow = tb + (pr + (lane & 7) + 8 * (lane >> 3)) * pitch;
+#pragma unroll
+                for (int i = 0; i < kDBW; ++i) {
+                    const int db = dh * kDBW + i;
+                    unsigned m[4];
+                    ldsm_x4_t(vrow + db * 16, m);
+                    const unsigned b00 = __byte_perm(m[0], m[1], 0x6420), b01 = __byte_perm(m[2], m[3], 0x6420);
+                    const unsigned b10 = __byte_perm(m[0], m[1], 0x7531), b11 = __byte_perm(m[2], m[3], 0x7531);
                     if (KVB == 1) {
-                        kv_levels<1>(*reinterpret_cast<const unsigned*>(vp), v);
+                        mma_i8<true, false>(acc[i][0], a, b00, b01);   // even columns
+                        mma_i8<true, false>(acc[i][1], a, b10, b11);   // odd columns
                     } else {
-                        const uint2 w2 = *reinterpret_cast<const uint2*>(vp);
-                        kv_levels<2>(w2.x, v);
-                        kv_levels<2>(w2.y, v + 2);
-                    }
-#pragma unroll
-                    for (int hh = 0; hh < HQ; ++hh) {
-                        const double e = sm.ed[hh * d.seq + t];
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) acc[hh][j] = __fma_rn(e, v[j], acc[hh][j]);
+                        mma_i8<true, false>(acc[i][0], a, b00, b01);   // high bytes (signed)
+                        mma_i8<true, true>(acc[i][1], a, b10, b11);    // low bytes (unsigned)
                     }
                 }
+            }
         }
         __syncthreads();
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
-    // add the slices' exact partials and store
-    double* part = reinterpret_cast<double*>(sm.ring);
-    if (sl < ns)
+    // add the exact limb products: row m = h*NL + limb, columns as the B operand
 #pragma unroll
-        for (int hh = 0; hh < HQ; ++hh)
+    for (int i = 0; i < kDBW; ++i) {
+        const int db = dh * kDBW + i;
 #pragma unroll
-            for (int j = 0; j < 4; ++j) part[((size_t)sl * hq + hh) * hd + cq * 4 + j] = acc[hh][j];
+        for (int j = 0; j < 4; ++j) {
+            const int m = gq + 8 * (j >> 1), col = 2 * tq + (j & 1);
+            if (m >= hq * nl) continue;
+            const int hh = m / nl, l = m % nl;
+            if (KVB == 1) {
+                atomicAdd(reinterpret_cast<unsigned long long*>(sm.num + hh * hd + db * 16 + 2 * col),
+                          (unsigned long long)((long long)acc[i][0][j] * (1LL << (8 * l))));
+                atomicAdd(reinterpret_cast<unsigned long long*>(sm.num + hh * hd + db * 16 + 2 * col + 1),
+                          (unsigned long long)((long long)acc[i][1][j] * (1LL << (8 * l))));
+            } else {
+                const long long v = (long long)acc[i][0][j] * 256 + acc[i][1][j];
+                atomicAdd(reinterpret_cast<unsigned long long*>(sm.num + hh * hd + db * 8 + col),
+                          (unsigned long long)(v * (1LL << (8 * l))));
+            }
+        }
+    }
     __syncthreads();
     for (int o = threadIdx.x; o < hq * hd; o += kThreads) {
         const int hh = o / hd, i = o % hd;
-        double a = 0.0;
-        for (int k = 0; k < ns; ++k) a = __dadd_rn(a, part[((size_t)k * hq + hh) * hd + i]);
-        s.att[(size_t)b * d.dim + (size_t)(g * group + h0 + hh) * hd + i] = att_q16(a, sm.den[hh], KVB);
+        s.att[(size_t)b * d.dim + (size_t)(g * group + h0 + hh) * hd + i] = att_q16((double)sm.num[o], sm.den[hh], KVB);
     }
 }
 
@@ -2149,6 +2372,7 @@ inline DownSrc down_src(const DModel& m, int layer) {
     ds.layer = layer;
     ds.two = m.ffn_chunked ? 1 : 0;
     if (layer < 0) return ds;
+    ds.hs = layer < (int)m.h.hid_scale.size() ? (int)m.h.hid_scale[layer] : 0;
     if (m.h.experts) {
         const int eb = m.e_w1[(size_t)layer * m.h.experts];
         ds.dm = m.d_mats;
@@ -2467,7 +2691,7 @@ struct BOps {
                                            x_stride(W1), hs, dr, Finalize{}, st);
         if (!tc) mm<kOpGate>(m, s, bt, layer, M, d.experts, hs, Finalize{}, st, dr);
         if (tc && tc_launch<kOpDown>(m, s, bt, layer, Wa, two ? &Wb : nullptr, (int)dr.bytes, 1, (int)dr.lo_a,
-                                     (int)dr.hi_a, (int)dr.lo_b, (int)dr.hi_b, 0, dr, Finalize{}, st))
+                                     (int)dr.hi_a, (int)dr.lo_b, (int)dr.hi_b, hs, dr, Finalize{}, st))
             return;
         const int e = d.experts ? d.experts : 1;
         const int splits = mm_splits(m, Wa.rblocks * e, bt.n / e, kWarps * kMmNI);
@@ -2476,7 +2700,7 @@ struct BOps {
         const int group =
             std::max(1, std::min(std::min(want, kMmGroupMax), (int)((kMaxDynSmem - fixed) / down_rec(Wa, Wb, two).bytes)));
         launch_pdl(k_mmdown<WT>, dim3(Wa.rblocks, e, splits), mmdown_smem(Wa, Wb, two, group, bt.n), st, M2, s, bt, d,
-                   layer, group);
+                   layer, group, hs);
     }
 };
 

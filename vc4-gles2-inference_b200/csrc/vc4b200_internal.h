@@ -143,6 +143,7 @@ struct State {                      // per-slot activations, [slot][...]
     int* done = nullptr;             // CTA arrival counter of the logits kernel (reset by its last CTA)
     int* err = nullptr;              // kernel self-check word: nonzero = a launch reserved too little shared memory
     long long* sdown = nullptr;      // w2 partial sums [layers][slots][2][dim] (int64, zero between uses)
+    int* hmax = nullptr;             // host FFN: max |q16 hidden| per [layers][slots][2 halves] (w2 input scale)
     char* xrec = nullptr;            // many-sequence path: staged matvec inputs [slots][record]
     char* hrec = nullptr;            // many-sequence path: staged w2 inputs [slots][record]
     int batch_ok = 0;                // the many-sequence kernels fit this model

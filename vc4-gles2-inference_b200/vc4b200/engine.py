@@ -63,6 +63,7 @@ _PROTOS = {
     "vc4_step_batch_device": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                         C.c_int]),
     "vc4_session_stream": (C.c_void_p, [C.c_void_p]),
+    "vc4_session_check": (C.c_int, [C.c_void_p]),
     "vc4_prefill": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
     "vc4_kv_row_bytes": (C.c_int, [C.c_void_p]),
     "vc4_kv_read_rows": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p]),
@@ -228,6 +229,10 @@ class Session:
 
     def stream(self) -> int:
         return lib().vc4_session_stream(self._h) or 0
+
+    def check(self) -> None:
+        """Raise if a device-resident pass failed a kernel self-check."""
+        _check(lib().vc4_session_check(self._h))
 
     def prefill(self, tokens, pos0: int = 0, slot: int = 0, want_logits: bool = True):
         t = np.ascontiguousarray(tokens, np.int32)
