@@ -63,6 +63,8 @@ def pack_with_reference(ref: str, cfg: synth.Config, workdir: str) -> tuple:
            "--verify"]
     if cfg.head_dedup:
         cmd.append("--head-dedup")
+    if cfg.extra.get("q8_row"):
+        cmd.append("--q8-row-scale")
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise SystemExit("reference packer failed for %s:\n%s\n%s" % (cfg.key, r.stdout, r.stderr))
@@ -73,6 +75,8 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("VC4_REFERENCE"))
     ap.add_argument("--full", action="store_true", help="also pack the five full-size configurations")
+    ap.add_argument("--only", default="", help="comma-separated configurations to (re)pack; the others keep "
+                                               "their recorded entries")
     ap.add_argument("--session", action="store_true",
                     help="only record the reference layer loop's logits (oracle/_ref/ref_session) into "
                          "reference_logits.npz")
@@ -86,7 +90,10 @@ def main():
     golden = {"xformat": xformat_vectors(args.ref), "containers": {}}
     cfgs = dict(synth.TINY_CONFIGS)
     if args.full:
-        cfgs.update({k: v for k, v in synth.CONFIGS.items() if k in ("c0", "c1", "c2", "c3", "c4")})
+        cfgs.update({k: v for k, v in synth.CONFIGS.items() if k in ("c0", "c0r", "c1", "c2", "c3", "c4")})
+    if args.only:
+        allc = dict(synth.TINY_CONFIGS, **synth.CONFIGS)
+        cfgs = {k: allc[k] for k in args.only.split(",")}
     with tempfile.TemporaryDirectory() as wd:
         for key, cfg in cfgs.items():
             path, log = pack_with_reference(args.ref, cfg, wd)
@@ -116,7 +123,7 @@ def reference_session_logits() -> None:
     import refsession
     from vc4b200 import mmcf_writer
     out = {}
-    cfgs = dict(synth.TINY_CONFIGS, **{k: synth.CONFIGS[k] for k in ("c0", "c1", "c2", "c3", "c4")})
+    cfgs = dict(synth.TINY_CONFIGS, **{k: synth.CONFIGS[k] for k in ("c0", "c0r", "c1", "c2", "c3", "c4")})
     with tempfile.TemporaryDirectory() as wd:
         for key, n in refsession.POSITIONS.items():
             cfg = cfgs[key]

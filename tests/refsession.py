@@ -22,7 +22,7 @@ FIXTURE = os.path.join(HERE, "golden", "reference_logits.npz")
 
 # teacher-forced positions per configuration (the prompt's first n tokens)
 POSITIONS = {"tiny_q8": 8, "tiny_q4": 8, "tiny_flat_q8": 8, "tiny_moe_q4": 8, "tiny_t3": 8,
-             "c0": 6, "c1": 6, "c2": 6, "c3": 2, "c4": 6}
+             "c0": 6, "c0r": 6, "c1": 6, "c2": 6, "c3": 2, "c4": 6}
 
 
 def available() -> bool:

@@ -4,32 +4,20 @@ shapes, on shortened workloads the oracle finishes in seconds.
 Tolerance: max |dlogit| <= 1e-2 with greedy agreement (the north star's); the
 KV rows are compared bit for bit.
 """
-import os
-import tempfile
-
 import numpy as np
 import pytest
 
 import oracle
 import vc4b200
-from vc4b200 import mmcf_writer, synth
+from conftest import full_model_path
+from vc4b200 import synth
 
 TOL = 1e-2
 KV = {16: "q16", 8: "q8"}
-_CACHE = {}
 
 
 def _path(key):
-    if key not in _CACHE:
-        d = os.path.join(tempfile.gettempdir(), "vc4b200_models")
-        os.makedirs(d, exist_ok=True)
-        p = os.path.join(d, "%s_%d.mmcf" % (key, synth.CONFIGS[key].seed))
-        if not os.path.exists(p):
-            tmp = p + ".%d.tmp" % os.getpid()
-            mmcf_writer.write_config(synth.CONFIGS[key], tmp)
-            os.replace(tmp, p)
-        _CACHE[key] = p
-    return _CACHE[key]
+    return full_model_path(key)
 
 
 @pytest.fixture(scope="module")
@@ -38,7 +26,7 @@ def gpu():
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("key,prompt_len,steps", [("c0", 24, 8), ("c1", 24, 8), ("c3", 12, 4)])
+@pytest.mark.parametrize("key,prompt_len,steps", [("c0", 24, 8), ("c0r", 24, 8), ("c1", 24, 8), ("c3", 12, 4)])
 def test_single_stream_full_shape(gpu, key, prompt_len, steps):
     cfg = synth.CONFIGS[key]
     path = _path(key)

@@ -51,7 +51,8 @@ def _check(got, ref, what):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("key,positions", [("c0", [127, 128, 129, 255]), ("c1", [127, 128, 129, 255]),
+@pytest.mark.parametrize("key,positions", [("c0", [127, 128, 129, 255]), ("c0r", [128, 255]),
+                                           ("c1", [127, 128, 129, 255]),
                                            ("c4b1", [511, 512, 767]), ("c3", [1023])])
 def test_one_sequence_at_benchmark_positions(gpu, key, positions):
     cfg = synth.CONFIGS[key]

@@ -17,7 +17,7 @@ import pytest
 import oracle
 from vc4b200 import mmcf_writer, synth
 
-FULL = ["c0", "c1", "c2", "c3", "c4"]
+FULL = ["c0", "c0r", "c1", "c2", "c3", "c4"]
 
 
 def _container(key):

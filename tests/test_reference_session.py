@@ -31,7 +31,7 @@ from vc4b200 import mmcf_writer, synth
 
 ALL = dict(synth.TINY_CONFIGS, **synth.CONFIGS)
 KEYS = list(refsession.POSITIONS)
-FULL = ["c0", "c1", "c2", "c3", "c4"]
+FULL = ["c0", "c0r", "c1", "c2", "c3", "c4"]
 STEP = 1.0 / 256.0
 
 

@@ -71,6 +71,18 @@ def _q8_rows(w, via_i16):
     return lev, sc
 
 
+def _q8_per_row(w):
+    """--q8-row-scale: one scale per output row (max|w|/127, zero rows 1),
+    levels rint(w/s) clipped to +-127; the record carries the largest row
+    scale and part 3 the row scales relative to it (mmcf_hf.py q8_per_row)."""
+    w = np.asarray(w, np.float32)
+    s = np.abs(w).max(axis=1, keepdims=True) / np.float32(127.0)
+    s[s == 0] = 1.0
+    q = np.clip(np.rint(w / s), -127, 127).astype(np.int8)
+    unit = float(s.max())
+    return q, unit, (s[:, 0] / np.float32(unit)).astype(np.float32)
+
+
 def _q4(w):
     w = np.asarray(w, np.float32)
     rows, cols = w.shape
@@ -118,8 +130,9 @@ def _t3(w):
 # ---- records ----------------------------------------------------------------
 
 class _Records:
-    def __init__(self, scheme):
+    def __init__(self, scheme, q8_row=False):
         self.scheme = scheme
+        self.q8_row = q8_row
         self.items = []      # (id, dtype, rows, cols, group, payload, scale, aux)
 
     def add(self, tid, dt, rows, cols, group, payload, scale, aux=0):
@@ -129,7 +142,11 @@ class _Records:
         w = np.asarray(w, np.float32)
         rows, cols = w.shape
         base = kind | (layer << 8)
-        if self.scheme == "q8":
+        if self.scheme == "q8" and self.q8_row:
+            q, unit, plane = _q8_per_row(w)
+            self.add(base, DT_Q8I8, rows, cols, 0, q.tobytes(), unit, aux)
+            self.add(base | (3 << 14), DT_F32, rows, 1, 0, (plane / np.float32(1.0)).astype("<f4").tobytes(), 0.0, aux)
+        elif self.scheme == "q8":
             q, s = _q8_via_i16(w)
             self.add(base, DT_Q8I8, rows, cols, 0, q.tobytes(), s, aux)
         elif self.scheme == "t3":
@@ -150,10 +167,10 @@ def _tlv(key, payload):
 
 
 def pack(shape: synth.Shape, tensors: dict, scheme: str, seq: int, *,
-         head_dedup: bool = False, rms_eps: float = 1e-6) -> bytes:
+         head_dedup: bool = False, rms_eps: float = 1e-6, q8_row: bool = False) -> bytes:
     """Build the container bytes the reference packer writes for
     `mmcf_pack.py --in DIR --quant SCHEME --seq SEQ --rms-eps 1e-6
-    --template plain [--head-dedup]`."""
+    --template plain [--head-dedup] [--q8-row-scale]`."""
     f32 = lambda name: np.asarray(tensors[name], np.float32)   # noqa: E731
     s = shape
     moe = s.experts > 0
@@ -161,7 +178,7 @@ def pack(shape: synth.Shape, tensors: dict, scheme: str, seq: int, *,
     split = 1 if (moe or 2 * ffn_w > 2048) else 0
     if not split:
         raise ValueError("fused-W13 containers are not produced by this writer")
-    recs = _Records(scheme)
+    recs = _Records(scheme, q8_row=q8_row)
     emb = f32("model.embed_tokens.weight")
     lev, es = _q8_rows(emb, via_i16=(scheme == "q8"))
     recs.add(K_EMB, DT_Q8I8, s.vocab, s.dim, 0, lev.tobytes(), 0.0)
@@ -240,7 +257,7 @@ def pack(shape: synth.Shape, tensors: dict, scheme: str, seq: int, *,
 
 def pack_config(cfg: synth.Config) -> bytes:
     return pack(cfg.shape, synth.hf_tensors(cfg.shape, cfg.seed), cfg.quant, cfg.seq,
-                head_dedup=cfg.head_dedup)
+                head_dedup=cfg.head_dedup, q8_row=bool(cfg.extra.get("q8_row")))
 
 
 def write_config(cfg: synth.Config, path: str) -> str:

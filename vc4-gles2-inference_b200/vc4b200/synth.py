@@ -69,6 +69,9 @@ class Config:
 CONFIGS = {
     "c0": Config("c0", MM3, "q8", 16, 256, 128, 64),
     "c1": Config("c1", MM3, "q4", 16, 256, 128, 64),
+    # config 0 with one q8 scale per output row (the packer's --q8-row-scale,
+    # BASELINE's "per-row symmetric int8 + f32 scale" wording)
+    "c0r": Config("c0r", MM3, "q8", 16, 256, 128, 64, extra={"q8_row": True}),
     "c2": Config("c2", MM3_MOE, "q4", 8, 512, 256, 128, batch=64),
     "c3": Config("c3", BITCPM, "t3", 16, 1024, 512, 128, head_dedup=True),
     "c3b32": Config("c3b32", BITCPM, "t3", 16, 1024, 512, 128, batch=32, head_dedup=True),
