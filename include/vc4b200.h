@@ -197,6 +197,64 @@ VC4_API int vc4_kv_codec_probe(int device, int kv_bits, const float* x, int n, v
 VC4_API int vc4_matvec_s_noalloc(vc4_model* m, int which, int layer, int expert, const float* d_x,
                                  float* d_out, void* stream);
 
+/* ---- The per-op boundary ----------------------------------------------------
+   The calls the reference's fused GPU layer loop makes on class GPU
+   (Session::forward_gpu_hidden, session.cpp:1459-1584), one C function each.
+   GL textures become per-slot device rows of q16 ints named by vc4_buf.  The
+   reference's GPU path quantises at its own points; these calls compute what
+   vc4_step computes (the CPU path's quantisation points, exact integer dots), so
+   a layer loop written call for call against them gives vc4_step's token.  Work
+   is queued on the session stream; calls that return host data synchronise. */
+typedef enum {
+    VC4_BUF_HIDDEN = 0,   /* the residual h (GPU::hidden_a_ / hidden_b_) */
+    VC4_BUF_X1 = 1,       /* the residual after attention (hidden_b_ before the FFN) */
+    VC4_BUF_XB = 2,       /* rmsnorm before attention (xb_) */
+    VC4_BUF_XBF = 3,      /* rmsnorm before the FFN (xbf_) */
+    VC4_BUF_XF = 4,       /* rmsnorm before the logits (xf_) */
+    VC4_BUF_ATT = 5,      /* attention output (att_out_) */
+    VC4_BUF_HA = 6,       /* FFN hidden: the whole row, or its first chunk (ffn_h_a_) */
+    VC4_BUF_HB = 7,       /* FFN hidden: the second chunk (ffn_h_b_) */
+    VC4_BUF_TMP = 8       /* the residual between the two w2 halves (hidden_a_) */
+} vc4_buf;
+
+/* Session::embedding (session.cpp:342-371) of `token` into buffer dst. */
+VC4_API int vc4_embedding(vc4_session* s, int slot, int token, int dst);
+/* GPU::upload_hidden (gpu.h:169): host floats (dim), quantised to q16 (lrintf). */
+VC4_API int vc4_upload_hidden(vc4_session* s, int slot, const float* x, int dst);
+/* GPU::rmsnorm (gpu.h:173): dst = rmsnorm(src) with the model's weights
+   (weights 0: attention of `layer`, 1: FFN of `layer`, 2: final). */
+VC4_API int vc4_rmsnorm(vc4_session* s, int slot, int src, int weights, int layer, int dst);
+/* GPU::attention_block (gpu.h:142): qkv = matvec_s(qkv[layer], src), QK-norm,
+   RoPE at `pos`, the packed KV row appended to the slot's cache, attention over
+   positions 0..pos; the q16 attention output goes to dst. */
+VC4_API int vc4_attention_block(vc4_session* s, int slot, int layer, int pos, int src, int dst);
+/* GPU::matvec_add (gpu.h:175): dst = residual + the matrix times src.  which 1:
+   wo (matvec_s, add_q16).  which 4 / 7: w2 / its second half.  For a chunked FFN
+   the first half (4) goes to VC4_BUF_TMP and the second (7) takes VC4_BUF_TMP as
+   its residual: dst = add_q16(x1, add_q16(w2a out, w2b out)), the CPU path's
+   order (session.cpp:519-551).  The w2 input is read as matvec_s reads it in
+   the host FFN of a two-chunk dense model, as is otherwise. */
+VC4_API int vc4_matvec_add(vc4_session* s, int slot, int which, int layer, int expert, int src, int residual,
+                           int dst);
+/* GPU::matvec_from (gpu.h:84): the matrix times src read back as floats (rows).
+   which 0 qkv, 1 wo, 5 router.  input_scale 1 reads src as matvec_s does
+   (gpu_conv.cpp:271-287; the CPU path's router call, session.cpp:484), 0 as
+   uploaded. */
+VC4_API int vc4_matvec_from(vc4_session* s, int slot, int which, int layer, int expert, int src, int input_scale,
+                            float* out);
+/* GPU::ffn_split / ffn_split_chunked (gpu.h:89,107-108): the FFN hidden row of
+   src for `layer` (and `expert`) into dst_a, and for a chunked FFN its second
+   chunk into dst_b.  A two-chunk dense model uses the CPU path's host FFN
+   (matvec_s gate/up, quantize_act); MoE and one-chunk FFNs the GPU FFN kernels'
+   rounding. */
+VC4_API int vc4_ffn_split(vc4_session* s, int slot, int layer, int expert, int src, int dst_a, int dst_b);
+/* GPU::logits_from (gpu.h:256): the vocab logits (q16 grid, as floats) of src. */
+VC4_API int vc4_logits_from(vc4_session* s, int slot, int src, float* logits);
+/* GPU::logits_argmax_from (gpu.h:263-264): the first-maximum token of src. */
+VC4_API int vc4_logits_argmax_from(vc4_session* s, int slot, int src, int* token);
+/* GPU::read_bytes (gpu.h:270) of a buffer, as floats (n values, q16 / 256). */
+VC4_API int vc4_read_buffer(vc4_session* s, int slot, int buf, int n, float* out);
+
 /* draws()/syncs() (gpu.h:44-48): kernels launched and host syncs so far. */
 VC4_API int vc4_counters(const vc4_session* s, long long* launches, long long* syncs);
 /* Kernels one decode pass of n sequences launches. */

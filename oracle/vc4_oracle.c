@@ -830,19 +830,20 @@ static void attention(orc_session* s, int layer, int pos) {
         } else {
             /* Canonical: q on a per-head power-of-two grid (orc_q_grid_exp),
                an exact integer dot with the cache levels, one rounding to
-               float, then the power-of-two grid scale and / sqrt(hd). */
+               float, times the head's constant c = fl(2^-F / grid / sqrt(hd)). */
             float qm = 0.0f;
             for (int i = 0; i < hd; ++i) { const float a = fabsf(qh[i]); if (a > qm) qm = a; }
             const int F = orc_q_grid_exp(qm);
             const float sF = ldexpf(1.0f, F);
             for (int i = 0; i < hd; ++i) s->qi[i] = (int32_t)rintf(qh[i] * sF);
             const float gscale = ldexpf(1.0f, -F - (s->kv_bits == 16 ? 11 : 4));
+            const float ch = gscale / sq;               /* one rounding, once per head */
             const float vgrid = s->kv_bits == 16 ? 2048.0f : 16.0f;
             for (int t = 0; t <= pos; ++t) {
                 const float* kr = kb + (size_t)t * KD;
                 int64_t S = 0;
                 for (int i = 0; i < hd; ++i) S += (int64_t)s->qi[i] * (int64_t)(kr[i] * vgrid);
-                const float acc = ((float)S * gscale) / sq;
+                const float acc = (float)S * ch;
                 s->scores[t] = acc;
                 if (acc > mx) mx = acc;
             }

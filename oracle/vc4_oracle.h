@@ -19,8 +19,9 @@
  *     fmaf() is spelled out;
  *   - a query head is put on a power-of-two integer grid (orc_q_grid_exp)
  *     and its score with a cached key is the exact integer dot with the
- *     cache levels, rounded once to float and scaled by the grids and
- *     1/sqrt(head_dim); the reference sums q*k sequentially in fp32;
+ *     cache levels, rounded once to float, times the head's constant
+ *     fl(2^-F / cache grid / sqrt(head_dim)); the reference sums q*k
+ *     sequentially in fp32;
  *   - attention weights are integers E_t = rint(exp(s_t - max) * 2^k) on a grid
  *     fine enough for k to keep every sum of E_t and E_t x (cache level) an
  *     exact integer in double (orc_attn_weight_exp), so the softmax

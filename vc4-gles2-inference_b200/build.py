@@ -23,7 +23,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-std=c++17", "-O3", "-lineinfo", "--fmad=false", "-I" + INCLUDE, "-I" + CSRC,
          "-Xcompiler", "-fPIC,-ffp-contract=off,-fvisibility=hidden", "-diag-suppress", "177"]
-SOURCES = ["kernels.cu", "ops_q8.cu", "ops_q4.cu", "ops_t3.cu", "engine.cu", "noalloc.cu", "mmcf.cpp"]
+SOURCES = ["kernels.cu", "ops_q8.cu", "ops_q4.cu", "ops_t3.cu", "engine.cu", "noalloc.cu", "ops.cu", "mmcf.cpp"]
 HEADERS = ["vc4b200_internal.h", "kernels.cuh", "batch.cuh", "ops_wt.inc"]
 
 

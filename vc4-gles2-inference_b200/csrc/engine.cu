@@ -75,6 +75,7 @@ struct vc4_session {
     std::map<PassArgs, cudaGraphExec_t> graphs;
     long long launches = 0, syncs = 0;
     cudaStream_t stream = nullptr;
+    void* ops = nullptr;                      // buffers of the per-op calls (ops.cu), made on first use
 };
 
 // ---------------------------------------------------------------------------
@@ -509,6 +510,8 @@ void vc4_session_destroy(vc4_session* s) {
     if (!s) return;
     cudaSetDevice(s->m->d.device);
     cudaStreamSynchronize(s->stream);
+    free_op_buffers(s->ops);
+    s->ops = nullptr;
     for (auto& kv : s->graphs) cudaGraphExecDestroy(kv.second);
     s->graphs.clear();
     State& st = s->st;
@@ -932,6 +935,20 @@ namespace vc4 {
 int set_error(int code, const char* msg) { return fail(code, msg); }
 
 const DModel& model_of(const vc4_model* m) { return m->d; }
+
+SessionView session_view(vc4_session* s) {
+    SessionView v;
+    v.st = &s->st;
+    v.m = &s->m->d;
+    v.stream = s->stream;
+    v.slots = s->slots;
+    v.ops = &s->ops;
+    v.launches = &s->launches;
+    v.syncs = &s->syncs;
+    return v;
+}
+
+int kernel_check(vc4_session* s) { return check_kernel_word(s); }
 
 cudaStream_t model_stream(const vc4_model* m) { return m->g->stream; }
 

@@ -1419,7 +1419,7 @@ struct AttnSmem {
     float* redf;     // kWarps: softmax maxima per warp
     float* sc;       // group x seq: scores, then probabilities (cluster-written)
     int* qi;         // group x hd: the q heads on their integer grids
-    float* gsc;      // group: 2^-F / cache grid of each q head
+    float* gsc;      // group: each q head's score constant (warp_q_grid)
 };
 
 __host__ __device__ inline size_t attn_carve(int group, int hd, int seq, int kv_bits, char* base, AttnSmem* sm) {
@@ -1539,7 +1539,8 @@ __device__ __forceinline__ int q_grid_exp(float qmax) {
 __device__ __forceinline__ float pow2f(int k) { return __int_as_float((127 + k) << 23); }   // 2^k, -126 <= k <= 127
 
 // One warp puts q head v (hd floats) on its integer grid: qi[i] = rint(v[i]
-// * 2^F); returns 2^-F / grid (kvb 2: grid 2048, 1: grid 16).
+// * 2^F); returns the head's score constant fl(2^-F / grid / sqrt(hd)) (kvb 2:
+// grid 2048, 1: grid 16), so a score is float(S) * constant.
 __device__ __forceinline__ float warp_q_grid(const float* v, int hd, int kvb, int* qi) {
     const int lane = threadIdx.x & 31;
     float m = 0.0f;
@@ -1548,7 +1549,7 @@ __device__ __forceinline__ float warp_q_grid(const float* v, int hd, int kvb, in
     const int F = q_grid_exp(m);
     const float sF = pow2f(F);
     for (int i = lane; i < hd; i += 32) qi[i] = __float2int_rn(__fmul_rn(v[i], sF));
-    return pow2f(-F - (kvb == 2 ? 11 : 4));
+    return __fdiv_rn(pow2f(-F - (kvb == 2 ? 11 : 4)), __fsqrt_rn((float)hd));
 }
 
 __device__ void attn_weights(float* scores, int seq, int len, int hq, int kvb, float* redf, double* redd,
@@ -1723,9 +1724,8 @@ k_attn(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int 
     __syncthreads();
 
     // 4. scores of this CTA's positions: the exact integer dot of the q head
-    //    on its grid with the cache levels, one rounding to float, the grid
-    //    scale, / sqrt(hd); stored into every CTA of the cluster
-    const float sq = __fsqrt_rn((float)hd);
+    //    on its grid with the cache levels, one rounding to float, times the
+    //    head's constant; stored into every CTA of the cluster
     for (int e = threadIdx.x; e < nt * hq; e += kThreads) {
         const int r = e / hq, hh = e % hq;
         const float4* kr = reinterpret_cast<const float4*>(sm.kt + r * hp);
@@ -1738,7 +1738,7 @@ k_attn(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int 
             S += (long long)q4.x * (int)k4.x + (long long)q4.y * (int)k4.y + (long long)q4.z * (int)k4.z +
                  (long long)q4.w * (int)k4.w;
         }
-        const float acc = __fdiv_rn(__fmul_rn(__ll2float_rn(S), sm.gsc[hh]), sq);
+        const float acc = __fmul_rn(__ll2float_rn(S), sm.gsc[hh]);
         float* dst = sm.sc + hh * d.seq + t0 + r;
 #pragma unroll
         for (int c = 0; c < kAttnCtas; ++c) *cluster.map_shared_rank(dst, c) = acc;

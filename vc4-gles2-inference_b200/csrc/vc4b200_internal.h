@@ -178,9 +178,23 @@ int max_input_cols();
 // Accessors engine.cu gives the library's other translation units.
 }  // namespace vc4
 struct vc4_model;
+struct vc4_session;
 namespace vc4 {
 int set_error(int code, const char* msg);
 const DModel& model_of(const vc4_model* m);
+// What the per-op calls (ops.cu) need of a session.
+struct SessionView {
+    State* st;
+    const DModel* m;
+    cudaStream_t stream;
+    int slots;
+    void** ops;                      // the per-op buffers (owned through free_op_buffers)
+    long long* launches;
+    long long* syncs;
+};
+SessionView session_view(vc4_session* s);
+void free_op_buffers(void* ops);
+int kernel_check(vc4_session* s);    // the kernels' self-check word (synchronises)
 cudaStream_t model_stream(const vc4_model* m);
 int lookup_matrix(const vc4_model* m, int which, int layer, int expert, int* idx);
 }  // namespace vc4

@@ -75,6 +75,16 @@ _PROTOS = {
     "vc4_matvec_s": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
     "vc4_matvec_s_noalloc": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
                                        C.c_void_p]),
+    "vc4_embedding": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int]),
+    "vc4_upload_hidden": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int]),
+    "vc4_rmsnorm": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]),
+    "vc4_attention_block": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]),
+    "vc4_matvec_add": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]),
+    "vc4_matvec_from": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p]),
+    "vc4_ffn_split": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]),
+    "vc4_logits_from": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
+    "vc4_logits_argmax_from": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_int)]),
+    "vc4_read_buffer": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p]),
     "vc4_counters": (C.c_int, [C.c_void_p, C.POINTER(C.c_longlong), C.POINTER(C.c_longlong)]),
     "vc4_launches_per_step": (C.c_int, [C.c_void_p, C.c_int]),
 }
