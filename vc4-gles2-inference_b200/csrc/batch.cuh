@@ -693,6 +693,9 @@ __global__ void __launch_bounds__(kTcThreads) k_tmm(const __grid_constant__ TcMa
                     kexp[q] = reinterpret_cast<const int*>(recs + (size_t)(g0 + q) * a.rec_bytes +
                                                            2 * (size_t)x_stride(a.p[0].W))[g_stride(a.p[0].W)];
             }
+            if (OP == kOpDown && d.hostffn)   // the w2 input exponents of both hidden halves
+                for (int q = lane - 1; q < gn; q += 31)
+                    kexp[q] = (hidden_exp(s, layer, g0 + q, 0) & 0xFFFF) | (hidden_exp(s, layer, g0 + q, 1) << 16);
         }
         __syncwarp();
     }
@@ -779,8 +782,9 @@ __global__ void __launch_bounds__(kTcThreads) k_tmm(const __grid_constant__ TcMa
                 if (!live) continue;
                 float o2;
                 if (d.hostffn) {
-                    const float oa = host_w2_out(S0, rs0, hidden_exp(s, layer, b, 0), a.hs, s.err);
-                    const float ob = host_w2_out(S1, rs1, hidden_exp(s, layer, b, 1), a.hs, s.err);
+                    const int kk = kexp[q];
+                    const float oa = host_w2_out(S0, rs0, (int)(short)(kk & 0xFFFF), a.hs, s.err);
+                    const float ob = host_w2_out(S1, rs1, kk >> 16, a.hs, s.err);
                     o2 = __fmul_rn((float)q16h(__fadd_rn(oa, ob)), 1.0f / 256.0f);
                 } else {
                     o2 = __fmul_rn((float)mv_epi(S0, rs0), 1.0f / 256.0f);

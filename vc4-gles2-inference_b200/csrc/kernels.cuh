@@ -781,8 +781,11 @@ __device__ __forceinline__ void rebuild_x(const State& s, const Dims& d, const D
     }
     const long long* S = s.sdown + sdown_at(ds.layer, bi, 0, d.dim, s.slots);
     const int16_t* x1 = s.x1 + (size_t)bi * d.dim;
-    const int ka = d.hostffn ? hidden_exp(s, ds.layer, bi, 0) : 0;
-    const int kb = d.hostffn ? hidden_exp(s, ds.layer, bi, 1) : 0;
+    // the host FFN's w2 input exponents: their loads go out with the first
+    // round's, the exponents are taken after
+    const int ma = d.hostffn ? __ldcg(s.hmax + hmax_at(ds.layer, bi, 0, s.slots)) : 0;
+    const int mb = d.hostffn ? __ldcg(s.hmax + hmax_at(ds.layer, bi, 1, s.slots)) : 0;
+    int ka = 0, kb = 0;
     // kU rows per thread per round: every load of a round is issued before the first use
     constexpr int kU = 4;
     for (int base = 0; base < d.dim; base += kU * kThreads) {
@@ -801,6 +804,10 @@ __device__ __forceinline__ void rebuild_x(const State& s, const Dims& d, const D
                 if (ds.two) { sb[u] = __ldcg(S + d.dim + r); fb[u] = __ldg(rb + r); }
                 xv[u] = __ldcg(x1 + r);
             }
+        }
+        if (d.hostffn && base == 0) {
+            ka = exp_from_max(ma);
+            kb = exp_from_max(mb);
         }
 #pragma unroll
         for (int u = 0; u < kU; ++u) {
@@ -1815,12 +1822,11 @@ __host__ __device__ inline int attnb_k_of(int p) {
 }
 
 struct AbSmem {
-    uint8_t* ring;   // kAbStages x kAbRows x pitch cache bytes
+    uint8_t* ring;   // kAbStages x kAbRows x pitch cache bytes; at the end the P.V partial sums
     uint8_t* newrow; // 2 x hbytes: this step's K and V row
     uint8_t* ea;     // 16 x epitch: weight limbs, row h*NL + limb, positions in MMA k order
-    uint8_t* qb;     // 8 x hd: q limbs, column 2*limb + head, dims in MMA k order
-    long long* num;  // hq x hd: exact P.V sums
-    double* redd;
+    uint8_t* qb;     // 8 x hd: q limbs, column 4*head + limb, dims in MMA k order
+    double* redd;    // kWarps x 2: per-warp sums of the weights
     double* den;     // hq
     float* q;        // (hq + 1) x hd: q heads, then the new k
     float* vn;       // hd: the new v
@@ -1828,8 +1834,8 @@ struct AbSmem {
     float* rsn;
     float* wq;
     float* wk;
-    float* redf;
-    float* gsc;      // hq: 2^-F / cache grid per q head
+    float* redf;     // kWarps x 2: per-warp score maxima
+    float* gsc;      // hq: each q head's score constant (warp_q_grid)
     float* sc;       // hq x seq: scores, then E_t
     int* qi;         // hq x hd: the q heads on their integer grids
 };
@@ -1841,8 +1847,7 @@ __host__ __device__ inline size_t attnb_carve(int hq, int hd, int seq, int kv_bi
     const size_t nr = o;   o = align16(o + 2 * (size_t)hbytes);
     const size_t ea = o;   o = align16(o + 16 * (size_t)attnb_epitch(seq));
     const size_t qb = o;   o = align16(o + 8 * (size_t)hd);
-    const size_t num = o;  o = align16(o + sizeof(long long) * (size_t)hq * hd);
-    const size_t redd = o; o = align16(o + sizeof(double) * kWarps);
+    const size_t redd = o; o = align16(o + sizeof(double) * kWarps * 2);
     const size_t den = o;  o = align16(o + sizeof(double) * hq);
     const size_t q = o;    o = align16(o + sizeof(float) * (size_t)(hq + 1) * hd);
     const size_t vn = o;   o += sizeof(float) * hd;
@@ -1850,7 +1855,7 @@ __host__ __device__ inline size_t attnb_carve(int hq, int hd, int seq, int kv_bi
     const size_t rsn = o;  o += sizeof(float) * (hd / 2);
     const size_t wq = o;   o += sizeof(float) * hd;
     const size_t wk = o;   o += sizeof(float) * hd;
-    const size_t redf = o; o += sizeof(float) * kWarps;
+    const size_t redf = o; o += sizeof(float) * kWarps * 2;
     const size_t gsc = o;  o += sizeof(float) * hq;
     const size_t sc = o;   o += sizeof(float) * (size_t)hq * seq;
     const size_t qi = o;   o += sizeof(int) * (size_t)hq * hd;
@@ -1859,7 +1864,6 @@ __host__ __device__ inline size_t attnb_carve(int hq, int hd, int seq, int kv_bi
         sm->newrow = reinterpret_cast<uint8_t*>(base + nr);
         sm->ea = reinterpret_cast<uint8_t*>(base + ea);
         sm->qb = reinterpret_cast<uint8_t*>(base + qb);
-        sm->num = reinterpret_cast<long long*>(base + num);
         sm->redd = reinterpret_cast<double*>(base + redd);
         sm->den = reinterpret_cast<double*>(base + den);
         sm->q = reinterpret_cast<float*>(base + q);
@@ -1933,15 +1937,14 @@ k_attn_b(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, in
     // tile u < ntile: K rows of positions [u*R, ...); ntile <= u < 2*ntile: V rows.
     // Thread (row r0, 16-byte column cc) copies rows r0, r0 + rpp, ...
     const int rpp = kThreads / kvec, cc = threadIdx.x % kvec, r0 = threadIdx.x / kvec;
+    const size_t rstep = (size_t)rpp * d.row_bytes;
     auto issue = [&](int u) {
         if (u < 2 * ntile && r0 < rpp) {
             const int kind = u >= ntile, t0 = (u % ntile) * kAbRows, nt = min(kAbRows, len - t0);
-            uint8_t* dst = sm.ring + (size_t)(u % kAbStages) * kAbRows * pitch + cc * 16;
-            const uint8_t* src = kvrd + (kind ? vofs : 0) + cc * 16;
-            for (int r = r0; r < nt; r += rpp) {
-                const int t = t0 + r;
-                if (t != pos) cp_async16(dst + r * pitch, src + (size_t)t * d.row_bytes);
-            }
+            uint8_t* dst = sm.ring + (size_t)(u % kAbStages) * kAbRows * pitch + cc * 16 + r0 * pitch;
+            const uint8_t* src = kvrd + (kind ? vofs : 0) + cc * 16 + (size_t)(t0 + r0) * d.row_bytes;
+            for (int r = r0; r < nt; r += rpp, dst += rpp * pitch, src += rstep)
+                if (t0 + r != pos) cp_async16(dst, src);
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
@@ -1960,7 +1963,6 @@ k_attn_b(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, in
     // positions past the sequence multiply as zero)
     for (int i = threadIdx.x; i < 16 * epitch / 16; i += kThreads) reinterpret_cast<int4*>(sm.ea)[i] = make_int4(0, 0, 0, 0);
     for (int i = threadIdx.x; i < 8 * hd / 16; i += kThreads) reinterpret_cast<int4*>(sm.qb)[i] = make_int4(0, 0, 0, 0);
-    for (int i = threadIdx.x; i < hq * hd; i += kThreads) sm.num[i] = 0;
     pdl_launch_dependents();
     pdl_wait();
 
@@ -2005,7 +2007,7 @@ k_attn_b(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, in
         *reinterpret_cast<unsigned*>(sm.newrow + w * hbytes + c * 4) = word;
     }
     // each q head on its integer grid, split into balanced signed bytes: the
-    // score MMAs' B operand, column 2*limb + head, dims in MMA k order
+    // score MMAs' B operand, column 4*head + limb (limb 3 zero), dims in MMA k order
     if (warp < hq) {
         const float gs = warp_q_grid(sm.q + warp * hd, hd, KVB, sm.qi + warp * hd);
         if (lane == 0) sm.gsc[warp] = gs;
@@ -2019,12 +2021,12 @@ k_attn_b(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, in
         const int l1 = ((v + 128) & 255) - 128;
         const int l2 = (v - l1) >> 8;
         const int k = KVB == 2 ? (i & ~31) + attnb_k_of(i & 31) : i;
-        sm.qb[(0 + hh) * hd + k] = (uint8_t)l0;
-        sm.qb[(2 + hh) * hd + k] = (uint8_t)l1;
-        sm.qb[(4 + hh) * hd + k] = (uint8_t)l2;
+        sm.qb[(4 * hh + 0) * hd + k] = (uint8_t)l0;
+        sm.qb[(4 * hh + 1) * hd + k] = (uint8_t)l1;
+        sm.qb[(4 * hh + 2) * hd + k] = (uint8_t)l2;
     }
     __syncthreads();
-    // B fragments of the q limbs for every k block (column n = lane/4)
+    // B fragments of the q limbs for every k block (column n = lane/4 = 4*head + limb)
     unsigned bq[KS][2];
 #pragma unroll
     for (int ks = 0; ks < KS; ++ks) {
@@ -2032,7 +2034,6 @@ k_attn_b(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, in
         bq[ks][1] = *reinterpret_cast<const unsigned*>(sm.qb + gq * hd + ks * 32 + 16 + 4 * tq);
     }
 
-    const float sq = __fsqrt_rn((float)hd);
     // P.V work of a warp: position block pb (32 of a tile's 128 rows) and half
     // of the V columns; q8 blocks of 16 columns (even and odd MMAs), q16
     // blocks of 8 (high and low byte MMAs)
@@ -2087,38 +2088,73 @@ k_attn_b(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, in
                         mma_i8<true, false>(dlo, al, bq[ks][0], bq[ks][1]);
                     }
                 }
-                // column 2*limb + head: lane tq holds limb tq of heads 0 and 1
-                long long v[4];
+                // column 4*head + limb: lane tq holds (head tq/2, limbs 0 and 1) for
+                // tq even, (head tq/2, limb 2) for tq odd; one shuffle per row
+                // brings limb 2 to the even lane
+                int v[4];
 #pragma unroll
-                for (int j = 0; j < 4; ++j) v[j] = KVB == 1 ? (long long)dhi[j] : (long long)dhi[j] * 256 + dlo[j];
-                long long S[4];
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const long long v1 = __shfl_down_sync(0xffffffffu, v[j], 1);
-                    const long long v2 = __shfl_down_sync(0xffffffffu, v[j], 2);
-                    S[j] = v[j] + v1 * 256 + v2 * 65536;
+                for (int j = 0; j < 4; ++j) v[j] = KVB == 1 ? dhi[j] : dhi[j] * 256 + dlo[j];
+                const int l2a = __shfl_down_sync(0xffffffffu, v[0], 1);
+                const int l2b = __shfl_down_sync(0xffffffffu, v[2], 1);
+                const int hh = tq >> 1;
+                if (!(tq & 1) && hh < hq) {
+                    const float ch = sm.gsc[hh];
+                    const long long Sa = (long long)v[0] + 256LL * v[1] + 65536LL * l2a;
+                    const long long Sb = (long long)v[2] + 256LL * v[3] + 65536LL * l2b;
+                    const int ra = rb + gq, rbb = rb + gq + 8;
+                    if (ra < nt) sm.sc[hh * d.seq + t0 + ra] = __fmul_rn(__ll2float_rn(Sa), ch);
+                    if (rbb < nt) sm.sc[hh * d.seq + t0 + rbb] = __fmul_rn(__ll2float_rn(Sb), ch);
                 }
-                if (tq == 0)
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const int r = rb + gq + 8 * (j >> 1), hh = j & 1;
-                        if (hh < hq && r < nt)
-                            sm.sc[hh * d.seq + t0 + r] = __fdiv_rn(__fmul_rn(__ll2float_rn(S[j]), sm.gsc[hh]), sq);
-                    }
             }
         } else {
             if (u == ntile) {
-                attn_weights(sm.sc, d.seq, len, hq, KVB, sm.redf, sm.redd, sm.den);
-                // limbs of E_t (< 2^kexp + 1): row h*NL + limb, position t at
+                // the weights E_t = rint(exp(s_t - max) * 2^k) of every position,
+                // their exact sum, and their limbs: row h*NL + limb, position t at
                 // column 32*(t/32) + attnb_k_of(t%32)
-                nl = (attn_weight_exp(len, KVB) + 8) / 8;
-                for (int e = threadIdx.x; e < hq * len; e += kThreads) {
-                    const int hh = e / len, t = e % len;
-                    unsigned long long E = (unsigned long long)sm.sc[hh * d.seq + t];
-                    uint8_t* dst = sm.ea + (size_t)(hh * nl) * epitch + (t & ~31) + attnb_k_of(t & 31);
-                    for (int l = 0; l < nl; ++l, E >>= 8) dst[(size_t)l * epitch] = (uint8_t)E;
+                const int kexp = attn_weight_exp(len, KVB);
+                const float wscale = __int_as_float((127 + kexp) << 23);   // 2^k, exact
+                nl = (kexp + 8) / 8;
+                float mx[HQ];
+#pragma unroll
+                for (int hh = 0; hh < HQ; ++hh) mx[hh] = -1e30f;
+                for (int t = threadIdx.x; t < len; t += kThreads)
+#pragma unroll
+                    for (int hh = 0; hh < HQ; ++hh) mx[hh] = fmaxf(mx[hh], sm.sc[hh * d.seq + t]);
+#pragma unroll
+                for (int hh = 0; hh < HQ; ++hh) {
+                    for (int o = 16; o; o >>= 1) mx[hh] = fmaxf(mx[hh], __shfl_xor_sync(0xffffffffu, mx[hh], o));
+                    if (lane == 0) sm.redf[warp * HQ + hh] = mx[hh];
                 }
                 __syncthreads();
+#pragma unroll
+                for (int hh = 0; hh < HQ; ++hh) {
+                    mx[hh] = sm.redf[hh];
+                    for (int w = 1; w < kWarps; ++w) mx[hh] = fmaxf(mx[hh], sm.redf[w * HQ + hh]);
+                }
+                double dn[HQ];
+#pragma unroll
+                for (int hh = 0; hh < HQ; ++hh) dn[hh] = 0.0;
+                for (int t = threadIdx.x; t < len; t += kThreads) {
+                    uint8_t* col = sm.ea + (t & ~31) + attnb_k_of(t & 31);
+#pragma unroll
+                    for (int hh = 0; hh < HQ; ++hh) {
+                        const float e = rintf(__fmul_rn(vexp(__fsub_rn(sm.sc[hh * d.seq + t], mx[hh])), wscale));
+                        dn[hh] = __dadd_rn(dn[hh], (double)e);
+                        unsigned long long E = (unsigned long long)e;
+                        for (int l = 0; l < nl; ++l, E >>= 8) col[(size_t)(hh * nl + l) * epitch] = (uint8_t)E;
+                    }
+                }
+#pragma unroll
+                for (int hh = 0; hh < HQ; ++hh) {
+                    for (int o = 16; o; o >>= 1) dn[hh] = __dadd_rn(dn[hh], __shfl_xor_sync(0xffffffffu, dn[hh], o));
+                    if (lane == 0) sm.redd[warp * HQ + hh] = dn[hh];
+                }
+                __syncthreads();
+                if (threadIdx.x < HQ) {
+                    double tot = 0.0;
+                    for (int w = 0; w < kWarps; ++w) tot = __dadd_rn(tot, sm.redd[w * HQ + threadIdx.x]);
+                    sm.den[threadIdx.x] = tot;
+                }
             }
             // P.V of this V tile
             const int pr = pb * 32;
@@ -2146,31 +2182,34 @@ k_attn_b(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, in
         __syncthreads();
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
-    // add the exact limb products: row m = h*NL + limb, columns as the B operand
+    __syncthreads();   // the ring is free: it takes the partial sums
+    // each warp's exact limb products of its position block: part[pb][m][column]
+    // (int64) for the rows m = h*NL + limb that exist
+    long long* part = reinterpret_cast<long long*>(sm.ring);
+    const int rows = hq * nl;
 #pragma unroll
     for (int i = 0; i < kDBW; ++i) {
         const int db = dh * kDBW + i;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const int m = gq + 8 * (j >> 1), col = 2 * tq + (j & 1);
-            if (m >= hq * nl) continue;
-            const int hh = m / nl, l = m % nl;
+            if (m >= rows) continue;
+            long long* pm = part + ((size_t)pb * rows + m) * hd;
             if (KVB == 1) {
-                atomicAdd(reinterpret_cast<unsigned long long*>(sm.num + hh * hd + db * 16 + 2 * col),
-                          (unsigned long long)((long long)acc[i][0][j] * (1LL << (8 * l))));
-                atomicAdd(reinterpret_cast<unsigned long long*>(sm.num + hh * hd + db * 16 + 2 * col + 1),
-                          (unsigned long long)((long long)acc[i][1][j] * (1LL << (8 * l))));
+                pm[db * 16 + 2 * col] = acc[i][0][j];
+                pm[db * 16 + 2 * col + 1] = acc[i][1][j];
             } else {
-                const long long v = (long long)acc[i][0][j] * 256 + acc[i][1][j];
-                atomicAdd(reinterpret_cast<unsigned long long*>(sm.num + hh * hd + db * 8 + col),
-                          (unsigned long long)(v * (1LL << (8 * l))));
+                pm[db * 8 + col] = (long long)acc[i][0][j] * 256 + acc[i][1][j];
             }
         }
     }
     __syncthreads();
     for (int o = threadIdx.x; o < hq * hd; o += kThreads) {
         const int hh = o / hd, i = o % hd;
-        s.att[(size_t)b * d.dim + (size_t)(g * group + h0 + hh) * hd + i] = att_q16((double)sm.num[o], sm.den[hh], KVB);
+        long long num = 0;
+        for (int q = 0; q < 4; ++q)
+            for (int l = 0; l < nl; ++l) num += part[((size_t)q * rows + hh * nl + l) * hd + i] * (1LL << (8 * l));
+        s.att[(size_t)b * d.dim + (size_t)(g * group + h0 + hh) * hd + i] = att_q16((double)num, sm.den[hh], KVB);
     }
 }
 
