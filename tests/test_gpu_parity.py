@@ -5,6 +5,10 @@ Tolerance (the north star's): max |dlogit| <= 1e-2 with greedy agreement.  The
 canonical arithmetic is shared, so the expected difference is zero; the KV
 bytes are compared bit for bit.
 """
+import os
+import subprocess
+import sys
+
 import numpy as np
 import pytest
 
@@ -89,12 +93,14 @@ def test_matvec_s_matches_oracle(gpu, tiny_paths, key):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("key", ["tiny_q8", "tiny_moe_q4", "tiny_t3"])
-@pytest.mark.parametrize("n", [6, 10, 33, 64])
+@pytest.mark.parametrize("n", [6, 10, 33, 64, 300])
 def test_batched_equals_serial(gpu, tiny_paths, key, n):
     """Several sequences in one pass give each sequence's serial result: 6
     runs the one-sequence kernels four inputs at a time, 10 the many-sequence
     (prep + matmat) kernels, 33 their tensor-core (tcgen05) form for q8, 64
-    also the one-CTA-per-head attention for many sequences."""
+    also the one-CTA-per-head attention for many sequences, 300 more
+    16-sequence units than SMs (tensor-core ranges run in several rounds
+    under the balanced split)."""
     cfg = synth.TINY_CONFIGS[key]
     model = vc4b200.Model(gpu, tiny_paths[key])
     prompts = [synth.prompt_tokens(cfg, i)[:10] for i in range(n)]
@@ -108,6 +114,21 @@ def test_batched_equals_serial(gpu, tiny_paths, key, n):
         for pos in range(10):
             lg = ss.step(prompts[i][pos], pos)
             assert np.array_equal(lg, logs_b[pos][i]), "sequence %d position %d" % (i, pos)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("split", ["aligned", "balanced"])
+def test_tensor_core_splits(split):
+    """Both work splits of the tensor-core matmats give the serial results:
+    groups of sequences inside a tile, one CTA each, and equal ranges of
+    16-sequence units per SM run in rounds.  A process fixes its split once
+    (VC4_TC_SPLIT), so the batched tests run again in a child process."""
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, VC4_TC_SPLIT=split)
+    r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-x", "-m", "gpu", "-p", "no:cacheprovider",
+                        os.path.abspath(__file__) + "::test_batched_equals_serial", "-k", "tiny_q8 or tiny_t3"],
+                       env=env, cwd=root, capture_output=True, text=True, timeout=1200)
+    assert r.returncode == 0, (r.stdout[-4000:], r.stderr[-2000:])
 
 
 @pytest.mark.gpu

@@ -61,7 +61,7 @@ __device__ int route_block(const int16_t* xn, const DMat& R, int D, int experts,
         for (int c = threadIdx.x; c < D; c += kThreads) acc += (long long)R.w16[(size_t)e * D + c] * xscale(xn[c], k, sk);
         acc = block_sum_i64(acc, r);
         const int v = mv_epi(acc, R.rscale[e]);
-        const float g = __fmul_rn(__fmul_rn((float)v, 1.0f / 256.0f), ldexpf(1.0f, -k));
+        const float g = __fmul_rn(__fmul_rn((float)v, 1.0f / 256.0f), pow2f(-k));
         if (e == 0 || g > bestv) { best = e; bestv = g; }
     }
     return best;
@@ -254,10 +254,10 @@ __global__ void __launch_bounds__(kThreads) k_mm(MatSet M, State s, Batch bt, Di
                 if (OP == kOpQkv) {
                     if (live)
                         s.qkv[(size_t)b * (d.dim + 2 * d.kv_dim) + row] =
-                            __fmul_rn(__fmul_rn((float)v, 1.0f / 256.0f), ldexpf(1.0f, -k));
+                            __fmul_rn(__fmul_rn((float)v, 1.0f / 256.0f), pow2f(-k));
                 } else if (OP == kOpWo) {
                     if (live) {
-                        const float wo = __fmul_rn(__fmul_rn((float)v, 1.0f / 256.0f), ldexpf(1.0f, -k));
+                        const float wo = __fmul_rn(__fmul_rn((float)v, 1.0f / 256.0f), pow2f(-k));
                         const float xr = __fmul_rn((float)__ldcg(s.x + (size_t)b * d.dim + row), 1.0f / 256.0f);
                         s.x1[(size_t)b * d.dim + row] = (int16_t)q16h(__fadd_rn(xr, wo));
                     }
@@ -441,19 +441,20 @@ __global__ void __launch_bounds__(kThreads) k_mmdown(MatSet M2, State s, Batch b
 // through `empty` (tcgen05.commit), so copies and MMAs overlap and K has no
 // shared-memory limit.
 //  - A (weights): the matrix's row-major int8 copy (q8 levels, or t3's
-//    -1/0/+1, so S is the plain integer dot); one box is 128 rows x 128
-//    bytes.  Rows past the matrix and K past its end read as zero
-//    (out-of-bounds fill).
-//  - B (inputs): the sequences' staged records, n rows of rec_bytes; one box
-//    is N rows x 128 bytes of the lo or hi plane.  x' = lo + 256*hi with lo
+//    -1/0/+1, so S is the plain integer dot); a stage holds 128 rows x 128
+//    bytes, copied as two boxes of 64 rows.  Rows past the matrix and K past
+//    its end read as zero (out-of-bounds fill).
+//  - B (inputs): the sequences' staged records, n rows of rec_bytes; a stage
+//    holds N rows x 128 bytes of the lo and of the hi plane, each copied as
+//    two boxes of N/2 rows.  x' = lo + 256*hi with lo
 //    unsigned and hi signed, so every K step is two MMAs (s8 x u8 into one
 //    accumulator, s8 x s8 into another) and S = D_lo + 256*D_hi is the exact
 //    integer dot (|D| < 2^31 for every shape here).
 // Measured on B200: one thread's TMA copies complete one after another (about
 // 0.2 us for a box with 16-byte rows, 0.55 us for a 16 KB box of 128-byte
 // rows), while copies issued by different warps proceed side by side.  So
-// every box is 128 bytes wide and three producer threads on three SM
-// sub-partitions take the stages in turn.
+// every box is 128 bytes wide and each box of a stage has an issuing thread
+// of its own (lane 0 of one warp each, up to 12).
 // tcgen05.ld brings row r of the accumulators to lane r%32 of the warps of
 // quarter r/32; sixteen warps share the epilogues (those of the CUDA-core
 // kernels, so the results are theirs bit for bit), which are instruction-bound:
@@ -461,10 +462,19 @@ __global__ void __launch_bounds__(kThreads) k_mmdown(MatSet M2, State s, Batch b
 // ---------------------------------------------------------------------------
 
 constexpr int kOpDown = 4;
-constexpr int kTcThreads = 512;          // warps 0-3 copy and issue; all 16 run the epilogue
+// Epilogue variants for measurement builds (-D): the ffn matmats' piece width,
+// and the double-precision rounding path instead of the integer form.
+#ifndef VC4_TMM_PW_FFN
+#define VC4_TMM_PW_FFN 8
+#endif
+#ifndef VC4_TMM_DBL
+#define VC4_TMM_DBL 1
+#endif
+constexpr int kTcPwFfn = VC4_TMM_PW_FFN;
+constexpr bool kTcDoubleEpi = VC4_TMM_DBL != 0;
+constexpr int kTcThreads = 512;          // lane 0 of warp 1 issues the MMAs, of others the copies; all 16 run the epilogue
 constexpr int kTcKs = 8;                  // 16-byte K chunks per ring stage: one 128-byte swizzle row
 constexpr int kTcMaxStages = 8;
-constexpr int kTcProducers = 3;           // threads issuing the stages' copies
 constexpr size_t kTcTileA = 128 * 128;    // bytes of one stage of a 128-row weight tile
 
 // K-major operand in the 128-byte swizzle layout that a SWIZZLE_128B TMA box
@@ -502,6 +512,25 @@ __device__ __forceinline__ void tmem_ld16(uint32_t addr, uint32_t (&v)[16]) {
                    "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
                  : "r"(addr));
 }
+__device__ __forceinline__ void tmem_ld8(uint32_t addr, uint32_t (&v)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void tmem_ld4(uint32_t addr, uint32_t (&v)[4]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]) : "r"(addr));
+}
+__device__ __forceinline__ void tmem_ld2(uint32_t addr, uint32_t (&v)[2]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0,%1}, [%2];" : "=r"(v[0]), "=r"(v[1]) : "r"(addr));
+}
+template <int W>
+__device__ __forceinline__ void tmem_ld(uint32_t addr, uint32_t (&v)[W]) {
+    if constexpr (W == 16) tmem_ld16(addr, v);
+    else if constexpr (W == 8) tmem_ld8(addr, v);
+    else if constexpr (W == 4) tmem_ld4(addr, v);
+    else tmem_ld2(addr, v);
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 // Adds `bytes` to the transaction count of the barrier's current phase
 // without arriving (the copies of a stage issued before its arrival).
@@ -528,10 +557,11 @@ struct TcArgs {
     int nin;             // distinct B inputs: 2 when the passes read different record bytes
     int rec_bytes;       // bytes per sequence record (State::xrec or State::hrec)
     int from_hrec;       // the records are w2 inputs (State::hrec)
-    int group;           // N: sequences per CTA (multiple of 16, at most 256)
+    int tiles;           // 128-row tiles of the matrix
+    int groups;          // > 0: aligned split, CTA c = group c % groups of tile c / groups; 0: balanced ranges
+    int group;           // N: sequences per round (multiple of 16, at most 256)
     int tmem_cols;       // power of two >= 2 * npass * group
-    int stages;          // ring depth, a multiple of producers
-    int producers;       // threads issuing copies; slot k is always refilled by producer k % producers
+    int stages;          // ring depth (at least 2)
     int kc;              // 16-byte K chunks of the longer pass (even)
     int t3;              // ternary weights: the gate also adds the hidden totals the CUDA-core w2 uses
     int hs;
@@ -543,33 +573,76 @@ __host__ __device__ inline int tc_kchunks(const DMat& W) { return (x_stride(W) /
 __host__ __device__ inline size_t tc_stage_bytes(const TcArgs& a) {
     return (size_t)a.npass * kTcTileA + (size_t)a.nin * 2 * a.group * 128;
 }
-// ring (1024-byte aligned) | full[stages] | empty[stages] | done | TMEM address |
-// failure flag | the group's input exponents
+// ring (1024-byte aligned) | full[stages] | empty[stages] | done | tfree |
+// TMEM address (16 bytes) | two rounds' input exponents
 __host__ __device__ inline size_t tc_smem(const TcArgs& a) {
-    return 1024 + (size_t)a.stages * tc_stage_bytes(a) + 8 * (2 * (size_t)a.stages + 1) + 16 + 4 * (size_t)a.group;
+    return 1024 + (size_t)a.stages * tc_stage_bytes(a) + 8 * (2 * (size_t)a.stages + 2) + 16 + 8 * (size_t)a.group;
 }
 
+// The work split.  The (tile, unit of 16 sequences) pairs, tile-major, are
+// either cut into gridDim.x equal ranges (balanced) or grouped N/16 units at
+// a time inside each tile (aligned, one CTA per group); a CTA takes its range
+// in rounds, each inside one tile and at most N sequences.
+struct TcRound {
+    int tile, g0, gn;
+};
+__device__ __forceinline__ bool tc_round_at(int r, int u_begin, int u_end, int upt, int umax, int n, TcRound& o) {
+    int u = u_begin;
+    for (int i = 0;; ++i) {
+        if (u >= u_end) return false;
+        const int tile = u / upt, ut = u - tile * upt;
+        const int nu = min(min(u_end - u, upt - ut), umax);
+        if (i == r) {
+            o.tile = tile;
+            o.g0 = 16 * ut;
+            o.gn = min(16 * nu, n - 16 * ut);
+            return true;
+        }
+        u += nu;
+    }
+}
+__device__ __forceinline__ void mbar_arrive(unsigned long long* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+// Single-matrix matmats (qkv, wo, logits) keep to 64 registers so that two
+// CTAs share an SM: one's epilogue then overlaps the other's copies and MMAs.
 template <int OP>
-__global__ void __launch_bounds__(kTcThreads) k_tmm(const __grid_constant__ TcMaps maps, TcArgs a, State s, Batch bt,
-                                                    Dims d, int layer, Finalize fz) {
-    const int tile = blockIdx.x, N = a.group, S = a.stages, P = a.producers;
-    const int n = bt.n, g0 = (int)blockIdx.z * N, gn = min(N, n - g0);
+__global__ void __launch_bounds__(kTcThreads, OP == kOpGate || OP == kOpDown ? 1 : 2) k_tmm(const __grid_constant__ TcMaps maps, TcArgs a, State s, Batch bt,
+                                                       Dims d, int layer, Finalize fz) {
+    const int N = a.group, S = a.stages;
+    const int n = bt.n, upt = (n + 15) / 16, umax = N / 16;
+    const long long U = (long long)a.tiles * upt;
+    int u_begin, u_end;
+    if (a.groups) {   // aligned: CTA c is group c % groups of tile c / groups
+        const int tile = (int)blockIdx.x / a.groups, grp = (int)blockIdx.x % a.groups;
+        u_begin = tile * upt + grp * umax;
+        u_end = min(u_begin + umax, (tile + 1) * upt);
+    } else {          // balanced: equal ranges of the tile-major units
+        u_begin = (int)(U * blockIdx.x / gridDim.x);
+        u_end = (int)(U * (blockIdx.x + 1) / gridDim.x);
+    }
     if (!smem_ok(tc_smem(a), s.err)) return;
-    if (P < 1 || P > kTcProducers || S % P) {   // see the producers below
+    if (S < 2 || N % 16 || N < 16 || 2 * a.npass + 4 * a.nin > kTcThreads / 32 - 1) {   // see the issuers below
         if (threadIdx.x == 0) atomicExch(s.err, kErrRingShape);
         return;
     }
+    int R = 0;
+    for (TcRound t; tc_round_at(R, u_begin, u_end, upt, umax, n, t);) ++R;
     char* base = SmemLayout::base();
     char* ring = base + ((1024u - (smem_addr(base) & 1023u)) & 1023u);
     const size_t sb = tc_stage_bytes(a);
     unsigned long long* full = reinterpret_cast<unsigned long long*>(ring + (size_t)S * sb);
     unsigned long long* empty = full + S;
     unsigned long long* done = empty + S;
-    uint32_t* tslot = reinterpret_cast<uint32_t*>(done + 1);
-    int* fail = reinterpret_cast<int*>(tslot + 1);
-    int* kexp = fail + 1;
+    unsigned long long* tfree = done + 1;
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(tfree + 1);
+    int* kexp2 = reinterpret_cast<int*>(tslot + 4);        // [2][N]: the rounds' input exponents
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int npass = a.npass, nin = a.nin, kc = a.kc, nst = (kc + kTcKs - 1) / kTcKs;
+    // qkv, wo and logits read one matrix: a constant, so the second
+    // accumulator's code and registers compile away
+    constexpr bool kOne = OP == kOpQkv || OP == kOpWo || OP == kOpLogits;
+    const int npass = kOne ? 1 : a.npass, nin = kOne ? 1 : a.nin, kc = a.kc, nst = (kc + kTcKs - 1) / kTcKs;
     const int kcp[2] = {tc_kchunks(a.p[0].W), tc_kchunks(a.p[npass > 1 ? 1 : 0].W)};
     const size_t boff = (size_t)npass * kTcTileA;          // B planes inside a stage
     const unsigned bplane = (unsigned)N * 128u;            // bytes of one plane of one stage
@@ -580,7 +653,7 @@ __global__ void __launch_bounds__(kTcThreads) k_tmm(const __grid_constant__ TcMa
                 mbar_init(&empty[i], 1);
             }
             mbar_init(done, 1);
-            *fail = 0;
+            mbar_init(tfree, kTcThreads / 32);
             mbar_fence_init();
         }
         __syncwarp();
@@ -596,8 +669,9 @@ __global__ void __launch_bounds__(kTcThreads) k_tmm(const __grid_constant__ TcMa
     const uint32_t tmem = *tslot;
     pdl_launch_dependents();
 
-    // stage i covers K chunks 8i .. 8i+7 (128 bytes of every row): one box per
-    // pass of the weights, one per plane and input of the records
+    // Global stage gi = r * nst + i covers K chunks 8i .. 8i+7 (128 bytes of
+    // every row) of round r: one box per pass of the weights, one per plane
+    // and input of the records.
     auto a_live = [&](int i, int p) { return i * kTcKs < kcp[p]; };
     auto b_live = [&](int i, int in) { return i * kTcKs < (nin > 1 ? kcp[in] : kc); };
     auto a_bytes = [&](int i) {
@@ -610,213 +684,339 @@ __global__ void __launch_bounds__(kTcThreads) k_tmm(const __grid_constant__ TcMa
         for (int in = 0; in < nin; ++in) b += b_live(i, in) ? 2u * bplane : 0u;
         return b;
     };
-    auto issue_a = [&](int i) {
-        char* st = ring + (size_t)(i % S) * sb;
-        for (int p = 0; p < npass; ++p)
-            if (a_live(i, p)) tma_load_2d(st + (size_t)p * kTcTileA, &maps.a[p], i * 128, tile * 128, &full[i % S]);
+    // Box j of every stage has its own issuing thread (one thread's bulk
+    // copies complete one after another, copies from different threads side
+    // by side).  Each box is half of a tile: 64 weight rows, or N/2 records,
+    // both whole 1024-byte swizzle atoms, so the halves land exactly where one
+    // box of the whole tile would.  Boxes 0 .. 2*npass-1 are the weights
+    // (pass j/2), then four per record input (plane, half).
+    const int nbA = 2 * npass, nb = nbA + 4 * nin;
+    const int my_box = warp == 0 ? 0 : warp - 1;        // warp 1 issues the MMAs
+    const bool issuer = warp != 1 && lane == 0 && my_box < nb;
+    auto box_live = [&](int i, int j) {
+        return j < nbA ? a_live(i, j >> 1) : b_live(i, (j - nbA) >> 2);
     };
-    auto issue_b = [&](int i) {
-        char* st = ring + (size_t)(i % S) * sb + boff;
-        for (int in = 0; in < nin; ++in) {
-            if (!b_live(i, in)) continue;
+    auto issue_box = [&](int gi, int j, const TcRound& rd) {
+        const int i = gi % nst;
+        char* st = ring + (size_t)(gi % S) * sb;
+        unsigned long long* bar = &full[gi % S];
+        if (j < nbA) {
+            const int p = j >> 1, h = j & 1;
+            tma_load_2d(st + (size_t)p * kTcTileA + (size_t)h * (kTcTileA / 2), &maps.a[p], i * 128,
+                        rd.tile * 128 + 64 * h, bar);
+        } else {
+            const int jb = j - nbA, in = jb >> 2, plane = (jb >> 1) & 1, h = jb & 1;
             const TcPass& Pi = a.p[in];
-            tma_load_2d(st + (size_t)(in * 2 + 0) * bplane, &maps.b, Pi.lo_off + i * 128, g0, &full[i % S]);
-            tma_load_2d(st + (size_t)(in * 2 + 1) * bplane, &maps.b, Pi.hi_off + i * 128, g0, &full[i % S]);
+            tma_load_2d(st + boff + (size_t)(in * 2 + plane) * bplane + (size_t)h * (bplane / 2), &maps.b,
+                        (plane ? Pi.hi_off : Pi.lo_off) + i * 128, rd.g0 + h * (N / 2), bar);
         }
     };
 
-    // producers: lane 0 of warps 0, 2 and 3 take the stages in turn.  The ring
-    // depth is a multiple of the producer count and the count is at most the
-    // depth, so a slot is always refilled by the same producer and every wait
-    // on its `empty` barrier is for the phase right after the one that
-    // producer saw last (a parity wait cannot tell phases two apart).
-    if (warp != 1) {
-        const int pid = warp == 0 ? 0 : warp - 1;
-        if (lane == 0 && pid < P) {
-            if (pid == 0) {
-                asm volatile("prefetch.tensormap [%0];" ::"l"(&maps.a[0]) : "memory");
-                if (npass > 1) asm volatile("prefetch.tensormap [%0];" ::"l"(&maps.a[1]) : "memory");
-                asm volatile("prefetch.tensormap [%0];" ::"l"(&maps.b) : "memory");
-            }
-            // the first stages' weights before the grid-dependency wait
-            const int pre = min(S, nst);
-            for (int i = pid; i < pre; i += P) {
-                mbar_add_tx(&full[i], a_bytes(i));
-                issue_a(i);
-            }
-            pdl_wait();
-            for (int i = pid; i < nst; i += P) {
-                if (i >= S) {
-                    if (!mbar_wait(&empty[i % S], (unsigned)(i / S - 1) & 1u)) { atomicExch(fail, 1); break; }
-                    mbar_expect_tx(&full[i % S], a_bytes(i) + b_bytes(i));
-                    issue_a(i);
-                } else {
-                    mbar_expect_tx(&full[i % S], b_bytes(i));
-                }
-                issue_b(i);
-            }
+    // Every issuer takes every stage in order, so it refills a slot only after
+    // the MMAs read the slot's previous contents, and the slot cannot be
+    // consumed again before this issuer's own box of the next contents lands:
+    // each wait on an `empty` barrier is for the phase right after the one the
+    // issuer saw last (a parity wait cannot tell phases two apart).  Issuer 0
+    // also arrives on the stage's `full` barrier with the stage's bytes.
+    bool bad = false;        // one of this thread's bounded waits gave up
+    int next = 0;            // the issuer's next global stage
+    TcRound r0{0, 0, 0};
+    if (R > 0) tc_round_at(0, u_begin, u_end, upt, umax, n, r0);
+    const int pre = min(S, nst);
+    if (issuer && R > 0) {
+        if (my_box == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&maps.a[0]) : "memory");
+            if (npass > 1) asm volatile("prefetch.tensormap [%0];" ::"l"(&maps.a[1]) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&maps.b) : "memory");
+            for (int gi = 0; gi < pre; ++gi) mbar_expect_tx(&full[gi], a_bytes(gi) + b_bytes(gi));
         }
+        // the first stages' weights before the grid-dependency wait
+        if (my_box < nbA)
+            for (int gi = 0; gi < pre; ++gi)
+                if (box_live(gi, my_box)) issue_box(gi, my_box, r0);
+    }
+    pdl_wait();
+    if (issuer && R > 0) {
+        if (my_box >= nbA)
+            for (int gi = 0; gi < pre; ++gi)
+                if (box_live(gi, my_box)) issue_box(gi, my_box, r0);
+        next = pre;
+    }
+    // Issues this thread's box of the stages below `limit`; a stage waits only
+    // for the MMAs that read its slot before.
+    auto produce_until = [&](int limit) {
+        while (!bad && next < limit) {
+            const int gi = next, i = gi % nst;
+            TcRound rd;
+            tc_round_at(gi / nst, u_begin, u_end, upt, umax, n, rd);
+            if (gi >= S && !mbar_wait(&empty[gi % S], (unsigned)(gi / S - 1) & 1u)) {
+                bad = true;
+                break;
+            }
+            if (my_box == 0) mbar_expect_tx(&full[gi % S], a_bytes(i) + b_bytes(i));
+            if (box_live(i, my_box)) issue_box(gi, my_box, rd);
+            ++next;
+        }
+    };
+
+    const TcPass P0 = a.p[0], P1 = a.p[npass > 1 ? 1 : 0];
+    const int quarter = warp & 3, slice = warp >> 2, nslice = kTcThreads / 128;
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * quarter) << 16);
+    bool failed = false;
+    for (int r = 0; r < R; ++r) {
+        TcRound rd;
+        tc_round_at(r, u_begin, u_end, upt, umax, n, rd);
+        const int g0 = rd.g0, gn = rd.gn, Nr = (gn + 15) & ~15;
+        int* kexp = kexp2 + (r & 1) * N;
+        // this round's remaining stages and the next round's first ones (their
+        // slots are freed by this round's MMAs, never by its epilogue)
+        if (issuer) produce_until(min(R * nst, (r + 1) * nst + (r + 1 < R ? pre : 0)));
         __syncwarp();
-    } else {
-        if (lane == 0) {
-            // MMA issuer: four K steps of 32 bytes per stage, inside the 128-byte
-            // swizzle row by advancing the descriptors' start address
-            const uint32_t il = umma_idesc_i8(false, 128, N), ih = umma_idesc_i8(true, 128, N);
-            for (int i = 0; i < nst; ++i) {
-                if (!mbar_wait(&full[i % S], (unsigned)(i / S) & 1u)) { atomicExch(fail, 1); break; }
+        if (warp == 1) {
+            if (lane == 0) {
+                // MMA issuer: four K steps of 32 bytes per stage, inside the
+                // 128-byte swizzle row by advancing the descriptors' start
+                // address; the accumulators are free once every warp has read
+                // the previous round's
+                if (r > 0 && !mbar_wait(tfree, (unsigned)(r - 1) & 1u)) bad = true;
                 tc_fence_after();
-                const char* st = ring + (size_t)(i % S) * sb;
-                for (int kk = 0; kk < kTcKs / 2; ++kk) {
-                    const int j = i * kTcKs + 2 * kk;
-                    for (int p = 0; p < npass; ++p) {
-                        if (j >= kcp[p]) continue;
-                        const int in = nin > 1 ? p : 0;
-                        const uint64_t da = umma_sdesc_sw128(smem_addr(st + (size_t)p * kTcTileA) + 32u * kk);
-                        const uint64_t dbl =
-                            umma_sdesc_sw128(smem_addr(st + boff + (size_t)(in * 2 + 0) * bplane) + 32u * kk);
-                        const uint64_t dbh =
-                            umma_sdesc_sw128(smem_addr(st + boff + (size_t)(in * 2 + 1) * bplane) + 32u * kk);
-                        const uint32_t dlo = tmem + (uint32_t)(p * 2 * N);
-                        umma_i8(dlo, da, dbl, il, j > 0);
-                        umma_i8(dlo + (uint32_t)N, da, dbh, ih, j > 0);
+                const uint32_t il = umma_idesc_i8(false, 128, Nr), ih = umma_idesc_i8(true, 128, Nr);
+                for (int i = 0; i < nst && !bad; ++i) {
+                    const int gi = r * nst + i;
+                    if (!mbar_wait(&full[gi % S], (unsigned)(gi / S) & 1u)) {
+                        bad = true;
+                        break;
+                    }
+                    tc_fence_after();
+                    const char* st = ring + (size_t)(gi % S) * sb;
+                    for (int kk = 0; kk < kTcKs / 2; ++kk) {
+                        const int j = i * kTcKs + 2 * kk;
+                        for (int p = 0; p < npass; ++p) {
+                            if (j >= kcp[p]) continue;
+                            const int in = nin > 1 ? p : 0;
+                            const uint64_t da = umma_sdesc_sw128(smem_addr(st + (size_t)p * kTcTileA) + 32u * kk);
+                            const uint64_t dbl =
+                                umma_sdesc_sw128(smem_addr(st + boff + (size_t)(in * 2 + 0) * bplane) + 32u * kk);
+                            const uint64_t dbh =
+                                umma_sdesc_sw128(smem_addr(st + boff + (size_t)(in * 2 + 1) * bplane) + 32u * kk);
+                            const uint32_t dlo = tmem + (uint32_t)(p * 2 * N);
+                            umma_i8(dlo, da, dbl, il, j > 0);
+                            umma_i8(dlo + (uint32_t)N, da, dbh, ih, j > 0);
+                        }
+                    }
+                    umma_commit(&empty[gi % S]);
+                }
+                umma_commit(done);   // every MMA issued above, also after a failure
+            } else {
+                // the other lanes fetch the round's input exponents for the epilogue
+                if (OP == kOpQkv || OP == kOpWo || (OP == kOpGate && d.hostffn)) {
+                    const char* recs = a.from_hrec ? s.hrec : s.xrec;
+                    for (int q = lane - 1; q < gn; q += 31)
+                        kexp[q] = reinterpret_cast<const int*>(recs + (size_t)(g0 + q) * a.rec_bytes +
+                                                               2 * (size_t)x_stride(P0.W))[g_stride(P0.W)];
+                }
+                if (OP == kOpDown && d.hostffn)   // the w2 input exponents of both hidden halves
+                    for (int q = lane - 1; q < gn; q += 31) {
+                        const int ka = hidden_exp(s, layer, g0 + q, 0), kb = hidden_exp(s, layer, g0 + q, 1);
+                        // a negative exponent (hidden value >= 64) is refused here, once per sequence
+                        if (ka < 0 || kb < 0) atomicExch(s.err, kErrHiddenRange);
+                        kexp[q] = (max(ka, 0) & 0xFFFF) | (max(kb, 0) << 16);
+                    }
+            }
+            __syncwarp();
+        }
+        // epilogue of the round, by all sixteen warps once its accumulators are
+        // complete: warp w reads TMEM lanes 32*(w%4) .. +31 (its rows) and
+        // every fourth piece of sequences starting at piece w/4.  The
+        // residuals it reads come from the previous grids.
+        if (!mbar_wait(done, (unsigned)r & 1u)) bad = true;
+        tc_fence_after();
+        if (__syncthreads_or(bad)) {
+            failed = true;
+            break;
+        }
+        __syncwarp();   // tcgen05.ld below is warp-aligned
+        // pieces of PW sequences: independent chains per warp, within the
+        // registers of two CTAs per SM (single-matrix ops, 8) or of the two
+        // accumulator pairs (ffn, VC4_TMM_PW_FFN: 8 or 16)
+        constexpr int PW = kOne ? 8 : kTcPwFfn;
+        const int row = rd.tile * 128 + 32 * quarter + lane;
+        const bool live = row < P0.W.rows;
+        const float rs0 = live ? __ldg(P0.W.rscale + row) : 0.0f;
+        const float rs1 = live && npass > 1 ? __ldg(P1.W.rscale + row) : 0.0f;
+        const RowScale q0 = row_scale(rs0), q1 = row_scale(rs1);
+        for (int c = PW * slice; c < gn; c += PW * nslice) {
+            uint32_t lo0[PW], hi0[PW], lo1[PW], hi1[PW];
+            tmem_ld<PW>(lane_base + c, lo0);
+            tmem_ld<PW>(lane_base + N + c, hi0);
+            if (npass > 1) {
+                tmem_ld<PW>(lane_base + 2 * N + c, lo1);
+                tmem_ld<PW>(lane_base + 3 * N + c, hi1);
+            }
+            int16_t res[PW];
+            if (OP == kOpWo || OP == kOpDown) {
+                const int16_t* src = OP == kOpWo ? s.x : s.x1;
+#pragma unroll
+                for (int i = 0; i < PW; ++i)
+                    res[i] = live && c + i < gn ? __ldcg(src + (size_t)(g0 + c + i) * d.dim + row) : (int16_t)0;
+            }
+            tmem_wait_ld();
+            // Every output of the piece is computed without branches (sequences
+            // past the group's end compute on whatever their columns hold and are
+            // not stored), so the piece's sequences' chains interleave; the stores
+            // and the warp reductions follow in a loop of their own.  c and gn are
+            // warp-uniform.
+            auto S0 = [&](int i) { return (long long)(int)lo0[i] + 256LL * (long long)(int)hi0[i]; };
+            auto S1 = [&](int i) { return npass > 1 ? (long long)(int)lo1[i] + 256LL * (long long)(int)hi1[i] : 0LL; };
+            // w2 of the host FFN: each half's dot times its input scale 2^k
+            auto sh0 = [&](int i) { return OP == kOpDown && d.hostffn ? (kexp[c + i] & 0xFFFF) : 0; };
+            auto sh1 = [&](int i) { return OP == kOpDown && d.hostffn ? (kexp[c + i] >> 16) : 0; };
+            // the exact rounding of every dot in the integer form, then (rarely,
+            // |S| >= 2^28) the double path for the ones it cannot take
+            int v0[PW], v1[PW];
+            bool slow = false;
+#pragma unroll
+            for (int i = 0; i < PW; ++i) {
+                if (kTcDoubleEpi) {
+                    v0[i] = mv_epi(S0(i) * (1LL << sh0(i)), q0.sc);
+                    v1[i] = npass > 1 ? mv_epi(S1(i) * (1LL << sh1(i)), q1.sc) : 0;
+                    continue;
+                }
+                bool ok0, ok1 = true;
+                v0[i] = mv_epi_int(S0(i) * (1LL << sh0(i)), q0, ok0);
+                v1[i] = npass > 1 ? mv_epi_int(S1(i) * (1LL << sh1(i)), q1, ok1) : 0;
+                slow |= !(ok0 && ok1);
+            }
+            if (__any_sync(0xffffffffu, slow)) {
+                // the accumulators are read again (TMEM still holds them), so the
+                // common path need not keep them live
+                uint32_t l0[PW], h0[PW], l1[PW], h1[PW];
+                tmem_ld<PW>(lane_base + c, l0);
+                tmem_ld<PW>(lane_base + N + c, h0);
+                if (npass > 1) {
+                    tmem_ld<PW>(lane_base + 2 * N + c, l1);
+                    tmem_ld<PW>(lane_base + 3 * N + c, h1);
+                }
+                tmem_wait_ld();
+                for (int i = 0; i < PW; ++i) {
+                    v0[i] = mv_epi(((long long)(int)l0[i] + 256LL * (long long)(int)h0[i]) * (1LL << sh0(i)), q0);
+                    if (npass > 1)
+                        v1[i] = mv_epi(((long long)(int)l1[i] + 256LL * (long long)(int)h1[i]) * (1LL << sh1(i)), q1);
+                }
+            }
+            if (OP == kOpQkv || OP == kOpWo) {
+                float o[PW];
+#pragma unroll
+                for (int i = 0; i < PW; ++i)
+                    o[i] = __fmul_rn(__fmul_rn(i2f_small(v0[i]), 1.0f / 256.0f), pow2f(-kexp[c + i]));
+                if (live) {
+#pragma unroll
+                    for (int i = 0; i < PW; ++i) {
+                        if (c + i >= gn) continue;
+                        const int b = g0 + c + i;
+                        if (OP == kOpQkv) {
+                            s.qkv[(size_t)b * (d.dim + 2 * d.kv_dim) + row] = o[i];
+                        } else {
+                            const float xr = __fmul_rn(i2f_small(res[i]), 1.0f / 256.0f);
+                            s.x1[(size_t)b * d.dim + row] = (int16_t)q16h(__fadd_rn(xr, o[i]));
+                        }
                     }
                 }
-                umma_commit(&empty[i % S]);
-            }
-            umma_commit(done);   // every MMA issued above, also after a failure
-        } else {
-            // the other lanes fetch the group's input exponents for the epilogue
-            pdl_wait();
-            if (OP == kOpQkv || OP == kOpWo || (OP == kOpGate && d.hostffn)) {
-                const char* recs = a.from_hrec ? s.hrec : s.xrec;
-                for (int q = lane - 1; q < gn; q += 31)
-                    kexp[q] = reinterpret_cast<const int*>(recs + (size_t)(g0 + q) * a.rec_bytes +
-                                                           2 * (size_t)x_stride(a.p[0].W))[g_stride(a.p[0].W)];
-            }
-            if (OP == kOpDown && d.hostffn)   // the w2 input exponents of both hidden halves
-                for (int q = lane - 1; q < gn; q += 31)
-                    kexp[q] = (hidden_exp(s, layer, g0 + q, 0) & 0xFFFF) | (hidden_exp(s, layer, g0 + q, 1) << 16);
-        }
-        __syncwarp();
-    }
-    // epilogue: all four warps once the accumulators are complete (the
-    // residuals it reads come from the previous grids).  The row scales sit in
-    // registers and each piece of 16 sequences loads its residuals before it
-    // stores anything, so no global load waits on another.
-    pdl_wait();
-    const TcPass P0 = a.p[0], P1 = a.p[npass > 1 ? 1 : 0];
-    if (!mbar_wait(done, 0u)) atomicExch(fail, 1);
-    tc_fence_after();
-    __syncthreads();
-    const bool ok = *fail == 0;
-    // warp w reads TMEM lanes 32*(w%4) .. +31 (its rows) and every fourth
-    // piece of 16 sequences starting at piece w/4
-    const int quarter = warp & 3, slice = warp >> 2, nslice = kTcThreads / 128;
-    const int row = tile * 128 + 32 * quarter + lane;
-    const bool live = row < P0.W.rows;
-    const float rs0 = live ? __ldg(P0.W.rscale + row) : 0.0f;
-    const float rs1 = live && npass > 1 ? __ldg(P1.W.rscale + row) : 0.0f;
-    const uint32_t lane_base = tmem + ((uint32_t)(32 * quarter) << 16);
-    for (int c = 16 * slice; ok && c < gn; c += 16 * nslice) {
-        uint32_t lo0[16], hi0[16], lo1[16], hi1[16];
-        tmem_ld16(lane_base + c, lo0);
-        tmem_ld16(lane_base + N + c, hi0);
-        if (npass > 1) {
-            tmem_ld16(lane_base + 2 * N + c, lo1);
-            tmem_ld16(lane_base + 3 * N + c, hi1);
-        }
-        int16_t res[16];
-        if (OP == kOpWo || OP == kOpDown) {
-            const int16_t* src = OP == kOpWo ? s.x : s.x1;
-#pragma unroll
-            for (int i = 0; i < 16; ++i)
-                res[i] = live && c + i < gn ? __ldcg(src + (size_t)(g0 + c + i) * d.dim + row) : (int16_t)0;
-        }
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            const int q = c + i;
-            if (q >= gn) break;
-            const int b = g0 + q;
-            const long long S0 = (long long)(int)lo0[i] + 256LL * (long long)(int)hi0[i];
-            const long long S1 = npass > 1 ? (long long)(int)lo1[i] + 256LL * (long long)(int)hi1[i] : 0;
-            if (OP == kOpQkv || OP == kOpWo) {
-                if (!live) continue;
-                const float o = __fmul_rn(__fmul_rn((float)mv_epi(S0, rs0), 1.0f / 256.0f), ldexpf(1.0f, -kexp[q]));
-                if (OP == kOpQkv) {
-                    s.qkv[(size_t)b * (d.dim + 2 * d.kv_dim) + row] = o;
-                } else {
-                    const float xr = __fmul_rn((float)res[i], 1.0f / 256.0f);
-                    s.x1[(size_t)b * d.dim + row] = (int16_t)q16h(__fadd_rn(xr, o));
-                }
             } else if (OP == kOpGate) {
-                int qv = 0;
-                if (live) {
-                    const int g = mv_epi(S0, rs0);
-                    const int u = mv_epi(S1, rs1);
-                    if (d.hostffn) {
-                        qv = host_hidden(g, u, kexp[q]);
-                    } else {
-                        float y = swiglu1(__fmul_rn((float)g, 1.0f / 256.0f), __fmul_rn((float)u, 1.0f / 256.0f));
-                        if (a.hs > 0) y = __fmul_rn(y, ldexpf(1.0f, -a.hs));   // metadata key 15 store scale
-                        qv = q16s(y);
+                // dead rows have zero row scales, so g = u = 0 and their hidden value is 0
+                int qv[PW];
+                if (d.hostffn) {
+#pragma unroll
+                    for (int i = 0; i < PW; ++i) qv[i] = host_hidden(v0[i], v1[i], kexp[c + i]);
+                } else {
+                    const float hsc = pow2f(-a.hs);   // metadata key 15 store scale (exact)
+#pragma unroll
+                    for (int i = 0; i < PW; ++i) {
+                        float y = swiglu1(__fmul_rn(i2f_small(v0[i]), 1.0f / 256.0f),
+                                          __fmul_rn(i2f_small(v1[i]), 1.0f / 256.0f));
+                        if (a.hs > 0) y = __fmul_rn(y, hsc);
+                        qv[i] = q16s(y);
                     }
                 }
                 // a warp's 32 rows lie in one w2 column half (the chunk is a multiple of 32)
                 const int half = (d.chunk < d.ffn && row >= d.chunk) ? 1 : 0;
                 const int col = row - (half ? d.chunk : 0);
-                char* hr = s.hrec + (size_t)b * a.dr.bytes;
-                if (live) {
-                    hr[(half ? a.dr.lo_b : a.dr.lo_a) + col] = (char)(qv & 0xFF);
-                    hr[(half ? a.dr.hi_b : a.dr.hi_a) + col] = (char)(qv >> 8);
-                }
-                if (a.t3) {   // the hidden total of the CUDA-core w2's offset codes
-                    const int sum = __reduce_add_sync(0xffffffffu, qv);
-                    if (lane == 0) atomicAdd(reinterpret_cast<int*>(hr + (half ? a.dr.g_b : a.dr.g_a)), sum);
-                }
-                if (d.hostffn) {
-                    const int mq = __reduce_max_sync(0xffffffffu, abs(qv));
-                    if (lane == 0 && mq) atomicMax(s.hmax + hmax_at(layer, b, half, s.slots), mq);
-                }
-            } else if (OP == kOpDown) {
-                if (!live) continue;
-                float o2;
-                if (d.hostffn) {
-                    const int kk = kexp[q];
-                    const float oa = host_w2_out(S0, rs0, (int)(short)(kk & 0xFFFF), a.hs, s.err);
-                    const float ob = host_w2_out(S1, rs1, kk >> 16, a.hs, s.err);
-                    o2 = __fmul_rn((float)q16h(__fadd_rn(oa, ob)), 1.0f / 256.0f);
-                } else {
-                    o2 = __fmul_rn((float)mv_epi(S0, rs0), 1.0f / 256.0f);
-                    if (npass > 1) {
-                        const int vb = mv_epi(S1, rs1);
-                        // add_q16 of the two chunk outputs (session.cpp:2052-2067)
-                        o2 = __fmul_rn((float)q16h(__fadd_rn(o2, __fmul_rn((float)vb, 1.0f / 256.0f))), 1.0f / 256.0f);
+                const int off_lo = (half ? a.dr.lo_b : a.dr.lo_a) + col, off_hi = (half ? a.dr.hi_b : a.dr.hi_a) + col;
+                const int off_g = half ? a.dr.g_b : a.dr.g_a;
+#pragma unroll
+                for (int i = 0; i < PW; ++i) {
+                    if (c + i >= gn) continue;
+                    char* hr = s.hrec + (size_t)(g0 + c + i) * a.dr.bytes;
+                    if (live) {
+                        hr[off_lo] = (char)(qv[i] & 0xFF);
+                        hr[off_hi] = (char)(qv[i] >> 8);
+                    }
+                    if (a.t3) {   // the hidden total of the CUDA-core w2's offset codes
+                        const int sum = __reduce_add_sync(0xffffffffu, qv[i]);
+                        if (lane == 0) atomicAdd(reinterpret_cast<int*>(hr + off_g), sum);
+                    }
+                    if (d.hostffn) {
+                        const int mq = __reduce_max_sync(0xffffffffu, abs(qv[i]));
+                        if (lane == 0 && mq) atomicMax(s.hmax + hmax_at(layer, g0 + c + i, half, s.slots), mq);
                     }
                 }
-                const float x1 = __fmul_rn((float)res[i], 1.0f / 256.0f);
-                s.x[(size_t)b * d.dim + row] = (int16_t)q16h(__fadd_rn(x1, o2));
-            } else {
-                unsigned long long key = 0ull;
+            } else if (OP == kOpDown) {
+                float o2[PW];
+                if (d.hostffn) {
+                    // host_w2_out of each half, then add_q16 of the halves
+#pragma unroll
+                    for (int i = 0; i < PW; ++i) {
+                        const float oa = __fmul_rn(__fmul_rn(i2f_small(v0[i]), 1.0f / 256.0f), pow2f(-(sh0(i) + a.hs)));
+                        const float ob = __fmul_rn(__fmul_rn(i2f_small(v1[i]), 1.0f / 256.0f), pow2f(-(sh1(i) + a.hs)));
+                        o2[i] = __fmul_rn(i2f_small(q16h(__fadd_rn(oa, ob))), 1.0f / 256.0f);
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < PW; ++i) {
+                        o2[i] = __fmul_rn(i2f_small(v0[i]), 1.0f / 256.0f);
+                        if (npass > 1)   // add_q16 of the two chunk outputs (session.cpp:2052-2067)
+                            o2[i] = __fmul_rn(i2f_small(q16h(__fadd_rn(o2[i], __fmul_rn(i2f_small(v1[i]), 1.0f / 256.0f)))),
+                                              1.0f / 256.0f);
+                    }
+                }
                 if (live) {
-                    const int v = mv_epi(S0, rs0);
-                    s.logits[(size_t)b * d.vocab + row] = v;
-                    key = logit_key(v, row);
+#pragma unroll
+                    for (int i = 0; i < PW; ++i) {
+                        if (c + i >= gn) continue;
+                        const float x1 = __fmul_rn(i2f_small(res[i]), 1.0f / 256.0f);
+                        s.x[(size_t)(g0 + c + i) * d.dim + row] = (int16_t)q16h(__fadd_rn(x1, o2[i]));
+                    }
                 }
-                for (int o = 16; o; o >>= 1) {
-                    const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, key, o);
-                    key = k2 > key ? k2 : key;
+            } else {
+#pragma unroll
+                for (int i = 0; i < PW; ++i) {
+                    const int q = c + i;
+                    if (q >= gn) continue;
+                    const int b = g0 + q;
+                    unsigned long long key = 0ull;
+                    if (live) {
+                        s.logits[(size_t)b * d.vocab + row] = v0[i];
+                        key = logit_key(v0[i], row);
+                    }
+                    for (int o = 16; o; o >>= 1) {
+                        const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, key, o);
+                        key = k2 > key ? k2 : key;
+                    }
+                    if (lane == 0 && key) atomicMax(&s.best[b], key);
                 }
-                if (lane == 0 && key) atomicMax(&s.best[b], key);
             }
         }
+        // the accumulators may be overwritten once every warp has read them
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(tfree);
     }
-    if (!ok && tid == 0) {
+    if (failed && tid == 0) {
         // a copy or the MMAs did not complete in time: report, and wait (bounded)
         // for the stages still in flight before the shared memory and TMEM go
         atomicExch(s.err, kErrCopyTimeout);
         for (int i = 0; i < S; ++i) mbar_wait(&full[i], 0u, 10000000ull), mbar_wait(&full[i], 1u, 10000000ull);
-        mbar_wait(done, 0u, 10000000ull);
+        mbar_wait(done, 0u, 10000000ull), mbar_wait(done, 1u, 10000000ull);
     }
     tc_fence_before();
     __syncthreads();

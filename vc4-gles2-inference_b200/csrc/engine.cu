@@ -297,7 +297,7 @@ static int check_kernel_word(vc4_session* s) {
     CK(cudaMemcpy(&w, s->st.err, sizeof(int), cudaMemcpyDeviceToHost));
     if (w > 0) return fail(VC4_ECUDA, "a kernel found its shared-memory reservation too small (needs " + std::to_string(w) + " bytes)");
     if (w == -2) return fail(VC4_ECUDA, "a kernel's bulk copy did not complete within its time limit");
-    if (w == -3) return fail(VC4_ECUDA, "a tensor-core matmat was launched with a copy ring its producers cannot share");
+    if (w == -3) return fail(VC4_ECUDA, "a tensor-core matmat was launched with a copy ring or box plan it cannot run");
     if (w == -4)
         return fail(VC4_ERANGE, "an FFN hidden value reached 64 or more: the w2 input scale of the host FFN would "
                                 "round its input, which this engine does not compute (the session's results are void)");

@@ -52,10 +52,29 @@ __device__ __forceinline__ int dp4a_us(unsigned a, int b, int c) {
     int d; asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
 }
 
-// q16 host quantisation: lrintf(v*256) clamped (common.h:188-193).
+// Exact conversions on the integer and FMA pipes instead of the conversion
+// (XU) pipe, which bounds the instruction-heavy epilogues.  1.5 * 2^23 has a
+// unit ulp: adding it to |v| < 2^22 rounds v to the nearest integer (ties to
+// even, the rounding of cvt.rni and of lrintf) and leaves that integer in the
+// low mantissa bits.
+constexpr float kMagic = 12582912.0f;   // 1.5 * 2^23
+constexpr int kMagicBits = 0x4B400000;
+__device__ __forceinline__ float i2f_small(int i) {   // (float)i, |i| < 2^22
+    return __fsub_rn(__int_as_float(kMagicBits + i), kMagic);
+}
+__device__ __forceinline__ int f2i_rn_small(float v) {   // __float2int_rn(v), |v| < 2^22
+    return __float_as_int(__fadd_rn(v, kMagic)) - kMagicBits;
+}
+__device__ __forceinline__ float rint_small(float v) {   // rintf(v) up to the sign of a zero, |v| < 2^22
+    return __fsub_rn(__fadd_rn(v, kMagic), kMagic);
+}
+
+// q16 host quantisation: lrintf(v*256) clamped (common.h:188-193).  Values
+// beyond +-2^22 clamp to the rail either way; NaN gives 0 (cvt.rni's value).
 __device__ __forceinline__ int q16h(float v) {
-    const int q = __float2int_rn(__fmul_rn(v, 256.0f));
-    return q < -32768 ? -32768 : q > 32767 ? 32767 : q;
+    const float t = fminf(fmaxf(__fmul_rn(v, 256.0f), -4194304.0f), 4194303.0f);
+    const int q = f2i_rn_small(t);
+    return v != v ? 0 : q < -32768 ? -32768 : q > 32767 ? 32767 : q;
 }
 // q16 shader store: clamp(floor(v*256+0.5)) (xformat.cpp x_st2).
 __device__ __forceinline__ int q16s(float v) {
@@ -63,19 +82,70 @@ __device__ __forceinline__ int q16s(float v) {
     f = f < -32768.0f ? -32768.0f : f > 32767.0f ? 32767.0f : f;
     return (int)f;
 }
-// Matvec epilogue: floor(S*sc + 0.5) clamped to the q16 rail.
+// Matvec epilogue: floor(S*sc + 0.5) clamped to the q16 rail, in double.
 __device__ __forceinline__ int mv_epi(long long S, float sc) {
     double v = floor(__dadd_rn(__dmul_rn(__ll2double_rn(S), (double)sc), 0.5));
     v = v < -32768.0 ? -32768.0 : v > 32767.0 ? 32767.0 : v;
     return (int)v;
 }
+__device__ __noinline__ int mv_epi_dbl(long long S, float sc) { return mv_epi(S, sc); }
+// A row scale as sc = m * 2^-sh with an integer mantissa m (carrying the
+// sign; zero is m = 0, sh = 1).  sh = 0 marks a scale (subnormal, inf, NaN)
+// that only the double path takes.
+struct RowScale {
+    int m, sh;
+    float sc;
+};
+__device__ __forceinline__ RowScale row_scale(float sc) {
+    const unsigned u = __float_as_uint(sc);
+    const int e = (int)((u >> 23) & 0xFFu);
+    RowScale r;
+    r.sc = sc;
+    if (e == 0 && (u & 0x7FFFFFu) == 0) {
+        r.m = 0;
+        r.sh = 1;
+    } else if (e == 0 || e == 0xFF) {
+        r.m = 0;
+        r.sh = 0;
+    } else {
+        const int mant = (int)((u & 0x7FFFFFu) | 0x800000u);
+        r.m = (u >> 31) ? -mant : mant;
+        r.sh = 150 - e;
+    }
+    return r;
+}
+// The same value without the conversion pipe.  For |S| < 2^28 and
+// 1 <= sh <= 53, |S*m| < 2^52 and |S*m| + 2^(sh-1) < 2^53, so the double
+// path's product and its +0.5 are exact and its floor is the integer
+// (S*m + 2^(sh-1)) >> sh (an arithmetic shift floors).  Other inputs take the
+// double path.
+// The integer form, without branches; `ok` is false where the double path
+// must be taken instead (the caller fixes those up outside its chains).
+__device__ __forceinline__ int mv_epi_int(long long S, const RowScale& r, bool& ok) {
+    ok = r.sh >= 1 && r.sh <= 53 && S > -(1LL << 28) && S < (1LL << 28);
+    const int sh = min(max(r.sh, 1), 53);
+    const long long v = ((long long)(int)S * r.m + (1LL << (sh - 1))) >> sh;
+    return v < -32768 ? -32768 : v > 32767 ? 32767 : (int)v;
+}
+__device__ __forceinline__ int mv_epi(long long S, const RowScale& r) {
+    bool ok;
+    const int v = mv_epi_int(S, r, ok);
+    return ok ? v : mv_epi_dbl(S, r.sc);
+}
+// 2^k for -126 <= k <= 127, built in the exponent field (exact).
+__device__ __forceinline__ float pow2f(int k) { return __int_as_float((127 + k) << 23); }
+
 // Portable exp: Cody-Waite reduction + degree-7 Taylor (same ops as orc_expf).
+// Written without branches, so that the many independent exps of an epilogue
+// interleave: the reduction runs on x clamped to the finite range, the
+// scaling p * 2^k is (p * 2^a) * 2^b with a + b = k and both factors normal
+// (a = 1 for k = 128, as p*2 then 2^(k-1); a = k + 64, b = -64 below 2^-126;
+// b = 0 otherwise, an exact multiply by one), and the out-of-range and NaN
+// inputs are selected at the end.
 __device__ __forceinline__ float vexp(float x) {
-    if (x != x) return x;
-    if (x > 88.72283935546875f) return __int_as_float(0x7f800000);
-    if (x < -103.97208404541016f) return 0.0f;
-    const float k = rintf(__fmul_rn(x, 1.44269502162933349609375f));
-    float r = __fmaf_rn(-k, 0.693145751953125f, x);
+    const float xc = fminf(fmaxf(x, -103.97208404541016f), 88.72283935546875f);
+    const float k = rint_small(__fmul_rn(xc, 1.44269502162933349609375f));   // |k| <= 150
+    float r = __fmaf_rn(-k, 0.693145751953125f, xc);
     r = __fmaf_rn(-k, 1.428606765330187045037746429443359375e-06f, r);
     float p = 1.98412698412698412698e-4f;
     p = __fmaf_rn(p, r, 1.38888888888888888889e-3f);
@@ -85,10 +155,13 @@ __device__ __forceinline__ float vexp(float x) {
     p = __fmaf_rn(p, r, 0.5f);
     p = __fmaf_rn(p, r, 1.0f);
     p = __fmaf_rn(p, r, 1.0f);
-    int ki = (int)k;
-    if (ki > 127) { p = __fmul_rn(p, 2.0f); ki -= 1; }
-    if (ki < -126) return __fmul_rn(__fmul_rn(p, __int_as_float((ki + 64 + 127) << 23)), __int_as_float((-64 + 127) << 23));
-    return __fmul_rn(p, __int_as_float((ki + 127) << 23));
+    const int ki = f2i_rn_small(k);
+    const int ea = ki > 127 ? 1 : ki < -126 ? ki + 64 : ki;
+    const int eb = ki - ea;
+    float y = __fmul_rn(__fmul_rn(p, __int_as_float((ea + 127) << 23)), __int_as_float((eb + 127) << 23));
+    y = x > 88.72283935546875f ? __int_as_float(0x7f800000) : y;
+    y = x < -103.97208404541016f ? 0.0f : y;
+    return x != x ? x : y;
 }
 // SiLU(g)*u in the shaders' order.
 __device__ __forceinline__ float swiglu1(float g, float u) {
@@ -324,7 +397,7 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 
 // Error word values besides shared-memory shortfalls (which record the bytes needed).
 constexpr int kErrCopyTimeout = -2;
-constexpr int kErrRingShape = -3;   // a tensor-core ring whose stage count its producers cannot share
+constexpr int kErrRingShape = -3;   // a tensor-core matmat launched with a ring or box plan it cannot run
 constexpr int kStreamStages = 4;   // ring depth of the streaming kernels
 
 template <int MAXC>
@@ -528,20 +601,28 @@ __device__ __forceinline__ int hidden_exp(const State& s, int layer, int b, int 
     return 6 - e;
 }
 // One w2 half of the host FFN: (floor(S * 2^k * ws + 0.5) clamped)/256 * 2^-(k + hs).
+// k >= 0 (the caller has refused negative exponents).
+__device__ __forceinline__ float host_w2_out(long long S, const RowScale& ws, int k, int hs) {
+    const float v = __fmul_rn(i2f_small(mv_epi(S * (1LL << k), ws)), 1.0f / 256.0f);
+    return __fmul_rn(v, pow2f(-(k + hs)));
+}
+__device__ __forceinline__ float host_w2_out(long long S, float ws, int k, int hs) {
+    const float v = __fmul_rn((float)mv_epi(S * (1LL << k), ws), 1.0f / 256.0f);
+    return __fmul_rn(v, pow2f(-(k + hs)));
+}
 __device__ __forceinline__ float host_w2_out(long long S, float ws, int k, int hs, int* err) {
     if (k < 0) {
         atomicExch(err, kErrHiddenRange);
         k = 0;
     }
-    const float v = __fmul_rn((float)mv_epi(S * (1LL << k), ws), 1.0f / 256.0f);
-    return __fmul_rn(v, ldexpf(1.0f, -(k + hs)));
+    return host_w2_out(S, ws, k, hs);
 }
 // The host FFN's gate value: the hidden q16 int of SiLU(g)*u with g, u the
 // matvec_s outputs of a 2^k scaled input (quantize_act: lrintf).
 __device__ __forceinline__ int host_hidden(int g, int u, int k) {
-    const float sk = ldexpf(1.0f, -k);
-    const float gf = __fmul_rn(__fmul_rn((float)g, 1.0f / 256.0f), sk);
-    const float uf = __fmul_rn(__fmul_rn((float)u, 1.0f / 256.0f), sk);
+    const float sk = pow2f(-k);
+    const float gf = __fmul_rn(__fmul_rn(i2f_small(g), 1.0f / 256.0f), sk);
+    const float uf = __fmul_rn(__fmul_rn(i2f_small(u), 1.0f / 256.0f), sk);
     return q16h(swiglu1(gf, uf));
 }
 
@@ -910,7 +991,7 @@ __global__ void __launch_bounds__(kThreads) k_qkv(DMat W, DMat E, const float* e
         if (row < W.rows) {
             const long long St = WT == W_T3 ? tot[0] - ws.gsum[warp * ws.gst] : tot[0];
             const int v = mv_epi(St, R.rs);
-            const float out = __fmul_rn(__fmul_rn((float)v, 1.0f / 256.0f), ldexpf(1.0f, -kw));
+            const float out = __fmul_rn(__fmul_rn((float)v, 1.0f / 256.0f), pow2f(-kw));
             s.qkv[(size_t)(b0 + warp) * (d.dim + 2 * d.kv_dim) + row] = out;
         }
     }
@@ -958,7 +1039,7 @@ __global__ void __launch_bounds__(kThreads) k_wo(DMat W, State s, Batch bt, Dims
     if (warp < nb && row < W.rows) {
         const long long St = WT == W_T3 ? tot[0] - ws.gsum[warp * ws.gst] : tot[0];
         const int v = mv_epi(St, R.rs);
-        const float wo = __fmul_rn(__fmul_rn((float)v, 1.0f / 256.0f), ldexpf(1.0f, -kw));
+        const float wo = __fmul_rn(__fmul_rn((float)v, 1.0f / 256.0f), pow2f(-kw));
         const float xr = __fmul_rn((float)xres, 1.0f / 256.0f);
         s.x1[(size_t)(b0 + warp) * d.dim + row] = (int16_t)q16h(__fadd_rn(xr, wo));
     }
@@ -1543,7 +1624,6 @@ __device__ __forceinline__ int q_grid_exp(float qmax) {
     const int F = 22 - e;
     return F > 100 ? 100 : F < -100 ? -100 : F;
 }
-__device__ __forceinline__ float pow2f(int k) { return __int_as_float((127 + k) << 23); }   // 2^k, -126 <= k <= 127
 
 // One warp puts q head v (hd floats) on its integer grid: qi[i] = rint(v[i]
 // * 2^F); returns the head's score constant fl(2^-F / grid / sqrt(hd)) (kvb 2:
@@ -1789,16 +1869,22 @@ k_attn(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int 
 //    tiles of kAbRows positions (cp.async), rows padded to an odd number of
 //    16-byte units so ldmatrix reads hit distinct banks;
 //  - scores: each q head on its integer grid (warp_q_grid) is split into
-//    three balanced signed bytes, the B operand (column 2*limb + head); the
-//    A operand is a K tile: q8 levels as they are, q16 levels as a signed
-//    high-byte and an unsigned low-byte plane; S = sum_limb 256^limb (256 D_hi
-//    + D_lo) is the exact integer dot;
-//  - weights: attn_weights (integer E_t < 2^47, exact double sums);
+//    three balanced signed bytes, the B operand (column 4*head + limb, so a
+//    lane and its neighbour hold a head's limbs and one shuffle combines
+//    them); the A operand is a K tile: q8 levels as they are, q16 levels as
+//    a signed high-byte and an unsigned low-byte plane; S = sum_limb
+//    256^limb (256 D_hi + D_lo) is the exact integer dot, and the score is
+//    float(S) times one per-head constant;
+//  - weights: at the last K tile one pass takes the maximum, E_t (integers
+//    < 2^47), their exact double sum and E_t's byte limbs;
 //  - P.V: E_t split into unsigned byte limbs is the A operand (row h*NL +
 //    limb), a V tile read with ldmatrix.trans the B operand (q8: even and odd
 //    columns; q16: high and low byte planes); every limb product and their
-//    combination into num = sum_t E_t * level_t are exact integers, added into
-//    shared int64 sums in any order.
+//    combination into num = sum_t E_t * level_t are exact integers.  Each
+//    warp keeps its position block's limb products in its int32 MMA
+//    accumulators across the V tiles (at most seq/4 * 255 * 255 < 2^31) and
+//    writes them once, as int64, into the freed ring; the blocks and limbs
+//    are combined at the end (no atomics).
 // A sequence's output is therefore the cluster kernel's, bit for bit.
 // Positions inside a 32-wide MMA k block are taken in the order ldmatrix of
 // 16-bit pairs delivers them (attnb_k_of); the weight limbs are stored in it.
@@ -2571,29 +2657,39 @@ inline PFN_cuTensorMapEncodeTiled_v12000 tmap_encode_fn() {
     });
     return fn;
 }
-// A q8 or t3 matrix's row-major int8 copy, rows of x_stride bytes; one box is 128 rows x
-// 128 bytes in the 128-byte swizzle layout (a weight tile's stage).
+// A q8 or t3 matrix's row-major int8 copy, rows of x_stride bytes; one box is 64 rows x
+// 128 bytes in the 128-byte swizzle layout (half of a weight tile's stage).
 inline bool tmap_weights(CUtensorMap* map, const DMat& W) {
     const auto enc = tmap_encode_fn();
     if (!enc || !W.rm) return false;
     const cuuint64_t dims[2] = {(cuuint64_t)x_stride(W), (cuuint64_t)W.rblocks * 32};
     const cuuint64_t strides[1] = {(cuuint64_t)x_stride(W)};
-    const cuuint32_t box[2] = {128, 128}, es[2] = {1, 1};
+    const cuuint32_t box[2] = {128, 64}, es[2] = {1, 1};
     return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, W.rm, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
-// n staged records of rec_bytes (a multiple of 16); one box is N records x
-// 128 bytes in the 128-byte swizzle layout (a stage of one input plane).
+// n staged records of rec_bytes (a multiple of 16); one box is N/2 records x
+// 128 bytes in the 128-byte swizzle layout (half of a stage of one input plane).
 inline bool tmap_records(CUtensorMap* map, const char* recs, int rec_bytes, int n, int N) {
     const auto enc = tmap_encode_fn();
     if (!enc || rec_bytes % 16) return false;
     const cuuint64_t dims[2] = {(cuuint64_t)rec_bytes, (cuuint64_t)n};
     const cuuint64_t strides[1] = {(cuuint64_t)rec_bytes};
-    const cuuint32_t box[2] = {128, (cuuint32_t)N}, es[2] = {1, 1};
+    const cuuint32_t box[2] = {128, (cuuint32_t)(N / 2)}, es[2] = {1, 1};
     return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<char*>(recs), dims, strides, box, es,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// VC4_TC_SPLIT=aligned|balanced pins the tensor-core matmats' work split
+// (measurement sweeps); unset, the launch estimates which is shorter.
+inline int tc_split_override() {
+    static const int v = [] {
+        const char* e = getenv("VC4_TC_SPLIT");
+        return !e ? 0 : !strcmp(e, "aligned") ? 1 : !strcmp(e, "balanced") ? 2 : 0;
+    }();
+    return v;
 }
 
 template <int OP>
@@ -2617,41 +2713,66 @@ inline bool tc_launch(const DModel& m, const State& s, const Batch& bt, int laye
     a.t3 = W0.wtype == W_T3;
     const int tiles = (W0.rows + 127) / 128;
     const int nsm = std::max(1, m.num_sms);
+    a.tiles = tiles;
+    // The work is (tile, 16-sequence unit) pairs.  Aligned split: groups of N
+    // sequences inside a tile, one CTA each, N chosen for the fewest bytes
+    // streamed into the busiest SM (the tile's weights once per CTA, the
+    // group's inputs once per tile).  Balanced split: one CTA per SM, equal
+    // ranges of units, run in rounds of at most N sequences.  The epilogue is
+    // done in pieces of 16 sequences per warp quarter, so a CTA's time is its
+    // pieces per warp; the balanced split pays when the aligned one would
+    // leave a second wave.
+    const int units_pt = (bt.n + 15) / 16;
+    const long long units = (long long)tiles * units_pt;
+    const int cap = std::min(256, 512 / (2 * a.npass));   // TMEM: 2 * npass * N columns
     const int nmax = (bt.n + 15) & ~15;
-    // sequences per CTA: the fewest bytes streamed into the busiest SM (the
-    // tile's weights once per CTA, the group's inputs once per tile)
-    int N = 0, ctas = 0;
-    double best = 0.0;
-    for (int c = 16; c <= 256; c *= 2) {
-        if (2 * a.npass * c > 512 || (c > 16 && c / 2 >= nmax)) break;
-        if ((size_t)a.npass * kTcTileA * 2 + (size_t)a.nin * 2 * c * 128 * 2 > kMaxDynSmem) continue;   // two stages
-        const int k = tiles * ((bt.n + c - 1) / c);
-        const double per = (double)a.npass * a.kc * 2048 + (double)a.nin * a.kc * std::min(c, nmax) * 32;
-        const double load = (double)((k + nsm - 1) / nsm) * per;
-        if (N == 0 || load <= best) { N = c; ctas = k; best = load; }
+    int Na = 0, ctas_a = 0;
+    {
+        double best = 0.0;
+        for (int c = 16; c <= cap; c *= 2) {
+            if (c > 16 && c / 2 >= nmax) break;
+            if ((size_t)a.npass * kTcTileA * 2 + (size_t)a.nin * 2 * c * 128 * 2 > kMaxDynSmem) continue;   // two stages
+            const int k = tiles * ((bt.n + c - 1) / c);
+            const double per = (double)a.npass * a.kc * 2048 + (double)a.nin * a.kc * std::min(c, nmax) * 32;
+            const double load = (double)((k + nsm - 1) / nsm) * per;
+            if (Na == 0 || load <= best) { Na = c; ctas_a = k; best = load; }
+        }
     }
-    if (N == 0) return false;
-    a.group = N;
+    const int ctas_b = (int)std::min<long long>(units, nsm);
+    const int per_b = (int)((units + ctas_b - 1) / ctas_b);
+    const int Nb = 16 * std::min(per_b, cap / 16);
+    // pieces per warp of the busiest SM (4 warp quarters share a round's pieces)
+    const int pieces_a = ((ctas_a + nsm - 1) / nsm) * ((Na / 16 + 3) / 4);
+    // a range cut by a tile boundary or by N costs at most one partial piece more
+    const int pieces_b = (per_b + 3) / 4 + (per_b > 1 ? 1 : 0);
+    const int split = tc_split_override();   // 1 aligned, 2 balanced, 0 by the estimate
+    const bool balanced = split == 2 || (split == 0 && Na > 0 && pieces_b < pieces_a);
+    if (!balanced && Na == 0) return false;
+    a.group = balanced ? Nb : Na;
+    a.groups = balanced ? 0 : (bt.n + Na - 1) / Na;
+    const int ctas = balanced ? ctas_b : ctas_a;
+    static const int max_res = [] {   // the register file: 64K registers per SM
+        cudaFuncAttributes fa{};
+        if (cudaFuncGetAttributes(&fa, k_tmm<OP>) != cudaSuccess || fa.numRegs <= 0) return 1;
+        return std::max(1, 65536 / (kTcThreads * fa.numRegs));
+    }();
+    const int resident = balanced ? 1 : std::max(1, std::min(std::min((ctas + nsm - 1) / nsm, 4), max_res));
     int cols = 32;
-    while (cols < 2 * a.npass * N) cols *= 2;
+    while (cols < 2 * a.npass * a.group) cols *= 2;
     a.tmem_cols = cols;
-    // ring depth: the shared memory of the CTAs that share an SM; the producer
-    // count divides it and does not exceed it (k_tmm relies on both)
-    const int resident = std::max(1, std::min(std::min((ctas + nsm - 1) / nsm, 512 / cols), 4));
-    const size_t budget = std::min(kMaxDynSmem, kSmemPerSm / resident - 1024);
+    // ring depth: the shared memory of the CTAs that share an SM
+    const size_t budget = std::min(kMaxDynSmem, kSmemPerSm / std::min(resident, 512 / cols) - 1024);
     a.stages = 0;
     const size_t fixed = tc_smem(a), per_stage = tc_stage_bytes(a) + 16;   // ring stage + its two mbarriers
     a.stages = budget > fixed ? (int)std::min<size_t>(kTcMaxStages, (budget - fixed) / per_stage) : 0;
-    if (a.stages < 2) return false;
-    a.producers = std::min(kTcProducers, a.stages);
-    a.stages -= a.stages % a.producers;
+    if (a.stages < 2 || 2 * a.npass + 4 * a.nin > kTcThreads / 32 - 1) return false;
+    const int N = a.group;
     TcMaps maps;
     if (!tmap_weights(&maps.a[0], W0) || !tmap_weights(&maps.a[1], W1 ? *W1 : W0) ||
         !tmap_records(&maps.b, from_hrec ? s.hrec : s.xrec, rec_bytes, bt.n, N))
         return false;
     Dims d = dims_of(m, s);
-    launch_pdl_block(k_tmm<OP>, dim3(tiles, 1, (bt.n + N - 1) / N), kTcThreads, tc_smem(a), st, maps, a, s, bt, d,
-                     layer, fz);
+    launch_pdl_block(k_tmm<OP>, dim3(ctas), kTcThreads, tc_smem(a), st, maps, a, s, bt, d, layer, fz);
     return true;
 }
 

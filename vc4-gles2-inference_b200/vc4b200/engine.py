@@ -15,7 +15,8 @@ import os
 import numpy as np
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "_lib", "libvc4b200.so")
+# VC4B200_LIB names another build of the library (a measurement variant)
+LIB_PATH = os.environ.get("VC4B200_LIB") or os.path.join(_HERE, "_lib", "libvc4b200.so")
 
 WQ8, WQ4, WT3 = 0, 1, 2
 MATS = {"qkv": 0, "wo": 1, "w1": 2, "w3": 3, "w2": 4, "router": 5, "logits": 6}
