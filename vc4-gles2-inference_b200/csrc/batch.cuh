@@ -465,7 +465,7 @@ constexpr int kOpDown = 4;
 // Epilogue variants for measurement builds (-D): the ffn matmats' piece width,
 // and the double-precision rounding path instead of the integer form.
 #ifndef VC4_TMM_PW_FFN
-#define VC4_TMM_PW_FFN 8
+#define VC4_TMM_PW_FFN 2
 #endif
 #ifndef VC4_TMM_DBL
 #define VC4_TMM_DBL 1
@@ -605,10 +605,11 @@ __device__ __forceinline__ void mbar_arrive(unsigned long long* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
-// Single-matrix matmats (qkv, wo, logits) keep to 64 registers so that two
-// CTAs share an SM: one's epilogue then overlaps the other's copies and MMAs.
+// Every instance keeps to 64 registers so that two CTAs share an SM: one's
+// epilogue then overlaps the other's copies and MMAs, and each sub-partition
+// has eight warps to hide the epilogue's latencies.
 template <int OP>
-__global__ void __launch_bounds__(kTcThreads, OP == kOpGate || OP == kOpDown ? 1 : 2) k_tmm(const __grid_constant__ TcMaps maps, TcArgs a, State s, Batch bt,
+__global__ void __launch_bounds__(kTcThreads, 2) k_tmm(const __grid_constant__ TcMaps maps, TcArgs a, State s, Batch bt,
                                                        Dims d, int layer, Finalize fz) {
     const int N = a.group, S = a.stages;
     const int n = bt.n, upt = (n + 15) / 16, umax = N / 16;
@@ -829,16 +830,18 @@ __global__ void __launch_bounds__(kTcThreads, OP == kOpGate || OP == kOpDown ? 1
         // complete: warp w reads TMEM lanes 32*(w%4) .. +31 (its rows) and
         // every fourth piece of sequences starting at piece w/4.  The
         // residuals it reads come from the previous grids.
-        if (!mbar_wait(done, (unsigned)r & 1u)) bad = true;
-        tc_fence_after();
+        // One thread waits for the MMAs; the others wait at the block barrier
+        // (in hardware, taking no issue slots from the copies and MMAs).
+        if (tid == 0 && !mbar_wait(done, (unsigned)r & 1u)) bad = true;
         if (__syncthreads_or(bad)) {
             failed = true;
             break;
         }
+        tc_fence_after();
         __syncwarp();   // tcgen05.ld below is warp-aligned
-        // pieces of PW sequences: independent chains per warp, within the
-        // registers of two CTAs per SM (single-matrix ops, 8) or of the two
-        // accumulator pairs (ffn, VC4_TMM_PW_FFN: 8 or 16)
+        // pieces of PW sequences: independent chains per warp within the 64
+        // registers of two CTAs per SM (single-matrix ops 8; the ffn's two
+        // accumulator pairs and SwiGLU or residual chains VC4_TMM_PW_FFN, 2)
         constexpr int PW = kOne ? 8 : kTcPwFfn;
         const int row = rd.tile * 128 + 32 * quarter + lane;
         const bool live = row < P0.W.rows;

@@ -2722,10 +2722,17 @@ inline bool tc_launch(const DModel& m, const State& s, const Batch& bt, int laye
     // done in pieces of 16 sequences per warp quarter, so a CTA's time is its
     // pieces per warp; the balanced split pays when the aligned one would
     // leave a second wave.
+    static const int max_res = [] {   // the register file: 64K registers per SM
+        cudaFuncAttributes fa{};
+        if (cudaFuncGetAttributes(&fa, k_tmm<OP>) != cudaSuccess || fa.numRegs <= 0) return 1;
+        return std::max(1, std::min(2, 65536 / (kTcThreads * fa.numRegs)));
+    }();
     const int units_pt = (bt.n + 15) / 16;
     const long long units = (long long)tiles * units_pt;
-    const int cap = std::min(256, 512 / (2 * a.npass));   // TMEM: 2 * npass * N columns
+    // TMEM: 2 * npass * N columns per CTA, shared by the CTAs of an SM
+    const int cap = std::min(256, 512 / max_res / (2 * a.npass)) & ~15;
     const int nmax = (bt.n + 15) & ~15;
+    const int slots = nsm * max_res;   // CTAs resident at once
     int Na = 0, ctas_a = 0;
     {
         double best = 0.0;
@@ -2734,15 +2741,15 @@ inline bool tc_launch(const DModel& m, const State& s, const Batch& bt, int laye
             if ((size_t)a.npass * kTcTileA * 2 + (size_t)a.nin * 2 * c * 128 * 2 > kMaxDynSmem) continue;   // two stages
             const int k = tiles * ((bt.n + c - 1) / c);
             const double per = (double)a.npass * a.kc * 2048 + (double)a.nin * a.kc * std::min(c, nmax) * 32;
-            const double load = (double)((k + nsm - 1) / nsm) * per;
+            const double load = (double)((k + slots - 1) / slots) * per;
             if (Na == 0 || load <= best) { Na = c; ctas_a = k; best = load; }
         }
     }
-    const int ctas_b = (int)std::min<long long>(units, nsm);
+    const int ctas_b = (int)std::min<long long>(units, slots);
     const int per_b = (int)((units + ctas_b - 1) / ctas_b);
     const int Nb = 16 * std::min(per_b, cap / 16);
-    // pieces per warp of the busiest SM (4 warp quarters share a round's pieces)
-    const int pieces_a = ((ctas_a + nsm - 1) / nsm) * ((Na / 16 + 3) / 4);
+    // pieces per warp of the busiest slot (4 warp quarters share a round's pieces)
+    const int pieces_a = ((ctas_a + slots - 1) / slots) * ((Na / 16 + 3) / 4);
     // a range cut by a tile boundary or by N costs at most one partial piece more
     const int pieces_b = (per_b + 3) / 4 + (per_b > 1 ? 1 : 0);
     const int split = tc_split_override();   // 1 aligned, 2 balanced, 0 by the estimate
@@ -2751,12 +2758,7 @@ inline bool tc_launch(const DModel& m, const State& s, const Batch& bt, int laye
     a.group = balanced ? Nb : Na;
     a.groups = balanced ? 0 : (bt.n + Na - 1) / Na;
     const int ctas = balanced ? ctas_b : ctas_a;
-    static const int max_res = [] {   // the register file: 64K registers per SM
-        cudaFuncAttributes fa{};
-        if (cudaFuncGetAttributes(&fa, k_tmm<OP>) != cudaSuccess || fa.numRegs <= 0) return 1;
-        return std::max(1, 65536 / (kTcThreads * fa.numRegs));
-    }();
-    const int resident = balanced ? 1 : std::max(1, std::min(std::min((ctas + nsm - 1) / nsm, 4), max_res));
+    const int resident = std::max(1, std::min(std::min((ctas + nsm - 1) / nsm, 4), max_res));
     int cols = 32;
     while (cols < 2 * a.npass * a.group) cols *= 2;
     a.tmem_cols = cols;
