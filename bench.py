@@ -61,6 +61,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="bounded CPU baseline sample")
+    ap.add_argument("--private-prefix", action="store_true",
+                    help="restore the prefix into every slot's own rows instead of holding it once (shared)")
     ap.add_argument("--seq", type=int, default=0,
                     help="shorter KV cache (and prompt at most half of it) for small profiling captures")
     return ap.parse_args()
@@ -261,9 +263,12 @@ class Dist:
 # workload description (identical in both arms)
 # ---------------------------------------------------------------------------
 
-def config_of(cfg, world: int) -> dict:
+def config_of(cfg, world: int, private_prefix: bool = False) -> dict:
+    restore = bool(cfg.extra.get("prefix_restore"))
     return {"workload": workload_desc(cfg), "batch_per_gpu": cfg.batch, "seq": cfg.seq, "quant": cfg.quant,
-            "kv": KV_NAME[cfg.kv_bits], "prefix_restore": bool(cfg.extra.get("prefix_restore")),
+            "kv": KV_NAME[cfg.kv_bits], "prefix_restore": restore,
+            "prefix_rows": ("each slot's own copy" if private_prefix else "held once per GPU, read by every slot")
+                           if restore else None,
             "parallelism": ("dp%d (sequences sharded by rank)" % world) if cfg.batch > 1 else
                            ("dp%d replicas" % world),
             "l2": "flushed between timed steps (256 MiB write, then read back so no dirty line is left)"}
@@ -359,7 +364,7 @@ def run_reference(args, cfg, dist):
             "warmup": args.warmup, "ms_per_step": 1000.0 / r["value"] * len(cd.prompts), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": DTYPE,
             "data": "synthetic (seeded weights and prompts of the configuration's shape)",
-            "config": config_of(cfg, args.gpus),
+            "config": config_of(cfg, args.gpus, args.private_prefix),
             "impl": "reference", "cpu_baseline": r,
             "e2e": {"value": r["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -399,20 +404,33 @@ def measure(args, cfg, dist, full: bool = True) -> dict:
     prompts = decode_prompts(cfg, dist.rank)
     t0 = time.perf_counter()
     if cfg.extra.get("prefix_restore"):
-        # one prefix prefilled once, saved as MMKV1 and restored into every slot
+        # one prefix prefilled once (batched prefill: its positions run as one
+        # batch of the many-sequence path), saved as MMKV1 and restored into every slot
         prefix = prompts[0][:-1]
-        sess.prefill(prefix, 0, slot=0, want_logits=False)
+        sess.prefill(prefix, 0, slot=0, want_logits=False, batched=True)
+        prefill_tok = len(prefix)
+        prefill_only_s = time.perf_counter() - t0
         mmkv = os.path.join(tempfile.gettempdir(), "vc4b200_prefix_%d_%d.mmkv" % (os.getpid(), dist.rank))
         sess.save_prefix_cache(mmkv, prefix)
-        for b in range(1, B):
-            sess.load_prefix_cache(mmkv, slot=b)
+        if args.private_prefix:
+            for b in range(1, B):
+                sess.load_prefix_cache(mmkv, slot=b)
+        else:
+            # restored into every slot, the rows held once on the GPU
+            sess.load_prefix_cache_shared(mmkv, list(range(B)))
         os.unlink(mmkv)
         if os.path.exists(mmkv + ".json"):
             os.unlink(mmkv + ".json")
     else:
         for b in range(B):
-            sess.prefill(prompts[b][:-1], 0, slot=b, want_logits=False)
+            sess.prefill(prompts[b][:-1], 0, slot=b, want_logits=False, batched=True)
+        prefill_tok = sum(len(p) - 1 for p in prompts)
+        prefill_only_s = time.perf_counter() - t0
     prefill_s = time.perf_counter() - t0
+    prefill = {"tokens": prefill_tok, "s": prefill_only_s, "tokens_per_s": prefill_tok / prefill_only_s,
+               "how": "vc4_prefill_batch (up to %d positions of a prompt per pass; the serial loop below 16 "
+                      "positions), host wall clock with a synchronize per pass, first-call graph capture included"
+                      % B}
     P = len(prompts[0])
     stream = torch.cuda.ExternalStream(sess.stream())
     d_slots = torch.arange(B, dtype=torch.int32, device="cuda")
@@ -521,7 +539,7 @@ def measure(args, cfg, dist, full: bool = True) -> dict:
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": DTYPE,
             "data": "synthetic (seeded weights and prompts of the configuration's shape)",
-            "config": config_of(cfg, dist.world), "prefill_s": prefill_s,
+            "config": config_of(cfg, dist.world, args.private_prefix), "prefill_s": prefill_s, "prefill": prefill,
             "roofline": roofline, "e2e": e2e, "clocks": clk, "gpu_launches": l1 - l0}
     sess.close()
     model.close()
@@ -576,7 +594,7 @@ def run_ours(args, cfg, dist):
         for key in args.secondary.split(","):
             c2 = synth.CONFIGS[key]
             l2 = measure(args, c2, dist, full=False)
-            ent = {k: l2[k] for k in ("value", "ms_per_step", "e2e", "gpu_launches", "clocks")}
+            ent = {k: l2[k] for k in ("value", "ms_per_step", "e2e", "gpu_launches", "clocks", "prefill")}
             ent["config"] = l2["config"]
             ent["roofline"] = {k: l2["roofline"][k] for k in ("kernel", "op", "achieved", "frac", "step_frac",
                                                              "per_op_ms", "share_per_step")}

@@ -119,6 +119,15 @@ VC4_API int vc4_session_check(vc4_session* s);
    (the serial prompt loop, chat.cpp:245-297); the logits of the last position
    are returned when logits is not NULL. */
 VC4_API int vc4_prefill(vc4_session* s, int slot, const int* tokens, int n, int pos0, float* logits);
+/* Batched prefill (the reference's step_pair / PREFILL_BATCH,
+   session.cpp:1598-1795, which it accepts only byte-identical to the serial
+   loop): the prompt's positions run as one batch of the many-sequence path,
+   up to the session's slot count per pass (the activations are sized by it),
+   with each layer's new K/V rows appended before any position attends.  The
+   logits of the last position and every K/V row are those of vc4_prefill bit
+   for bit.  Chunks below 16 positions, and models or sequence lengths the
+   many-sequence kernels do not hold, run through the serial loop. */
+VC4_API int vc4_prefill_batch(vc4_session* s, int slot, const int* tokens, int n, int pos0, float* logits);
 
 /* KV rows of one layer in the MMKV1 texel layout (the bytes
    prefix_cache.cpp:59-67 reads with glReadPixels and 176-189 writes with
@@ -134,6 +143,32 @@ VC4_API int vc4_save_prefix_cache(vc4_session* s, int slot, const char* path, co
                           uint64_t system_fnv, uint64_t tools_fnv);
 VC4_API int vc4_load_prefix_cache(vc4_session* s, int slot, const char* path, int* toks_out, int cap,
                           int* n_out);
+/* load_prefix_cache restored into many slots at once, with the rows held
+   once: the MMKV1 file (validated as vc4_load_prefix_cache does) is read into
+   the session's shared-prefix rows, and each listed slot reads its positions
+   below the prefix length from there instead of from a copy of its own.  A
+   slot's own rows, and every result, are as after vc4_load_prefix_cache on
+   that slot: vc4_kv_read_rows returns the prefix rows, and a write into the
+   prefix (vc4_kv_write_rows, a prefill or a host-array step at such a
+   position) first gives the slot its own copy.  A device-array step
+   (vc4_step_batch_device) at a position inside a slot's shared prefix does
+   not write the row and makes vc4_session_check report VC4_ESTATE.  One
+   shared prefix per session: loading another one first gives the slots still
+   reading the old one their own copies.  No counterpart in the reference,
+   which restores a prefix into its one sequence (prefix_cache.cpp:135-207);
+   this is the many-sequence form of that restore. */
+VC4_API int vc4_load_prefix_cache_shared(vc4_session* s, const char* path, const int* slots, int count,
+                                         int* toks_out, int cap, int* n_out);
+
+/* build_prefix_cache (prefix_build.cpp:22-83, the `--build-prefix-cache
+   PROMPTFILE OUT` mode) for a prompt the caller has already tokenised:
+   refuses an empty prompt or one longer than the session's sequence length,
+   prefills toks[0..n) on `slot` from position 0 with the serial prompt loop,
+   then writes the MMKV1 file and its sidecar as vc4_save_prefix_cache does.
+   system_fnv / tools_fnv are FNV-1a-64 hashes of the raw system prompt and
+   tools text (common.cpp:63-67; 0 when the prompt came from a file). */
+VC4_API int vc4_build_prefix_cache(vc4_session* s, int slot, const int* toks, int n, const char* path,
+                                   uint64_t system_fnv, uint64_t tools_fnv);
 
 /* GPU::matvec_s (gpu_conv.cpp:271-287), the CPU path's matvec: x (host
    floats, cols) is scaled by 2^k, quantised to q16, multiplied by one model
@@ -155,8 +190,8 @@ VC4_API int vc4_matvec_s(vc4_model* m, int which, int layer, int expert, const f
 VC4_API int vc4_profile_op(vc4_session* s, int op, int layer, int n, const int* slots, const int* tokens,
                            const int* pos, int reps, int flush, double* avg_ms);
 /* Algorithmic bytes one launch of `op` moves for n sequences at the given
-   positions: weights (with scale planes) + KV rows read and written +
-   activations in and out. */
+   positions (sequence i in slot i): weights (with scale planes) + distinct KV
+   rows read (a shared prefix once) and written + activations in and out. */
 VC4_API int vc4_op_bytes(const vc4_session* s, int op, int layer, int n, const int* pos, double* bytes);
 
 /* No counterpart in the reference (a measurement helper for the batch-1
@@ -191,7 +226,13 @@ VC4_API int vc4_kv_codec_probe(int device, int kv_bits, const float* x, int n, v
    VC4_EINVAL.  Nothing is allocated or freed.  The work is queued on `stream`
    (NULL: the model's stream) and the call returns without waiting.  The first
    call on a device looks up the array's device address (cudaGetSymbolAddress)
-   and caches it, so make that first call before any stream capture.  Every
+   and caches it, so make that first call before any stream capture.  Under
+   CUDA's lazy module loading (the default since CUDA 12.2) that first call
+   also loads the library's kernels onto the device, which the driver may pay
+   for with an allocation and a synchronisation of its own: make it during
+   set-up.  The cached address belongs to the device's primary context; after
+   cudaDeviceReset it is stale, so do not call this entry point again in that
+   process.  Every
    call shares the one array, so calls whose work can overlap on the GPU race:
    keep them on one stream. */
 VC4_API int vc4_matvec_s_noalloc(vc4_model* m, int which, int layer, int expert, const float* d_x,

@@ -166,3 +166,118 @@ def test_batch_1024_equals_serial(gpu, tmp_path):
         for k in range(steps):
             lg = one.step(fed[k][s], len(prefix) + k)
             assert np.array_equal(lg, outs[k][s]), "sequence %d step %d" % (s, k)
+
+
+# the sidecar's field set (prefix_cache.cpp:104-128)
+SIDECAR_KEYS = {"format", "version", "source_size", "source_mtime", "dim", "hidden", "layers", "heads", "kv_heads",
+                "vocab", "seq", "head_dim", "rope_theta", "kv_bits", "act_fmt", "hybrid", "kv_scale", "kv_width",
+                "vstep", "n_tokens", "tokens_fnv64", "system_fnv64", "tools_fnv64", "template"}
+
+
+@pytest.mark.gpu
+def test_build_prefix_cache(gpu, tmp_path):
+    """`--build-prefix-cache` for a tokenised prompt (prefix_build.cpp:22-83):
+    the file equals a serial prefill plus save_prefix_cache byte for byte, its
+    rows are the oracle's, the sidecar carries the reference's field set with
+    the container's template name and the FNV-1a hashes, and an empty or too
+    long prompt is refused."""
+    import json
+    from vc4b200.engine import fnv64
+    cfg = synth.CONFIGS["c4"]
+    path = _path("c4")
+    model = vc4b200.Model(gpu, path)
+    prefix = synth.prompt_tokens(cfg)[:40]
+    built = str(tmp_path / "built.mmkv")
+    s = vc4b200.Session(model, slots=2, seq=cfg.seq, kv="q8")
+    system = "You are a helpful assistant."
+    s.build_prefix_cache(built, prefix, slot=1, system=system, tools="[]")
+    saved = str(tmp_path / "saved.mmkv")
+    ref = vc4b200.Session(model, slots=1, seq=cfg.seq, kv="q8")
+    ref.prefill(prefix, 0, want_logits=False)
+    ref.save_prefix_cache(saved, prefix, system_fnv=fnv64(system.encode()), tools_fnv=fnv64(b"[]"))
+    assert open(built, "rb").read() == open(saved, "rb").read()
+    om = oracle.Model(path)
+    os_ = oracle.Session(om, 8)
+    for p, t in enumerate(prefix):
+        os_.step(t, p, want_logits=False)
+    for l in range(om.info.layers):
+        assert s.kv_rows(l, len(prefix), slot=1) == os_.kv_rows(l, len(prefix)), "layer %d" % l
+    meta = json.load(open(built + ".json"))
+    assert set(meta) == SIDECAR_KEYS
+    assert meta["template"] == "plain" and meta["n_tokens"] == len(prefix) and meta["kv_bits"] == 8
+    tok_fnv = fnv64(b"".join(int(t).to_bytes(4, "little") for t in prefix))
+    assert meta["tokens_fnv64"] == "%016x" % tok_fnv
+    assert meta["system_fnv64"] == "%016x" % fnv64(system.encode())
+    assert meta["tools_fnv64"] == "%016x" % fnv64(b"[]")
+    assert json.load(open(saved + ".json")) == meta
+    for bad in ([], list(range(cfg.seq + 1))):
+        with pytest.raises(vc4b200.EngineError):
+            s.build_prefix_cache(str(tmp_path / "bad.mmkv"), bad)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("n", [9, 33])
+def test_shared_prefix_equals_private_restore(gpu, tmp_path, n):
+    """c4 with the prefix held once (vc4_load_prefix_cache_shared) against the
+    same prefix restored into every slot's own rows: logits, greedy tokens
+    and KV rows equal bit for bit (9 slots: cluster attention; 33: the
+    many-sequence kernel, whose 300-row prefix spans three K/V tiles).  Then
+    copy on write: a row write, a host-array step inside the prefix and a
+    prefill over it each give only that slot its own rows; a device-array
+    step inside the prefix is refused through the session's check word."""
+    cfg = synth.CONFIGS["c4"]
+    model = vc4b200.Model(gpu, _path("c4"))
+    prefix = synth.prompt_tokens(cfg)[:300]
+    first = vc4b200.Session(model, slots=64, seq=cfg.seq, kv="q8")
+    first.prefill(prefix, 0, want_logits=False, batched=True)
+    mmkv = str(tmp_path / "prefix.mmkv")
+    first.save_prefix_cache(mmkv, prefix)
+    priv = vc4b200.Session(model, slots=n, seq=cfg.seq, kv="q8")
+    shar = vc4b200.Session(model, slots=n, seq=cfg.seq, kv="q8")
+    for s in range(n):
+        assert priv.load_prefix_cache(mmkv, slot=s) == prefix
+    assert shar.load_prefix_cache_shared(mmkv, list(range(n))) == prefix
+    P = len(prefix)
+    toks = [(prefix[-1] + 97 * s) % cfg.shape.vocab for s in range(n)]
+    pos = P
+    for _ in range(4):
+        na, la = priv.step_batch(list(range(n)), toks, [pos] * n, want_logits=True)
+        nb, lb = shar.step_batch(list(range(n)), toks, [pos] * n, want_logits=True)
+        assert np.array_equal(la, lb) and list(na) == list(nb)
+        toks = [int(t) for t in na]
+        pos += 1
+    L = model.info.layers
+    for s in (0, n - 1):
+        for l in (0, L - 1):
+            assert shar.kv_rows(l, pos, slot=s) == priv.kv_rows(l, pos, slot=s)
+    # a row write into slot 1's prefix: slot 1 alone sees it
+    rb = shar.kv_row_bytes()
+    rows = bytearray(shar.kv_rows(0, 2, slot=1))
+    rows[:rb] = bytes((b + 1) & 0xFF for b in rows[:rb])
+    shar.kv_write(0, 2, bytes(rows), slot=1)
+    assert shar.kv_rows(0, 2, slot=1) == bytes(rows)
+    assert shar.kv_rows(0, P, slot=2) == priv.kv_rows(0, P, slot=2)
+    assert shar.kv_rows(1, pos, slot=1) == priv.kv_rows(1, pos, slot=1)
+    # a host-array step inside slot 2's prefix: the same as in a private slot
+    la = priv.step(prefix[100], 100, slot=2)
+    lb = shar.step(prefix[100], 100, slot=2)
+    assert np.array_equal(la, lb)
+    assert shar.kv_rows(0, P, slot=3) == priv.kv_rows(0, P, slot=3)
+    # a prefill over slot 3's prefix
+    la = priv.prefill(prefix[50:80], 50, slot=3)
+    lb = shar.prefill(prefix[50:80], 50, slot=3)
+    assert np.array_equal(la, lb)
+    for l in (0, L - 1):
+        assert shar.kv_rows(l, pos, slot=3) == priv.kv_rows(l, pos, slot=3)
+    # a device-array step inside slot 4's prefix is refused, its row unwritten
+    import torch
+    d_slots = torch.tensor([4], dtype=torch.int32, device="cuda")
+    d_tok = torch.tensor([prefix[10]], dtype=torch.int32, device="cuda")
+    d_pos = torch.tensor([10], dtype=torch.int32, device="cuda")
+    d_next = torch.zeros(1, dtype=torch.int32, device="cuda")
+    before = shar.kv_rows(0, P, slot=4)
+    with pytest.raises(vc4b200.EngineError, match="shared prefix"):
+        # the first pass of a shape checks the word itself; a replay would at check()
+        shar.step_batch_device(1, d_slots.data_ptr(), d_tok.data_ptr(), d_pos.data_ptr(), d_next.data_ptr(), False)
+        shar.check()
+    assert shar.kv_rows(0, P, slot=4) == before

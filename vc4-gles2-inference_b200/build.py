@@ -56,10 +56,13 @@ def build(force: bool = False, verbose: bool = False) -> str:
         for f in [ex.submit(subprocess.run, cmd, check=True) for cmd in cmds]:
             f.result()
     if force or _newer(OUT, objs):
-        cmd = [NVCC] + ARCH + ["-shared", "-o", OUT] + objs
+        # link next to the target and rename, so a reader never sees a partial file
+        tmp = OUT + ".%d.tmp" % os.getpid()
+        cmd = [NVCC] + ARCH + ["-shared", "-o", tmp] + objs
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)
+        os.replace(tmp, OUT)
     return OUT
 
 

@@ -59,9 +59,10 @@ struct vc4_model {
 // One decode pass's device arguments; a captured graph is keyed by them.
 struct PassArgs {
     int n; const int* slots; int* tokens; int* pos; int* next; int advance; const int* forced;
+    int prefill = 0;   // the entries are positions of one sequence: attention appends, then attends
     bool operator<(const PassArgs& o) const {
-        return std::tie(n, slots, tokens, pos, next, advance, forced) <
-               std::tie(o.n, o.slots, o.tokens, o.pos, o.next, o.advance, o.forced);
+        return std::tie(n, slots, tokens, pos, next, advance, forced, prefill) <
+               std::tie(o.n, o.slots, o.tokens, o.pos, o.next, o.advance, o.forced, o.prefill);
     }
 };
 
@@ -76,6 +77,7 @@ struct vc4_session {
     long long launches = 0, syncs = 0;
     cudaStream_t stream = nullptr;
     void* ops = nullptr;                      // buffers of the per-op calls (ops.cu), made on first use
+    std::vector<int> plen;                    // host mirror of st.plen (shared-prefix rows per slot)
 };
 
 // ---------------------------------------------------------------------------
@@ -280,7 +282,12 @@ void enqueue_pass(vc4_session* s, const PassArgs& a, cudaStream_t st) {
     b.n = a.n; b.slot = a.slots; b.token = a.tokens; b.pos = a.pos;
     for (int l = 0; l < m.h.layers; ++l) {
         launch_embed_qkv(m, s->st, b, l, st);
-        launch_attention(m, s->st, b, l, st);
+        if (a.prefill) {
+            launch_attention(m, s->st, b, l, st, 1);   // every position's K/V row first,
+            launch_attention(m, s->st, b, l, st, 2);   // then attention over the whole prefix
+        } else {
+            launch_attention(m, s->st, b, l, st);
+        }
         launch_wo(m, s->st, b, l, st);
         launch_ffn_gate(m, s->st, b, l, st);   // gate/up, SwiGLU and the w2 partial sums
     }
@@ -298,6 +305,9 @@ static int check_kernel_word(vc4_session* s) {
     if (w > 0) return fail(VC4_ECUDA, "a kernel found its shared-memory reservation too small (needs " + std::to_string(w) + " bytes)");
     if (w == -2) return fail(VC4_ECUDA, "a kernel's bulk copy did not complete within its time limit");
     if (w == -3) return fail(VC4_ECUDA, "a tensor-core matmat was launched with a copy ring or box plan it cannot run");
+    if (w == -5)
+        return fail(VC4_ESTATE, "a decode step appended at a position the slot's shared prefix serves (those rows are "
+                                "read-only; the row was not written)");
     if (w == -4)
         return fail(VC4_ERANGE, "an FFN hidden value reached 64 or more: the w2 input scale of the host FFN would "
                                 "round its input, which this engine does not compute (the session's results are void)");
@@ -327,7 +337,7 @@ static int run_pass(vc4_session* s, const PassArgs& a) {
         if (e != cudaSuccess) return fail(VC4_ECUDA, std::string("cudaGraphInstantiate: ") + cudaGetErrorString(e));
         tab[a] = ex;
     }
-    s->launches += kernel_launches_per_step(s->m->d, s->st, a.n);
+    s->launches += kernel_launches_per_step(s->m->d, s->st, a.n) + (a.prefill ? s->m->d.h.layers : 0);
     return VC4_OK;
 }
 
@@ -479,9 +489,11 @@ int vc4_session_create(vc4_model* m, int slots, int seq, int kv_bits, const floa
               alloc((void**)&s->d_pos, (size_t)seq * 4 + 16) && alloc((void**)&st.done, 16) && alloc((void**)&st.err, 16) &&
               alloc((void**)&st.sdown, (size_t)L * slots * 2 * D * 8) &&
               alloc((void**)&st.hmax, (size_t)L * slots * 2 * 4) &&
+              alloc((void**)&st.plen, (size_t)slots * 4) &&
               alloc((void**)&st.xrec, (size_t)slots * batch_record_bytes(m->d)) &&
               alloc((void**)&st.hrec, (size_t)slots * batch_hidden_bytes(m->d));
     st.batch_ok = batch_path_fits(m->d, slots) ? 1 : 0;
+    s->plen.assign(slots, 0);
     if (!ok) { vc4_session_destroy(s); return fail(VC4_ECUDA, "session allocation failed (slots*seq too large?)"); }
     s->d_tok = s->d_slot + slots;
     if (cudaMallocHost((void**)&s->h_pin, (size_t)(5 * slots + 16) * 4) != cudaSuccess ||
@@ -518,7 +530,7 @@ void vc4_session_destroy(vc4_session* s) {
     for (void* p : {(void*)st.x, (void*)st.x1, (void*)st.qkv, (void*)st.att, (void*)st.h, (void*)st.logits,
                     (void*)st.best, (void*)st.next, (void*)st.route, (void*)st.kv, (void*)st.rope_cos,
                     (void*)st.rope_sin, (void*)s->d_slot, (void*)s->d_next, (void*)s->d_pos, (void*)st.done, (void*)st.err,
-                    (void*)st.sdown, (void*)st.hmax, (void*)st.xrec, (void*)st.hrec})
+                    (void*)st.sdown, (void*)st.hmax, (void*)st.xrec, (void*)st.hrec, (void*)st.plen, (void*)st.pkv})
         if (p) cudaFree(p);
     if (s->h_pin) cudaFreeHost(s->h_pin);
     if (s->h_logits) cudaFreeHost(s->h_logits);
@@ -551,6 +563,8 @@ static int host_step(vc4_session* s, int n, const int* slots, const int* tokens,
         if (seen[slots[i]]++) return fail(VC4_EINVAL, "a slot appears twice in one batch");
     }
     CK(cudaSetDevice(s->m->d.device));
+    for (int i = 0; i < n; ++i)
+        if (int e = session_unshare(s, slots[i], pos[i])) return e;
     int* hp = s->h_pin;
     for (int i = 0; i < n; ++i) { hp[i] = slots[i]; hp[n + i] = tokens[i]; hp[2 * n + i] = pos[i]; }
     int* dcall = s->d_slot;   // [slots | tokens | pos] for this n
@@ -600,6 +614,7 @@ int vc4_prefill(vc4_session* s, int slot, const int* tokens, int n, int pos0, fl
     for (int i = 0; i < n; ++i)
         if (tokens[i] < 0 || tokens[i] >= V) return fail(VC4_EINVAL, "token id out of range");
     CK(cudaSetDevice(s->m->d.device));
+    if (int e = session_unshare(s, slot, pos0)) return e;
     // prompt[p] at absolute position p; the pass replays with `forced` so each
     // replay moves to the next prompt token on the device.
     std::vector<int> prompt(s->st.seq + 1, 0);
@@ -622,10 +637,86 @@ int vc4_prefill(vc4_session* s, int slot, const int* tokens, int n, int pos0, fl
     return VC4_OK;
 }
 
+// Batched prefill: up to `slots` positions of the prompt per pass, as one
+// batch of the many-sequence path (tensor-core matmats for q8 and t3) whose
+// entries are (slot, prompt[i], pos0 + i).  Every sum of the pass is exact,
+// so each position's results, and the K/V rows it appends, are the serial
+// loop's bit for bit.  A chunk too small for the many-sequence kernels runs
+// through the serial loop.
+constexpr int kPrefillBatchMin = 16;
+
+// The batched prefill; with `all` set, every position's logits go to
+// all[i*vocab ..] (positions of a serial tail are stepped one at a time).
+static int prefill_batched(vc4_session* s, int slot, const int* tokens, int n, int pos0, float* logits, float* all) {
+    if (n <= 0) return fail(VC4_EINVAL, "empty prompt");
+    if (int e = check_slot_pos(s, slot, pos0)) return e;
+    if (pos0 + n > s->st.seq) return fail(VC4_EINVAL, "prompt runs past the sequence length");
+    const DModel& m = s->m->d;
+    const int V = m.h.vocab;
+    for (int i = 0; i < n; ++i)
+        if (tokens[i] < 0 || tokens[i] >= V) return fail(VC4_EINVAL, "token id out of range");
+    CK(cudaSetDevice(m.device));
+    if (int e = session_unshare(s, slot, pos0)) return e;
+    const bool can = s->st.batch_ok && prefill_attention_fits(m, s->st);
+    int done = 0, last = 0;   // last: the batch size of the pass that held the final position (0: serial)
+    while (done < n) {
+        const int c = std::min(n - done, s->slots);
+        if (!can || c < kPrefillBatchMin) {
+            if (all) {
+                for (int i = done; i < n; ++i) {
+                    const int p = pos0 + i;
+                    if (int e = host_step(s, 1, &slot, tokens + i, &p, nullptr, all + (size_t)i * V)) return e;
+                }
+                if (logits) memcpy(logits, all + (size_t)(n - 1) * V, sizeof(float) * V);
+                return VC4_OK;
+            }
+            if (int e = vc4_prefill(s, slot, tokens + done, n - done, pos0 + done, nullptr)) return e;
+            last = 0;
+            break;
+        }
+        int* hp = s->h_pin;
+        for (int i = 0; i < c; ++i) { hp[i] = slot; hp[c + i] = tokens[done + i]; hp[2 * c + i] = pos0 + done + i; }
+        int* dcall = s->d_slot;   // [slots | tokens | pos] of this chunk
+        CK(cudaMemcpyAsync(dcall, hp, sizeof(int) * 3 * c, cudaMemcpyHostToDevice, s->stream));
+        PassArgs a{c, dcall, dcall + c, dcall + 2 * c, s->d_next, 0, nullptr, 1};
+        if (int e = run_pass(s, a)) return e;
+        if (all) {
+            int32_t* hl = s->h_logits;   // pinned, slots x vocab
+            CK(cudaMemcpyAsync(hl, s->st.logits, sizeof(int32_t) * (size_t)c * V, cudaMemcpyDeviceToHost, s->stream));
+            CK(cudaStreamSynchronize(s->stream));
+            if (int e = check_kernel_word(s)) return e;
+            for (size_t i = 0; i < (size_t)c * V; ++i) all[(size_t)done * V + i] = (float)hl[i] / 256.0f;
+        }
+        CK(cudaStreamSynchronize(s->stream));   // the pinned staging is reused by the next chunk
+        s->syncs++;
+        done += c;
+        last = c;
+    }
+    const int32_t* src = last ? s->st.logits + (size_t)(last - 1) * V : s->st.logits;
+    if (logits) CK(cudaMemcpyAsync(s->h_logits, src, sizeof(int32_t) * V, cudaMemcpyDeviceToHost, s->stream));
+    CK(cudaStreamSynchronize(s->stream));
+    if (int e = check_kernel_word(s)) return e;
+    if (logits) for (int i = 0; i < V; ++i) logits[i] = (float)s->h_logits[i] / 256.0f;
+    return VC4_OK;
+}
+
+int vc4_prefill_batch(vc4_session* s, int slot, const int* tokens, int n, int pos0, float* logits) {
+    return prefill_batched(s, slot, tokens, n, pos0, logits, nullptr);
+}
+
+int vc4_prefill_logits(vc4_session* s, int slot, const int* tokens, int n, int pos0, float* logits_all) {
+    if (!logits_all) return fail(VC4_EINVAL, "logits_all is required");
+    return prefill_batched(s, slot, tokens, n, pos0, nullptr, logits_all);
+}
+
 int vc4_kv_row_bytes(const vc4_session* s) { return s->st.row_bytes; }
 
 static uint8_t* kv_rows_ptr(vc4_session* s, int slot, int layer) {
     return s->st.kv + ((size_t)slot * s->m->d.h.layers + layer) * s->st.seq * s->st.row_bytes;
+}
+
+static uint8_t* prefix_rows_ptr(vc4_session* s, int layer) {
+    return s->st.pkv + (size_t)layer * s->st.pcap * s->st.row_bytes;
 }
 
 int vc4_kv_read_rows(vc4_session* s, int slot, int layer, int n, void* out) {
@@ -633,7 +724,12 @@ int vc4_kv_read_rows(vc4_session* s, int slot, int layer, int n, void* out) {
         return fail(VC4_EINVAL, "kv read out of range");
     CK(cudaSetDevice(s->m->d.device));
     CK(cudaStreamSynchronize(s->stream));
-    CK(cudaMemcpy(out, kv_rows_ptr(s, slot, layer), (size_t)n * s->st.row_bytes, cudaMemcpyDeviceToHost));
+    // rows below the slot's shared-prefix length come from the shared prefix
+    const size_t rb = s->st.row_bytes, shared = (size_t)std::min(n, s->plen[slot]);
+    if (shared) CK(cudaMemcpy(out, prefix_rows_ptr(s, layer), shared * rb, cudaMemcpyDeviceToHost));
+    if ((size_t)n > shared)
+        CK(cudaMemcpy((uint8_t*)out + shared * rb, kv_rows_ptr(s, slot, layer) + shared * rb, (n - shared) * rb,
+                      cudaMemcpyDeviceToHost));
     s->syncs++;
     return VC4_OK;
 }
@@ -642,6 +738,8 @@ int vc4_kv_write_rows(vc4_session* s, int slot, int layer, int n, const void* in
     if (slot < 0 || slot >= s->slots || layer < 0 || layer >= s->m->d.h.layers || n < 0 || n > s->st.seq)
         return fail(VC4_EINVAL, "kv write out of range");
     CK(cudaSetDevice(s->m->d.device));
+    if (n > 0)
+        if (int e = session_unshare(s, slot, 0)) return e;
     CK(cudaStreamSynchronize(s->stream));
     CK(cudaMemcpy(kv_rows_ptr(s, slot, layer), in, (size_t)n * s->st.row_bytes, cudaMemcpyHostToDevice));
     s->syncs++;
@@ -721,6 +819,18 @@ uint32_t mmkv_flags(const vc4_session* s) {
     return (h.qk_norm ? 1u : 0u) | (h.rope_half ? 2u : 0u) | (s->st.kv_bits == 16 ? 4u : 8u);
 }
 float kv_scale_of(const vc4_session* s) { return s->st.kv_bits == 16 ? 2048.0f : 16.0f; }
+// A JSON string body: quote, backslash and control bytes escaped; other bytes
+// (UTF-8 included) pass through.
+std::string json_escape(const std::string& t) {
+    std::string o;
+    for (unsigned char c : t) {
+        if (c == '"' || c == '\\') { o += '\\'; o += (char)c; }
+        else if (c == '\n') o += "\\n";
+        else if (c < 0x20) { char b[8]; snprintf(b, sizeof(b), "\\u%04x", c); o += b; }
+        else o += (char)c;
+    }
+    return o;
+}
 uint32_t kv_width_of(const vc4_session* s) {
     const HModel& h = s->m->d.h;
     return (uint32_t)(s->st.kv_bits == 16 ? h.kv_dim : h.kv_dim / 2);
@@ -771,19 +881,87 @@ extern "C" int vc4_save_prefix_cache(vc4_session* s, int slot, const char* path,
                 "\"hidden\":%d,\"layers\":%d,\"heads\":%d,\"kv_heads\":%d,\"vocab\":%d,\"seq\":%d,\"head_dim\":%d,"
                 "\"rope_theta\":%.9g,\"kv_bits\":%d,\"act_fmt\":\"x16_2\",\"hybrid\":false,\"kv_scale\":%.9g,"
                 "\"kv_width\":%u,\"vstep\":0,\"n_tokens\":%d,\"tokens_fnv64\":\"%016llx\",\"system_fnv64\":\"%016llx\","
-                "\"tools_fnv64\":\"%016llx\"}\n",
+                "\"tools_fnv64\":\"%016llx\",\"template\":\"%s\"}\n",
                 (unsigned long long)h.source_size, (unsigned long long)h.source_mtime, h.dim, h.hidden, h.layers,
                 h.heads, h.kv_heads, h.vocab, s->st.seq, h.head_dim, (double)h.rope_theta, s->st.kv_bits, (double)ks,
                 kv_width_of(s), n, (unsigned long long)fnv, (unsigned long long)system_fnv,
-                (unsigned long long)tools_fnv);
+                (unsigned long long)tools_fnv, json_escape(h.template_name).c_str());
         fclose(j);
     }
     return VC4_OK;
 }
 
-extern "C" int vc4_load_prefix_cache(vc4_session* s, int slot, const char* path, int* toks_out, int cap, int* n_out) {
+static int read_mmkv(vc4_session* s, const char* path, std::vector<uint32_t>& toks, std::vector<uint8_t>& all);
+
+// Copy on write: a slot whose shared prefix covers `pos` gets the prefix rows
+// in its own cache rows (every layer) and stops reading the shared copy.
+int vc4::session_unshare(vc4_session* s, int slot, int pos) {
+    const int pl = s->plen[slot];
+    if (pl == 0 || pos >= pl) return VC4_OK;
+    const size_t rb = s->st.row_bytes;
+    for (int l = 0; l < s->m->d.h.layers; ++l)
+        CK(cudaMemcpyAsync(kv_rows_ptr(s, slot, l), prefix_rows_ptr(s, l), (size_t)pl * rb, cudaMemcpyDeviceToDevice,
+                           s->stream));
+    CK(cudaMemsetAsync(s->st.plen + slot, 0, sizeof(int), s->stream));
+    s->plen[slot] = 0;
+    return VC4_OK;
+}
+
+extern "C" int vc4_load_prefix_cache_shared(vc4_session* s, const char* path, const int* slots, int count,
+                                            int* toks_out, int cap, int* n_out) {
     const HModel& h = s->m->d.h;
-    if (slot < 0 || slot >= s->slots) return fail(VC4_EINVAL, "slot out of range");
+    if (count <= 0 || count > s->slots) return fail(VC4_EINVAL, "slot count out of range");
+    std::vector<char> listed(s->slots, 0);
+    for (int i = 0; i < count; ++i) {
+        if (slots[i] < 0 || slots[i] >= s->slots) return fail(VC4_EINVAL, "slot out of range");
+        if (listed[slots[i]]++) return fail(VC4_EINVAL, "a slot appears twice");
+    }
+    std::vector<uint32_t> toks;
+    std::vector<uint8_t> rows;
+    if (int e = read_mmkv(s, path, toks, rows)) return e;
+    const int n = (int)toks.size();
+    if (n > cap) return fail(VC4_EINVAL, "token buffer too small for the cache");
+    CK(cudaSetDevice(s->m->d.device));
+    // slots still reading the previous shared prefix keep it as their own rows
+    for (int i = 0; i < s->slots; ++i)
+        if (s->plen[i] && !listed[i])
+            if (int e = session_unshare(s, i, 0)) return e;
+    CK(cudaStreamSynchronize(s->stream));
+    if (s->st.pcap < n) {
+        // the kernels of captured passes hold the State by value: drop them
+        for (auto& kv : s->graphs) cudaGraphExecDestroy(kv.second);
+        s->graphs.clear();
+        if (s->st.pkv) cudaFree(s->st.pkv);
+        s->st.pkv = nullptr;
+        s->st.pcap = 0;
+        CK(cudaMalloc((void**)&s->st.pkv, (size_t)h.layers * s->st.seq * s->st.row_bytes));
+        s->st.pcap = s->st.seq;
+    }
+    const size_t lb = (size_t)n * s->st.row_bytes;
+    for (int l = 0; l < h.layers; ++l)
+        CK(cudaMemcpy(prefix_rows_ptr(s, l), rows.data() + l * lb, lb, cudaMemcpyHostToDevice));
+    std::vector<int> pl(s->plen);
+    for (int i = 0; i < count; ++i) pl[slots[i]] = n;
+    CK(cudaMemcpy(s->st.plen, pl.data(), sizeof(int) * s->slots, cudaMemcpyHostToDevice));
+    s->plen = pl;
+    for (int i = 0; i < n; ++i) toks_out[i] = (int)toks[i];
+    *n_out = n;
+    return VC4_OK;
+}
+
+extern "C" int vc4_build_prefix_cache(vc4_session* s, int slot, const int* toks, int n, const char* path,
+                                      uint64_t system_fnv, uint64_t tools_fnv) {
+    // prefix_build.cpp:66-83: refuse an empty or too long prompt, prefill it
+    // from position 0 with the serial loop, then write the file and sidecar
+    if (n <= 0 || n > s->st.seq) return fail(VC4_EINVAL, "cache prompt empty or too long (" + std::to_string(n) + ")");
+    if (int e = vc4_prefill(s, slot, toks, n, 0, nullptr)) return e;
+    return vc4_save_prefix_cache(s, slot, path, toks, n, system_fnv, tools_fnv);
+}
+
+// Read and validate an MMKV1 file (prefix_cache.cpp:135-207): the token list
+// and every layer's rows, layer after layer.
+static int read_mmkv(vc4_session* s, const char* path, std::vector<uint32_t>& toks, std::vector<uint8_t>& all) {
+    const HModel& h = s->m->d.h;
     FILE* f = fopen(path, "rb");
     if (!f) return fail(VC4_EIO, std::string("cannot read ") + path);
     auto rd = [&](void* p, size_t k) { return fread(p, 1, k, f) == k; };
@@ -806,17 +984,26 @@ extern "C" int vc4_load_prefix_cache(vc4_session* s, int slot, const char* path,
         fclose(f);
         return fail(VC4_ESTATE, "prefix cache does not match this model, sequence length or KV axis");
     }
-    if ((int)n > cap) { fclose(f); return fail(VC4_EINVAL, "token buffer too small for the cache"); }
-    std::vector<uint32_t> t(n);
-    std::vector<uint8_t> rows((size_t)n * s->st.row_bytes);
-    if (!rd(t.data(), 4 * (size_t)n)) { fclose(f); return fail(VC4_EIO, "truncated prefix cache"); }
-    for (int l = 0; l < h.layers; ++l) {
-        if (!rd(rows.data(), rows.size())) { fclose(f); return fail(VC4_EIO, "truncated prefix cache"); }
-        if (int e = vc4_kv_write_rows(s, slot, l, (int)n, rows.data())) { fclose(f); return e; }
-    }
+    toks.assign(n, 0);
+    all.assign((size_t)h.layers * n * s->st.row_bytes, 0);
+    const bool got = rd(toks.data(), 4 * (size_t)n) && rd(all.data(), all.size());
     fclose(f);
-    for (uint32_t i = 0; i < n; ++i) toks_out[i] = (int)t[i];
-    *n_out = (int)n;
+    if (!got) return fail(VC4_EIO, "truncated prefix cache");
+    return VC4_OK;
+}
+
+extern "C" int vc4_load_prefix_cache(vc4_session* s, int slot, const char* path, int* toks_out, int cap, int* n_out) {
+    if (slot < 0 || slot >= s->slots) return fail(VC4_EINVAL, "slot out of range");
+    std::vector<uint32_t> t;
+    std::vector<uint8_t> rows;
+    if (int e = read_mmkv(s, path, t, rows)) return e;
+    const int n = (int)t.size();
+    if (n > cap) return fail(VC4_EINVAL, "token buffer too small for the cache");
+    const size_t lb = (size_t)n * s->st.row_bytes;
+    for (int l = 0; l < s->m->d.h.layers; ++l)
+        if (int e = vc4_kv_write_rows(s, slot, l, n, rows.data() + l * lb)) return e;
+    for (int i = 0; i < n; ++i) toks_out[i] = (int)t[i];
+    *n_out = n;
     return VC4_OK;
 }
 
@@ -900,8 +1087,15 @@ extern "C" int vc4_op_bytes(const vc4_session* s, int op, int layer, int n, cons
     switch (op) {
         case 0: b = wbytes(m.qkv[layer]) + n * (2 * D + 4 * Q); break;
         case 1: {
+            // distinct cache rows read: a shared prefix counts once
             double kv = 0.0;
-            for (int i = 0; i < n; ++i) kv += (double)(pos[i] + 1) * s->st.row_bytes;
+            int shared = 0;
+            for (int i = 0; i < n; ++i) {
+                const int pl = std::min(s->plen[std::min(i, s->slots - 1)], pos[i] + 1);
+                kv += (double)(pos[i] + 1 - pl) * s->st.row_bytes;
+                shared = std::max(shared, pl);
+            }
+            kv += (double)shared * s->st.row_bytes;
             b = kv + n * (4 * Q + 2 * D + s->st.row_bytes);
             break;
         }

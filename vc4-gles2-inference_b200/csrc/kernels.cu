@@ -87,29 +87,37 @@ constexpr int kAttnBatchUnits = 128;
 
 template <int KVB, int HQ>
 static void launch_attn_b(const DModel& m, const State& s, const Batch& b, const Dims& d, int layer, size_t smb,
-                          cudaStream_t st) {
+                          int mode, cudaStream_t st) {
     const int group = d.heads / d.kv_heads;
     const dim3 grid(d.kv_heads * (group / HQ), b.n);
     const float *qn = m.d_q_norm, *kn = m.d_k_norm;
-    if (d.head_dim == 96) launch_pdl(k_attn_b<KVB, HQ, 96>, grid, smb, st, qn, kn, s, b, d, layer);
-    else if (d.head_dim == 64) launch_pdl(k_attn_b<KVB, HQ, 64>, grid, smb, st, qn, kn, s, b, d, layer);
-    else launch_pdl(k_attn_b<KVB, HQ, 128>, grid, smb, st, qn, kn, s, b, d, layer);
+    if (d.head_dim == 96) launch_pdl(k_attn_b<KVB, HQ, 96>, grid, smb, st, qn, kn, s, b, d, layer, mode);
+    else if (d.head_dim == 64) launch_pdl(k_attn_b<KVB, HQ, 64>, grid, smb, st, qn, kn, s, b, d, layer, mode);
+    else launch_pdl(k_attn_b<KVB, HQ, 128>, grid, smb, st, qn, kn, s, b, d, layer, mode);
 }
 
-void launch_attention(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st) {
+bool prefill_attention_fits(const DModel& m, const State& s) {
+    const int group = m.h.heads / m.h.kv_heads;
+    const bool hd_ok = m.h.head_dim == 64 || m.h.head_dim == 96 || m.h.head_dim == 128;
+    return hd_ok && attnb_smem_bytes(attn_heads_per_cluster(group), m.h.head_dim, s.seq, s.kv_bits) <= kMaxDynSmem;
+}
+
+void launch_attention(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st, int mode) {
     Dims d = dims_of(m, s);
     const int group = d.heads / d.kv_heads, hq = attn_heads_per_cluster(group);
     const int units = b.n * d.kv_heads * (group / hq);
     const size_t smb = attnb_smem_bytes(hq, d.head_dim, d.seq, d.kv_bits);
-    // the many-sequence kernel is instantiated for head sizes 64, 96 and 128
+    // the many-sequence kernel is instantiated for head sizes 64, 96 and 128;
+    // a prefill's append / attend launches (mode 1, 2) always take it (the
+    // caller checked prefill_attention_fits)
     const bool hd_ok = d.head_dim == 64 || d.head_dim == 96 || d.head_dim == 128;
-    if (units >= kAttnBatchUnits && smb <= kMaxDynSmem && hd_ok) {
+    if ((units >= kAttnBatchUnits || mode) && smb <= kMaxDynSmem && hd_ok) {
         if (d.kv_bits == 8) {
-            if (hq == 2) launch_attn_b<1, 2>(m, s, b, d, layer, smb, st);
-            else launch_attn_b<1, 1>(m, s, b, d, layer, smb, st);
+            if (hq == 2) launch_attn_b<1, 2>(m, s, b, d, layer, smb, mode, st);
+            else launch_attn_b<1, 1>(m, s, b, d, layer, smb, mode, st);
         } else {
-            if (hq == 2) launch_attn_b<2, 2>(m, s, b, d, layer, smb, st);
-            else launch_attn_b<2, 1>(m, s, b, d, layer, smb, st);
+            if (hq == 2) launch_attn_b<2, 2>(m, s, b, d, layer, smb, mode, st);
+            else launch_attn_b<2, 1>(m, s, b, d, layer, smb, mode, st);
         }
         return;
     }

@@ -558,6 +558,27 @@ struct Dims {
     float eps;
 };
 
+// The cache rows of (slot, layer): a position below the slot's shared-prefix
+// length is a row of the session's shared prefix, any other its own row.
+struct KvRows {
+    uint8_t* own;
+    const uint8_t* shared;
+    int plen;
+    __device__ __forceinline__ const uint8_t* at(int t, int row_bytes) const {
+        return (t < plen ? shared : own) + (size_t)t * row_bytes;
+    }
+};
+__device__ __forceinline__ KvRows kv_rows_of(const State& s, int slot, int layer, int layers, int seq, int row_bytes) {
+    KvRows r;
+    r.own = s.kv + ((size_t)slot * layers + layer) * seq * row_bytes;
+    r.plen = s.plen ? __ldg(s.plen + slot) : 0;
+    r.shared = s.pkv ? s.pkv + (size_t)layer * s.pcap * row_bytes : r.own;
+    return r;
+}
+// An append at a position the shared prefix serves: recorded in the error
+// word (the host reports it) and not written.
+constexpr int kErrSharedAppend = -5;
+
 Dims dims_of(const DModel& m, const State& s) {
     Dims d;
     d.dim = m.h.dim; d.kv_dim = m.h.kv_dim; d.heads = m.h.heads; d.kv_heads = m.h.kv_heads;
@@ -1711,20 +1732,19 @@ k_attn(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int 
     const int vs = attn_vs(hd), c0 = min(hd, rank * vs), c1 = min(hd, c0 + vs), nc = c1 - c0;
     const int vrow = vs * kvb;                    // staged bytes per position of the V slice
     const int vpw = 4 / kvb;                      // values per 32-bit word
-    uint8_t* kvbase = s.kv + ((size_t)slot * d.layers + layer) * d.seq * d.row_bytes;
+    const KvRows kr = kv_rows_of(s, slot, layer, d.layers, d.seq, d.row_bytes);
 
     // 1. stage and decode the cached rows (every position but `pos`, which
     //    this step writes), the RoPE row and the norm weights
     const int kvec = hbytes / 16;
     for (int v = threadIdx.x; v < nt * kvec; v += kThreads) {
         const int r = v / kvec, c = v % kvec, t = t0 + r;
-        if (t != pos) cp_async16(sm.kraw + r * hbytes + c * 16, kvbase + (size_t)t * d.row_bytes + g * hbytes + c * 16);
+        if (t != pos) cp_async16(sm.kraw + r * hbytes + c * 16, kr.at(t, d.row_bytes) + g * hbytes + c * 16);
     }
     const int vw = nc * kvb / 4;                  // words per position of the V slice
     for (int v = threadIdx.x; v < pos * vw; v += kThreads) {
         const int t = v / vw, c = v % vw;
-        cp_async4(sm.vraw + (size_t)t * vrow + c * 4,
-                  kvbase + (size_t)t * d.row_bytes + vofs + g * hbytes + c0 * kvb + c * 4);
+        cp_async4(sm.vraw + (size_t)t * vrow + c * 4, kr.at(t, d.row_bytes) + vofs + g * hbytes + c0 * kvb + c * 4);
     }
     for (int i = threadIdx.x; i < half; i += kThreads) {
         sm.rc[i] = s.rope_cos[(size_t)pos * half + i];
@@ -1793,8 +1813,9 @@ k_attn(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int 
     //    every CTA encodes it identically, the one whose share holds `pos`
     //    writes it to the cache (the first split of the KV head)
     const bool owner = pos >= t0 && pos < t1;
-    const bool writer = owner && split == 0;
-    uint8_t* row = kvbase + (size_t)pos * d.row_bytes;
+    const bool writer = owner && split == 0 && pos >= kr.plen;
+    if (owner && split == 0 && pos < kr.plen && threadIdx.x == 0) atomicMin(s.err, kErrSharedAppend);
+    uint8_t* row = kr.own + (size_t)pos * d.row_bytes;
     for (int e = threadIdx.x; e < 2 * kw; e += kThreads) {
         const int w = e / kw, c = e % kw, i0 = c * vpw;
         const float* src = w ? sm.vn : sm.q + hq * hd;
@@ -2002,9 +2023,14 @@ __device__ __forceinline__ void mma_i8(int (&d)[4], const unsigned (&a)[4], unsi
 }
 
 // HD: the head size (a multiple of 32, at most 128); HQ: q heads per CTA (1 or 2).
+// mode 0 (decode): append this step's K/V row, then attend.  A batched prefill
+// holds several positions of one sequence in one pass, where a CTA's cache
+// reads would race with the rows the other positions' CTAs append; it runs
+// the kernel twice: mode 1 appends every row and returns, mode 2 (the next
+// launch, so every row is in the cache) attends without writing.
 template <int KVB, int HQ, int HD>
 __global__ void __launch_bounds__(kThreads, KVB == 1 && HD <= 96 ? 3 : 2)
-k_attn_b(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int layer) {
+k_attn_b(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int layer, int mode) {
     static_assert(HD % 32 == 0 && HD <= 128 && (HQ == 1 || HQ == 2), "k_attn_b shape");
     extern __shared__ __align__(16) char smem[];
     constexpr int hq = HQ, hd = HD, half = HD / 2, hbytes = HD * KVB, kw = hbytes / 4, kvec = hbytes / 16;
@@ -2017,25 +2043,28 @@ k_attn_b(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, in
     const int h0 = split * hq, b = blockIdx.y;
     const int slot = bt.slot[b], pos = bt.pos[b], len = pos + 1;
     const int vofs = d.kv_dim * KVB, pitch = attnb_pitch(hbytes), epitch = attnb_epitch(d.seq);
-    const int ntile = (len + kAbRows - 1) / kAbRows;
-    const uint8_t* kvrd = s.kv + ((size_t)slot * d.layers + layer) * d.seq * d.row_bytes + g * hbytes;
+    const int ntile = mode == 1 ? 0 : (len + kAbRows - 1) / kAbRows;   // an append launch reads no tile
+    const KvRows kr = kv_rows_of(s, slot, layer, d.layers, d.seq, d.row_bytes);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gq = lane >> 2, tq = lane & 3;
     // tile u < ntile: K rows of positions [u*R, ...); ntile <= u < 2*ntile: V rows.
     // Thread (row r0, 16-byte column cc) copies rows r0, r0 + rpp, ...
     const int rpp = kThreads / kvec, cc = threadIdx.x % kvec, r0 = threadIdx.x / kvec;
-    const size_t rstep = (size_t)rpp * d.row_bytes;
     auto issue = [&](int u) {
         if (u < 2 * ntile && r0 < rpp) {
             const int kind = u >= ntile, t0 = (u % ntile) * kAbRows, nt = min(kAbRows, len - t0);
             uint8_t* dst = sm.ring + (size_t)(u % kAbStages) * kAbRows * pitch + cc * 16 + r0 * pitch;
-            const uint8_t* src = kvrd + (kind ? vofs : 0) + cc * 16 + (size_t)(t0 + r0) * d.row_bytes;
-            for (int r = r0; r < nt; r += rpp, dst += rpp * pitch, src += rstep)
-                if (t0 + r != pos) cp_async16(dst, src);
+            const int cofs = (kind ? vofs : 0) + g * hbytes + cc * 16;
+            for (int r = r0; r < nt; r += rpp, dst += rpp * pitch)
+                if (t0 + r != pos) cp_async16(dst, kr.at(t0 + r, d.row_bytes) + cofs);
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
+    // the first tiles' copies go out before the grid-dependency wait, except
+    // in an attend launch, whose rows the append launch just before it wrote
+    if (mode != 2) {
 #pragma unroll
-    for (int u = 0; u < kAbStages - 1; ++u) issue(u);
+        for (int u = 0; u < kAbStages - 1; ++u) issue(u);
+    }
     for (int i = threadIdx.x; i < half; i += kThreads) {
         sm.rc[i] = s.rope_cos[(size_t)pos * half + i];
         sm.rsn[i] = s.rope_sin[(size_t)pos * half + i];
@@ -2051,6 +2080,10 @@ k_attn_b(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, in
     for (int i = threadIdx.x; i < 8 * hd / 16; i += kThreads) reinterpret_cast<int4*>(sm.qb)[i] = make_int4(0, 0, 0, 0);
     pdl_launch_dependents();
     pdl_wait();
+    if (mode == 2) {
+#pragma unroll
+        for (int u = 0; u < kAbStages - 1; ++u) issue(u);
+    }
 
     // q heads, new k and v, qk-norm and RoPE (as the cluster kernel)
     const float* qkv = s.qkv + (size_t)b * (d.dim + 2 * d.kv_dim);
@@ -2082,16 +2115,19 @@ k_attn_b(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, in
     __syncthreads();
     // encode the new row; the first q-head split's CTA writes it to the cache,
     // every CTA keeps its bytes for position `pos`
-    uint8_t* row = s.kv + ((size_t)slot * d.layers + layer) * d.seq * d.row_bytes + (size_t)pos * d.row_bytes + g * hbytes;
+    uint8_t* row = kr.own + (size_t)pos * d.row_bytes + g * hbytes;
+    const bool writer = split == 0 && mode != 2 && pos >= kr.plen;
+    if (split == 0 && mode != 2 && pos < kr.plen && threadIdx.x == 0) atomicMin(s.err, kErrSharedAppend);
     for (int e = threadIdx.x; e < 2 * kw; e += kThreads) {
         const int w = e / kw, c = e % kw, i0 = c * (4 / KVB);
         const float* src = w ? sm.vn : sm.q + hq * hd;
         unsigned word = 0;
         float dec;
         for (int j = 0; j < 4 / KVB; ++j) word |= kv_encode(src[i0 + j], KVB, &dec) << (8 * KVB * j);
-        if (split == 0) *reinterpret_cast<unsigned*>(row + (w ? vofs : 0) + c * 4) = word;
+        if (writer) *reinterpret_cast<unsigned*>(row + (w ? vofs : 0) + c * 4) = word;
         *reinterpret_cast<unsigned*>(sm.newrow + w * hbytes + c * 4) = word;
     }
+    if (mode == 1) return;   // the copies of an append launch are empty groups
     // each q head on its integer grid, split into balanced signed bytes: the
     // score MMAs' B operand, column 4*head + limb (limb 3 zero), dims in MMA k order
     if (warp < hq) {

@@ -155,6 +155,16 @@ std::string load_mmcf_bytes(const uint8_t* h, size_t sz, HModel& m) {
                 m.rope_theta = rdf(pl); m.rope_half = pl[4] != 0; m.qk_norm = pl[5] != 0;
             } else if (key == 3 && len >= 4) {
                 split = pl[3];
+            } else if (key == 4 && len >= 3) {
+                // template kind byte, default system prompt NUL, template name NUL
+                // (model.cpp:684-695); only the name is kept, for the MMKV1 sidecar
+                const char* c = (const char*)pl + 1;
+                const char* e = (const char*)pl + len;
+                const char* nul = (const char*)memchr(c, 0, (size_t)(e - c));
+                if (nul) {
+                    const char* nul2 = (const char*)memchr(nul + 1, 0, (size_t)(e - nul - 1));
+                    if (nul2) m.template_name.assign(nul + 1, (size_t)(nul2 - nul - 1));
+                }
             } else if (key == 11 && len >= 4) {
                 const float e = rdf(pl);
                 if (e > 0.0f) m.rms_eps = e;

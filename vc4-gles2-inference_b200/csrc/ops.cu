@@ -281,6 +281,7 @@ int vc4_attention_block(vc4_session* s, int slot, int layer, int pos, int src, i
     // attention.  The attention kernel reads its (slot, pos) before its
     // grid-dependency wait, so they are written ahead of the matvec, not by the
     // kernel right before it.
+    if (int e = session_unshare(s, slot, pos)) return e;   // the append below writes row pos
     k_op_set_call<<<1, 1, 0, v.stream>>>(o->call, slot, 0, pos);
     matvec(v, o, m.qkv[layer], buf_row(*o, src, slot, v.slots), D, 1, 0);
     k_op_floats<<<grid_of(Q), 256, 0, v.stream>>>(o->out, Q, o->kexp, st.qkv);

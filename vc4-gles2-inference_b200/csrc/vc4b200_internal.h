@@ -64,6 +64,7 @@ struct HModel {
     std::vector<float> rope_factors;
     std::vector<uint8_t> hid_scale;
     uint64_t source_size = 0, source_mtime = 0;
+    std::string template_name;        // metadata key 4: the chat template's name (MMKV1 sidecar)
     std::vector<int8_t> emb;          // vocab*dim signed levels
     std::vector<float> emb_scale;     // vocab
     std::vector<float> rms_att, rms_ffn, rms_final, q_norm, k_norm;
@@ -137,6 +138,13 @@ struct State {                      // per-slot activations, [slot][...]
     int* next = nullptr;             // greedy token [slots]
     int* route = nullptr;            // MoE expert [slots][layers]
     uint8_t* kv = nullptr;           // [slots][layers][seq][row_bytes]
+    // Shared prefix: one MMKV1 prefix held once for many slots.  Slot s reads
+    // its positions t < plen[s] from pkv (row t of layer l at
+    // pkv + (l*pcap + t)*row_bytes) and every other position from kv; those
+    // rows are read-only (an append below plen is refused).
+    uint8_t* pkv = nullptr;          // [layers][pcap][row_bytes]
+    int* plen = nullptr;             // [slots], 0: the slot holds all its rows
+    int pcap = 0;
     int kv_bits = 16, row_bytes = 0, seq = 0, slots = 0;
     float* rope_cos = nullptr;       // [seq][head_dim/2]
     float* rope_sin = nullptr;
@@ -151,7 +159,12 @@ struct State {                      // per-slot activations, [slot][...]
 
 // Kernel launchers (kernels.cu).  All enqueue on `st`; none synchronises.
 void launch_embed_qkv(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st);
-void launch_attention(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st);
+// mode 0: decode; 1 / 2: the append and attend launches of a batched prefill
+// (several positions of one sequence in one pass; see k_attn_b).
+void launch_attention(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st, int mode = 0);
+// Whether the many-sequence attention kernel, which a batched prefill needs,
+// holds this session's sequence length and head shape.
+bool prefill_attention_fits(const DModel& m, const State& s);
 void launch_wo(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st);
 void launch_ffn_gate(const DModel& m, const State& s, const Batch& b, int layer, cudaStream_t st);
 // Logits + first-max argmax; the launch's last CTA writes the greedy tokens to
@@ -193,6 +206,9 @@ struct SessionView {
     long long* syncs;
 };
 SessionView session_view(vc4_session* s);
+// Before a write at `pos` of `slot`: a slot whose shared prefix covers pos gets
+// its own copy of the prefix rows first (copy on write).
+int session_unshare(vc4_session* s, int slot, int pos);
 void free_op_buffers(void* ops);
 int kernel_check(vc4_session* s);    // the kernels' self-check word (synchronises)
 cudaStream_t model_stream(const vc4_model* m);

@@ -66,6 +66,7 @@ _PROTOS = {
     "vc4_session_stream": (C.c_void_p, [C.c_void_p]),
     "vc4_session_check": (C.c_int, [C.c_void_p]),
     "vc4_prefill": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
+    "vc4_prefill_batch": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
     "vc4_kv_row_bytes": (C.c_int, [C.c_void_p]),
     "vc4_kv_read_rows": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p]),
     "vc4_kv_write_rows": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p]),
@@ -73,6 +74,10 @@ _PROTOS = {
                                         C.c_uint64]),
     "vc4_load_prefix_cache": (C.c_int, [C.c_void_p, C.c_int, C.c_char_p, C.c_void_p, C.c_int,
                                         C.POINTER(C.c_int)]),
+    "vc4_load_prefix_cache_shared": (C.c_int, [C.c_void_p, C.c_char_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int,
+                                               C.POINTER(C.c_int)]),
+    "vc4_build_prefix_cache": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_char_p, C.c_uint64,
+                                         C.c_uint64]),
     "vc4_matvec_s": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
     "vc4_matvec_s_noalloc": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
                                        C.c_void_p]),
@@ -245,10 +250,14 @@ class Session:
         """Raise if a device-resident pass failed a kernel self-check."""
         _check(lib().vc4_session_check(self._h))
 
-    def prefill(self, tokens, pos0: int = 0, slot: int = 0, want_logits: bool = True):
+    def prefill(self, tokens, pos0: int = 0, slot: int = 0, want_logits: bool = True, batched: bool = False):
+        """The prompt's positions pos0.. on `slot`; returns the last
+        position's logits.  batched=True runs them as batches of the
+        many-sequence path (vc4_prefill_batch), with the serial loop's results."""
         t = np.ascontiguousarray(tokens, np.int32)
         out = np.empty(self.vocab, np.float32) if want_logits else None
-        _check(lib().vc4_prefill(self._h, slot, _p(t), len(t), pos0, _p(out) if want_logits else None))
+        fn = lib().vc4_prefill_batch if batched else lib().vc4_prefill
+        _check(fn(self._h, slot, _p(t), len(t), pos0, _p(out) if want_logits else None))
         return out
 
     # -- KV rows and the MMKV1 prefix cache ---------------------------------
@@ -268,10 +277,31 @@ class Session:
         t = np.ascontiguousarray(toks, np.int32)
         _check(lib().vc4_save_prefix_cache(self._h, slot, path.encode(), _p(t), len(t), system_fnv, tools_fnv))
 
+    def build_prefix_cache(self, path: str, toks, slot: int = 0, system: str = None, tools: str = None):
+        """`--build-prefix-cache` (prefix_build.cpp:22-83) for a tokenised
+        prompt: prefill `toks` on `slot` from position 0, then write the
+        MMKV1 file and its sidecar.  `system` / `tools` are the raw texts
+        whose FNV-1a-64 the sidecar records (0 when absent, as for a prompt
+        file)."""
+        t = np.ascontiguousarray(toks, np.int32)
+        sf = fnv64(system.encode()) if system is not None else 0
+        tf = fnv64(tools.encode()) if tools is not None else 0
+        _check(lib().vc4_build_prefix_cache(self._h, slot, _p(t), len(t), path.encode(), sf, tf))
+
     def load_prefix_cache(self, path: str, slot: int = 0):
         buf = np.empty(self.seq, np.int32)
         n = C.c_int()
         _check(lib().vc4_load_prefix_cache(self._h, slot, path.encode(), _p(buf), len(buf), C.byref(n)))
+        return [int(v) for v in buf[:n.value]]
+
+    def load_prefix_cache_shared(self, path: str, slots):
+        """Restore one MMKV1 prefix into every slot of `slots`, held once on
+        the device (vc4_load_prefix_cache_shared); returns its tokens."""
+        sl = np.ascontiguousarray(slots, np.int32)
+        buf = np.empty(self.seq, np.int32)
+        n = C.c_int()
+        _check(lib().vc4_load_prefix_cache_shared(self._h, path.encode(), _p(sl), len(sl), _p(buf), len(buf),
+                                                  C.byref(n)))
         return [int(v) for v in buf[:n.value]]
 
     def counters(self):
@@ -292,6 +322,15 @@ class Session:
             self.close()
         except Exception:
             pass
+
+
+def fnv64(data: bytes) -> int:
+    """FNV-1a-64 over bytes (common.cpp:63-67): the sidecar's system_fnv64
+    and tools_fnv64."""
+    h = 1469598103934665603
+    for b in data:
+        h = ((h ^ b) * 1099511628211) & 0xFFFFFFFFFFFFFFFF
+    return h
 
 
 def generate(session: Session, prompt, steps: int, slot: int = 0):
