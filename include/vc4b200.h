@@ -128,6 +128,11 @@ VC4_API int vc4_prefill(vc4_session* s, int slot, const int* tokens, int n, int 
    for bit.  Chunks below 16 positions, and models or sequence lengths the
    many-sequence kernels do not hold, run through the serial loop. */
 VC4_API int vc4_prefill_batch(vc4_session* s, int slot, const int* tokens, int n, int pos0, float* logits);
+/* vc4_prefill_batch that keeps every position's logits: logits_all receives
+   n x vocab floats, row i the logits position pos0 + i produces (what
+   Session::step returns for each scored token of the `--ppl` loop,
+   ppl.cpp:50-75).  Positions of a serial tail are stepped one at a time. */
+VC4_API int vc4_prefill_logits(vc4_session* s, int slot, const int* tokens, int n, int pos0, float* logits_all);
 
 /* KV rows of one layer in the MMKV1 texel layout (the bytes
    prefix_cache.cpp:59-67 reads with glReadPixels and 176-189 writes with

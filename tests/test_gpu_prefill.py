@@ -66,3 +66,29 @@ def test_prefill_batch_from_a_later_position(gpu):
     assert np.array_equal(got, want)
     for l in (0, model.info.layers - 1):
         assert bat.kv_rows(l, 300) == ser.kv_rows(l, 300)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("key,stride", [("tiny_q8", -1), ("tiny_moe_q4", -1), ("tiny_t3", 0)])
+def test_perplexity_windows_match_the_oracle(tiny_paths, key, stride):
+    """`--ppl` windows (ppl.cpp:23-88) over 150 tokens of a tiny model (span =
+    SEQ 64): context positions prefilled in batches, the scored positions'
+    logits from one batched pass, against the oracle stepping every position
+    of every window; stride -1 is the default span/2, 0 cold windows."""
+    import oracle
+    cfg = synth.TINY_CONFIGS[key]
+    toks = sum((synth.prompt_tokens(cfg, i) for i in range(8)), [])[:150]
+    model = vc4b200.Model(vc4b200.GPU(0), tiny_paths[key])
+    sess = vc4b200.Session(model, slots=64, seq=cfg.seq, kv=KV[cfg.kv_bits])
+    got = vc4b200.perplexity(sess, toks, stride=stride)
+    om = oracle.Model(tiny_paths[key])
+
+    def scorer(win, first):
+        s = oracle.Session(om, cfg.kv_bits)
+        out = [s.step(t, j, want_logits=j >= first) for j, t in enumerate(win)]
+        s.close()
+        return out[first:]
+    want = vc4b200.perplexity(None, toks, span=cfg.seq, stride=stride, scorer=scorer)
+    assert (got["tokens"], got["windows"], got["span"], got["stride"]) == \
+        (want["tokens"], want["windows"], want["span"], want["stride"]) and got["tokens"] == 149
+    assert abs(got["nll"] - want["nll"]) <= 1e-4, (got, want)

@@ -153,3 +153,45 @@ def test_gloo_rank_failure_is_detected_not_hung(tiny_paths):
     res = _run_ranks("fail", tiny_paths["tiny_q8"])
     assert res[1][4] and "rank 1 fails" in res[1][4]
     assert res[0][4] is not None                              # rank 0 saw an error, not a hang
+
+
+@pytest.mark.parametrize("stride", [-1, 0, 10])
+def test_perplexity_windows_follow_the_reference_loop(tiny_paths, stride):
+    """vc4b200.perplexity's windowing against a literal restatement of
+    run_ppl's loop (ppl.cpp:23-88: a fresh session per window, every position
+    stepped, a token scored once), both scoring through the CPU oracle."""
+    import oracle
+    from vc4b200 import perplexity, synth
+    from vc4b200.engine import log_prob
+    cfg = synth.TINY_CONFIGS["tiny_q8"]
+    toks = sum((synth.prompt_tokens(cfg, i) for i in range(8)), [])[:150]
+    om = oracle.Model(tiny_paths["tiny_q8"])
+    span = cfg.seq
+
+    def scorer(win, first):
+        s = oracle.Session(om, cfg.kv_bits)
+        out = [s.step(t, j, want_logits=j >= first) for j, t in enumerate(win)]
+        s.close()
+        return out[first:]
+    got = perplexity(None, toks, span=span, stride=stride, scorer=scorer)
+    st = span // 2 if stride < 0 else stride
+    st = min(st or span - 1, span - 1)
+    warm, n, nxt, windows, nll, cnt = span - st, len(toks), 1, 0, 0.0, 0
+    while nxt < n:
+        a = 0 if windows == 0 else nxt - warm
+        ln = min(span, n - a)
+        if ln < 2 or a < 0:
+            break
+        s = oracle.Session(om, cfg.kv_bits)
+        for j in range(ln - 1):
+            t = a + j + 1
+            lg = s.step(toks[a + j], j, want_logits=t >= nxt)
+            if t < nxt:
+                continue
+            nll += -log_prob(lg, toks[t])
+            cnt += 1
+            nxt = t + 1
+        s.close()
+        windows += 1
+    assert (got["tokens"], got["windows"], got["stride"]) == (cnt, windows, st)
+    assert got["nll"] == nll / cnt

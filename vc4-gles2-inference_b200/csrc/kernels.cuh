@@ -1910,7 +1910,7 @@ k_attn(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int 
 // Positions inside a 32-wide MMA k block are taken in the order ldmatrix of
 // 16-bit pairs delivers them (attnb_k_of); the weight limbs are stored in it.
 constexpr int kAbRows = 128;
-constexpr int kAbStages = 3;
+constexpr int kAbStages = 2;
 constexpr int kAbMaxLimbs = 6;      // E_t < 2^47: six bytes
 
 __host__ __device__ inline int attnb_pitch(int hbytes) { return (hbytes / 16) % 2 ? hbytes : hbytes + 16; }
@@ -1929,7 +1929,7 @@ __host__ __device__ inline int attnb_k_of(int p) {
 }
 
 struct AbSmem {
-    uint8_t* ring;   // kAbStages x kAbRows x pitch cache bytes; at the end the P.V partial sums
+    uint8_t* ring;   // kAbStages x kAbRows x pitch cache bytes; at the end (with newrow and ea) the P.V partial sums
     uint8_t* newrow; // 2 x hbytes: this step's K and V row
     uint8_t* ea;     // 16 x epitch: weight limbs, row h*NL + limb, positions in MMA k order
     uint8_t* qb;     // 8 x hd: q limbs, column 4*head + limb, dims in MMA k order
@@ -1950,7 +1950,13 @@ struct AbSmem {
 __host__ __device__ inline size_t attnb_carve(int hq, int hd, int seq, int kv_bits, char* base, AbSmem* sm) {
     const int hbytes = hd * (kv_bits / 8);
     size_t o = 0;
-    const size_t ring = o; o = align16(o + (size_t)kAbStages * kAbRows * attnb_pitch(hbytes));
+    // ring, newrow and ea are dead once the last V tile is multiplied; the
+    // P.V partial sums (4 position blocks x hq*NL rows x hd int64) take their
+    // place, so the three together are at least that large
+    const size_t part = (size_t)4 * hq * kAbMaxLimbs * hd * sizeof(long long);
+    const size_t rows = align16((size_t)kAbStages * kAbRows * attnb_pitch(hbytes));
+    const size_t rest = align16(2 * (size_t)hbytes) + align16(16 * (size_t)attnb_epitch(seq));
+    const size_t ring = o; o = rows + rest >= part ? rows : align16(part - rest);
     const size_t nr = o;   o = align16(o + 2 * (size_t)hbytes);
     const size_t ea = o;   o = align16(o + 16 * (size_t)attnb_epitch(seq));
     const size_t qb = o;   o = align16(o + 8 * (size_t)hd);
@@ -2029,7 +2035,7 @@ __device__ __forceinline__ void mma_i8(int (&d)[4], const unsigned (&a)[4], unsi
 // the kernel twice: mode 1 appends every row and returns, mode 2 (the next
 // launch, so every row is in the cache) attends without writing.
 template <int KVB, int HQ, int HD>
-__global__ void __launch_bounds__(kThreads, KVB == 1 && HD <= 96 ? 3 : 2)
+__global__ void __launch_bounds__(kThreads, KVB == 1 && HD <= 96 ? 4 : 2)
 k_attn_b(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int layer, int mode) {
     static_assert(HD % 32 == 0 && HD <= 128 && (HQ == 1 || HQ == 2), "k_attn_b shape");
     extern __shared__ __align__(16) char smem[];

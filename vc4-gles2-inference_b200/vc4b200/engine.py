@@ -67,6 +67,7 @@ _PROTOS = {
     "vc4_session_check": (C.c_int, [C.c_void_p]),
     "vc4_prefill": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
     "vc4_prefill_batch": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
+    "vc4_prefill_logits": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
     "vc4_kv_row_bytes": (C.c_int, [C.c_void_p]),
     "vc4_kv_read_rows": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p]),
     "vc4_kv_write_rows": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p]),
@@ -260,6 +261,13 @@ class Session:
         _check(fn(self._h, slot, _p(t), len(t), pos0, _p(out) if want_logits else None))
         return out
 
+    def prefill_logits(self, tokens, pos0: int = 0, slot: int = 0):
+        """Batched prefill returning every position's logits (len x vocab)."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        out = np.empty((len(t), self.vocab), np.float32)
+        _check(lib().vc4_prefill_logits(self._h, slot, _p(t), len(t), pos0, _p(out)))
+        return out
+
     # -- KV rows and the MMKV1 prefix cache ---------------------------------
     def kv_row_bytes(self) -> int:
         return lib().vc4_kv_row_bytes(self._h)
@@ -322,6 +330,58 @@ class Session:
             self.close()
         except Exception:
             pass
+
+
+def log_prob(logits, token: int) -> float:
+    """log softmax(logits)[token] in double, as run_ppl sums it
+    (ppl.cpp:66-71): max, sum of exp(v - max), (l[token] - max) - log(sum)."""
+    v = np.asarray(logits, np.float64)
+    mx = float(v.max())
+    return (float(v[token]) - mx) - float(np.log(np.exp(v - mx).sum()))
+
+
+def perplexity(session: "Session", tokens, span: int = 0, stride: int = -1, slot: int = 0,
+               scorer=None) -> dict:
+    """`--ppl` (ppl.cpp:23-88): windows of `span` positions (the session's
+    sequence length by default) advancing by `stride` (span/2 by default; 0:
+    cold windows of span-1), each window restarted at position 0 with
+    span - stride tokens of context.  Context positions are prefilled in
+    batches; every scored position's logits come from one batched pass
+    (vc4_prefill_logits), which equals Session::step position by position.
+    `scorer(window_tokens, first_scored)` replaces the session (for a CPU
+    check); it returns the logits of positions first_scored.. of the window."""
+    tokens = [int(t) for t in tokens]
+    if len(tokens) < 4:
+        raise EngineError("not enough tokens")
+    span = span or session.seq
+    stride = span // 2 if stride < 0 else stride
+    stride = max(stride, 0) or span - 1
+    stride = min(stride, span - 1)
+    warm = span - stride
+    n, nxt, windows, nll, cnt = len(tokens), 1, 0, 0.0, 0
+    while nxt < n:
+        a = 0 if windows == 0 else nxt - warm
+        ln = min(span, n - a)
+        if ln < 2 or a < 0:
+            break
+        win = tokens[a:a + ln]
+        first = max(0, nxt - a - 1)          # positions before this one predict tokens already scored
+        if scorer is not None:
+            lg = scorer(win[:ln - 1], first)
+        else:
+            if first:
+                session.prefill(win[:first], 0, slot=slot, want_logits=False, batched=True)
+            lg = session.prefill_logits(win[first:ln - 1], first, slot=slot)
+        for j in range(first, ln - 1):
+            t = a + j + 1
+            nll += -log_prob(lg[j - first], tokens[t])
+            cnt += 1
+            nxt = t + 1
+        windows += 1
+    if not cnt:
+        raise EngineError("no tokens scored")
+    return {"ppl": float(np.exp(nll / cnt)), "nll": nll / cnt, "tokens": cnt, "windows": windows,
+            "span": span, "stride": stride}
 
 
 def fnv64(data: bytes) -> int:
