@@ -2057,7 +2057,7 @@ k_attn_b(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, in
     const int rpp = kThreads / kvec, cc = threadIdx.x % kvec, r0 = threadIdx.x / kvec;
     auto issue = [&](int u) {
         if (u < 2 * ntile && r0 < rpp) {
-            const int kind = u >= ntile, t0 = (u % ntile) * kAbRows, nt = min(kAbRows, len - t0);
+            const int kind = u >= ntile, t0 = (kind ? u - ntile : u) * kAbRows, nt = min(kAbRows, len - t0);
             uint8_t* dst = sm.ring + (size_t)(u % kAbStages) * kAbRows * pitch + cc * 16 + r0 * pitch;
             const int cofs = (kind ? vofs : 0) + g * hbytes + cc * 16;
             for (int r = r0; r < nt; r += rpp, dst += rpp * pitch)
@@ -2183,7 +2183,7 @@ k_attn_b(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, in
         asm volatile("cp.async.wait_group %0;" ::"n"(kAbStages - 1) : "memory");
         __syncthreads();
         uint8_t* tile = sm.ring + (size_t)(u % kAbStages) * kAbRows * pitch;
-        const int kind = u >= ntile, t0 = (u % ntile) * kAbRows, nt = min(kAbRows, len - t0);
+        const int kind = u >= ntile, t0 = (kind ? u - ntile : u) * kAbRows, nt = min(kAbRows, len - t0);
         if (pos >= t0 && pos < t0 + nt) {
             // this step's row, which the copies skipped
             for (int i = threadIdx.x; i < hbytes / 4; i += kThreads)
@@ -2268,8 +2268,13 @@ k_attn_b(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, in
                     for (int hh = 0; hh < HQ; ++hh) {
                         const float e = rintf(__fmul_rn(vexp(__fsub_rn(sm.sc[hh * d.seq + t], mx[hh])), wscale));
                         dn[hh] = __dadd_rn(dn[hh], (double)e);
-                        unsigned long long E = (unsigned long long)e;
-                        for (int l = 0; l < nl; ++l, E >>= 8) col[(size_t)(hh * nl + l) * epitch] = (uint8_t)E;
+                        // E < 2^47: bytes 0-3 from the low word, 4-5 from the high one
+                        const unsigned long long E = (unsigned long long)e;
+                        const unsigned lo = (unsigned)E, hi = (unsigned)(E >> 32);
+                        uint8_t* c = col + (size_t)hh * nl * epitch;
+#pragma unroll
+                        for (int l = 0; l < kAbMaxLimbs; ++l)
+                            if (l < nl) c[l * epitch] = (uint8_t)((l < 4 ? lo : hi) >> (8 * (l & 3)));
                     }
                 }
 #pragma unroll
