@@ -134,23 +134,28 @@ def test_prefix_restore_batch_full_shape(gpu, tmp_path, n):
 
 
 @pytest.mark.gpu
-def test_batch_1024_equals_serial(gpu, tmp_path):
+@pytest.mark.parametrize("shared", [False, True])
+def test_batch_1024_equals_serial(gpu, tmp_path, shared):
     """c4 at the bench's 1024 sequences per pass: the tensor-core matmats run
     their largest sequence groups (64-128 per CTA, all 512 TMEM columns for
     w1/w3), two CTAs per SM with two-stage copy rings for the logits and
     19-stage rings for w2; each sampled sequence gets its one-sequence result
-    bit for bit."""
+    bit for bit.  With the 300-row prefix held once (shared), every sequence
+    reads its three prefix tiles from the session's one copy."""
     cfg = synth.CONFIGS["c4"]
     model = vc4b200.Model(gpu, _path("c4"))
-    prefix = synth.prompt_tokens(cfg)[:32]
+    prefix = synth.prompt_tokens(cfg)[:300]
     first = vc4b200.Session(model, slots=1, seq=cfg.seq, kv="q8")
     first.prefill(prefix, 0, want_logits=False)
     mmkv = str(tmp_path / "prefix.mmkv")
     first.save_prefix_cache(mmkv, prefix)
     n, steps = 1024, 3
     batch = vc4b200.Session(model, slots=n, seq=cfg.seq, kv="q8")
-    for s in range(n):
-        batch.load_prefix_cache(mmkv, slot=s)
+    if shared:
+        batch.load_prefix_cache_shared(mmkv, list(range(n)))
+    else:
+        for s in range(n):
+            batch.load_prefix_cache(mmkv, slot=s)
     toks = [(prefix[-1] + 97 * s) % cfg.shape.vocab for s in range(n)]
     fed, outs = [], []
     pos = len(prefix)
@@ -213,6 +218,42 @@ def test_build_prefix_cache(gpu, tmp_path):
     for bad in ([], list(range(cfg.seq + 1))):
         with pytest.raises(vc4b200.EngineError):
             s.build_prefix_cache(str(tmp_path / "bad.mmkv"), bad)
+
+
+@pytest.mark.gpu
+def test_shared_and_private_prefixes_in_one_batch(gpu, tmp_path):
+    """Slots that read the shared prefix next to slots restored into their own
+    rows in one many-sequence pass (slots 32-63 alternate shared and private
+    restores, slots 48-63 run at scattered positions): every sequence equals
+    the same restore in a session without a shared prefix, bit for bit."""
+    cfg = synth.CONFIGS["c4"]
+    model = vc4b200.Model(gpu, _path("c4"))
+    prefix = synth.prompt_tokens(cfg)[:200]
+    first = vc4b200.Session(model, slots=16, seq=cfg.seq, kv="q8")
+    first.prefill(prefix, 0, want_logits=False, batched=True)
+    mmkv = str(tmp_path / "prefix.mmkv")
+    first.save_prefix_cache(mmkv, prefix)
+    n = 64
+    priv = vc4b200.Session(model, slots=n, seq=cfg.seq, kv="q8")
+    mix = vc4b200.Session(model, slots=n, seq=cfg.seq, kv="q8")
+    for s in range(n):
+        priv.load_prefix_cache(mmkv, slot=s)
+    sharing = [s for s in range(n) if s < 32 or s % 2 == 0]
+    mix.load_prefix_cache_shared(mmkv, sharing)
+    for s in range(n):
+        if s not in sharing:
+            mix.load_prefix_cache(mmkv, slot=s)
+    P = len(prefix)
+    toks = [(prefix[-1] + 31 * s) % cfg.shape.vocab for s in range(n)]
+    pos = [P + (s % 5 if s >= 48 else 0) for s in range(n)]
+    for _ in range(3):
+        na, la = priv.step_batch(list(range(n)), toks, pos, want_logits=True)
+        nb, lb = mix.step_batch(list(range(n)), toks, pos, want_logits=True)
+        assert np.array_equal(la, lb) and list(na) == list(nb)
+        toks = [int(t) for t in na]
+        pos = [p + 1 for p in pos]
+    for s in (0, 33, 50, 63):
+        assert mix.kv_rows(3, pos[s], slot=s) == priv.kv_rows(3, pos[s], slot=s)
 
 
 @pytest.mark.gpu

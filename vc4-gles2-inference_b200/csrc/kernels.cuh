@@ -1911,6 +1911,7 @@ k_attn(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, int 
 // 16-bit pairs delivers them (attnb_k_of); the weight limbs are stored in it.
 constexpr int kAbRows = 128;
 constexpr int kAbStages = 2;
+static_assert(kAbStages >= 2, "the tile loop keeps kAbStages - 1 tiles in flight");
 constexpr int kAbMaxLimbs = 6;      // E_t < 2^47: six bytes
 
 __host__ __device__ inline int attnb_pitch(int hbytes) { return (hbytes / 16) % 2 ? hbytes : hbytes + 16; }
@@ -2178,10 +2179,12 @@ k_attn_b(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, in
     int nl = 0;                                         // weight limbs
     const unsigned ea_base = smem_addr(sm.ea);
 
+    // One barrier per tile: it makes tile u visible and retires tile u-1, whose
+    // slot the copy of tile u + stages - 1 then refills during tile u's work.
     for (int u = 0; u < 2 * ntile; ++u) {
-        issue(u + kAbStages - 1);
-        asm volatile("cp.async.wait_group %0;" ::"n"(kAbStages - 1) : "memory");
+        asm volatile("cp.async.wait_group %0;" ::"n"(kAbStages - 2) : "memory");
         __syncthreads();
+        issue(u + kAbStages - 1);
         uint8_t* tile = sm.ring + (size_t)(u % kAbStages) * kAbRows * pitch;
         const int kind = u >= ntile, t0 = (kind ? u - ntile : u) * kAbRows, nt = min(kAbRows, len - t0);
         if (pos >= t0 && pos < t0 + nt) {
@@ -2312,7 +2315,6 @@ k_attn_b(const float* q_norm, const float* k_norm, State s, Batch bt, Dims d, in
                 }
             }
         }
-        __syncthreads();
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncthreads();   // the ring is free: it takes the partial sums
