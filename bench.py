@@ -526,7 +526,7 @@ def measure(args, cfg, dist, full: bool = True) -> dict:
     achieved = op_bytes[dom] / (op_ms[dom] / 1000.0) / 1e9
     step_bytes = sum(op_bytes[k] * (1 if k == "logits" else L) for k in op_bytes)
     roofline = {"bound": "hbm", "kernel": KERNEL_OF[dom](B, info), "op": dom, "achieved": achieved, "peak": hbm,
-                "unit": "GB/s", "frac": achieved / hbm,
+                "unit": "GB/s", "frac": achieved / hbm, "limit": LIMIT_OF.get((dom, B >= 8), ""),
                 # DRAM bytes need an ncu capture, which this run does not make
                 "traffic": None, "peak_source": peak_src,
                 "bytes_per_launch": op_bytes[dom], "ms_per_launch": op_ms[dom], "kv_position": int(prof_pos[0]),
@@ -556,6 +556,17 @@ KERNEL_OF = {
     "ffn": lambda B, i: "k_tmm<w13>+k_tmm<w2> (tcgen05)" if B >= 32 and i.wtype == 0 else
                         "k_gate" if B < 8 else "k_mm<ffn>+k_mmdown",
     "logits": lambda B, i: "k_tmm<logits> (tcgen05)" if B >= 8 else "k_logits",
+}
+
+
+# What bounds the dominant kernel, from its ncu captures (the HBM fraction
+# alone does not say it for these kernels)
+LIMIT_OF = {
+    ("attention", True): "instruction issue and per-CTA barrier chain, not DRAM: ncu issue active 47%, L2 hit rate "
+                         "94% (the prefix held once is read from L2), see profiles/attn_b_c4b128.md",
+    ("attention", False): "dependency latency: one launch moves well under 1 MB, see profiles/attn_c1.md",
+    ("ffn", True): "epilogue instructions (exact row scalings, SwiGLU, w2 records), tensor pipe 5-9%, "
+                   "see profiles/tmm_c4b1024.md",
 }
 
 
