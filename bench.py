@@ -551,7 +551,7 @@ def measure(args, cfg, dist, full: bool = True) -> dict:
 KERNEL_OF = {
     "qkv": lambda B, i: "k_tmm<qkv> (tcgen05)" if B >= 32 and i.wtype == 0 else "k_qkv" if B < 8 else "k_mm<qkv>",
     "attention": lambda B, i: "k_attn_b" if B * i.kv_heads * (1 if (i.heads // i.kv_heads) % 2 else
-                                                                (i.heads // i.kv_heads) // 2) >= 128 else "k_attn",
+                                                                (i.heads // i.kv_heads) // 2) >= 32 else "k_attn",
     "wo": lambda B, i: "k_tmm<wo> (tcgen05)" if B >= 32 and i.wtype == 0 else "k_wo" if B < 8 else "k_mm<wo>",
     "ffn": lambda B, i: "k_tmm<w13>+k_tmm<w2> (tcgen05)" if B >= 32 and i.wtype == 0 else
                         "k_gate" if B < 8 else "k_mm<ffn>+k_mmdown",
