@@ -2909,7 +2909,10 @@ struct BOps {
                                      (int)dr.hi_a, (int)dr.lo_b, (int)dr.hi_b, hs, dr, Finalize{}, st))
             return;
         const int e = d.experts ? d.experts : 1;
-        const int splits = mm_splits(m, Wa.rblocks * e, bt.n / e, kWarps * kMmNI);
+        // dense: as few as four sequences per CTA (c4 at 16: ffn 55.4 -> 51.7 us,
+        // c3b32 57.5 -> 56.4 us); MoE keeps whole sweeps of the expert's
+        // sequences (c2 took 85 -> 102 us split finer)
+        const int splits = mm_splits(m, Wa.rblocks * e, bt.n / e, d.experts ? kWarps * kMmNI : 2 * kMmNI);
         const size_t fixed = mmdown_smem(Wa, Wb, two, 0, bt.n);
         const int want = (bt.n + splits - 1) / splits;
         const int group =
