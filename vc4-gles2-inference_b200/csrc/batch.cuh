@@ -150,8 +150,8 @@ __device__ __forceinline__ int mm_members(const State& s, const Dims& d, int n, 
 // Dot products of `ni` staged inputs (records in shared memory) with the
 // 32 rows of one weight block in shared memory; lane = row.
 template <int WT>
-__device__ __forceinline__ void mm_dots(const char* wsm, int nch, int stride, int gst, const char* const (&recs)[kMmNI],
-                                        int ni, long long (&S)[kMmNI]) {
+__device__ __forceinline__ void mm_dots(const char* wsm, int nch, int stride, int ja, int jb,
+                                        const char* const (&recs)[kMmNI], int ni, long long (&S)[kMmNI]) {
     constexpr int cpc = WT == W_Q8 ? 16 : WT == W_Q4 ? 32 : 64;
     const int lane = threadIdx.x & 31;
     const int4* wv = reinterpret_cast<const int4*>(wsm) + lane;
@@ -159,7 +159,7 @@ __device__ __forceinline__ void mm_dots(const char* wsm, int nch, int stride, in
 #pragma unroll
     for (int i = 0; i < kMmNI; ++i) S[i] = 0;
 #pragma unroll 2
-    for (int j = 0; j < nch; ++j) {
+    for (int j = ja; j < jb; ++j) {
         const int4 w = wv[(size_t)j * 32];
         const int sp = WT == W_Q4 ? qp[(size_t)j * 32] : 0;
 #pragma unroll
@@ -171,11 +171,13 @@ __device__ __forceinline__ void mm_dots(const char* wsm, int nch, int stride, in
                                   WT == W_Q4 ? reinterpret_cast<const int*>(r + 2 * (size_t)stride)[j] : 0);
         }
     }
-    (void)gst;
 }
 
+// partial dot products when the warps of a sequence pair split its chunks
+constexpr size_t kMmPartBytes = sizeof(long long) * kWarps * kMmNI * 32 * 2;
 __host__ __device__ inline size_t mm_smem(const DMat& W, int nmat, int group, int n) {
-    return align128(nmat * mm_wbytes(W)) + (size_t)group * xrec_bytes(W) + align16(sizeof(int) * (size_t)n) + 64;
+    return align128(nmat * mm_wbytes(W)) + (size_t)group * xrec_bytes(W) + align16(sizeof(int) * (size_t)n) + 64 +
+           kMmPartBytes;
 }
 
 // matmat: one CTA per 32-row block (blockIdx.x) and expert (blockIdx.y).
@@ -194,6 +196,7 @@ __global__ void __launch_bounds__(kThreads) k_mm(MatSet M, State s, Batch bt, Di
     int* members = reinterpret_cast<int*>(rsm + (size_t)group * rb);
     unsigned long long* bar = reinterpret_cast<unsigned long long*>(
         sm + align128(NM * wb) + (size_t)group * rb + align16(sizeof(int) * (size_t)n));
+    long long* part = reinterpret_cast<long long*>(reinterpret_cast<char*>(bar) + 64);
     const unsigned wbody = (unsigned)nch * 512u, qbytes = WT == W_Q4 ? (unsigned)nch * 128u : 0u;
     if (threadIdx.x == 0) {
         mbar_init(&bar[0], 1);
@@ -233,14 +236,51 @@ __global__ void __launch_bounds__(kThreads) k_mm(MatSet M, State s, Batch bt, Di
         }
         ok = mbar_wait(&bar[1], (unsigned)gi & 1u);
         if (__syncthreads_or(!ok)) { ok = false; break; }
+        // At most two sequence pairs (six of the eight warps would idle): the
+        // warps of a pair split its chunks into nsl slices and add their exact
+        // partial sums through shared memory.  (With three or more pairs the
+        // extra barrier and sums cost more than the idle warps: c2's wo.)
+        const int npair = (gn + kMmNI - 1) / kMmNI;
+        const int nsl = npair > 2 ? 1 : kWarps / npair;
+        if (nsl > 1) {
+            const int p = warp % npair, sl = warp / npair;
+            if (sl < nsl) {
+                const int i0 = p * kMmNI, ni = min(kMmNI, gn - i0);
+                const char* recs[kMmNI];
+#pragma unroll
+                for (int i = 0; i < kMmNI; ++i) recs[i] = rsm + (size_t)(i0 + (i < ni ? i : 0)) * rb;
+                long long S[kMmNI], S3[kMmNI];
+                const int ja = sl * nch / nsl, jb = (sl + 1) * nch / nsl;
+                mm_dots<WT>(sm, nch, stride, ja, jb, recs, ni, S);
+                if (OP == kOpGate) mm_dots<WT>(sm + wb, nch, stride, ja, jb, recs, ni, S3);
+#pragma unroll
+                for (int i = 0; i < kMmNI; ++i) {
+                    part[((sl * npair + p) * kMmNI + i) * 32 + lane] = S[i];
+                    if (OP == kOpGate) part[((kWarps + sl * npair + p) * kMmNI + i) * 32 + lane] = S3[i];
+                }
+            }
+            __syncthreads();
+        }
         for (int i0 = warp * kMmNI; i0 < gn; i0 += kWarps * kMmNI) {
             const int ni = min(kMmNI, gn - i0);
             const char* recs[kMmNI];
 #pragma unroll
             for (int i = 0; i < kMmNI; ++i) recs[i] = rsm + (size_t)(i0 + (i < ni ? i : 0)) * rb;
             long long S[kMmNI], S3[kMmNI];
-            mm_dots<WT>(sm, nch, stride, gst, recs, ni, S);
-            if (OP == kOpGate) mm_dots<WT>(sm + wb, nch, stride, gst, recs, ni, S3);
+            if (nsl > 1) {   // this warp's pair is warp; its slices' sums
+#pragma unroll
+                for (int i = 0; i < kMmNI; ++i) {
+                    S[i] = 0;
+                    S3[i] = 0;
+                    for (int sl = 0; sl < nsl; ++sl) {
+                        S[i] += part[((sl * npair + warp) * kMmNI + i) * 32 + lane];
+                        if (OP == kOpGate) S3[i] += part[((kWarps + sl * npair + warp) * kMmNI + i) * 32 + lane];
+                    }
+                }
+            } else {
+                mm_dots<WT>(sm, nch, stride, 0, nch, recs, ni, S);
+                if (OP == kOpGate) mm_dots<WT>(sm + wb, nch, stride, 0, nch, recs, ni, S3);
+            }
 #pragma unroll
             for (int i = 0; i < kMmNI; ++i) {
                 best[i] = 0ull;
@@ -393,8 +433,8 @@ __global__ void __launch_bounds__(kThreads) k_mmdown(MatSet M2, State s, Batch b
                 rb2[i] = ra[i] + R.lo_b;
             }
             long long Sa[kMmNI], Sb[kMmNI];
-            mm_dots<WT>(sm, Wa.nchunks, sa, g_stride(Wa), ra, ni, Sa);
-            if (two) mm_dots<WT>(sm + wba, Wb.nchunks, sb, g_stride(Wb), rb2, ni, Sb);
+            mm_dots<WT>(sm, Wa.nchunks, sa, 0, Wa.nchunks, ra, ni, Sa);
+            if (two) mm_dots<WT>(sm + wba, Wb.nchunks, sb, 0, Wb.nchunks, rb2, ni, Sb);
 #pragma unroll
             for (int i = 0; i < kMmNI; ++i) {
                 if (i >= ni || row >= Wa.rows) continue;
