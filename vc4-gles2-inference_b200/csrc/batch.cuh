@@ -173,11 +173,13 @@ __device__ __forceinline__ void mm_dots(const char* wsm, int nch, int stride, in
     }
 }
 
-// partial dot products when the warps of a sequence pair split its chunks
+// partial dot products when the warps of a sequence pair split its chunks:
+// reserved only for groups of at most two pairs, the ones that split
 constexpr size_t kMmPartBytes = sizeof(long long) * kWarps * kMmNI * 32 * 2;
+__host__ __device__ inline bool mm_splits_chunks(int group) { return group <= 2 * kMmNI; }
 __host__ __device__ inline size_t mm_smem(const DMat& W, int nmat, int group, int n) {
     return align128(nmat * mm_wbytes(W)) + (size_t)group * xrec_bytes(W) + align16(sizeof(int) * (size_t)n) + 64 +
-           kMmPartBytes;
+           (mm_splits_chunks(group) ? kMmPartBytes : 0);
 }
 
 // matmat: one CTA per 32-row block (blockIdx.x) and expert (blockIdx.y).
@@ -236,12 +238,15 @@ __global__ void __launch_bounds__(kThreads) k_mm(MatSet M, State s, Batch bt, Di
         }
         ok = mbar_wait(&bar[1], (unsigned)gi & 1u);
         if (__syncthreads_or(!ok)) { ok = false; break; }
-        // At most two sequence pairs (six of the eight warps would idle): the
-        // warps of a pair split its chunks into nsl slices and add their exact
-        // partial sums through shared memory.  (With three or more pairs the
-        // extra barrier and sums cost more than the idle warps: c2's wo.)
+        // Groups of at most two sequence pairs (six of the eight warps would
+        // idle): the warps of a pair split its chunks into nsl slices and add
+        // their exact partial sums through shared memory.  Larger groups keep
+        // one warp per pair and no partial-sum space (its 8 KB per CTA cost
+        // c2, whose groups are larger, about 4%).
+        // (not for q4: its gate form then needs 108 registers instead of 68, and
+        // c2, the q4 many-sequence configuration, runs groups too large to split)
         const int npair = (gn + kMmNI - 1) / kMmNI;
-        const int nsl = npair > 2 ? 1 : kWarps / npair;
+        const int nsl = WT != W_Q4 && mm_splits_chunks(group) ? kWarps / npair : 1;
         if (nsl > 1) {
             const int p = warp % npair, sl = warp / npair;
             if (sl < nsl) {
