@@ -195,3 +195,24 @@ def test_perplexity_windows_follow_the_reference_loop(tiny_paths, stride):
         windows += 1
     assert (got["tokens"], got["windows"], got["stride"]) == (cnt, windows, st)
     assert got["nll"] == nll / cnt
+
+
+def test_fnv64_matches_the_reference_constants():
+    """The sidecar's FNV-1a-64 as the reference computes it (common.cpp:63-67,
+    prefix_cache.cpp:94-104): offset basis 1469598103934665603 (the reference's
+    constant; the published FNV basis has one more digit,
+    14695981039346656037, and the sidecar must carry the reference's value),
+    prime 1099511628211, tokens hashed as four little-endian bytes each."""
+    from vc4b200.engine import fnv64
+    basis, prime = 1469598103934665603, 1099511628211
+    assert fnv64(b"") == basis
+    h = basis
+    for b in b"foobar":
+        h = ((h ^ b) * prime) & 0xFFFFFFFFFFFFFFFF
+    assert fnv64(b"foobar") == h == 0x88FAD7C0A8FF07F2
+    toks = [1, 258, 70000]
+    h = basis
+    for t in toks:
+        for k in range(4):
+            h = ((h ^ ((t >> (8 * k)) & 0xFF)) * prime) & 0xFFFFFFFFFFFFFFFF
+    assert fnv64(b"".join(t.to_bytes(4, "little") for t in toks)) == h
